@@ -1,0 +1,112 @@
+"""Fused-MoE math restated in numpy (test infrastructure only).
+
+The pipeline is the reference's 2-stage torch path as its test drives it
+(op_tests/test_moe_2stage.py:187-231):
+
+1. activations quantised 1x128 to fp8 (`pertoken_quant`, aiter/ops/quant.py:42);
+2. `torch_moe_stage1` (aiter/fused_moe.py:1483-1585): dequantise, per-expert
+   `x @ w1[e].T`, then act(gate) * up with gate = first I columns (:1578-1582),
+   cast to bf16;
+3. 1x128 requant of the bf16 intermediate (op_tests/test_moe_2stage.py:203-207);
+4. `torch_moe_stage2` (aiter/fused_moe.py:1588-1666): dequantise, per-expert
+   `a2 @ w2[e].T`, multiply by the top-k weight, sum over the k slots, cast to bf16.
+
+Weights are either fp8 with 128x128 fp32 block scales (QuantType.per_1x128) or
+MXFP4 with e8m0 scales per 32 along K (the A8W4 contract: fp8 1x128 activations
+and intermediate, MXFP4 weights).
+"""
+import numpy as np
+
+from . import codecs, quant
+
+F32 = np.float32
+
+
+def silu(x):
+    x = np.asarray(x, dtype=F32)
+    return (x / (F32(1.0) + np.exp(-x))).astype(F32)
+
+
+def gelu(x):
+    from math import sqrt
+    import numpy as _np
+    x = _np.asarray(x, dtype=_np.float64)
+    from scipy.special import erf  # exact-erf gelu, torch F.gelu default
+    return (0.5 * x * (1.0 + erf(x / sqrt(2.0)))).astype(F32)
+
+
+def stage1(a_deq, w1_deq, topk_ids, activation="silu", expert_list=None):
+    """a_deq: [M, D] f32, w1_deq: callable e -> [2I, D] f32 (or array [E,2I,D]).
+    Returns bf16-rounded f32 [M, k, I]."""
+    M, k = topk_ids.shape
+    get_w = w1_deq if callable(w1_deq) else (lambda e: w1_deq[e])
+    E = int(topk_ids.max()) + 1 if expert_list is None else None
+    experts = np.unique(topk_ids) if expert_list is None else expert_list
+    out = None
+    for e in experts:
+        tok, slot = np.nonzero(topk_ids == e)
+        if tok.size == 0:
+            continue
+        w = get_w(int(e))
+        h = a_deq[tok] @ w.T
+        if out is None:
+            out = np.zeros((M, k, w.shape[0]), dtype=F32)
+        out[tok, slot] = h
+    if out is None:
+        raise ValueError("no routed tokens")
+    inter = out.shape[-1] // 2
+    gate, up = out[..., :inter], out[..., inter:]
+    act = silu(gate) if activation == "silu" else gelu(gate)
+    return codecs.round_bf16((act * up).astype(F32))
+
+
+def stage2(a2_deq, w2_deq, topk_weights, topk_ids, expert_list=None):
+    """a2_deq: [M, k, I] f32; w2_deq: callable e -> [D, I] or array [E, D, I].
+    Returns bf16-rounded f32 [M, D]."""
+    M, k = topk_ids.shape
+    get_w = w2_deq if callable(w2_deq) else (lambda e: w2_deq[e])
+    experts = np.unique(topk_ids) if expert_list is None else expert_list
+    out = None
+    for e in experts:
+        tok, slot = np.nonzero(topk_ids == e)
+        if tok.size == 0:
+            continue
+        w = get_w(int(e))
+        y = a2_deq[tok, slot] @ w.T
+        if out is None:
+            out = np.zeros((M, k, w.shape[0]), dtype=F32)
+        out[tok, slot] = y
+    out = out * np.asarray(topk_weights, dtype=F32)[:, :, None]
+    return codecs.round_bf16(out.sum(axis=1, dtype=F32))
+
+
+def fused_moe_fp8_blockscale(hidden, w1_q, w1_s, w2_q, w2_s, topk_weights, topk_ids,
+                             activation="silu", return_intermediate=False):
+    """QuantType.per_1x128 end to end. hidden: [M, D] bf16 values (f32 array)."""
+    a1_q, a1_s = quant.per_1x128_quant(hidden)
+    a1 = quant.dequant_1x128(a1_q, a1_s)
+    w1 = lambda e: quant.dequant_128x128(w1_q[e:e + 1], w1_s[e:e + 1])[0]
+    w2 = lambda e: quant.dequant_128x128(w2_q[e:e + 1], w2_s[e:e + 1])[0]
+    out1 = stage1(a1, w1, topk_ids, activation)
+    a2_q, a2_s = quant.per_1x128_quant(out1)
+    a2 = quant.dequant_1x128(a2_q, a2_s)
+    out = stage2(a2, w2, topk_weights, topk_ids)
+    if return_intermediate:
+        return out, dict(a1_q=a1_q, a1_s=a1_s, out1=out1, a2_q=a2_q, a2_s=a2_s)
+    return out
+
+
+def fused_moe_a8w4(hidden, w1_p, w1_e, w2_p, w2_e, topk_weights, topk_ids,
+                   activation="silu", return_intermediate=False):
+    """A8W4 as BASELINE defines it: fp8 1x128 activations, MXFP4 weights."""
+    a1_q, a1_s = quant.per_1x128_quant(hidden)
+    a1 = quant.dequant_1x128(a1_q, a1_s)
+    w1 = lambda e: quant.dequant_mxfp4(w1_p[e], w1_e[e])
+    w2 = lambda e: quant.dequant_mxfp4(w2_p[e], w2_e[e])
+    out1 = stage1(a1, w1, topk_ids, activation)
+    a2_q, a2_s = quant.per_1x128_quant(out1)
+    a2 = quant.dequant_1x128(a2_q, a2_s)
+    out = stage2(a2, w2, topk_weights, topk_ids)
+    if return_intermediate:
+        return out, dict(a1_q=a1_q, a1_s=a1_s, out1=out1, a2_q=a2_q, a2_s=a2_s)
+    return out

@@ -1,0 +1,175 @@
+"""Pin the CPU oracle against the reference's own outputs (tests/golden/golden.npz,
+produced by tests/golden/make_golden.py from the reference's torch functions)."""
+import hashlib
+
+import numpy as np
+import pytest
+
+from conftest import golden_group
+from oracle import codecs, inputs, moe, quant, routing, sorting
+
+
+def _sha(a):
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+# ------------------------------------------------------------------ codecs
+
+
+def test_fp8_encode_matches_torch_cast(golden):
+    x = golden["codec/fp8_in"]
+    ref = golden["codec/fp8_out"]
+    got = codecs.fp8_e4m3_encode(x)
+    # NaN codes may differ in sign bit only; compare finite
+    fin = (ref & 0x7F) != 0x7F
+    assert np.array_equal(got[fin], ref[fin])
+    assert np.all((got[~fin] & 0x7F) == 0x7F)
+
+
+def test_mxfp4_decode_all_bytes(golden):
+    ref = golden["codec/mxfp4_all"]            # [512]: 256 bytes -> 2 values each
+    got = codecs.mxfp4_to_f32(np.arange(256, dtype=np.uint8))
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+def test_e8m0_decode_all(golden):
+    ref = golden["codec/e8m0_to_f32_all"]
+    got = codecs.e8m0_to_f32(np.arange(256, dtype=np.uint8))
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+def test_e8m0_encode(golden):
+    got = codecs.f32_to_e8m0(golden["codec/e8m0_in"])
+    assert np.array_equal(got, golden["codec/e8m0_out"])
+
+
+def test_e2m1_encode_grid(golden):
+    got = codecs.pack_fp4(codecs.e2m1_encode(golden["codec/e2m1_in"]))
+    assert np.array_equal(got, golden["codec/e2m1_out"])
+
+
+# ------------------------------------------------------------------ quantisers
+
+
+def test_per_1x128_quant(golden):
+    q, s = quant.per_1x128_quant(golden["quant1x128/x"])
+    assert np.array_equal(s.view(np.uint32), golden["quant1x128/scale"].view(np.uint32))
+    assert np.array_equal(q, golden["quant1x128/q"])
+
+
+def test_weight_128x128_quant(golden):
+    q, s = quant.weight_128x128_quant(golden["quant128x128/w"])
+    assert np.array_equal(s.view(np.uint32), golden["quant128x128/scale"].view(np.uint32))
+    assert np.array_equal(q, golden["quant128x128/q"])
+
+
+def test_per_1x32_f4_quant(golden):
+    q, s = quant.per_1x32_f4_quant(golden["quant1x32/x"])
+    assert np.array_equal(s.reshape(-1), golden["quant1x32/scale"].reshape(-1))
+    assert np.array_equal(q.reshape(-1), golden["quant1x32/q"].reshape(-1))
+
+
+# ------------------------------------------------------------------ sorting
+
+
+@pytest.mark.parametrize("case", ["kat_doc", "m32_e8_k2_b32", "m1_e128_k8_b128", "m100_e16_k4_b32",
+                                  "m300_e128_k8_b64", "m2000_e128_k8_b128", "mask_m64_e16_k4_b32",
+                                  "local_m80_e16_k4_b16"])
+def test_sorting_matches_reference(golden, case):
+    g = golden_group(golden, "sort")[case]
+    M, E, k, B, local = [int(v) for v in g["meta"]]
+    sid, sw, seid, nv = sorting.moe_sorting(g["topk_ids"], g["topk_weights"], E, B,
+                                            g.get("expert_mask"), None if local < 0 else local)
+    assert np.array_equal(nv, g["num_valid_ids"])
+    n = int(nv[0])
+    assert np.array_equal(sid[:n], g["sorted_ids"][:n])
+    init = (k << 24) | M
+    valid = g["sorted_ids"] != init
+    assert np.array_equal(sw[valid].view(np.uint32), g["sorted_weights_valid"].view(np.uint32))
+    m = g["sorted_expert_ids"] != -1
+    assert np.array_equal(seid[m], g["sorted_expert_ids"][m])
+
+
+def test_sorting_doc_kat_layout():
+    """The worked example of csrc/include/moe_sorting_opus.h:276-298, with ids packed
+    as token | slot << 24 and zero-token experts skipped."""
+    ids = np.array([[0, 3, 5], [2, 3, 5], [1, 3, 5], [1, 2, 3], [1, 3, 5]], dtype=np.int32)
+    w = np.arange(15, dtype=np.float32).reshape(5, 3)
+    sid, sw, seid, nv = sorting.moe_sorting(ids, w, 6, 4)
+    tok = sid & 0xFFFFFF
+    assert list(tok[:24]) == [0, 5, 5, 5, 2, 3, 4, 5, 1, 3, 5, 5, 0, 1, 2, 3, 4, 5, 5, 5, 0, 1, 2, 4]
+    assert list(seid[:6]) == [0, 1, 2, 3, 3, 5]
+    assert list(nv) == [24, 5]
+
+
+# ------------------------------------------------------------------ routing
+
+
+def test_topk_softmax_matches_reference(golden):
+    for case, g in golden_group(golden, "topk").items():
+        renorm = case.endswith("_r1")
+        k = g["ids"].shape[1]
+        w, ids, tei = routing.topk_softmax(g["gating"], k, renorm)
+        assert np.array_equal(ids, g["ids"]), case
+        np.testing.assert_allclose(w, g["weights"], rtol=2e-6, atol=1e-7, err_msg=case)
+        M = g["gating"].shape[0]
+        assert tei[1, 0] == 1 and tei[0, 1] == M
+
+
+def _sorted_by_id(ids, w):
+    o = np.argsort(ids, axis=-1)
+    return np.take_along_axis(ids, o, -1), np.take_along_axis(w, o, -1)
+
+
+def test_grouped_topk_matches_reference(golden):
+    for case, g in golden_group(golden, "gtopk").items():
+        M, E, G, TG, k = [int(v) for v in g["meta"]]
+        w, ids = routing.grouped_topk(g["gating"], k, G, TG, True, is_softmax=case.endswith("softmax"))
+        i0, w0 = _sorted_by_id(ids, w)
+        i1, w1 = _sorted_by_id(g["ids"], g["weights"])
+        assert np.array_equal(i0, i1), case
+        np.testing.assert_allclose(w0, w1, rtol=2e-6, atol=1e-7, err_msg=case)
+
+
+def test_biased_grouped_topk_matches_reference(golden):
+    for case, g in golden_group(golden, "btopk").items():
+        M, E, G, TG, k = [int(v) for v in g["meta"]]
+        w, ids = routing.biased_grouped_topk(g["gating"], g["bias"], k, G, TG, True)
+        i0, w0 = _sorted_by_id(ids, w)
+        i1, w1 = _sorted_by_id(g["ids"], g["weights"])
+        assert np.array_equal(i0, i1), case
+        np.testing.assert_allclose(w0, w1, rtol=2e-6, atol=1e-7, err_msg=case)
+
+
+# ------------------------------------------------------------------ MoE pipeline
+
+
+@pytest.mark.parametrize("tag,shape", [("cfg0", (0, 32, 1024, 512, 8, 2)), ("cfg0_m7", (7, 7, 1024, 256, 8, 2))])
+def test_moe_fp8_blockscale_matches_reference(golden, tag, shape):
+    g = golden_group(golden, "moe_fp8")[tag]
+    seed, M, D, I, E, k = shape
+    c = inputs.make_moe_case(seed, M, D, I, E, k)
+    assert np.array_equal(c["topk_ids"], g["topk_ids"])
+    assert _sha(c["w1_q"]) == bytes(g["w1q_sha"]).decode()
+    assert _sha(c["w2_q"]) == bytes(g["w2q_sha"]).decode()
+    assert np.array_equal(c["w1_s"].view(np.uint32), g["w1s"].view(np.uint32))
+    out, st = moe.fused_moe_fp8_blockscale(c["hidden"], c["w1_q"], c["w1_s"], c["w2_q"], c["w2_s"],
+                                           c["topk_weights"], c["topk_ids"], return_intermediate=True)
+    assert np.array_equal(st["a1_q"], g["a1q"])
+    assert np.array_equal(st["a1_s"].view(np.uint32), g["a1s"].view(np.uint32))
+    # fp32 GEMM summation order differs between numpy and torch: bf16 results agree
+    # to a bf16 ulp or so
+    np.testing.assert_allclose(st["out1"], g["out1"], rtol=1e-2, atol=1e-3)
+    np.testing.assert_allclose(out, g["out"], rtol=2e-2, atol=2e-2)
+    assert np.mean(np.abs(out - g["out"]) > 1e-3) < 0.02
+
+
+def test_moe_a8w4_matches_reference(golden):
+    g = golden_group(golden, "moe_a8w4")["cfg0"]
+    c = inputs.make_moe_case(11, 32, 1024, 512, 8, 2, wfmt="mxfp4")
+    assert _sha(c["w1_q"]) == bytes(g["w1p_sha"]).decode()
+    assert np.array_equal(c["w1_s"], g["w1e"])
+    out, st = moe.fused_moe_a8w4(c["hidden"], c["w1_q"], c["w1_s"], c["w2_q"], c["w2_s"],
+                                 c["topk_weights"], c["topk_ids"], return_intermediate=True)
+    np.testing.assert_allclose(st["out1"], g["out1"], rtol=1e-2, atol=1e-3)
+    np.testing.assert_allclose(out, g["out"], rtol=2e-2, atol=2e-2)
