@@ -1,0 +1,27 @@
+"""aiter_b200: the quantised fused-MoE hot path of AITER, written from scratch for
+NVIDIA B200 (sm_100a), behind AITER's Python operator surface.
+
+    import aiter_b200 as aiter
+    w, ids = aiter.fused_topk(x, logits, topk=8, renormalize=True)
+    y = aiter.fused_moe(x, w1, w2, w, ids, quant_type=aiter.QuantType.per_1x128,
+                        w1_scale=s1, w2_scale=s2)
+
+All compute runs in hand-written CUDA kernels of libaiter_b200.so (C ABI,
+include/aiter_b200.h), called through ctypes; there is no CPU fallback.
+"""
+from . import dtypes
+from .enums import ActivationType, QuantType
+from .moe_op import (biased_grouped_topk, biased_grouped_topk_hip, dynamic_per_token_scaled_quant,
+                     grouped_topk, moe_sorting_fwd, moe_sorting_get_workspace_size,
+                     moe_stage1_fp8_blockscale, moe_stage2_fp8_blockscale, per_group_quant_hip,
+                     topk_softmax)
+from .fused_moe import fused_moe, fused_topk, moe_sorting, get_inter_dim
+from ._lib import device_error
+
+__all__ = [
+    "dtypes", "ActivationType", "QuantType", "topk_softmax", "grouped_topk", "biased_grouped_topk",
+    "biased_grouped_topk_hip", "moe_sorting_fwd", "moe_sorting_get_workspace_size",
+    "dynamic_per_token_scaled_quant", "per_group_quant_hip", "moe_stage1_fp8_blockscale",
+    "moe_stage2_fp8_blockscale", "fused_moe", "fused_topk", "moe_sorting", "get_inter_dim",
+    "device_error",
+]

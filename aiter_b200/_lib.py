@@ -1,0 +1,188 @@
+"""ctypes binding of the in-tree C-ABI library (libaiter_b200.so).
+
+Mirrors the reference's torch-free ctypes call path (aiter/jit/core.py:1105-1363):
+tensors travel as `aiter_tensor_t*` (NULL for None), Optional[int] as -1, bools as
+int, floats as float, strings as bytes, and the current CUDA stream of the first
+tensor's device is appended.  A non-zero status raises
+`RuntimeError("<fn> failed: <message>")` with the thread-local message of
+`aiter_get_last_error()`.
+
+There is no fallback: if the library is missing, every op raises.
+"""
+import ctypes
+import os
+import threading
+
+import torch
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libaiter_b200.so")
+
+# AiterDtype values (csrc/include/aiter_enum.h:26-41)
+_DTYPE_CODES = {
+    torch.float8_e4m3fn: 0,
+    torch.float8_e8m0fnu: 1,
+    torch.float16: 2,
+    torch.bfloat16: 3,
+    torch.float32: 4,
+    torch.float4_e2m1fn_x2: 6,
+    torch.uint32: 7,
+    torch.int32: 8,
+    torch.int16: 9,
+    torch.int8: 10,
+    torch.uint8: 11,
+    torch.int64: 12,
+    torch.uint64: 13,
+}
+
+
+class aiter_tensor_t(ctypes.Structure):
+    """Byte-compatible with aiter_tensor_t (csrc/include/aiter_tensor.h:8-18)."""
+    _fields_ = [
+        ("ptr", ctypes.c_void_p),
+        ("numel_", ctypes.c_size_t),
+        ("ndim", ctypes.c_int),
+        ("shape", ctypes.c_int64 * 8),
+        ("strides", ctypes.c_int64 * 8),
+        ("dtype_", ctypes.c_int),
+        ("device_id", ctypes.c_int),
+    ]
+
+
+assert ctypes.sizeof(aiter_tensor_t) == 160
+
+
+def dtype_code(dt):
+    try:
+        return _DTYPE_CODES[dt]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {dt}") from None
+
+
+def to_aiter(t: torch.Tensor) -> aiter_tensor_t:
+    if t.dim() > 8:
+        raise ValueError("at most 8 dims")
+    a = aiter_tensor_t()
+    a.ptr = t.data_ptr() if t.numel() > 0 else 0
+    a.numel_ = t.numel()
+    a.ndim = t.dim()
+    for i, (s, st) in enumerate(zip(t.shape, t.stride())):
+        a.shape[i] = s
+        a.strides[i] = st
+    a.dtype_ = dtype_code(t.dtype)
+    a.device_id = t.device.index if t.is_cuda else -1
+    return a
+
+
+_lock = threading.Lock()
+_lib = None
+
+T = "tensor"
+OT = "opt_tensor"
+I64 = "int"
+OI64 = "opt_int"
+B = "bool"
+F = "float"
+S = "str"
+
+# name -> argument kinds (stream appended) ; ret int status
+SIGNATURES = {
+    "topk_softmax": [T, T, OT, T, B, I64, S],
+    "grouped_topk": [T, T, T, I64, I64, B, B, F],
+    "biased_grouped_topk": [T, T, T, T, I64, I64, B, F],
+    "moe_sorting_fwd": [T, T, T, T, T, T, OT, I64, I64, OT, OT, I64, OT],
+    "dynamic_per_token_scaled_quant": [T, T, T, OT, B, OT, I64],
+    "moe_stage1_fp8_blockscale": [T, T, T, T, T, T, T, I64, T, T, I64, I64],
+    "moe_stage2_fp8_blockscale": [T, T, T, T, T, T, I64, T, T, T, I64],
+}
+
+_CT = {T: ctypes.POINTER(aiter_tensor_t), OT: ctypes.POINTER(aiter_tensor_t), I64: ctypes.c_int64,
+       OI64: ctypes.c_int64, B: ctypes.c_int, F: ctypes.c_float, S: ctypes.c_char_p}
+
+
+def lib():
+    """Load libaiter_b200.so (raises if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing: build it with `python -m aiter_b200.build`")
+        L = ctypes.CDLL(LIB_PATH)
+        L.aiter_ctypes_abi_version.restype = ctypes.c_int
+        L.aiter_get_last_error.restype = ctypes.c_char_p
+        L.aiter_clear_last_error.restype = None
+        L.moe_sorting_get_workspace_size.restype = ctypes.c_int64
+        L.moe_sorting_get_workspace_size.argtypes = [ctypes.c_int64] * 4
+        L.aiter_device_error.restype = ctypes.c_int
+        L.aiter_device_error.argtypes = [ctypes.c_int]
+        for name, kinds in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = ctypes.c_int
+            fn.argtypes = [_CT[k] for k in kinds] + [ctypes.c_void_p]
+        if L.aiter_ctypes_abi_version() != 2:
+            raise RuntimeError("unexpected C ABI version")
+        _lib = L
+    return _lib
+
+
+def call(name, *args, stream=None):
+    """Call entry `name` with Python values converted per SIGNATURES[name]."""
+    L = lib()
+    kinds = SIGNATURES[name]
+    if len(args) != len(kinds):
+        raise TypeError(f"{name}: expected {len(kinds)} arguments, got {len(args)}")
+    cargs = []
+    keep = []
+    device = None
+    for k, v in zip(kinds, args):
+        if k in (T, OT):
+            if v is None:
+                if k == T:
+                    raise TypeError(f"{name}: a required tensor is None")
+                cargs.append(ctypes.POINTER(aiter_tensor_t)())
+            else:
+                if not isinstance(v, torch.Tensor):
+                    raise TypeError(f"{name}: expected a tensor, got {type(v).__name__}")
+                if device is None and v.is_cuda:
+                    device = v.device
+                a = to_aiter(v)
+                keep.append(a)
+                cargs.append(ctypes.byref(a))
+        elif k == OI64:
+            cargs.append(-1 if v is None else int(v))
+        elif k == I64:
+            cargs.append(int(v))
+        elif k == B:
+            cargs.append(1 if v else 0)
+        elif k == F:
+            cargs.append(float(v))
+        elif k == S:
+            cargs.append(None if v is None else v.encode())
+    if stream is None:
+        stream = torch.cuda.current_stream(device).cuda_stream if device is not None else 0
+    L.aiter_clear_last_error()
+    ret = getattr(L, name)(*cargs, ctypes.c_void_p(stream))
+    if ret != 0:
+        raw = L.aiter_get_last_error()
+        msg = raw.decode(errors="replace") if raw else f"status={ret}"
+        L.aiter_clear_last_error()
+        raise RuntimeError(f"{name} failed: {msg}")
+    return None
+
+
+def device_error(clear=True):
+    """Error word of the device-side bounded waits (0 = none, 1 = a wait timed out)."""
+    return lib().aiter_device_error(1 if clear else 0)
+
+
+def exported_symbols():
+    """Entry points declared in include/aiter_b200.h."""
+    import re
+    hdr = os.path.join(os.path.dirname(_PKG), "include", "aiter_b200.h")
+    src = open(hdr).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    names = re.findall(r"^\s*(?:int|int64_t|void|const char\*)\s+\**(\w+)\s*\(", src, flags=re.M)
+    return names

@@ -1,0 +1,492 @@
+// FP8 block-scale grouped GEMMs of the fused MoE, written for sm_100a.
+//
+// Both stages run one persistent, warp-specialised kernel:
+//   warp 0       TMA producer.  A rows are gathered straight from the activation
+//                matrix with tile::gather4 (4 sorted rows per instruction, one
+//                instruction per lane), B tiles are 2-D TMA loads of the expert's
+//                weight rows.  128-byte swizzle, 4-stage smem ring.
+//   warp 1       TMEM allocator and single-thread tcgen05.mma issuer
+//                (kind::f8f6f4, M=128, N=256, K=32 x 4 per 128-wide K block).
+//   warps 4..11  epilogue.  Every 128-wide K block lands in one of two TMEM
+//                accumulator slabs; the epilogue promotes it into fp32 registers
+//                with the block scales, acc += slab * a_scale[row, kb] * w_scale[n, kb]
+//                (the 1x128 / 128x128 scale contract of torch_moe_stage1/2,
+//                aiter/fused_moe.py:1523-1536,1623-1634), while the MMA fills the
+//                other slab.
+// Stage 1 epilogue: act(gate) * up (gate = columns [0, I), up = [I, 2I) of w1,
+// aiter/fused_moe.py:1578-1582), rounded to bf16, then 1x128 fp8 requant
+// (amax / 448) -- the separate requant of aiter/fused_moe.py:1306-1314 fused in.
+// Stage 2 epilogue: multiply by the row's top-k weight and add into the bf16
+// output row of its token with vector red.global.add (the output is zeroed by
+// moe_sorting_fwd), i.e. the scatter-reduce over the k slots.
+#include "sm100.cuh"
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 128, STAGES = 4;
+constexpr int A_TILE = BM * BK;
+constexpr int B_TILE = BN * BK;
+constexpr int STAGE_BYTES = A_TILE + B_TILE;
+constexpr int NUM_THREADS = 384;
+constexpr int TMEM_COLS = 512;
+constexpr uint32_t IDESC = sm100::idesc_e4m3_f32(BM, BN);
+constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + 256 /*barriers*/ + 2 * 256 * 4;
+
+struct GemmArgs {
+    const int* sorted_ids;
+    const int* sorted_eids;
+    const int* num_valid;
+    const float* a_scale;   // [rows of A, num_kb]
+    const float* b_scale;   // [E, N/128, num_kb]
+    const float* sorted_w;  // stage 2
+    void* out;
+    float* out_scale;       // stage 1
+    int M, topk, N, n_tiles, num_kb, max_m_blocks, act, out_cols, E;
+};
+
+__device__ __forceinline__ float act_fn(float g, int act) {
+    if (act == AITER_ACT_GELU) return 0.5f * g * (1.0f + erff(g * 0.70710678118654752f));
+    return g / (1.0f + expf(-g));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ void red_add_bf16x8(__nv_bfloat16* dst, uint32_t a, uint32_t b, uint32_t c,
+                                               uint32_t d) {
+    asm volatile("red.global.add.noftz.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(dst), "r"(a), "r"(b), "r"(c),
+                 "r"(d)
+                 : "memory");
+}
+
+template <int STAGE>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const GemmArgs args) {
+    using namespace sm100;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    float* red = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES + 256);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&tfull[s], 1);
+            mbar_init(&tempty[s], 8);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+        prefetch_tensormap(&tmA);
+        prefetch_tensormap(&tmB);
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int num_m_blocks = min(args.num_valid[0] / BM, args.max_m_blocks);
+    const int num_tiles = num_m_blocks * args.n_tiles;
+
+    if (warp < 4) {
+    setmaxnreg_dec<40>();
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        int it = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+            const int m_blk = tile / args.n_tiles, n_blk = tile % args.n_tiles;
+            const int e = min(max(args.sorted_eids[m_blk], 0), args.E - 1);
+            int rows[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int sid = args.sorted_ids[m_blk * BM + lane * 4 + j];
+                const int tok = sid & 0xFFFFFF, slot = (int)((unsigned)sid >> 24);
+                rows[j] = tok < args.M ? (STAGE == 1 ? tok : tok * args.topk + slot) : 0;
+            }
+            int brow0, brow1;
+            if (STAGE == 1) {
+                brow0 = e * args.N + n_blk * 128;                 // gate rows
+                brow1 = e * args.N + (args.N >> 1) + n_blk * 128; // up rows
+            } else {
+                brow0 = e * args.N + n_blk * 256;
+                brow1 = brow0 + 128;
+            }
+            for (int kb = 0; kb < args.num_kb; ++kb, ++it) {
+                const int s = it % STAGES;
+                const uint32_t ph = (it / STAGES) & 1;
+                ok = __all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1, abort_flag));
+                if (!ok) break;
+                if (lane == 0) mbar_expect_tx(&full[s], STAGE_BYTES);
+                __syncwarp();
+                uint8_t* a = smem + s * STAGE_BYTES;
+                uint8_t* b = a + A_TILE;
+                tma_gather4(a + lane * 512, &tmA, &full[s], kb * BK, rows[0], rows[1], rows[2], rows[3]);
+                if (lane == 0) {
+                    tma_load_2d(b, &tmB, &full[s], kb * BK, brow0);
+                    tma_load_2d(b + 128 * BK, &tmB, &full[s], kb * BK, brow1);
+                }
+            }
+        }
+        // drain: wait for the loads of the last STAGES iterations (bounded)
+        if (!ok) {
+            for (int d = 0; d < STAGES && it - 1 - d >= 0; ++d) {
+                const int j = it - 1 - d;
+                mbar_wait(&full[j % STAGES], (j / STAGES) & 1, abort_flag, 200000000ull, false);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            int it = 0, acc_it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+                for (int kb = 0; kb < args.num_kb; ++kb, ++it, ++acc_it) {
+                    const int s = it % STAGES;
+                    const uint32_t ph = (it / STAGES) & 1;
+                    const int as = acc_it & 1;
+                    const uint32_t aph = (acc_it >> 1) & 1;
+                    if (!mbar_wait(&tempty[as], aph ^ 1, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+                    if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint8_t* a = smem + s * STAGE_BYTES;
+                    const uint64_t adesc = smem_desc_sw128(a);
+                    const uint64_t bdesc = smem_desc_sw128(a + A_TILE);
+                    const uint32_t d = tmem_base + as * BN;
+#pragma unroll
+                    for (int kk = 0; kk < BK / 32; ++kk)
+                        mma_f8f6f4(d, adesc + 2 * kk, bdesc + 2 * kk, IDESC, kk > 0 ? 1u : 0u);
+                    mma_commit(&empty[s]);
+                    mma_commit(&tfull[as]);
+                }
+            }
+            // make sure no MMA is still writing TMEM before teardown
+            if (acc_it > 0) {
+                const int j = acc_it - 1;
+                mbar_wait(&tfull[j & 1], (j >> 1) & 1, abort_flag, 200000000ull, false);
+            }
+        }
+        __syncwarp();
+    }
+    } else {
+        setmaxnreg_inc<232>();
+        // ------------------------------------------------------------ epilogue
+        const int q = warp & 3, h = (warp - 4) >> 2;
+        const int row = q * 32 + lane;
+        const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
+        int acc_it = 0, tcount = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++tcount) {
+            const int m_blk = tile / args.n_tiles, n_blk = tile % args.n_tiles;
+            const int e = min(max(args.sorted_eids[m_blk], 0), args.E - 1);
+            const int sid = args.sorted_ids[m_blk * BM + row];
+            const int tok = sid & 0xFFFFFF, slot = (int)((unsigned)sid >> 24);
+            const bool valid = tok < args.M;
+            const int arow = STAGE == 1 ? tok : tok * args.topk + slot;
+            const float* sa_p = args.a_scale + (int64_t)(valid ? arow : 0) * args.num_kb;
+            const int nblk128 = args.N / 128;
+            const float* sb0_p;
+            const float* sb1_p;
+            if (STAGE == 1) {
+                sb0_p = args.b_scale + ((int64_t)e * nblk128 + n_blk) * args.num_kb;
+                sb1_p = args.b_scale + ((int64_t)e * nblk128 + (nblk128 >> 1) + n_blk) * args.num_kb;
+            } else {
+                sb0_p = args.b_scale + ((int64_t)e * nblk128 + n_blk * 2 + h) * args.num_kb;
+                sb1_p = sb0_p;
+            }
+            float acc[128];
+            float v[64];
+            for (int kb = 0; kb < args.num_kb; ++kb, ++acc_it) {
+                const float sa = valid ? __ldg(sa_p + kb) : 0.f;
+                const float s0 = sa * __ldg(sb0_p + kb);
+                const float s1 = sa * __ldg(sb1_p + kb);
+                const int as = acc_it & 1;
+                const uint32_t aph = (acc_it >> 1) & 1;
+                if (!__all_sync(0xffffffffu, mbar_wait(&tfull[as], aph, abort_flag))) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t t = lane_base + as * BN;
+                // two 64-column halves of this thread's 128 columns
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    const uint32_t col = STAGE == 1 ? (half == 0 ? 64 * h : 128 + 64 * h) : 128 * h + 64 * half;
+                    const float sc = (STAGE == 1 && half == 1) ? s1 : s0;
+                    tmem_ld32(t + col, *reinterpret_cast<float(*)[32]>(&v[0]));
+                    tmem_ld32(t + col + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
+                    tmem_wait_ld();
+                    if (kb == 0) {
+#pragma unroll
+                        for (int j = 0; j < 64; ++j) acc[64 * half + j] = v[j] * sc;
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 64; ++j) acc[64 * half + j] = fmaf(v[j], sc, acc[64 * half + j]);
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[as]);
+            }
+            if (!ok) break;
+            if (STAGE == 1) {
+                float amax = 0.f;
+#pragma unroll
+                for (int j = 0; j < 64; ++j) {
+                    const float y = act_fn(acc[j], args.act) * acc[64 + j];
+                    const float yb = __bfloat162float(__float2bfloat16_rn(y));
+                    acc[j] = yb;
+                    amax = fmaxf(amax, fabsf(yb));
+                }
+                float* rb = red + (tcount & 1) * 256;
+                rb[h * 128 + row] = amax;
+                named_barrier(1, 256);
+                amax = fmaxf(rb[row], rb[128 + row]);
+                float scale = amax / 448.0f;
+                if (scale == 0.f) scale = 1.0f;
+                if (valid) {
+                    const int64_t orow = (int64_t)tok * args.topk + slot;
+                    uint8_t* dst = reinterpret_cast<uint8_t*>(args.out) + orow * args.out_cols + n_blk * 128 + 64 * h;
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        uint32_t w[4];
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const int j = 16 * c + 4 * i;
+                            __nv_fp8x4_e4m3 p4(make_float4(acc[j] / scale, acc[j + 1] / scale, acc[j + 2] / scale,
+                                                           acc[j + 3] / scale));
+                            w[i] = *reinterpret_cast<uint32_t*>(&p4);
+                        }
+                        *reinterpret_cast<uint4*>(dst + 16 * c) = make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+                    if (h == 0) args.out_scale[orow * (args.out_cols / 128) + n_blk] = scale;
+                }
+            } else {
+                const float w = args.sorted_w[m_blk * BM + row];
+                if (valid) {
+                    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.out) + (int64_t)tok * args.out_cols +
+                                         n_blk * 256 + 128 * h;
+#pragma unroll
+                    for (int c = 0; c < 16; ++c) {
+                        const int j = 8 * c;
+                        red_add_bf16x8(dst + j, pack_bf16x2(acc[j] * w, acc[j + 1] * w),
+                                       pack_bf16x2(acc[j + 2] * w, acc[j + 3] * w),
+                                       pack_bf16x2(acc[j + 4] * w, acc[j + 5] * w),
+                                       pack_bf16x2(acc[j + 6] * w, acc[j + 7] * w));
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeFn get_encode() {
+    static EncodeFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        AB_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+        if (q != cudaDriverEntryPointSuccess || !p) ab::fail("cuTensorMapEncodeTiled not available");
+        fn = reinterpret_cast<EncodeFn>(p);
+    }
+    return fn;
+}
+
+}  // namespace
+
+namespace ab {
+void make_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_cols,
+                     uint32_t box_rows, bool swizzle128) {
+    AB_CHECK(((uintptr_t)base & 15) == 0, "TMA base address must be 16-byte aligned");
+    AB_CHECK(cols % 16 == 0, "TMA row pitch must be a multiple of 16 bytes");
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols};
+    cuuint32_t box[2] = {box_cols, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = get_encode()(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
+                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) fail("cuTensorMapEncodeTiled failed with code ", (int)r);
+}
+}  // namespace ab
+
+namespace {
+
+struct Common {
+    int M, topk, E, rowsA, Kdim, Ndim, max_m_blocks;
+};
+
+Common check_sorting(aiter_tensor_t* sorted_token_ids, aiter_tensor_t* sorted_expert_ids,
+                     aiter_tensor_t* num_valid_ids, int64_t block_m) {
+    using namespace ab;
+    need(sorted_token_ids, "sorted_token_ids");
+    need(sorted_expert_ids, "sorted_expert_ids");
+    need(num_valid_ids, "num_valid_ids");
+    need_dtype(sorted_token_ids, AITER_DTYPE_i32, "sorted_token_ids");
+    need_dtype(sorted_expert_ids, AITER_DTYPE_i32, "sorted_expert_ids");
+    need_dtype(num_valid_ids, AITER_DTYPE_i32, "num_valid_ids");
+    AB_CHECK(block_m == BM, "block_m must be ", BM, " for the tcgen05 grouped GEMM, got ", block_m);
+    Common c{};
+    c.max_m_blocks = (int)std::min<int64_t>((int64_t)sorted_token_ids->numel_ / BM, (int64_t)sorted_expert_ids->numel_);
+    return c;
+}
+
+template <int STAGE>
+void launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& a, int dev, cudaStream_t st) {
+    const int tiles = a.max_m_blocks * a.n_tiles;
+    if (tiles == 0) return;
+    const int grid = std::min(tiles, ab::num_sms(dev));
+    AB_CUDA(cudaFuncSetAttribute(moe_gemm_fp8_kernel<STAGE>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    moe_gemm_fp8_kernel<STAGE><<<grid, NUM_THREADS, SMEM_BYTES, st>>>(tmA, tmB, a);
+    ab::check_launch(STAGE == 1 ? "moe_stage1_fp8_blockscale" : "moe_stage2_fp8_blockscale");
+}
+
+}  // namespace
+
+AB_ENTRY(moe_stage1_fp8_blockscale,
+         (aiter_tensor_t * hidden, aiter_tensor_t* w1, aiter_tensor_t* sorted_token_ids,
+          aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids, aiter_tensor_t* out,
+          aiter_tensor_t* out_scale, int64_t topk, aiter_tensor_t* w1_scale, aiter_tensor_t* a1_scale,
+          int64_t block_m, int64_t activation, void* stream),
+         (hidden, w1, sorted_token_ids, sorted_expert_ids, num_valid_ids, out, out_scale, topk, w1_scale,
+          a1_scale, block_m, activation, stream)) {
+    using namespace ab;
+    Common c = check_sorting(sorted_token_ids, sorted_expert_ids, num_valid_ids, block_m);
+    need(hidden, "hidden");
+    need(w1, "w1");
+    need(out, "out");
+    need(out_scale, "out_scale");
+    need(w1_scale, "w1_scale");
+    need(a1_scale, "a1_scale");
+    need_dtype(hidden, AITER_DTYPE_fp8, "hidden");
+    need_dtype(w1, AITER_DTYPE_fp8, "w1");
+    need_dtype(out, AITER_DTYPE_fp8, "out");
+    need_dtype(out_scale, AITER_DTYPE_fp32, "out_scale");
+    need_dtype(w1_scale, AITER_DTYPE_fp32, "w1_scale");
+    need_dtype(a1_scale, AITER_DTYPE_fp32, "a1_scale");
+    for (auto* t : {hidden, w1, out, out_scale, w1_scale, a1_scale}) need_contig(t, "operand");
+    need_ndim(hidden, 2, "hidden");
+    need_ndim(w1, 3, "w1");
+    AB_CHECK(activation == AITER_ACT_SILU || activation == AITER_ACT_GELU, "activation must be Silu or Gelu");
+    const int M = (int)hidden->shape[0], D = (int)hidden->shape[1];
+    const int E = (int)w1->shape[0], N = (int)w1->shape[1];
+    AB_CHECK(w1->shape[2] == D, "w1 K dim must equal hidden dim");
+    AB_CHECK(D % 128 == 0 && N % 256 == 0, "need D % 128 == 0 and 2I % 256 == 0");
+    const int I = N / 2;
+    AB_CHECK((int64_t)out->numel_ == (int64_t)M * topk * I, "out must be [M, topk, I]");
+    AB_CHECK((int64_t)out_scale->numel_ == (int64_t)M * topk * (I / 128), "out_scale must be [M*topk, I/128]");
+    AB_CHECK((int64_t)w1_scale->numel_ == (int64_t)E * (N / 128) * (D / 128), "w1_scale must be [E, 2I/128, D/128]");
+    AB_CHECK((int64_t)a1_scale->numel_ == (int64_t)M * (D / 128), "a1_scale must be [M, D/128]");
+    if (M == 0) return;
+    GemmArgs a{};
+    a.sorted_ids = (const int*)sorted_token_ids->ptr;
+    a.sorted_eids = (const int*)sorted_expert_ids->ptr;
+    a.num_valid = (const int*)num_valid_ids->ptr;
+    a.a_scale = (const float*)a1_scale->ptr;
+    a.b_scale = (const float*)w1_scale->ptr;
+    a.out = out->ptr;
+    a.out_scale = (float*)out_scale->ptr;
+    a.M = M;
+    a.topk = (int)topk;
+    a.N = N;
+    a.n_tiles = I / 128;
+    a.num_kb = D / 128;
+    a.max_m_blocks = c.max_m_blocks;
+    a.act = (int)activation;
+    a.out_cols = I;
+    a.E = E;
+    DeviceGuard dg(hidden->device_id);
+    CUtensorMap tmA, tmB;
+    make_tmap_2d_u8(&tmA, hidden->ptr, M, D, 128, 1, true);
+    make_tmap_2d_u8(&tmB, w1->ptr, (uint64_t)E * N, D, 128, 128, true);
+    launch<1>(tmA, tmB, a, hidden->device_id, as_stream(stream));
+}
+
+AB_ENTRY(moe_stage2_fp8_blockscale,
+         (aiter_tensor_t * inter, aiter_tensor_t* w2, aiter_tensor_t* sorted_token_ids,
+          aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids, aiter_tensor_t* out, int64_t topk,
+          aiter_tensor_t* w2_scale, aiter_tensor_t* a2_scale, aiter_tensor_t* sorted_weights, int64_t block_m,
+          void* stream),
+         (inter, w2, sorted_token_ids, sorted_expert_ids, num_valid_ids, out, topk, w2_scale, a2_scale,
+          sorted_weights, block_m, stream)) {
+    using namespace ab;
+    Common c = check_sorting(sorted_token_ids, sorted_expert_ids, num_valid_ids, block_m);
+    need(inter, "inter");
+    need(w2, "w2");
+    need(out, "out");
+    need(w2_scale, "w2_scale");
+    need(a2_scale, "a2_scale");
+    need(sorted_weights, "sorted_weights");
+    need_dtype(inter, AITER_DTYPE_fp8, "inter");
+    need_dtype(w2, AITER_DTYPE_fp8, "w2");
+    need_dtype(out, AITER_DTYPE_bf16, "out");
+    need_dtype(w2_scale, AITER_DTYPE_fp32, "w2_scale");
+    need_dtype(a2_scale, AITER_DTYPE_fp32, "a2_scale");
+    need_dtype(sorted_weights, AITER_DTYPE_fp32, "sorted_weights");
+    for (auto* t : {inter, w2, out, w2_scale, a2_scale}) need_contig(t, "operand");
+    need_ndim(inter, 3, "inter");
+    need_ndim(w2, 3, "w2");
+    need_ndim(out, 2, "out");
+    const int M = (int)inter->shape[0], I = (int)inter->shape[2];
+    AB_CHECK(inter->shape[1] == topk, "inter must be [M, topk, I]");
+    const int E = (int)w2->shape[0], D = (int)w2->shape[1];
+    AB_CHECK(w2->shape[2] == I, "w2 must be [E, D, I]");
+    AB_CHECK(out->shape[0] == M && out->shape[1] == D, "out must be [M, D]");
+    AB_CHECK(I % 128 == 0 && D % 256 == 0, "need I % 128 == 0 and D % 256 == 0");
+    AB_CHECK((int64_t)w2_scale->numel_ == (int64_t)E * (D / 128) * (I / 128), "w2_scale must be [E, D/128, I/128]");
+    AB_CHECK((int64_t)a2_scale->numel_ == (int64_t)M * topk * (I / 128), "a2_scale must be [M*topk, I/128]");
+    AB_CHECK(((uintptr_t)out->ptr & 15) == 0, "out must be 16-byte aligned");
+    if (M == 0) return;
+    GemmArgs a{};
+    a.sorted_ids = (const int*)sorted_token_ids->ptr;
+    a.sorted_eids = (const int*)sorted_expert_ids->ptr;
+    a.num_valid = (const int*)num_valid_ids->ptr;
+    a.a_scale = (const float*)a2_scale->ptr;
+    a.b_scale = (const float*)w2_scale->ptr;
+    a.sorted_w = (const float*)sorted_weights->ptr;
+    a.out = out->ptr;
+    a.M = M;
+    a.topk = (int)topk;
+    a.N = D;
+    a.n_tiles = D / 256;
+    a.num_kb = I / 128;
+    a.max_m_blocks = c.max_m_blocks;
+    a.out_cols = D;
+    a.E = E;
+    DeviceGuard dg(inter->device_id);
+    CUtensorMap tmA, tmB;
+    make_tmap_2d_u8(&tmA, inter->ptr, (uint64_t)M * topk, I, 128, 1, true);
+    make_tmap_2d_u8(&tmB, w2->ptr, (uint64_t)E * D, I, 128, 128, true);
+    launch<2>(tmA, tmB, a, inter->device_id, as_stream(stream));
+}
+
+extern "C" int aiter_device_error(int clear) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, sm100::g_device_error, sizeof(int)) != cudaSuccess) return -1;
+    if (clear) {
+        int z = 0;
+        cudaMemcpyToSymbol(sm100::g_device_error, &z, sizeof(int));
+    }
+    return v;
+}

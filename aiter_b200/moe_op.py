@@ -1,0 +1,112 @@
+"""Operator stubs of the path, same names and argument meaning as the reference's
+`@compile_ops` stubs, each calling one C-ABI entry point of libaiter_b200.so.
+
+Reference stubs:
+* topk_softmax              aiter/ops/moe_op.py:15-24
+* grouped_topk              aiter/ops/topk.py:28-38
+* biased_grouped_topk       aiter/ops/topk.py:75-113 (the HIP / moe_fused_gate
+                            split of :87-113 is one kernel here)
+* moe_sorting_fwd           aiter/ops/moe_sorting.py:11-24
+* dynamic_per_token_scaled_quant  aiter/ops/quant.py:473-481
+* per_group_quant_hip       aiter/ops/quant.py:261-292
+* ck_moe_stage1_fwd / ck_moe_stage2_fwd  aiter/ops/moe_op.py:534-615 -> here
+  moe_stage1_fp8_blockscale (with the fused fp8 requant) / moe_stage2_fp8_blockscale
+"""
+from typing import Optional, Tuple
+
+import torch
+from torch import Tensor
+
+from . import _lib, dtypes
+from .enums import ActivationType
+
+
+def topk_softmax(topk_weights: Tensor, topk_indices: Tensor, token_expert_indices: Tensor,
+                 gating_output: Tensor, need_renorm: bool, num_shared_experts: int = 0,
+                 shared_expert_scoring_func: str = "") -> None:
+    _lib.call("topk_softmax", topk_weights, topk_indices, token_expert_indices, gating_output,
+              need_renorm, num_shared_experts, shared_expert_scoring_func)
+
+
+def grouped_topk(gating_output: Tensor, topk_weights: Tensor, topk_ids: Tensor, num_expert_group: int,
+                 topk_group: int, need_renorm: bool, is_softmax: bool = True,
+                 routed_scaling_factor: float = 1.0) -> None:
+    _lib.call("grouped_topk", gating_output, topk_weights, topk_ids, num_expert_group, topk_group,
+              need_renorm, is_softmax, routed_scaling_factor)
+
+
+def biased_grouped_topk(gating_output: Tensor, correction_bias: Tensor, topk_weights: Tensor,
+                        topk_ids: Tensor, num_expert_group: int, topk_group: int, need_renorm: bool,
+                        routed_scaling_factor: float = 1.0) -> None:
+    _lib.call("biased_grouped_topk", gating_output, correction_bias, topk_weights, topk_ids,
+              num_expert_group, topk_group, need_renorm, routed_scaling_factor)
+
+
+biased_grouped_topk_hip = biased_grouped_topk
+
+
+def moe_sorting_get_workspace_size(num_tokens: int, num_experts: int, topk: int,
+                                   dispatch_policy: int = 0) -> int:
+    return int(_lib.lib().moe_sorting_get_workspace_size(num_tokens, num_experts, topk, dispatch_policy))
+
+
+def moe_sorting_fwd(topk_ids: Tensor, topk_weights: Tensor, sorted_token_ids: Tensor,
+                    sorted_weights: Tensor, sorted_expert_ids: Tensor, num_valid_ids: Tensor,
+                    moe_buf: Tensor, num_experts: int, unit_size: int,
+                    local_expert_mask: Optional[Tensor] = None,
+                    num_local_tokens: Optional[Tensor] = None, dispatch_policy: int = 0,
+                    workspace: Optional[Tensor] = None) -> None:
+    """In place.  Allocates the workspace itself when none is given, as the
+    reference binding does (csrc/py_itfs_ck/moe_sorting_kernels.cu:33-40)."""
+    M, topk = topk_ids.shape
+    if workspace is None:
+        ws = moe_sorting_get_workspace_size(M, num_experts, topk, dispatch_policy)
+        if ws > 0:
+            workspace = torch.empty(ws, dtype=torch.uint8, device=topk_ids.device)
+    _lib.call("moe_sorting_fwd", topk_ids, topk_weights, sorted_token_ids, sorted_weights,
+              sorted_expert_ids, num_valid_ids, moe_buf, num_experts, unit_size,
+              local_expert_mask, num_local_tokens, dispatch_policy, workspace)
+
+
+def dynamic_per_token_scaled_quant(out: Tensor, input: Tensor, scales: Tensor,
+                                   scale_ub: Optional[Tensor] = None, shuffle_scale: bool = False,
+                                   num_rows: Optional[Tensor] = None, num_rows_factor: int = 1) -> None:
+    _lib.call("dynamic_per_token_scaled_quant", out, input, scales, scale_ub, shuffle_scale,
+              num_rows, num_rows_factor)
+
+
+def per_group_quant_hip(x: Tensor, scale: Optional[Tensor] = None, quant_dtype=dtypes.fp8,
+                        group_size: int = 128, transpose_scale: bool = False,
+                        num_rows: Optional[Tensor] = None, num_rows_factor: int = 1) -> Tuple[Tensor, Tensor]:
+    """1 x group_size dynamic quantisation -> (fp8 [.., K], f32 scales [.., K/group])."""
+    if scale is not None:
+        raise ValueError("unsupported: static per group quant")
+    if quant_dtype != dtypes.fp8:
+        raise ValueError(f"unsupported quant dtype {quant_dtype}")
+    if group_size not in (32, 64, 128):
+        raise ValueError(f"unsupported group size {group_size=}, only support [32, 64, 128]")
+    shape = x.shape
+    x = x.contiguous()
+    scale = torch.empty((*shape[:-1], shape[-1] // group_size), dtype=dtypes.fp32, device=x.device)
+    y = torch.empty(shape, dtype=quant_dtype, device=x.device)
+    dynamic_per_token_scaled_quant(y, x.view(-1, group_size), scale, shuffle_scale=transpose_scale,
+                                   num_rows=num_rows, num_rows_factor=num_rows_factor)
+    return y, scale
+
+
+def moe_stage1_fp8_blockscale(hidden_states: Tensor, w1: Tensor, sorted_token_ids: Tensor,
+                              sorted_expert_ids: Tensor, num_valid_ids: Tensor, out: Tensor,
+                              out_scale: Tensor, topk: int, w1_scale: Tensor, a1_scale: Tensor,
+                              block_m: int = 128, activation=ActivationType.Silu) -> Tuple[Tensor, Tensor]:
+    _lib.call("moe_stage1_fp8_blockscale", hidden_states, w1, sorted_token_ids, sorted_expert_ids,
+              num_valid_ids, out, out_scale, topk, w1_scale, a1_scale, block_m, int(activation))
+    return out, out_scale
+
+
+def moe_stage2_fp8_blockscale(inter_states: Tensor, w2: Tensor, sorted_token_ids: Tensor,
+                              sorted_expert_ids: Tensor, num_valid_ids: Tensor, out: Tensor, topk: int,
+                              w2_scale: Tensor, a2_scale: Tensor, sorted_weights: Tensor,
+                              block_m: int = 128) -> Tensor:
+    _lib.call("moe_stage2_fp8_blockscale", inter_states, w2, sorted_token_ids, sorted_expert_ids,
+              num_valid_ids, out, topk, w2_scale, a2_scale, sorted_weights, block_m)
+    return out

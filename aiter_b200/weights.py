@@ -1,0 +1,93 @@
+"""Weight preparation on the device (host-side setup, not the hot path).
+
+* `quant_weight_128x128`  fp8 e4m3fn weights with fp32 scales per 128x128 block,
+  the quantiser of op_tests/test_moe_2stage.py:84-110 (amax / 448, 0 -> 1).
+* `quant_weight_mxfp4`    e2m1 values packed two per byte (low nibble first) with
+  e8m0 scales per 32 along K, the quantiser of aiter/ops/quant.py:75-106.
+Weights are [E, N, K] with K contiguous (no AMD pre-shuffle).
+"""
+import torch
+
+from . import dtypes
+
+
+@torch.no_grad()
+def quant_weight_128x128(w: torch.Tensor, chunk: int = 8):
+    E, N, K = w.shape
+    assert N % 128 == 0 and K % 128 == 0
+    q = torch.empty((E, N, K), dtype=dtypes.fp8, device=w.device)
+    s = torch.empty((E, N // 128, K // 128), dtype=torch.float32, device=w.device)
+    for e0 in range(0, E, chunk):
+        blk = w[e0:e0 + chunk].float().view(-1, N // 128, 128, K // 128, 128)
+        amax = blk.abs().amax(dim=(2, 4), keepdim=True)
+        sc = amax / dtypes.FP8_MAX
+        sc = torch.where(sc == 0, torch.ones_like(sc), sc)
+        q[e0:e0 + chunk] = (blk / sc).to(dtypes.fp8).view(-1, N, K)
+        s[e0:e0 + chunk] = sc.view(-1, N // 128, K // 128)
+    return q, s
+
+
+def _f32_to_e8m0(x: torch.Tensor) -> torch.Tensor:
+    """Biased exponent, rounded up when mantissa bit 22 is set and (bit 21, any
+    lower bit, or a non-zero exponent) -- aiter/utility/fp4_utils.py:49-58."""
+    u = x.contiguous().view(torch.int32)
+    exp = ((u >> 23) & 0xFF)
+    rnd = ((u & 0x400000) != 0) & (((u & 0x200000) != 0) | ((u & 0x1FFFFF) != 0) | (exp > 0))
+    out = exp + rnd.to(torch.int32)
+    out = torch.where(exp == 0xFF, torch.full_like(out, 0xFF), out & 0xFF)
+    return out.to(torch.uint8)
+
+
+def _e8m0_to_f32(e: torch.Tensor) -> torch.Tensor:
+    bits = e.to(torch.int32) << 23
+    bits = torch.where(e == 0, torch.full_like(bits, 0x00400000), bits)
+    bits = torch.where(e == 0xFF, torch.full_like(bits, 0x7F800001), bits)
+    return bits.view(torch.float32)
+
+
+_E2M1_POS = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0)
+
+
+def _e2m1_encode(y: torch.Tensor) -> torch.Tensor:
+    """Round-to-nearest-even onto the e2m1 grid, saturating at 6 (codes 0..15)."""
+    a = y.abs().clamp(max=6.0)
+    q = torch.where(a < 2.0, torch.full_like(a, 0.5), torch.where(a < 4.0, torch.ones_like(a), torch.full_like(a, 2.0)))
+    r = torch.round(a / q) * q                     # torch.round is half-to-even
+    r = r.clamp(max=6.0)
+    grid = torch.tensor(_E2M1_POS, device=y.device)
+    code = torch.searchsorted(grid, r.contiguous())
+    code = code | (torch.signbit(y).to(code.dtype) << 3)
+    return code.to(torch.uint8)
+
+
+@torch.no_grad()
+def quant_weight_mxfp4(w: torch.Tensor, chunk: int = 4):
+    """-> (packed fp4x2 as uint8 [E, N, K/2], e8m0 uint8 [E, N, K/32])."""
+    E, N, K = w.shape
+    assert K % 32 == 0
+    packed = torch.empty((E, N, K // 2), dtype=torch.uint8, device=w.device)
+    scales = torch.empty((E, N, K // 32), dtype=torch.uint8, device=w.device)
+    for e0 in range(0, E, chunk):
+        x = w[e0:e0 + chunk].float().reshape(-1, 32)
+        amax = x.abs().amax(dim=1)
+        e = _f32_to_e8m0(amax / 4.0)
+        y = x / _e8m0_to_f32(e)[:, None]
+        c = _e2m1_encode(y).view(-1, N, K)
+        n = c.shape[0]
+        packed[e0:e0 + n] = c[..., 0::2] | (c[..., 1::2] << 4)
+        scales[e0:e0 + n] = e.view(n, N, K // 32)
+    return packed, scales
+
+
+def dequant_128x128(q: torch.Tensor, s: torch.Tensor) -> torch.Tensor:
+    E, N, K = q.shape
+    return (q.float().view(E, N // 128, 128, K // 128, 128) * s[:, :, None, :, None]).view(E, N, K)
+
+
+def dequant_mxfp4(packed: torch.Tensor, e8m0: torch.Tensor) -> torch.Tensor:
+    grid = torch.tensor(_E2M1_POS + tuple(-v for v in _E2M1_POS), device=packed.device)
+    lo = grid[(packed & 0xF).long()]
+    hi = grid[(packed >> 4).long()]
+    v = torch.stack([lo, hi], dim=-1).flatten(-2)
+    sh = v.shape
+    return (v.view(*sh[:-1], sh[-1] // 32, 32) * _e8m0_to_f32(e8m0)[..., None]).view(sh)

@@ -1,0 +1,161 @@
+/*
+ * aiter_b200 -- C ABI of the B200 (sm_100a) fused-MoE hot path.
+ *
+ * Every entry point mirrors a ctypes-mode operator of the reference
+ * (aiter/jit/core.py:1105-1363): tensors are passed as `aiter_tensor_t*`
+ * (NULL for None), Python ints as int64_t (-1 for None), bools as int,
+ * floats as float, strings as const char* (may be NULL), and the CUDA stream is
+ * appended last.  Each call returns 0 on success and -1 on error; the message is
+ * kept in thread-local storage and read with aiter_get_last_error()
+ * (csrc/include/aiter_ctypes_error.h:56-130).  Exceptions never cross this
+ * boundary.  Kernels never allocate or free caller memory; every output tensor is
+ * owned by the caller.
+ */
+#ifndef AITER_B200_H
+#define AITER_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types: same values as AiterDtype (csrc/include/aiter_enum.h:26-41). */
+typedef enum {
+    AITER_DTYPE_fp8 = 0,      /* float8_e4m3fn */
+    AITER_DTYPE_fp8_e8m0 = 1,
+    AITER_DTYPE_fp16 = 2,
+    AITER_DTYPE_bf16 = 3,
+    AITER_DTYPE_fp32 = 4,
+    AITER_DTYPE_i4x2 = 5,
+    AITER_DTYPE_fp4x2 = 6,    /* two e2m1 values per byte, element 2i in the low nibble */
+    AITER_DTYPE_u32 = 7,
+    AITER_DTYPE_i32 = 8,
+    AITER_DTYPE_i16 = 9,
+    AITER_DTYPE_i8 = 10,
+    AITER_DTYPE_u8 = 11,
+    AITER_DTYPE_i64 = 12,
+    AITER_DTYPE_u64 = 13
+} AiterDtype;
+
+/* Activation / quantisation enums (csrc/include/aiter_enum.h:7-25). */
+enum { AITER_ACT_NO = -1, AITER_ACT_SILU = 0, AITER_ACT_GELU = 1, AITER_ACT_SWIGLU = 2 };
+enum {
+    AITER_QUANT_NO = 0, AITER_QUANT_PER_TENSOR = 1, AITER_QUANT_PER_TOKEN = 2,
+    AITER_QUANT_PER_1X32 = 3, AITER_QUANT_PER_1X128 = 4, AITER_QUANT_PER_128X128 = 5
+};
+
+/* Tensor descriptor, byte-compatible with aiter_tensor_t
+ * (csrc/include/aiter_tensor.h:8-18; 160 bytes, aiter/utility/aiter_types.py:68-86).
+ * Strides are in elements; `ptr` is device memory. */
+typedef struct aiter_tensor_t {
+    void* ptr;
+    size_t numel_;
+    int ndim;
+    int64_t shape[8];
+    int64_t strides[8];
+    int dtype_;
+    int device_id;
+} aiter_tensor_t;
+
+/* ---- error bridge: csrc/include/aiter_ctypes_error.h:56-67 ---------------- */
+int aiter_ctypes_abi_version(void);            /* returns 2 */
+const char* aiter_get_last_error(void);        /* NULL when no error */
+void aiter_clear_last_error(void);
+
+/* Device-side error word of the bounded waits inside the kernels: 0 = none,
+ * 1 = a wait ran out of time (the kernel then returned early).  `clear` resets it.
+ * Has no counterpart in the reference, whose waits are unbounded
+ * (csrc/include/custom_all_reduce.cuh:150-252). */
+int aiter_device_error(int clear);
+
+/* ---- routing ------------------------------------------------------------- */
+
+/* Replaces aiter.topk_softmax (aiter/ops/moe_op.py:15-24 ->
+ * csrc/kernels/topk_softmax_kernels.cu:760).  gating_output [M, E(+shared)]
+ * bf16/fp16/fp32 (row stride allowed); topk_weights [M, k(+shared)] f32,
+ * topk_indices [M, k] i32, token_expert_indices [M, k] i32 (= slot*M + row).
+ * Ties resolve to the lower expert index. */
+int topk_softmax(aiter_tensor_t* topk_weights, aiter_tensor_t* topk_indices,
+                 aiter_tensor_t* token_expert_indices, aiter_tensor_t* gating_output,
+                 int need_renorm, int64_t num_shared_experts,
+                 const char* shared_expert_scoring_func, void* stream);
+
+/* Replaces aiter.grouped_topk (aiter/ops/topk.py:28-38 ->
+ * csrc/kernels/topk_softmax_kernels_group.cu:1265-1300). */
+int grouped_topk(aiter_tensor_t* gating_output, aiter_tensor_t* topk_weights,
+                 aiter_tensor_t* topk_ids, int64_t num_expert_group, int64_t topk_group,
+                 int need_renorm, int is_softmax, float routed_scaling_factor, void* stream);
+
+/* Replaces aiter.biased_grouped_topk (aiter/ops/topk.py:15-25 / :75-113 ->
+ * csrc/kernels/topk_softmax_kernels_group.cu:1219-1263). */
+int biased_grouped_topk(aiter_tensor_t* gating_output, aiter_tensor_t* correction_bias,
+                        aiter_tensor_t* topk_weights, aiter_tensor_t* topk_ids,
+                        int64_t num_expert_group, int64_t topk_grp, int need_renorm,
+                        float routed_scaling_factor, void* stream);
+
+/* ---- sorting ------------------------------------------------------------- */
+
+/* Workspace bytes moe_sorting_fwd needs for these sizes (0 = none).
+ * Replaces moe_sorting_get_workspace_size (csrc/py_itfs_ck/moe_sorting_kernels.cu:35). */
+int64_t moe_sorting_get_workspace_size(int64_t num_tokens, int64_t num_experts, int64_t topk,
+                                       int64_t dispatch_policy);
+
+/* Replaces aiter.moe_sorting_fwd (aiter/ops/moe_sorting.py:11-24 ->
+ * csrc/py_itfs_ck/moe_sorting_kernels.cu:10-76).  Outputs are written in place;
+ * moe_buf[:tokens] is zeroed.  `workspace` (u8/i32, >= the size above) is the
+ * scratch the reference binding allocates itself; it may be NULL when the size
+ * above is 0.  num_local_tokens is read on the device (no host sync). */
+int moe_sorting_fwd(aiter_tensor_t* topk_ids, aiter_tensor_t* topk_weights,
+                    aiter_tensor_t* sorted_token_ids, aiter_tensor_t* sorted_weights,
+                    aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids,
+                    aiter_tensor_t* moe_buf, int64_t num_experts, int64_t unit_size,
+                    aiter_tensor_t* local_expert_mask, aiter_tensor_t* num_local_tokens,
+                    int64_t dispatch_policy, aiter_tensor_t* workspace, void* stream);
+
+/* ---- quantisation -------------------------------------------------------- */
+
+/* Replaces aiter.dynamic_per_token_scaled_quant as per_group_quant_hip drives it
+ * (aiter/ops/quant.py:261-292,473-481 -> csrc/kernels/quant_kernels.cu:20-133):
+ * input viewed as [rows, group] bf16/fp16/fp32 -> out fp8 e4m3fn, scales f32
+ * [rows] (= [M, K/group]); scale = amax/448 (0 -> 1), q = x / scale.
+ * shuffle_scale writes scales transposed ([K/group, M]).  num_rows (device i32
+ * [1], may be NULL) limits the rows processed to num_rows[0]*num_rows_factor*K/group. */
+int dynamic_per_token_scaled_quant(aiter_tensor_t* out, aiter_tensor_t* input,
+                                   aiter_tensor_t* scales, aiter_tensor_t* scale_ub,
+                                   int shuffle_scale, aiter_tensor_t* num_rows,
+                                   int64_t num_rows_factor, void* stream);
+
+/* ---- grouped GEMMs (FP8 block-scale, tcgen05) ----------------------------- */
+
+/* Stage 1: replaces ck_moe_stage1_fwd + the intermediate requant
+ * (aiter/ops/moe_op.py:534-575, aiter/fused_moe.py:1306-1314; CK template
+ * csrc/ck_gemm_moe_2stages_codegen/gemm_moe_ck2stages_common_blockscale.cuh:9-180).
+ * hidden [M, D] fp8 + a1_scale [M, D/128] f32; w1 [E, 2I, D] fp8 + w1_scale
+ * [E, 2I/128, D/128] f32; sorted ids / expert ids / num_valid_ids from
+ * moe_sorting_fwd with unit_size == block_m (64 or 128).
+ * Writes out [M, topk, I] fp8 = quant(act(gate)*up) and out_scale [M*topk, I/128] f32
+ * (1x128 groups).  activation: AITER_ACT_SILU or AITER_ACT_GELU. */
+int moe_stage1_fp8_blockscale(aiter_tensor_t* hidden, aiter_tensor_t* w1,
+                              aiter_tensor_t* sorted_token_ids, aiter_tensor_t* sorted_expert_ids,
+                              aiter_tensor_t* num_valid_ids, aiter_tensor_t* out,
+                              aiter_tensor_t* out_scale, int64_t topk, aiter_tensor_t* w1_scale,
+                              aiter_tensor_t* a1_scale, int64_t block_m, int64_t activation,
+                              void* stream);
+
+/* Stage 2: replaces ck_moe_stage2_fwd (aiter/ops/moe_op.py:578-615; CK template
+ * gemm_moe_ck2stages_common_blockscale.cuh:330-470).
+ * inter [M, topk, I] fp8 + a2_scale [M*topk, I/128] f32; w2 [E, D, I] fp8 +
+ * w2_scale [E, D/128, I/128] f32.  Adds sorted_weights[r] * (a2 @ w2[e]^T) of
+ * every sorted row r into out[token] (bf16 [M, D], zeroed by moe_sorting_fwd). */
+int moe_stage2_fp8_blockscale(aiter_tensor_t* inter, aiter_tensor_t* w2,
+                              aiter_tensor_t* sorted_token_ids, aiter_tensor_t* sorted_expert_ids,
+                              aiter_tensor_t* num_valid_ids, aiter_tensor_t* out, int64_t topk,
+                              aiter_tensor_t* w2_scale, aiter_tensor_t* a2_scale,
+                              aiter_tensor_t* sorted_weights, int64_t block_m, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* AITER_B200_H */
