@@ -12,7 +12,7 @@ include/aiter_b200.h), called through ctypes; there is no CPU fallback.
 from . import dtypes
 from .enums import ActivationType, QuantType
 from .moe_op import (biased_grouped_topk, biased_grouped_topk_hip, dynamic_per_token_scaled_quant,
-                     grouped_topk, moe_sorting_fwd, moe_sorting_get_workspace_size,
+                     grouped_topk, moe_gather_quant_1x128, moe_sorting_fwd, moe_sorting_get_workspace_size,
                      moe_stage1_fp8_blockscale, moe_stage2_fp8_blockscale, per_group_quant_hip,
                      topk_softmax)
 from .fused_moe import fused_moe, fused_topk, moe_sorting, get_inter_dim
@@ -20,7 +20,7 @@ from ._lib import device_error
 
 __all__ = [
     "dtypes", "ActivationType", "QuantType", "topk_softmax", "grouped_topk", "biased_grouped_topk",
-    "biased_grouped_topk_hip", "moe_sorting_fwd", "moe_sorting_get_workspace_size",
+    "biased_grouped_topk_hip", "moe_gather_quant_1x128", "moe_sorting_fwd", "moe_sorting_get_workspace_size",
     "dynamic_per_token_scaled_quant", "per_group_quant_hip", "moe_stage1_fp8_blockscale",
     "moe_stage2_fp8_blockscale", "fused_moe", "fused_topk", "moe_sorting", "get_inter_dim",
     "device_error",

@@ -90,10 +90,11 @@ SIGNATURES = {
     "topk_softmax": [T, T, OT, T, B, I64, S],
     "grouped_topk": [T, T, T, I64, I64, B, B, F],
     "biased_grouped_topk": [T, T, T, T, I64, I64, B, F],
-    "moe_sorting_fwd": [T, T, T, T, T, T, OT, I64, I64, OT, OT, I64, OT],
+    "moe_sorting_fwd": [T, T, T, T, T, T, OT, I64, I64, OT, OT, I64, OT, OT],
     "dynamic_per_token_scaled_quant": [T, T, T, OT, B, OT, I64],
-    "moe_stage1_fp8_blockscale": [T, T, T, T, T, T, T, I64, T, T, I64, I64],
-    "moe_stage2_fp8_blockscale": [T, T, T, T, T, T, I64, T, T, T, I64],
+    "moe_gather_quant_1x128": [T, OT, T, I64, T, T],
+    "moe_stage1_fp8_blockscale": [T, T, T, T, T, T, T, T, T, I64, I64, I64],
+    "moe_stage2_fp8_blockscale": [T, T, T, T, T, T, T, T, T, I64],
 }
 
 _CT = {T: ctypes.POINTER(aiter_tensor_t), OT: ctypes.POINTER(aiter_tensor_t), I64: ctypes.c_int64,

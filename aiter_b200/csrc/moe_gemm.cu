@@ -1,10 +1,11 @@
 // FP8 block-scale grouped GEMMs of the fused MoE, written for sm_100a.
 //
 // Both stages run one persistent, warp-specialised kernel:
-//   warp 0       TMA producer.  A rows are gathered straight from the activation
-//                matrix with tile::gather4 (4 sorted rows per instruction, one
-//                instruction per lane), B tiles are 2-D TMA loads of the expert's
-//                weight rows.  128-byte swizzle, 4-stage smem ring.
+//   warp 0       TMA producer.  A is stored in sorted-row order (written by
+//                moe_gather_quant_1x128 for stage 1 and by the stage-1 epilogue for
+//                stage 2), so every operand tile is one plain 2-D TMA box: A =
+//                128 sorted rows x 128 K, B = 2 x 128 weight rows x 128 K.
+//                128-byte swizzle, 4-stage smem ring.
 //   warp 1       TMEM allocator and single-thread tcgen05.mma issuer
 //                (kind::f8f6f4, M=128, N=256, K=32 x 4 per 128-wide K block).
 //   warps 4..11  epilogue.  Every 128-wide K block lands in one of two TMEM
@@ -15,7 +16,10 @@
 //                other slab.
 // Stage 1 epilogue: act(gate) * up (gate = columns [0, I), up = [I, 2I) of w1,
 // aiter/fused_moe.py:1578-1582), rounded to bf16, then 1x128 fp8 requant
-// (amax / 448) -- the separate requant of aiter/fused_moe.py:1306-1314 fused in.
+// (amax / 448) -- the separate requant of aiter/fused_moe.py:1306-1314 fused in --
+// written to the sorted row it was computed for.
+// Scales of the sorted activations are stored transposed, [K/128][rows], so each
+// epilogue warp reads its 32 rows' scales of one K block with one coalesced load.
 // Stage 2 epilogue: multiply by the row's top-k weight and add into the bf16
 // output row of its token with vector red.global.add (the output is zeroed by
 // moe_sorting_fwd), i.e. the scatter-reduce over the k slots.
@@ -36,12 +40,12 @@ struct GemmArgs {
     const int* sorted_ids;
     const int* sorted_eids;
     const int* num_valid;
-    const float* a_scale;   // [rows of A, num_kb]
+    const float* a_scale;   // [num_kb][rows_pad], sorted rows
     const float* b_scale;   // [E, N/128, num_kb]
     const float* sorted_w;  // stage 2
-    void* out;
-    float* out_scale;       // stage 1
-    int M, topk, N, n_tiles, num_kb, max_m_blocks, act, out_cols, E;
+    void* out;              // stage 1: fp8 [rows_pad, I] sorted; stage 2: bf16 [M, D]
+    float* out_scale;       // stage 1: [I/128][rows_pad]
+    int M, N, n_tiles, num_kb, max_m_blocks, act, out_cols, E, rows_pad;
 };
 
 __device__ __forceinline__ float act_fn(float g, int act) {
@@ -109,13 +113,6 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
             const int m_blk = tile / args.n_tiles, n_blk = tile % args.n_tiles;
             const int e = min(max(args.sorted_eids[m_blk], 0), args.E - 1);
-            int rows[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int sid = args.sorted_ids[m_blk * BM + lane * 4 + j];
-                const int tok = sid & 0xFFFFFF, slot = (int)((unsigned)sid >> 24);
-                rows[j] = tok < args.M ? (STAGE == 1 ? tok : tok * args.topk + slot) : 0;
-            }
             int brow0, brow1;
             if (STAGE == 1) {
                 brow0 = e * args.N + n_blk * 128;                 // gate rows
@@ -133,8 +130,8 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 __syncwarp();
                 uint8_t* a = smem + s * STAGE_BYTES;
                 uint8_t* b = a + A_TILE;
-                tma_gather4(a + lane * 512, &tmA, &full[s], kb * BK, rows[0], rows[1], rows[2], rows[3]);
                 if (lane == 0) {
+                    tma_load_2d(a, &tmA, &full[s], kb * BK, m_blk * BM);
                     tma_load_2d(b, &tmB, &full[s], kb * BK, brow0);
                     tma_load_2d(b + 128 * BK, &tmB, &full[s], kb * BK, brow1);
                 }
@@ -193,10 +190,10 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             const int m_blk = tile / args.n_tiles, n_blk = tile % args.n_tiles;
             const int e = min(max(args.sorted_eids[m_blk], 0), args.E - 1);
             const int sid = args.sorted_ids[m_blk * BM + row];
-            const int tok = sid & 0xFFFFFF, slot = (int)((unsigned)sid >> 24);
+            const int tok = sid & 0xFFFFFF;
             const bool valid = tok < args.M;
-            const int arow = STAGE == 1 ? tok : tok * args.topk + slot;
-            const float* sa_p = args.a_scale + (int64_t)(valid ? arow : 0) * args.num_kb;
+            const int srow = m_blk * BM + row;
+            const float* sa_p = args.a_scale + srow;
             const int nblk128 = args.N / 128;
             const float* sb0_p;
             const float* sb1_p;
@@ -209,16 +206,23 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             }
             float acc[128];
             float v[64];
+            float sa_next = valid ? __ldg(sa_p) : 0.f;
+            float sb0_next = __ldg(sb0_p), sb1_next = __ldg(sb1_p);
             for (int kb = 0; kb < args.num_kb; ++kb, ++acc_it) {
-                const float sa = valid ? __ldg(sa_p + kb) : 0.f;
-                const float s0 = sa * __ldg(sb0_p + kb);
-                const float s1 = sa * __ldg(sb1_p + kb);
+                const float s0 = sa_next * sb0_next;
+                const float s1 = sa_next * sb1_next;
+                if (kb + 1 < args.num_kb) {  // prefetch the next K block's scales
+                    sa_next = valid ? __ldg(sa_p + (int64_t)(kb + 1) * args.rows_pad) : 0.f;
+                    sb0_next = __ldg(sb0_p + kb + 1);
+                    sb1_next = __ldg(sb1_p + kb + 1);
+                }
                 const int as = acc_it & 1;
                 const uint32_t aph = (acc_it >> 1) & 1;
                 if (!__all_sync(0xffffffffu, mbar_wait(&tfull[as], aph, abort_flag))) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t t = lane_base + as * BN;
-                // two 64-column halves of this thread's 128 columns
+                // this thread's 128 columns in two 64-column halves; the slab is
+                // released as soon as the second half is in registers
 #pragma unroll
                 for (int half = 0; half < 2; ++half) {
                     const uint32_t col = STAGE == 1 ? (half == 0 ? 64 * h : 128 + 64 * h) : 128 * h + 64 * half;
@@ -226,6 +230,11 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                     tmem_ld32(t + col, *reinterpret_cast<float(*)[32]>(&v[0]));
                     tmem_ld32(t + col + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
                     tmem_wait_ld();
+                    if (half == 1) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&tempty[as]);
+                    }
                     if (kb == 0) {
 #pragma unroll
                         for (int j = 0; j < 64; ++j) acc[64 * half + j] = v[j] * sc;
@@ -234,9 +243,6 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                         for (int j = 0; j < 64; ++j) acc[64 * half + j] = fmaf(v[j], sc, acc[64 * half + j]);
                     }
                 }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&tempty[as]);
             }
             if (!ok) break;
             if (STAGE == 1) {
@@ -255,8 +261,7 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 float scale = amax / 448.0f;
                 if (scale == 0.f) scale = 1.0f;
                 if (valid) {
-                    const int64_t orow = (int64_t)tok * args.topk + slot;
-                    uint8_t* dst = reinterpret_cast<uint8_t*>(args.out) + orow * args.out_cols + n_blk * 128 + 64 * h;
+                    uint8_t* dst = reinterpret_cast<uint8_t*>(args.out) + (int64_t)srow * args.out_cols + n_blk * 128 + 64 * h;
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
                         uint32_t w[4];
@@ -269,10 +274,10 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                         }
                         *reinterpret_cast<uint4*>(dst + 16 * c) = make_uint4(w[0], w[1], w[2], w[3]);
                     }
-                    if (h == 0) args.out_scale[orow * (args.out_cols / 128) + n_blk] = scale;
+                    if (h == 0) args.out_scale[(int64_t)n_blk * args.rows_pad + srow] = scale;
                 }
             } else {
-                const float w = args.sorted_w[m_blk * BM + row];
+                const float w = args.sorted_w[srow];
                 if (valid) {
                     __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.out) + (int64_t)tok * args.out_cols +
                                          n_blk * 256 + 128 * h;
@@ -333,11 +338,12 @@ void make_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t
 
 namespace {
 
-struct Common {
-    int M, topk, E, rowsA, Kdim, Ndim, max_m_blocks;
+struct Sorted {
+    int rows_pad;       // sorted_token_ids length (max_num_tokens_padded)
+    int max_m_blocks;
 };
 
-Common check_sorting(aiter_tensor_t* sorted_token_ids, aiter_tensor_t* sorted_expert_ids,
+Sorted check_sorting(aiter_tensor_t* sorted_token_ids, aiter_tensor_t* sorted_expert_ids,
                      aiter_tensor_t* num_valid_ids, int64_t block_m) {
     using namespace ab;
     need(sorted_token_ids, "sorted_token_ids");
@@ -347,9 +353,25 @@ Common check_sorting(aiter_tensor_t* sorted_token_ids, aiter_tensor_t* sorted_ex
     need_dtype(sorted_expert_ids, AITER_DTYPE_i32, "sorted_expert_ids");
     need_dtype(num_valid_ids, AITER_DTYPE_i32, "num_valid_ids");
     AB_CHECK(block_m == BM, "block_m must be ", BM, " for the tcgen05 grouped GEMM, got ", block_m);
-    Common c{};
+    Sorted c{};
+    c.rows_pad = (int)sorted_token_ids->numel_;
     c.max_m_blocks = (int)std::min<int64_t>((int64_t)sorted_token_ids->numel_ / BM, (int64_t)sorted_expert_ids->numel_);
     return c;
+}
+
+// Sorted-row operand: [rows_pad, K] fp8 with scales [K/128, rows_pad] f32.
+void check_sorted_operand(aiter_tensor_t* a, aiter_tensor_t* sc, int rows_pad, const char* an, const char* sn) {
+    using namespace ab;
+    need(a, an);
+    need(sc, sn);
+    need_dtype(a, AITER_DTYPE_fp8, an);
+    need_dtype(sc, AITER_DTYPE_fp32, sn);
+    need_contig(a, an);
+    need_contig(sc, sn);
+    need_ndim(a, 2, an);
+    AB_CHECK(a->shape[0] == rows_pad, an, " must have one row per sorted slot (", rows_pad, ")");
+    AB_CHECK(a->shape[1] % 128 == 0, an, " K must be a multiple of 128");
+    AB_CHECK((int64_t)sc->numel_ == (a->shape[1] / 128) * (int64_t)rows_pad, sn, " must be [K/128, rows]");
 }
 
 template <int STAGE>
@@ -365,40 +387,33 @@ void launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& a, i
 }  // namespace
 
 AB_ENTRY(moe_stage1_fp8_blockscale,
-         (aiter_tensor_t * hidden, aiter_tensor_t* w1, aiter_tensor_t* sorted_token_ids,
-          aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids, aiter_tensor_t* out,
-          aiter_tensor_t* out_scale, int64_t topk, aiter_tensor_t* w1_scale, aiter_tensor_t* a1_scale,
-          int64_t block_m, int64_t activation, void* stream),
-         (hidden, w1, sorted_token_ids, sorted_expert_ids, num_valid_ids, out, out_scale, topk, w1_scale,
-          a1_scale, block_m, activation, stream)) {
+         (aiter_tensor_t * a1, aiter_tensor_t* a1_scale, aiter_tensor_t* w1, aiter_tensor_t* w1_scale,
+          aiter_tensor_t* sorted_token_ids, aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids,
+          aiter_tensor_t* out, aiter_tensor_t* out_scale, int64_t num_tokens, int64_t block_m, int64_t activation,
+          void* stream),
+         (a1, a1_scale, w1, w1_scale, sorted_token_ids, sorted_expert_ids, num_valid_ids, out, out_scale, num_tokens,
+          block_m, activation, stream)) {
     using namespace ab;
-    Common c = check_sorting(sorted_token_ids, sorted_expert_ids, num_valid_ids, block_m);
-    need(hidden, "hidden");
+    Sorted c = check_sorting(sorted_token_ids, sorted_expert_ids, num_valid_ids, block_m);
+    check_sorted_operand(a1, a1_scale, c.rows_pad, "a1", "a1_scale");
     need(w1, "w1");
-    need(out, "out");
-    need(out_scale, "out_scale");
     need(w1_scale, "w1_scale");
-    need(a1_scale, "a1_scale");
-    need_dtype(hidden, AITER_DTYPE_fp8, "hidden");
     need_dtype(w1, AITER_DTYPE_fp8, "w1");
-    need_dtype(out, AITER_DTYPE_fp8, "out");
-    need_dtype(out_scale, AITER_DTYPE_fp32, "out_scale");
     need_dtype(w1_scale, AITER_DTYPE_fp32, "w1_scale");
-    need_dtype(a1_scale, AITER_DTYPE_fp32, "a1_scale");
-    for (auto* t : {hidden, w1, out, out_scale, w1_scale, a1_scale}) need_contig(t, "operand");
-    need_ndim(hidden, 2, "hidden");
+    need_contig(w1, "w1");
+    need_contig(w1_scale, "w1_scale");
     need_ndim(w1, 3, "w1");
     AB_CHECK(activation == AITER_ACT_SILU || activation == AITER_ACT_GELU, "activation must be Silu or Gelu");
-    const int M = (int)hidden->shape[0], D = (int)hidden->shape[1];
+    const int D = (int)a1->shape[1];
     const int E = (int)w1->shape[0], N = (int)w1->shape[1];
-    AB_CHECK(w1->shape[2] == D, "w1 K dim must equal hidden dim");
-    AB_CHECK(D % 128 == 0 && N % 256 == 0, "need D % 128 == 0 and 2I % 256 == 0");
+    AB_CHECK(w1->shape[2] == D, "w1 K dim must equal the activation width");
+    AB_CHECK(N % 256 == 0, "2 * inter_dim must be a multiple of 256");
     const int I = N / 2;
-    AB_CHECK((int64_t)out->numel_ == (int64_t)M * topk * I, "out must be [M, topk, I]");
-    AB_CHECK((int64_t)out_scale->numel_ == (int64_t)M * topk * (I / 128), "out_scale must be [M*topk, I/128]");
+    check_sorted_operand(out, out_scale, c.rows_pad, "out", "out_scale");
+    AB_CHECK(out->shape[1] == I, "out must be [rows, inter_dim]");
     AB_CHECK((int64_t)w1_scale->numel_ == (int64_t)E * (N / 128) * (D / 128), "w1_scale must be [E, 2I/128, D/128]");
-    AB_CHECK((int64_t)a1_scale->numel_ == (int64_t)M * (D / 128), "a1_scale must be [M, D/128]");
-    if (M == 0) return;
+    AB_CHECK(num_tokens >= 0 && num_tokens < (1 << 24), "bad num_tokens");
+    if (num_tokens == 0) return;
     GemmArgs a{};
     a.sorted_ids = (const int*)sorted_token_ids->ptr;
     a.sorted_eids = (const int*)sorted_expert_ids->ptr;
@@ -407,8 +422,7 @@ AB_ENTRY(moe_stage1_fp8_blockscale,
     a.b_scale = (const float*)w1_scale->ptr;
     a.out = out->ptr;
     a.out_scale = (float*)out_scale->ptr;
-    a.M = M;
-    a.topk = (int)topk;
+    a.M = (int)num_tokens;
     a.N = N;
     a.n_tiles = I / 128;
     a.num_kb = D / 128;
@@ -416,46 +430,42 @@ AB_ENTRY(moe_stage1_fp8_blockscale,
     a.act = (int)activation;
     a.out_cols = I;
     a.E = E;
-    DeviceGuard dg(hidden->device_id);
+    a.rows_pad = c.rows_pad;
+    DeviceGuard dg(a1->device_id);
     CUtensorMap tmA, tmB;
-    make_tmap_2d_u8(&tmA, hidden->ptr, M, D, 128, 1, true);
+    make_tmap_2d_u8(&tmA, a1->ptr, (uint64_t)c.rows_pad, D, 128, 128, true);
     make_tmap_2d_u8(&tmB, w1->ptr, (uint64_t)E * N, D, 128, 128, true);
-    launch<1>(tmA, tmB, a, hidden->device_id, as_stream(stream));
+    launch<1>(tmA, tmB, a, a1->device_id, as_stream(stream));
 }
 
 AB_ENTRY(moe_stage2_fp8_blockscale,
-         (aiter_tensor_t * inter, aiter_tensor_t* w2, aiter_tensor_t* sorted_token_ids,
-          aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids, aiter_tensor_t* out, int64_t topk,
-          aiter_tensor_t* w2_scale, aiter_tensor_t* a2_scale, aiter_tensor_t* sorted_weights, int64_t block_m,
-          void* stream),
-         (inter, w2, sorted_token_ids, sorted_expert_ids, num_valid_ids, out, topk, w2_scale, a2_scale,
-          sorted_weights, block_m, stream)) {
+         (aiter_tensor_t * a2, aiter_tensor_t* a2_scale, aiter_tensor_t* w2, aiter_tensor_t* w2_scale,
+          aiter_tensor_t* sorted_token_ids, aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids,
+          aiter_tensor_t* sorted_weights, aiter_tensor_t* out, int64_t block_m, void* stream),
+         (a2, a2_scale, w2, w2_scale, sorted_token_ids, sorted_expert_ids, num_valid_ids, sorted_weights, out,
+          block_m, stream)) {
     using namespace ab;
-    Common c = check_sorting(sorted_token_ids, sorted_expert_ids, num_valid_ids, block_m);
-    need(inter, "inter");
+    Sorted c = check_sorting(sorted_token_ids, sorted_expert_ids, num_valid_ids, block_m);
+    check_sorted_operand(a2, a2_scale, c.rows_pad, "a2", "a2_scale");
     need(w2, "w2");
-    need(out, "out");
     need(w2_scale, "w2_scale");
-    need(a2_scale, "a2_scale");
+    need(out, "out");
     need(sorted_weights, "sorted_weights");
-    need_dtype(inter, AITER_DTYPE_fp8, "inter");
     need_dtype(w2, AITER_DTYPE_fp8, "w2");
-    need_dtype(out, AITER_DTYPE_bf16, "out");
     need_dtype(w2_scale, AITER_DTYPE_fp32, "w2_scale");
-    need_dtype(a2_scale, AITER_DTYPE_fp32, "a2_scale");
+    need_dtype(out, AITER_DTYPE_bf16, "out");
     need_dtype(sorted_weights, AITER_DTYPE_fp32, "sorted_weights");
-    for (auto* t : {inter, w2, out, w2_scale, a2_scale}) need_contig(t, "operand");
-    need_ndim(inter, 3, "inter");
+    for (auto* t : {w2, w2_scale, out}) need_contig(t, "operand");
     need_ndim(w2, 3, "w2");
     need_ndim(out, 2, "out");
-    const int M = (int)inter->shape[0], I = (int)inter->shape[2];
-    AB_CHECK(inter->shape[1] == topk, "inter must be [M, topk, I]");
+    AB_CHECK((int64_t)sorted_weights->numel_ >= c.rows_pad, "sorted_weights too small");
+    const int I = (int)a2->shape[1];
     const int E = (int)w2->shape[0], D = (int)w2->shape[1];
+    const int M = (int)out->shape[0];
     AB_CHECK(w2->shape[2] == I, "w2 must be [E, D, I]");
-    AB_CHECK(out->shape[0] == M && out->shape[1] == D, "out must be [M, D]");
-    AB_CHECK(I % 128 == 0 && D % 256 == 0, "need I % 128 == 0 and D % 256 == 0");
+    AB_CHECK(out->shape[1] == D, "out must be [M, D]");
+    AB_CHECK(D % 256 == 0, "model_dim must be a multiple of 256");
     AB_CHECK((int64_t)w2_scale->numel_ == (int64_t)E * (D / 128) * (I / 128), "w2_scale must be [E, D/128, I/128]");
-    AB_CHECK((int64_t)a2_scale->numel_ == (int64_t)M * topk * (I / 128), "a2_scale must be [M*topk, I/128]");
     AB_CHECK(((uintptr_t)out->ptr & 15) == 0, "out must be 16-byte aligned");
     if (M == 0) return;
     GemmArgs a{};
@@ -467,18 +477,18 @@ AB_ENTRY(moe_stage2_fp8_blockscale,
     a.sorted_w = (const float*)sorted_weights->ptr;
     a.out = out->ptr;
     a.M = M;
-    a.topk = (int)topk;
     a.N = D;
     a.n_tiles = D / 256;
     a.num_kb = I / 128;
     a.max_m_blocks = c.max_m_blocks;
     a.out_cols = D;
     a.E = E;
-    DeviceGuard dg(inter->device_id);
+    a.rows_pad = c.rows_pad;
+    DeviceGuard dg(a2->device_id);
     CUtensorMap tmA, tmB;
-    make_tmap_2d_u8(&tmA, inter->ptr, (uint64_t)M * topk, I, 128, 1, true);
+    make_tmap_2d_u8(&tmA, a2->ptr, (uint64_t)c.rows_pad, I, 128, 128, true);
     make_tmap_2d_u8(&tmB, w2->ptr, (uint64_t)E * D, I, 128, 128, true);
-    launch<2>(tmA, tmB, a, inter->device_id, as_stream(stream));
+    launch<2>(tmA, tmB, a, a2->device_id, as_stream(stream));
 }
 
 extern "C" int aiter_device_error(int clear) {

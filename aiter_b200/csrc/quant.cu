@@ -154,3 +154,133 @@ AB_ENTRY(dynamic_per_token_scaled_quant,
     }
     check_launch("dynamic_per_token_scaled_quant");
 }
+
+// ---------------------------------------------------------------------------
+// 1x128 quantisation scattered into sorted-row order (the A operand of the stage-1
+// grouped GEMM).  Token t is quantised once (the arithmetic of group_quant_kernel
+// above, `pertoken_quant` over 128 groups, aiter/ops/quant.py:42-72) and stored to
+// the sorted rows pos[t * topk + s] of its slots (-1 = not routed here).  Scales
+// are written transposed, [K/128][rows], for coalesced reads in the GEMM
+// epilogue.  With an fp8 input (`hidden_scale` given, [M, K/128]) the rows and
+// scales are copied instead -- fused_moe's pre-quantised input path
+// (aiter/fused_moe.py:259-265).
+namespace {
+
+template <typename T, bool PREQ>
+__global__ void __launch_bounds__(256)
+scatter_quant_kernel(const T* __restrict__ x, const float* __restrict__ xs, const int* __restrict__ pos,
+                     uint8_t* __restrict__ q, float* __restrict__ st, int M, int K, int topk, int rows_pad) {
+    const int gpr = K / 128;
+    const int64_t total_lanes = (int64_t)M * gpr * 16;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < ((total_lanes + 31) / 32) * 32;
+         t += stride) {
+        const int64_t g = t >> 4;
+        const int sub = (int)(t & 15);
+        const bool on = t < total_lanes;
+        const int tok = on ? (int)(g / gpr) : 0;
+        const int c = on ? (int)(g % gpr) : 0;
+        uint2 packed = make_uint2(0, 0);
+        float scale = 0.f;
+        if constexpr (PREQ) {
+            if (on) {
+                packed = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint8_t*>(x) + (int64_t)tok * K + c * 128 + sub * 8);
+                scale = xs[(int64_t)tok * gpr + c];
+            }
+        } else {
+            float v[8];
+            if (on) {
+                Vec8<T>::load(x + (int64_t)tok * K + c * 128 + sub * 8, v);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = 0.f;
+            }
+            float amax = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            scale = amax / 448.0f;
+            if (scale == 0.f) scale = 1.0f;
+            uint32_t w[2];
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                __nv_fp8x4_e4m3 p4(make_float4(v[4 * i] / scale, v[4 * i + 1] / scale, v[4 * i + 2] / scale,
+                                               v[4 * i + 3] / scale));
+                w[i] = *reinterpret_cast<uint32_t*>(&p4);
+            }
+            packed = make_uint2(w[0], w[1]);
+        }
+        if (!on) continue;
+        for (int s = 0; s < topk; ++s) {
+            const int r = pos[(int64_t)tok * topk + s];
+            if (r < 0 || r >= rows_pad) continue;
+            *reinterpret_cast<uint2*>(q + (int64_t)r * K + c * 128 + sub * 8) = packed;
+            if (sub == 0) st[(int64_t)c * rows_pad + r] = scale;
+        }
+    }
+}
+
+}  // namespace
+
+AB_ENTRY(moe_gather_quant_1x128,
+         (aiter_tensor_t * hidden, aiter_tensor_t* hidden_scale, aiter_tensor_t* token_sorted_pos, int64_t topk,
+          aiter_tensor_t* out, aiter_tensor_t* out_scale, void* stream),
+         (hidden, hidden_scale, token_sorted_pos, topk, out, out_scale, stream)) {
+    using namespace ab;
+    need(hidden, "hidden");
+    need(token_sorted_pos, "token_sorted_pos");
+    need(out, "out");
+    need(out_scale, "out_scale");
+    need_ndim(hidden, 2, "hidden");
+    need_contig(hidden, "hidden");
+    need_contig(out, "out");
+    need_contig(out_scale, "out_scale");
+    need_dtype(token_sorted_pos, AITER_DTYPE_i32, "token_sorted_pos");
+    need_dtype(out, AITER_DTYPE_fp8, "out");
+    need_dtype(out_scale, AITER_DTYPE_fp32, "out_scale");
+    const int M = (int)hidden->shape[0], K = (int)hidden->shape[1];
+    AB_CHECK(topk >= 1 && (int64_t)token_sorted_pos->numel_ >= M * topk, "token_sorted_pos must be [M * topk]");
+    AB_CHECK(K % 128 == 0, "hidden width must be a multiple of 128");
+    AB_CHECK(out->ndim == 2 && out->shape[1] == K, "out must be [rows, K]");
+    const int rows_pad = (int)out->shape[0];
+    AB_CHECK((int64_t)out_scale->numel_ == (int64_t)rows_pad * (K / 128), "out_scale must be [K/128, rows]");
+    AB_CHECK(((uintptr_t)hidden->ptr & 15) == 0 && ((uintptr_t)out->ptr & 15) == 0, "misaligned buffers");
+    const bool preq = hidden->dtype_ == AITER_DTYPE_fp8;
+    if (preq) {
+        need(hidden_scale, "hidden_scale");
+        need_dtype(hidden_scale, AITER_DTYPE_fp32, "hidden_scale");
+        need_contig(hidden_scale, "hidden_scale");
+        AB_CHECK((int64_t)hidden_scale->numel_ == (int64_t)M * (K / 128), "hidden_scale must be [M, K/128]");
+    }
+    if (M == 0 || rows_pad == 0) return;
+    DeviceGuard dg(hidden->device_id);
+    const int dev = hidden->device_id;
+    const int64_t lanes = (int64_t)M * (K / 128) * 16;
+    const int blocks = (int)std::min<int64_t>((lanes + 255) / 256, (int64_t)num_sms(dev) * 8);
+    cudaStream_t st = as_stream(stream);
+    const int* pos = (const int*)token_sorted_pos->ptr;
+    uint8_t* q = (uint8_t*)out->ptr;
+    float* sc = (float*)out_scale->ptr;
+    const int k = (int)topk;
+    switch (hidden->dtype_) {
+        case AITER_DTYPE_bf16:
+            scatter_quant_kernel<__nv_bfloat16, false><<<blocks, 256, 0, st>>>(
+                (const __nv_bfloat16*)hidden->ptr, nullptr, pos, q, sc, M, K, k, rows_pad);
+            break;
+        case AITER_DTYPE_fp16:
+            scatter_quant_kernel<__half, false><<<blocks, 256, 0, st>>>((const __half*)hidden->ptr, nullptr, pos, q, sc,
+                                                                       M, K, k, rows_pad);
+            break;
+        case AITER_DTYPE_fp32:
+            scatter_quant_kernel<float, false><<<blocks, 256, 0, st>>>((const float*)hidden->ptr, nullptr, pos, q, sc,
+                                                                      M, K, k, rows_pad);
+            break;
+        case AITER_DTYPE_fp8:
+            scatter_quant_kernel<uint8_t, true><<<blocks, 256, 0, st>>>(
+                (const uint8_t*)hidden->ptr, (const float*)hidden_scale->ptr, pos, q, sc, M, K, k, rows_pad);
+            break;
+        default: fail("hidden must be bf16, fp16, fp32 or fp8");
+    }
+    check_launch("moe_gather_quant_1x128");
+}

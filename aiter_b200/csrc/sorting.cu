@@ -38,6 +38,7 @@ struct SortArgs {
     uint8_t* moe_buf;
     int64_t moe_row_bytes;
     int* counts;  // workspace [nchunks][E]
+    int* inv;     // optional [M * topk]: sorted row of (token, slot), -1 if not routed here
 };
 
 __device__ __forceinline__ int num_tokens(const SortArgs& a) {
@@ -130,11 +131,14 @@ __device__ void scatter_chunk(const SortArgs& a, int chunk, const int* off, int*
     for (int i = tid; i < 32 * a.E; i += kThreads) wcnt[i] = 0;
     __syncthreads();
     const int t0 = chunk * a.tpc;
-    const int n_ent = max(0, min(a.tpc, tokens - t0)) * a.topk;
+    const int n_ent = max(0, min(a.tpc, tokens - t0)) * a.topk;   // routed entries
+    const int n_all = max(0, min(a.tpc, a.M - t0)) * a.topk;      // rows of the inverse map
     int e = -1, t = 0, s = 0;
-    if (tid < n_ent) {
+    if (tid < n_all) {
         t = t0 + tid / a.topk;
         s = tid % a.topk;
+    }
+    if (tid < n_ent) {
         e = a.topk_ids[(int64_t)t * a.topk + s];
         if (!expert_on(a, e)) e = -1;
     }
@@ -157,6 +161,9 @@ __device__ void scatter_chunk(const SortArgs& a, int chunk, const int* off, int*
         const int pos = off[e] + wcnt[warp * a.E + e] + rank;
         a.sorted_ids[pos] = t | (s << 24);
         a.sorted_w[pos] = a.topk_w[(int64_t)t * a.topk + s];
+        if (a.inv) a.inv[(int64_t)t * a.topk + s] = pos;
+    } else if (a.inv && tid < n_all) {
+        a.inv[(int64_t)t * a.topk + s] = -1;
     }
     __syncthreads();
 }
@@ -184,7 +191,8 @@ __global__ void __launch_bounds__(kThreads) sort_oneshot_kernel(SortArgs a) {
     __syncthreads();
     build_bases(a, tot, base, scratch, true);
     // base[e] advances chunk by chunk; tot is reused for the chunk counts
-    for (int c = 0; c * a.tpc < tokens; ++c) {
+    const int rows_done = a.inv ? a.M : tokens;
+    for (int c = 0; c * a.tpc < rows_done; ++c) {
         scatter_chunk(a, c, base, wcnt, tot);
         for (int e = tid; e < a.E; e += kThreads) base[e] += tot[e];
         __syncthreads();
@@ -263,10 +271,11 @@ AB_ENTRY(moe_sorting_fwd,
           aiter_tensor_t* sorted_weights, aiter_tensor_t* sorted_expert_ids,
           aiter_tensor_t* num_valid_ids, aiter_tensor_t* moe_buf, int64_t num_experts,
           int64_t unit_size, aiter_tensor_t* local_expert_mask, aiter_tensor_t* num_local_tokens,
-          int64_t dispatch_policy, aiter_tensor_t* workspace, void* stream),
+          int64_t dispatch_policy, aiter_tensor_t* workspace, aiter_tensor_t* token_sorted_pos,
+          void* stream),
          (topk_ids, topk_weights, sorted_token_ids, sorted_weights, sorted_expert_ids,
           num_valid_ids, moe_buf, num_experts, unit_size, local_expert_mask, num_local_tokens,
-          dispatch_policy, workspace, stream)) {
+          dispatch_policy, workspace, token_sorted_pos, stream)) {
     using namespace ab;
     need(topk_ids, "topk_ids");
     need(topk_weights, "topk_weights");
@@ -301,6 +310,10 @@ AB_ENTRY(moe_sorting_fwd,
         AB_CHECK((int64_t)local_expert_mask->numel_ >= num_experts, "local_expert_mask too small");
     }
     if (num_local_tokens) need_dtype(num_local_tokens, AITER_DTYPE_i32, "num_local_tokens");
+    if (token_sorted_pos) {
+        need_dtype(token_sorted_pos, AITER_DTYPE_i32, "token_sorted_pos");
+        AB_CHECK((int64_t)token_sorted_pos->numel_ >= M * K, "token_sorted_pos needs M*topk elements");
+    }
 
     SortArgs a{};
     a.topk_ids = (const int*)topk_ids->ptr;
@@ -317,6 +330,7 @@ AB_ENTRY(moe_sorting_fwd,
     a.B = (int)unit_size;
     a.tpc = tokens_per_chunk((int)K);
     a.nchunks = (int)((M + a.tpc - 1) / a.tpc);
+    a.inv = token_sorted_pos ? (int*)token_sorted_pos->ptr : nullptr;
     int64_t moe_bytes = 0;
     if (moe_buf && moe_buf->numel_ > 0) {
         need_contig(moe_buf, "moe_buf");

@@ -6,10 +6,11 @@
 * `get_inter_dim`, `get_padded_M`  aiter/fused_moe.py:108-115,606-612
 
 The per_1x128 (== per_128x128, aiter/fused_moe.py:597) path runs four kernels of
-libaiter_b200.so on the current stream, with no host synchronisation:
-moe_sorting_fwd (also zeroes the output) -> 1x128 fp8 activation quant ->
-stage-1 grouped GEMM (gate/up, act, fp8 requant fused) -> stage-2 grouped GEMM
-(top-k weighted scatter-add into the output).  Weights are taken unshuffled
+libaiter_b200.so on the current stream (five launches when sorting takes its
+multi-CTA form), with no host synchronisation: moe_sorting_fwd (also zeroes the
+output) -> gather + 1x128 fp8 activation quant into sorted-row order -> stage-1
+grouped GEMM (gate/up, act, fp8 requant fused; sorted rows out) -> stage-2
+grouped GEMM (top-k weighted scatter-add into the output).  Weights are taken unshuffled
 ([E, 2I, D] / [E, D, I], K contiguous); AMD pre-shuffled weights
 (`is_shuffled=True`, aiter/ops/shuffle.py:7-27) are rejected.
 """
@@ -66,10 +67,8 @@ def get_2stage_cfgs(padded_M, model_dim, inter_dim, expert, topk, dtype, q_dtype
     return MOEMetadata(block_m=BLOCK_SIZE_M)
 
 
-def moe_sorting(topk_ids, topk_weights, num_experts, model_dim, moebuf_dtype, block_size=BLOCK_SIZE_M,
-                expert_mask=None, num_local_tokens=None, dispatch_policy=0):
-    """Returns (sorted_ids, sorted_weights, sorted_expert_ids, num_valid_ids, moe_buf);
-    moe_buf [M, model_dim] is zeroed."""
+def _moe_sorting_ext(topk_ids, topk_weights, num_experts, model_dim, moebuf_dtype, block_size,
+                     expert_mask=None, num_local_tokens=None, dispatch_policy=0, with_pos=False):
     device = topk_ids.device
     M, topk = topk_ids.shape
     max_num_tokens_padded = int(topk_ids.numel() + num_experts * block_size - topk)
@@ -79,10 +78,19 @@ def moe_sorting(topk_ids, topk_weights, num_experts, model_dim, moebuf_dtype, bl
     sorted_expert_ids = torch.empty(max_num_m_blocks, dtype=dtypes.i32, device=device)
     num_valid_ids = torch.empty(2, dtype=dtypes.i32, device=device)
     moe_buf = torch.empty((M, model_dim), dtype=moebuf_dtype, device=device)
+    pos = torch.empty(M * topk, dtype=dtypes.i32, device=device) if with_pos else None
     moe_op.moe_sorting_fwd(topk_ids, topk_weights, sorted_ids, sorted_weights, sorted_expert_ids,
                            num_valid_ids, moe_buf, num_experts, int(block_size), expert_mask,
-                           num_local_tokens, dispatch_policy)
-    return sorted_ids, sorted_weights, sorted_expert_ids, num_valid_ids, moe_buf
+                           num_local_tokens, dispatch_policy, token_sorted_pos=pos)
+    return sorted_ids, sorted_weights, sorted_expert_ids, num_valid_ids, moe_buf, pos
+
+
+def moe_sorting(topk_ids, topk_weights, num_experts, model_dim, moebuf_dtype, block_size=BLOCK_SIZE_M,
+                expert_mask=None, num_local_tokens=None, dispatch_policy=0):
+    """Returns (sorted_ids, sorted_weights, sorted_expert_ids, num_valid_ids, moe_buf);
+    moe_buf [M, model_dim] is zeroed."""
+    return _moe_sorting_ext(topk_ids, topk_weights, num_experts, model_dim, moebuf_dtype, block_size,
+                            expert_mask, num_local_tokens, dispatch_policy)[:5]
 
 
 def fused_topk(hidden_states, gating_output, topk, renormalize, topk_ids=None, topk_weights=None):
@@ -136,19 +144,22 @@ def fused_moe(hidden_states, w1, w2, topk_weight, topk_ids, expert_mask: Optiona
         block_m = meta.block_m if not block_size_M else int(block_size_M)
         if block_m != BLOCK_SIZE_M:
             raise NotImplementedError(f"block_size_M={block_m}: the grouped GEMM tiles {BLOCK_SIZE_M} rows")
-        sorted_ids, sorted_weights, sorted_expert_ids, num_valid_ids, moe_buf = moe_sorting(
+        sorted_ids, sorted_weights, sorted_expert_ids, num_valid_ids, moe_buf, pos = _moe_sorting_ext(
             topk_ids, topk_weight, global_E, model_dim, dtype, block_m, expert_mask, num_local_tokens,
-            moe_sorting_dispatch_policy)
-        if hidden_states.dtype == dtypes.fp8 and a1_scale is not None:
-            a1 = hidden_states
+            moe_sorting_dispatch_policy, with_pos=True)
+        rows = sorted_ids.numel()
+        dev = hidden_states.device
+        if hidden_states.dtype == dtypes.fp8:
+            if a1_scale is None:
+                raise ValueError("a1_scale must be provided for quantized input for fused_moe")
+            a1, a1s = moe_op.moe_gather_quant_1x128(hidden_states, pos, topk, rows, hidden_scale=a1_scale)
         else:
-            a1, a1_scale = moe_op.per_group_quant_hip(hidden_states, quant_dtype=dtypes.fp8, group_size=128,
-                                                      num_rows=num_local_tokens)
-        a2 = torch.empty((M, topk, inter_dim), dtype=dtypes.fp8, device=hidden_states.device)
-        a2_scale = torch.empty((M * topk, inter_dim // 128), dtype=dtypes.fp32, device=hidden_states.device)
-        moe_op.moe_stage1_fp8_blockscale(a1, w1, sorted_ids, sorted_expert_ids, num_valid_ids, a2, a2_scale,
-                                         topk, w1_scale, a1_scale, block_m, activation)
-        moe_op.moe_stage2_fp8_blockscale(a2, w2, sorted_ids, sorted_expert_ids, num_valid_ids, moe_buf, topk,
-                                         w2_scale, a2_scale, sorted_weights, block_m)
+            a1, a1s = moe_op.moe_gather_quant_1x128(hidden_states, pos, topk, rows)
+        a2 = torch.empty((rows, inter_dim), dtype=dtypes.fp8, device=dev)
+        a2s = torch.empty((inter_dim // 128, rows), dtype=dtypes.fp32, device=dev)
+        moe_op.moe_stage1_fp8_blockscale(a1, a1s, w1, w1_scale, sorted_ids, sorted_expert_ids, num_valid_ids,
+                                         a2, a2s, M, block_m, activation)
+        moe_op.moe_stage2_fp8_blockscale(a2, a2s, w2, w2_scale, sorted_ids, sorted_expert_ids, num_valid_ids,
+                                         sorted_weights, moe_buf, block_m)
         return moe_buf
     raise NotImplementedError(f"quant_type {quant_type} is not supported by the B200 path")

@@ -55,7 +55,7 @@ def moe_sorting_fwd(topk_ids: Tensor, topk_weights: Tensor, sorted_token_ids: Te
                     moe_buf: Tensor, num_experts: int, unit_size: int,
                     local_expert_mask: Optional[Tensor] = None,
                     num_local_tokens: Optional[Tensor] = None, dispatch_policy: int = 0,
-                    workspace: Optional[Tensor] = None) -> None:
+                    workspace: Optional[Tensor] = None, token_sorted_pos: Optional[Tensor] = None) -> None:
     """In place.  Allocates the workspace itself when none is given, as the
     reference binding does (csrc/py_itfs_ck/moe_sorting_kernels.cu:33-40)."""
     M, topk = topk_ids.shape
@@ -65,7 +65,7 @@ def moe_sorting_fwd(topk_ids: Tensor, topk_weights: Tensor, sorted_token_ids: Te
             workspace = torch.empty(ws, dtype=torch.uint8, device=topk_ids.device)
     _lib.call("moe_sorting_fwd", topk_ids, topk_weights, sorted_token_ids, sorted_weights,
               sorted_expert_ids, num_valid_ids, moe_buf, num_experts, unit_size,
-              local_expert_mask, num_local_tokens, dispatch_policy, workspace)
+              local_expert_mask, num_local_tokens, dispatch_policy, workspace, token_sorted_pos)
 
 
 def dynamic_per_token_scaled_quant(out: Tensor, input: Tensor, scales: Tensor,
@@ -94,19 +94,34 @@ def per_group_quant_hip(x: Tensor, scale: Optional[Tensor] = None, quant_dtype=d
     return y, scale
 
 
-def moe_stage1_fp8_blockscale(hidden_states: Tensor, w1: Tensor, sorted_token_ids: Tensor,
-                              sorted_expert_ids: Tensor, num_valid_ids: Tensor, out: Tensor,
-                              out_scale: Tensor, topk: int, w1_scale: Tensor, a1_scale: Tensor,
-                              block_m: int = 128, activation=ActivationType.Silu) -> Tuple[Tensor, Tensor]:
-    _lib.call("moe_stage1_fp8_blockscale", hidden_states, w1, sorted_token_ids, sorted_expert_ids,
-              num_valid_ids, out, out_scale, topk, w1_scale, a1_scale, block_m, int(activation))
+def moe_gather_quant_1x128(hidden_states: Tensor, token_sorted_pos: Tensor, topk: int, rows: int,
+                           hidden_scale: Optional[Tensor] = None, out: Optional[Tensor] = None,
+                           out_scale: Optional[Tensor] = None) -> Tuple[Tensor, Tensor]:
+    """Sorted-row fp8 activations for stage 1: ([rows, D] fp8, [D/128, rows] f32)."""
+    D = hidden_states.shape[-1]
+    dev = hidden_states.device
+    if out is None:
+        out = torch.empty((rows, D), dtype=dtypes.fp8, device=dev)
+    if out_scale is None:
+        out_scale = torch.empty((D // 128, rows), dtype=dtypes.fp32, device=dev)
+    _lib.call("moe_gather_quant_1x128", hidden_states, hidden_scale, token_sorted_pos, topk, out, out_scale)
     return out, out_scale
 
 
-def moe_stage2_fp8_blockscale(inter_states: Tensor, w2: Tensor, sorted_token_ids: Tensor,
-                              sorted_expert_ids: Tensor, num_valid_ids: Tensor, out: Tensor, topk: int,
-                              w2_scale: Tensor, a2_scale: Tensor, sorted_weights: Tensor,
-                              block_m: int = 128) -> Tensor:
-    _lib.call("moe_stage2_fp8_blockscale", inter_states, w2, sorted_token_ids, sorted_expert_ids,
-              num_valid_ids, out, topk, w2_scale, a2_scale, sorted_weights, block_m)
+def moe_stage1_fp8_blockscale(a1: Tensor, a1_scale: Tensor, w1: Tensor, w1_scale: Tensor,
+                              sorted_token_ids: Tensor, sorted_expert_ids: Tensor, num_valid_ids: Tensor,
+                              out: Tensor, out_scale: Tensor, num_tokens: int, block_m: int = 128,
+                              activation=ActivationType.Silu) -> Tuple[Tensor, Tensor]:
+    """Gate/up grouped GEMM with fused act and 1x128 fp8 requant; sorted-row in and out."""
+    _lib.call("moe_stage1_fp8_blockscale", a1, a1_scale, w1, w1_scale, sorted_token_ids, sorted_expert_ids,
+              num_valid_ids, out, out_scale, num_tokens, block_m, int(activation))
+    return out, out_scale
+
+
+def moe_stage2_fp8_blockscale(a2: Tensor, a2_scale: Tensor, w2: Tensor, w2_scale: Tensor,
+                              sorted_token_ids: Tensor, sorted_expert_ids: Tensor, num_valid_ids: Tensor,
+                              sorted_weights: Tensor, out: Tensor, block_m: int = 128) -> Tensor:
+    """Down grouped GEMM; adds the top-k weighted rows into out [M, D] (bf16)."""
+    _lib.call("moe_stage2_fp8_blockscale", a2, a2_scale, w2, w2_scale, sorted_token_ids, sorted_expert_ids,
+              num_valid_ids, sorted_weights, out, block_m)
     return out

@@ -1,0 +1,395 @@
+"""Benchmark of the B200 fused-MoE hot path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--M 4096]
+
+One step = one fused MoE forward over one batch of M tokens with the config-1
+shapes (hidden 4096, intermediate 1536, 128 experts, top-8, SiLU gate, FP8 e4m3
+activations with 1x128 fp32 scales, FP8 weights with 128x128 fp32 block scales,
+uniform routing from N(0,1) logits): moe_sorting -> 1x128 quant -> stage-1
+grouped GEMM -> stage-2 grouped GEMM.  Inputs are seeded synthetic data with the
+reference's test distributions; weights (2.42 GB) exceed the 126 MB L2, so no L2
+flush is needed between steps.
+
+* value  : tokens/s over the K timed steps, inputs resident in HBM, CUDA events on
+           the launching stream, max over ranks; N > 1 runs independent replicas.
+* e2e    : the same metric through the public `aiter_b200.fused_moe` call with
+           pinned host buffers: H2D of hidden/topk_weights/topk_ids and D2H of the
+           output inside the timed region.
+* roofline: stage-1 grouped GEMM (the dominant kernel): algorithmic FP8 FLOPs per
+           launch / its mean CUDA-event duration, against the FP8 dense peak (2x
+           the measured bf16 cuBLAS burst of MEASURED_PEAKS.json).
+* cpu_baseline: the reference's torch path restated in numpy (oracle/, "port")
+           on a bounded token sample, on this host's cores (rank 0, N == 1 only).
+`--impl reference` times that CPU implementation alone as the reference arm.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+D, I, E, TOPK = 4096, 1536, 128, 8
+METRIC = "fused-MoE tokens/s (FP8 blockscale, E=128, top-8, hidden 4096, inter 1536)"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    p.add_argument("--M", type=int, default=4096)
+    p.add_argument("--E", type=int, default=128, help="experts (profiling cases use fewer)")
+    p.add_argument("--cpu-sample", type=int, default=128, help="tokens per CPU-baseline sample")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+# ----------------------------------------------------------------------------- utilities
+
+
+def dist_setup(n):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while active."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{gpu_index}.csv")
+
+    def __enter__(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.idx)], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"]}
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[3]) if v.lower().startswith("active")})
+        loaded = [r[0] for r in rows if r[2] > 300] or [r[0] for r in rows]
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(r[1] for r in rows),
+                "power_w_max": max(r[2] for r in rows), "samples": len(rows), "reasons": reasons}
+
+
+def peaks():
+    try:
+        p = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        return p, "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def traffic_from_profile():
+    """Per-launch DRAM bytes of the stage-1 kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "moe_stage1_fp8_cfg1_traffic.json")
+    try:
+        d = json.load(open(path))
+        return d.get("dram_bytes_per_launch"), d
+    except Exception:
+        return None, None
+
+
+# ----------------------------------------------------------------------------- workload
+
+
+def make_inputs(M, seed=1234, E=E):
+    import aiter_b200 as aiter
+    from aiter_b200 import weights as W
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device=dev).manual_seed(seed)
+    w1 = torch.randn(E, 2 * I, D, device=dev, generator=g) / D ** 0.5
+    w1q, w1s = W.quant_weight_128x128(w1)
+    del w1
+    w2 = torch.randn(E, D, I, device=dev, generator=g) / I ** 0.5
+    w2q, w2s = W.quant_weight_128x128(w2)
+    del w2
+    hidden = torch.randn(M, D, device=dev, generator=g).to(torch.bfloat16)
+    logits = torch.randn(M, E, device=dev, generator=g)
+    tw, tid = aiter.fused_topk(hidden, logits, TOPK, True)
+    torch.cuda.synchronize()
+    return dict(hidden=hidden, w1q=w1q, w1s=w1s, w2q=w2q, w2s=w2s, tw=tw, tid=tid)
+
+
+def flops(M):
+    return 6.0 * M * TOPK * D * I
+
+
+def run_b200(args, rank, world, local):
+    import aiter_b200 as aiter
+    from aiter_b200 import dtypes, moe_op
+    M = args.M
+    E = args.E
+    x = make_inputs(M, seed=1234 + rank, E=E)
+    stream = torch.cuda.current_stream()
+    B = 128
+    max_pad = M * TOPK + E * B - TOPK
+    dev = x["hidden"].device
+    # buffers of one step (the allocations fused_moe makes, hoisted out of the loop)
+    sid = torch.empty(max_pad, dtype=torch.int32, device=dev)
+    sw = torch.empty(max_pad, dtype=torch.float32, device=dev)
+    seid = torch.empty((max_pad + B - 1) // B, dtype=torch.int32, device=dev)
+    nv = torch.empty(2, dtype=torch.int32, device=dev)
+    pos = torch.empty(M * TOPK, dtype=torch.int32, device=dev)
+    out = torch.empty(M, D, dtype=torch.bfloat16, device=dev)
+    ws_n = moe_op.moe_sorting_get_workspace_size(M, E, TOPK, 0)
+    ws = torch.empty(max(ws_n, 1), dtype=torch.uint8, device=dev)
+    a1 = torch.empty(max_pad, D, dtype=dtypes.fp8, device=dev)
+    a1s = torch.empty(D // 128, max_pad, dtype=torch.float32, device=dev)
+    a2 = torch.empty(max_pad, I, dtype=dtypes.fp8, device=dev)
+    a2s = torch.empty(I // 128, max_pad, dtype=torch.float32, device=dev)
+    sort_launches = 1 if ws_n == 0 else 2
+    launches_per_step = sort_launches + 3
+
+    def step(ev=None):
+        if ev is not None:
+            ev[0].record(stream)
+        moe_op.moe_sorting_fwd(x["tid"], x["tw"], sid, sw, seid, nv, out, E, B, None, None, 0,
+                               ws if ws_n else None, pos)
+        if ev is not None:
+            ev[1].record(stream)
+        moe_op.moe_gather_quant_1x128(x["hidden"], pos, TOPK, max_pad, out=a1, out_scale=a1s)
+        if ev is not None:
+            ev[2].record(stream)
+        moe_op.moe_stage1_fp8_blockscale(a1, a1s, x["w1q"], x["w1s"], sid, seid, nv, a2, a2s, M, B)
+        if ev is not None:
+            ev[3].record(stream)
+        moe_op.moe_stage2_fp8_blockscale(a2, a2s, x["w2q"], x["w2s"], sid, seid, nv, sw, out, B)
+        if ev is not None:
+            ev[4].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    assert aiter.device_error() == 0
+    K = args.steps
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(K)]
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t0.record(stream)
+        for i in range(K):
+            step(evs[i])
+        t1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms_local = t0.elapsed_time(t1)
+    ms = max_over_ranks(ms_local, world)
+    if aiter.device_error() != 0:
+        raise RuntimeError("a device-side wait timed out during the timed region")
+    per_kernel = {name: [evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(K)]
+                  for j, name in enumerate(["moe_sorting", "gather_quant_1x128", "stage1_gemm", "stage2_gemm"])}
+    mean_ms = {k: sum(v) / len(v) for k, v in per_kernel.items()}
+
+    # ---------------------------------------------------------------- end to end, host buffers
+    h_hidden = x["hidden"].cpu().pin_memory()
+    h_tw = x["tw"].cpu().pin_memory()
+    h_tid = x["tid"].cpu().pin_memory()
+    h_out = torch.empty(M, D, dtype=torch.bfloat16).pin_memory()
+    d_hidden = torch.empty_like(x["hidden"])
+    d_tw = torch.empty_like(x["tw"])
+    d_tid = torch.empty_like(x["tid"])
+
+    def e2e_step():
+        d_hidden.copy_(h_hidden, non_blocking=True)
+        d_tw.copy_(h_tw, non_blocking=True)
+        d_tid.copy_(h_tid, non_blocking=True)
+        o = aiter.fused_moe(d_hidden, x["w1q"], x["w2q"], d_tw, d_tid, quant_type=aiter.QuantType.per_1x128,
+                            activation=aiter.ActivationType.Silu, w1_scale=x["w1s"], w2_scale=x["w2s"])
+        h_out.copy_(o, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(K):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    # the e2e output must match the device-resident run
+    ref_out = out.float()
+    assert torch.allclose(h_out.to(dev).float(), ref_out, atol=2e-2, rtol=2e-2)
+    h2d = h_hidden.numel() * 2 + h_tw.numel() * 4 + h_tid.numel() * 4
+    d2h = h_out.numel() * 2
+
+    pk, src = peaks()
+    fp8_peak_tflops = 2.0 * pk["bf16_tflops"]
+    s1_flops = 4.0 * M * TOPK * D * I
+    s1_ms = mean_ms["stage1_gemm"]
+    achieved = s1_flops / (s1_ms * 1e-3) / 1e12
+    traffic, _ = traffic_from_profile()
+    total_tokens = M * K * world
+    value = total_tokens / (ms * 1e-3)
+    res = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": K,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms / K, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp8-e4m3 (fp32 accumulate, bf16 out)",
+        "data": "synthetic (seeded N(0,1) activations/logits, N(0,1)/sqrt(K) weights)",
+        "config": {"workload": "BASELINE config 1: FP8 blockscale fused MoE", "M": M, "hidden": D, "inter": I,
+                   "experts": E, "topk": TOPK, "block_m": B, "routing": "uniform softmax top-8 (renormalised)",
+                   "parallelism": "replicas" if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2: 2.42 GB of weights per step, no flush"},
+        "tflops": round(flops(M) * K * world / (ms * 1e-3) / 1e12, 2),
+        "kernel_ms": {k: round(v, 4) for k, v in mean_ms.items()},
+        "roofline": {"bound": "tensor", "kernel": "moe_stage1_fp8_blockscale (tcgen05 kind::f8f6f4)",
+                     "achieved": round(achieved, 1), "peak": round(fp8_peak_tflops, 1), "unit": "TFLOP/s",
+                     "frac": round(achieved / fp8_peak_tflops, 4),
+                     "peak_source": f"2 x bf16_tflops of MEASURED_PEAKS.json ({src}); fp8 dense runs at 2x bf16",
+                     "traffic": traffic},
+        "gpu_launches": launches_per_step * K,
+        "e2e": {"value": round(M * K * world / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "api": "aiter_b200.fused_moe"},
+        "clocks": clk.summary(),
+    }
+    return res, x
+
+
+def cpu_baseline(x, sample, threads=None):
+    """Times the numpy restatement of the reference torch path on `sample` tokens."""
+    from oracle import moe as omoe
+    threads = threads or os.cpu_count() or 1
+    w1q = x["w1q"].view(torch.uint8).cpu().numpy()
+    w1s = x["w1s"].cpu().numpy()
+    w2q = x["w2q"].view(torch.uint8).cpu().numpy()
+    w2s = x["w2s"].cpu().numpy()
+    hid = x["hidden"][:sample].float().cpu().numpy()
+    tw = x["tw"][:sample].cpu().numpy()
+    tid = x["tid"][:sample].cpu().numpy()
+    t = time.perf_counter()
+    omoe.fused_moe_fp8_blockscale_threaded(hid, w1q, w1s, w2q, w2s, tw, tid, threads=threads)
+    dt = time.perf_counter() - t
+    return {"value": round(sample / dt, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{sample} tokens of the config-1 workload per call, all 128 experts dequantised "
+                      f"per call as the reference torch path does; {dt:.2f} s"}
+
+
+def run_reference(args, rank, world):
+    """Reference arm: the reference's torch CPU path (numpy port) on the host cores."""
+    if rank != 0:
+        return None
+    x = make_inputs(args.cpu_sample) if torch.cuda.is_available() else None
+    threads = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        cpu_baseline(x, args.cpu_sample, threads)
+    times = []
+    for _ in range(args.steps):
+        t = time.perf_counter()
+        cpu_baseline(x, args.cpu_sample, threads)
+        times.append(time.perf_counter() - t)
+    total = sum(times)
+    value = args.cpu_sample * args.steps / total
+    res = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * total / args.steps, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (dequantised fp8)",
+        "data": "synthetic", "config": {"workload": "BASELINE config 1: FP8 blockscale fused MoE",
+                                        "M": args.cpu_sample, "hidden": D, "inter": I, "experts": E, "topk": TOPK},
+        "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"{args.cpu_sample} tokens per step (bounded sample of the M=4096 workload)"},
+        "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    return res
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_setup(args.gpus)
+    try:
+        if args.impl == "reference":
+            res = run_reference(args, rank, world)
+            if res is not None:
+                print(json.dumps(res), flush=True)
+            return
+        res, x = run_b200(args, rank, world, local)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            res["cpu_baseline"] = cpu_baseline(x, args.cpu_sample)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+    finally:
+        if world > 1 and torch.distributed.is_initialized():
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

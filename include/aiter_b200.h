@@ -106,13 +106,17 @@ int64_t moe_sorting_get_workspace_size(int64_t num_tokens, int64_t num_experts, 
  * csrc/py_itfs_ck/moe_sorting_kernels.cu:10-76).  Outputs are written in place;
  * moe_buf[:tokens] is zeroed.  `workspace` (u8/i32, >= the size above) is the
  * scratch the reference binding allocates itself; it may be NULL when the size
- * above is 0.  num_local_tokens is read on the device (no host sync). */
+ * above is 0.  num_local_tokens is read on the device (no host sync).
+ * token_sorted_pos (optional, i32 [M*topk]; no reference counterpart) receives the
+ * sorted row of every (token, slot), -1 when the slot's expert is masked out: the
+ * map moe_gather_quant_1x128 uses to write each token's row once per slot. */
 int moe_sorting_fwd(aiter_tensor_t* topk_ids, aiter_tensor_t* topk_weights,
                     aiter_tensor_t* sorted_token_ids, aiter_tensor_t* sorted_weights,
                     aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids,
                     aiter_tensor_t* moe_buf, int64_t num_experts, int64_t unit_size,
                     aiter_tensor_t* local_expert_mask, aiter_tensor_t* num_local_tokens,
-                    int64_t dispatch_policy, aiter_tensor_t* workspace, void* stream);
+                    int64_t dispatch_policy, aiter_tensor_t* workspace,
+                    aiter_tensor_t* token_sorted_pos, void* stream);
 
 /* ---- quantisation -------------------------------------------------------- */
 
@@ -127,33 +131,50 @@ int dynamic_per_token_scaled_quant(aiter_tensor_t* out, aiter_tensor_t* input,
                                    int shuffle_scale, aiter_tensor_t* num_rows,
                                    int64_t num_rows_factor, void* stream);
 
+/* 1x128 fp8 quantisation of the activations, scattered into sorted-row order: the
+ * A operand of stage 1.  Replaces the activation quant of fused_moe_2stages
+ * (aiter/fused_moe.py:1201-1209 -> per_group_quant_hip, aiter/ops/quant.py:261-292)
+ * together with the row gather the CK stage-1 kernel does internally
+ * (gemm_moe_ck2stages_common_blockscale.cuh:9-180).  Each token is quantised once
+ * and stored to the sorted rows token_sorted_pos[token*topk + slot] (from
+ * moe_sorting_fwd; -1 = skip).
+ * hidden [M, D] bf16/fp16/fp32, or fp8 with hidden_scale [M, D/128] f32 (copied);
+ * out [rows, D] fp8 and out_scale [D/128, rows] f32; padding rows are not written
+ * (the GEMMs never store their results). */
+int moe_gather_quant_1x128(aiter_tensor_t* hidden, aiter_tensor_t* hidden_scale,
+                           aiter_tensor_t* token_sorted_pos, int64_t topk,
+                           aiter_tensor_t* out, aiter_tensor_t* out_scale, void* stream);
+
 /* ---- grouped GEMMs (FP8 block-scale, tcgen05) ----------------------------- */
 
 /* Stage 1: replaces ck_moe_stage1_fwd + the intermediate requant
  * (aiter/ops/moe_op.py:534-575, aiter/fused_moe.py:1306-1314; CK template
  * csrc/ck_gemm_moe_2stages_codegen/gemm_moe_ck2stages_common_blockscale.cuh:9-180).
- * hidden [M, D] fp8 + a1_scale [M, D/128] f32; w1 [E, 2I, D] fp8 + w1_scale
- * [E, 2I/128, D/128] f32; sorted ids / expert ids / num_valid_ids from
- * moe_sorting_fwd with unit_size == block_m (64 or 128).
- * Writes out [M, topk, I] fp8 = quant(act(gate)*up) and out_scale [M*topk, I/128] f32
- * (1x128 groups).  activation: AITER_ACT_SILU or AITER_ACT_GELU. */
-int moe_stage1_fp8_blockscale(aiter_tensor_t* hidden, aiter_tensor_t* w1,
-                              aiter_tensor_t* sorted_token_ids, aiter_tensor_t* sorted_expert_ids,
-                              aiter_tensor_t* num_valid_ids, aiter_tensor_t* out,
-                              aiter_tensor_t* out_scale, int64_t topk, aiter_tensor_t* w1_scale,
-                              aiter_tensor_t* a1_scale, int64_t block_m, int64_t activation,
-                              void* stream);
+ * a1 [rows, D] fp8 + a1_scale [D/128, rows] f32 (from moe_gather_quant_1x128);
+ * w1 [E, 2I, D] fp8 + w1_scale [E, 2I/128, D/128] f32; sorted ids / expert ids /
+ * num_valid_ids from moe_sorting_fwd with unit_size == block_m (128).
+ * Writes, for every real sorted row r, out[r, :] = fp8(act(gate) * up / s) and
+ * out_scale[:, r] = s per 128 columns (1x128 requant, s = amax/448); padding rows
+ * are not written.  num_tokens = M (the padding id).  activation: AITER_ACT_SILU
+ * or AITER_ACT_GELU. */
+int moe_stage1_fp8_blockscale(aiter_tensor_t* a1, aiter_tensor_t* a1_scale, aiter_tensor_t* w1,
+                              aiter_tensor_t* w1_scale, aiter_tensor_t* sorted_token_ids,
+                              aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids,
+                              aiter_tensor_t* out, aiter_tensor_t* out_scale, int64_t num_tokens,
+                              int64_t block_m, int64_t activation, void* stream);
 
 /* Stage 2: replaces ck_moe_stage2_fwd (aiter/ops/moe_op.py:578-615; CK template
  * gemm_moe_ck2stages_common_blockscale.cuh:330-470).
- * inter [M, topk, I] fp8 + a2_scale [M*topk, I/128] f32; w2 [E, D, I] fp8 +
- * w2_scale [E, D/128, I/128] f32.  Adds sorted_weights[r] * (a2 @ w2[e]^T) of
- * every sorted row r into out[token] (bf16 [M, D], zeroed by moe_sorting_fwd). */
-int moe_stage2_fp8_blockscale(aiter_tensor_t* inter, aiter_tensor_t* w2,
-                              aiter_tensor_t* sorted_token_ids, aiter_tensor_t* sorted_expert_ids,
-                              aiter_tensor_t* num_valid_ids, aiter_tensor_t* out, int64_t topk,
-                              aiter_tensor_t* w2_scale, aiter_tensor_t* a2_scale,
-                              aiter_tensor_t* sorted_weights, int64_t block_m, void* stream);
+ * a2 [rows, I] fp8 + a2_scale [I/128, rows] f32 (stage-1 output, sorted rows);
+ * w2 [E, D, I] fp8 + w2_scale [E, D/128, I/128] f32.  Adds
+ * sorted_weights[r] * (a2[r] @ w2[e]^T) of every real sorted row r into
+ * out[token(r)] (bf16 [M, D], zeroed by moe_sorting_fwd): the top-k weighted
+ * scatter-reduce back to token order. */
+int moe_stage2_fp8_blockscale(aiter_tensor_t* a2, aiter_tensor_t* a2_scale, aiter_tensor_t* w2,
+                              aiter_tensor_t* w2_scale, aiter_tensor_t* sorted_token_ids,
+                              aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids,
+                              aiter_tensor_t* sorted_weights, aiter_tensor_t* out, int64_t block_m,
+                              void* stream);
 
 #ifdef __cplusplus
 }

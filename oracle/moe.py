@@ -110,3 +110,45 @@ def fused_moe_a8w4(hidden, w1_p, w1_e, w2_p, w2_e, topk_weights, topk_ids,
     if return_intermediate:
         return out, dict(a1_q=a1_q, a1_s=a1_s, out1=out1, a2_q=a2_q, a2_s=a2_s)
     return out
+
+
+def fused_moe_fp8_blockscale_threaded(hidden, w1_q, w1_s, w2_q, w2_s, topk_weights, topk_ids,
+                                      threads=None, activation="silu"):
+    """Same arithmetic as `fused_moe_fp8_blockscale`, experts processed by a thread
+    pool (numpy releases the GIL in the decode and the matmuls).  Used as the timed
+    CPU baseline; every call dequantises the weights of every routed expert, as the
+    reference torch path does on each call (aiter/fused_moe.py:1502-1536)."""
+    import os
+    from concurrent.futures import ThreadPoolExecutor
+    threads = threads or os.cpu_count() or 1
+    M, k = topk_ids.shape
+    a1_q, a1_s = quant.per_1x128_quant(hidden)
+    a1 = quant.dequant_1x128(a1_q, a1_s)
+    experts = [int(e) for e in np.unique(topk_ids)]
+    inter = w2_q.shape[2]
+    D = w2_q.shape[1]
+    out1 = np.zeros((M, k, inter), dtype=F32)
+
+    def s1(e):
+        tok, slot = np.nonzero(topk_ids == e)
+        w = quant.dequant_128x128(w1_q[e:e + 1], w1_s[e:e + 1])[0]
+        h = a1[tok] @ w.T
+        g, u = h[:, :inter], h[:, inter:]
+        act = silu(g) if activation == "silu" else gelu(g)
+        out1[tok, slot] = codecs.round_bf16((act * u).astype(F32))
+
+    with ThreadPoolExecutor(threads) as ex:
+        list(ex.map(s1, experts))
+    a2_q, a2_s = quant.per_1x128_quant(out1)
+    a2 = quant.dequant_1x128(a2_q, a2_s)
+    out = np.zeros((M, k, D), dtype=F32)
+
+    def s2(e):
+        tok, slot = np.nonzero(topk_ids == e)
+        w = quant.dequant_128x128(w2_q[e:e + 1], w2_s[e:e + 1])[0]
+        out[tok, slot] = a2[tok, slot] @ w.T
+
+    with ThreadPoolExecutor(threads) as ex:
+        list(ex.map(s2, experts))
+    out = out * np.asarray(topk_weights, dtype=F32)[:, :, None]
+    return codecs.round_bf16(out.sum(axis=1, dtype=F32))

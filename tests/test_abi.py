@@ -49,8 +49,15 @@ def test_sorting_workspace_size_policy():
 
 def test_stage_gemm_rejects_unsupported_block_m():
     t = lambda *s, dt=torch.int32: torch.empty(*s, dtype=dt)
-    args = (t(16, 128, dt=torch.float8_e4m3fn), t(2, 256, 128, dt=torch.float8_e4m3fn), t(640), t(5), t(2),
-            t(16, 2, 128, dt=torch.float8_e4m3fn), t(32, 1, dt=torch.float32), 2,
-            t(2, 2, 1, dt=torch.float32), t(16, 1, dt=torch.float32), 32, 0)
+    f8 = torch.float8_e4m3fn
+    args = (t(640, 128, dt=f8), t(1, 640, dt=torch.float32), t(2, 256, 128, dt=f8), t(2, 2, 1, dt=torch.float32),
+            t(640), t(5), t(2), t(640, 128, dt=f8), t(1, 640, dt=torch.float32), 16, 32, 0)
     with pytest.raises(RuntimeError, match="block_m must be 128"):
         _lib.call("moe_stage1_fp8_blockscale", *args)
+
+
+def test_gather_quant_rejects_fp8_without_scale():
+    f8 = torch.float8_e4m3fn
+    with pytest.raises(RuntimeError, match="hidden_scale must not be None"):
+        _lib.call("moe_gather_quant_1x128", torch.empty(4, 128, dtype=f8), None, torch.empty(8, dtype=torch.int32),
+                  2, torch.empty(8, 128, dtype=f8), torch.empty(1, 8))

@@ -15,6 +15,7 @@ import torch
 
 import aiter_b200 as aiter
 from aiter_b200 import weights as W
+from aiter_b200.fused_moe import _moe_sorting_ext
 from conftest import golden_group
 from gpu_util import check_no_device_error, codes, dev, fp8_from_codes, requires_cuda, to_dev
 from oracle import inputs, moe, quant
@@ -56,27 +57,60 @@ def test_fused_moe_matches_reference_golden(golden, tag, shape):
     assert_moe_close(out, g["out"])
 
 
+def test_gather_quant_sorted_rows_vs_oracle():
+    """Sorted-row fp8 activations: each real row equals the oracle's 1x128 quant of
+    its token (bit-exact codes and scales); padding rows are zero."""
+    c = inputs.make_moe_case(0, 32, 1024, 512, 8, 2)
+    a1_q, a1_s = quant.per_1x128_quant(c["hidden"])
+    tid, tw = to_dev(c["topk_ids"]), to_dev(c["topk_weights"])
+    sids, sw, seids, nv, buf, pos = _moe_sorting_ext(tid, tw, 8, 1024, torch.bfloat16, 128, with_pos=True)
+    # every (token, slot) maps to the sorted row holding it
+    p = pos.cpu().numpy().reshape(32, 2)
+    sid = sids.cpu().numpy()
+    assert np.array_equal(sid[p] & 0xFFFFFF, np.repeat(np.arange(32)[:, None], 2, 1))
+    assert np.array_equal(sid[p] >> 24, np.repeat(np.arange(2)[None, :], 32, 0))
+    for hidden, hs in ((to_dev(c["hidden"], torch.bfloat16), None), (fp8_from_codes(a1_q), to_dev(a1_s))):
+        a1, a1s = aiter.moe_gather_quant_1x128(hidden, pos, 2, sids.numel(), hidden_scale=hs)
+        torch.cuda.synchronize()
+        n = int(nv[0])
+        tok = sid[:n] & 0xFFFFFF
+        q = codes(a1)[:n]
+        s = a1s.cpu().numpy()[:, :n].T
+        real = tok < 32
+        assert np.array_equal(q[real], a1_q[tok[real]])
+        assert np.array_equal(s[real].view(np.uint32), a1_s[tok[real]].view(np.uint32))
+
+
 def test_stage1_intermediate_vs_oracle():
-    """Stage 1 alone: fp8 codes / scales of act(gate)*up against the oracle."""
+    """Stage 1 alone: fp8 codes / scales of act(gate)*up per sorted row against the
+    oracle's intermediate of that (token, slot)."""
     c = inputs.make_moe_case(0, 32, 1024, 512, 8, 2)
     _, st = moe.fused_moe_fp8_blockscale(c["hidden"], c["w1_q"], c["w1_s"], c["w2_q"], c["w2_s"],
                                          c["topk_weights"], c["topk_ids"], return_intermediate=True)
     M, k, I = 32, 2, 512
     tid, tw = to_dev(c["topk_ids"]), to_dev(c["topk_weights"])
-    sids, sw, seids, nv, buf = aiter.moe_sorting(tid, tw, 8, 1024, torch.bfloat16, 128)
-    a1, a1s = fp8_from_codes(st["a1_q"]), to_dev(st["a1_s"])
-    a2 = torch.empty(M, k, I, dtype=torch.float8_e4m3fn, device=dev())
-    a2s = torch.empty(M * k, I // 128, device=dev())
-    aiter.moe_stage1_fp8_blockscale(a1, fp8_from_codes(c["w1_q"]), sids, seids, nv, a2, a2s, k,
-                                    to_dev(c["w1_s"]), a1s, 128)
+    sids, sw, seids, nv, buf, pos = _moe_sorting_ext(tid, tw, 8, 1024, torch.bfloat16, 128, with_pos=True)
+    a1, a1s = aiter.moe_gather_quant_1x128(to_dev(c["hidden"], torch.bfloat16), pos, 2, sids.numel())
+    rows = sids.numel()
+    a2 = torch.empty(rows, I, dtype=torch.float8_e4m3fn, device=dev())
+    a2s = torch.empty(I // 128, rows, device=dev())
+    aiter.moe_stage1_fp8_blockscale(a1, a1s, fp8_from_codes(c["w1_q"]), to_dev(c["w1_s"]), sids, seids, nv,
+                                    a2, a2s, M, 128)
     torch.cuda.synchronize()
     check_no_device_error()
-    s_ref = st["a2_s"].reshape(M * k, -1)
-    np.testing.assert_allclose(a2s.cpu().numpy(), s_ref, rtol=1e-2)
-    deq = quant.dequant_1x128(codes(a2).reshape(M * k, I), a2s.cpu().numpy())
-    ref = st["out1"].reshape(M * k, I)
+    n = int(nv[0])
+    sid = sids.cpu().numpy()[:n]
+    tok, slot = sid & 0xFFFFFF, sid >> 24
+    real = tok < M
+    q = codes(a2)[:n][real]
+    s = a2s.cpu().numpy()[:, :n].T[real]
+    s_ref = st["a2_s"][tok[real], slot[real]]
+    q_ref = st["a2_q"][tok[real], slot[real]]
+    ref = st["out1"][tok[real], slot[real]]
+    np.testing.assert_allclose(s, s_ref, rtol=1e-2)
+    deq = quant.dequant_1x128(q, s)
     np.testing.assert_allclose(deq, ref, rtol=0.07, atol=0.02 * np.abs(ref).max())
-    same = (codes(a2).reshape(M * k, I) == st["a2_q"].reshape(M * k, I)).mean()
+    same = (q == q_ref).mean()
     assert same > 0.97, f"only {same:.3f} of fp8 codes equal"
 
 
