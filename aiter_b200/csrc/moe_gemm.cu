@@ -23,18 +23,36 @@
 // Stage 2 epilogue: multiply by the row's top-k weight and add into the bf16
 // output row of its token with vector red.global.add (the output is zeroed by
 // moe_sorting_fwd), i.e. the scatter-reduce over the k slots.
+#include <cstdlib>
+
 #include "sm100.cuh"
 
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 128, STAGES = 4;
+constexpr int BM = 128, BK = 128;
 constexpr int A_TILE = BM * BK;
-constexpr int B_TILE = BN * BK;
-constexpr int STAGE_BYTES = A_TILE + B_TILE;
 constexpr int NUM_THREADS = 384;
 constexpr int TMEM_COLS = 512;
-constexpr uint32_t IDESC = sm100::idesc_e4m3_f32(BM, BN);
-constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + 256 /*barriers*/ + 2 * 256 * 4;
+
+// Tile configuration by accumulator width BN.  TMEM (512 fp32 columns x 128 lanes)
+// is split into 512/BN accumulator slabs: the MMA writes one slab per 128-wide K
+// block while the epilogue promotes the previous ones, so more slabs hide more of
+// the MMA -> commit -> epilogue -> MMA turnaround.  The smem ring takes what the
+// operand tiles leave of 192 KB.
+template <int BN_>
+struct Cfg {
+    static constexpr int BN = BN_;
+    static constexpr int SLABS = TMEM_COLS / BN_;
+    static constexpr int B_TILE = BN_ * BK;
+    static constexpr int STAGE_BYTES = A_TILE + B_TILE;
+    static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
+    static constexpr int CPT = BN_ / 2;  // accumulator columns per epilogue thread
+    static constexpr uint32_t IDESC = sm100::idesc_e4m3_f32(BM, BN_);
+    static constexpr int BAR_BYTES = 512;
+    static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + BAR_BYTES + 2 * 256 * 4;
+    static_assert(CPT % 64 == 0, "epilogue works in 64-column chunks");
+    static_assert(2 * (STAGES + SLABS) * 8 + 8 <= BAR_BYTES, "barrier area");
+};
 
 struct GemmArgs {
     const int* sorted_ids;
@@ -65,20 +83,26 @@ __device__ __forceinline__ void red_add_bf16x8(__nv_bfloat16* dst, uint32_t a, u
                  : "memory");
 }
 
-template <int STAGE>
+// STAGE 1: B tile = 128 gate rows + 128 up rows of w1 (BN must be 256), epilogue
+//          act(gate)*up -> 1x128 fp8 requant of the 128 outputs.
+// STAGE 2: B tile = BN consecutive rows of w2, epilogue weighted scatter-add.
+template <int STAGE, int BN_>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const GemmArgs args) {
     using namespace sm100;
+    using C = Cfg<BN_>;
+    static_assert(STAGE == 2 || BN_ == 256, "stage 1 pairs 128 gate with 128 up columns");
+    constexpr int STAGES = C::STAGES, SLABS = C::SLABS, CPT = C::CPT, STAGE_BYTES = C::STAGE_BYTES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
-    uint64_t* tempty = tfull + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    uint64_t* tempty = tfull + SLABS;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + SLABS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    float* red = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES + 256);
+    float* red = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES + C::BAR_BYTES);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -86,7 +110,7 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        for (int s = 0; s < 2; ++s) {
+        for (int s = 0; s < SLABS; ++s) {
             mbar_init(&tfull[s], 1);
             mbar_init(&tempty[s], 8);
         }
@@ -113,28 +137,26 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
             const int m_blk = tile / args.n_tiles, n_blk = tile % args.n_tiles;
             const int e = min(max(args.sorted_eids[m_blk], 0), args.E - 1);
-            int brow0, brow1;
-            if (STAGE == 1) {
-                brow0 = e * args.N + n_blk * 128;                 // gate rows
-                brow1 = e * args.N + (args.N >> 1) + n_blk * 128; // up rows
-            } else {
-                brow0 = e * args.N + n_blk * 256;
-                brow1 = brow0 + 128;
-            }
             for (int kb = 0; kb < args.num_kb; ++kb, ++it) {
                 const int s = it % STAGES;
                 const uint32_t ph = (it / STAGES) & 1;
                 ok = __all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1, abort_flag));
                 if (!ok) break;
-                if (lane == 0) mbar_expect_tx(&full[s], STAGE_BYTES);
-                __syncwarp();
-                uint8_t* a = smem + s * STAGE_BYTES;
-                uint8_t* b = a + A_TILE;
                 if (lane == 0) {
+                    mbar_expect_tx(&full[s], STAGE_BYTES);
+                    uint8_t* a = smem + s * STAGE_BYTES;
+                    uint8_t* b = a + A_TILE;
                     tma_load_2d(a, &tmA, &full[s], kb * BK, m_blk * BM);
-                    tma_load_2d(b, &tmB, &full[s], kb * BK, brow0);
-                    tma_load_2d(b + 128 * BK, &tmB, &full[s], kb * BK, brow1);
+                    if (STAGE == 1) {
+                        tma_load_2d(b, &tmB, &full[s], kb * BK, e * args.N + n_blk * 128);                    // gate
+                        tma_load_2d(b + 128 * BK, &tmB, &full[s], kb * BK, e * args.N + (args.N >> 1) + n_blk * 128);  // up
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < BN_ / 128; ++j)
+                            tma_load_2d(b + j * 128 * BK, &tmB, &full[s], kb * BK, e * args.N + n_blk * BN_ + j * 128);
+                    }
                 }
+                __syncwarp();
             }
         }
         // drain: wait for the loads of the last STAGES iterations (bounded)
@@ -153,19 +175,18 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 for (int kb = 0; kb < args.num_kb; ++kb, ++it, ++acc_it) {
                     const int s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1;
-                    const int as = acc_it & 1;
-                    const uint32_t aph = (acc_it >> 1) & 1;
+                    const int as = acc_it % SLABS;
+                    const uint32_t aph = (acc_it / SLABS) & 1;
                     if (!mbar_wait(&tempty[as], aph ^ 1, abort_flag)) { ok = false; break; }
-                    tc_fence_after();
                     if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
                     tc_fence_after();
                     const uint8_t* a = smem + s * STAGE_BYTES;
                     const uint64_t adesc = smem_desc_sw128(a);
                     const uint64_t bdesc = smem_desc_sw128(a + A_TILE);
-                    const uint32_t d = tmem_base + as * BN;
+                    const uint32_t d = tmem_base + as * BN_;
 #pragma unroll
                     for (int kk = 0; kk < BK / 32; ++kk)
-                        mma_f8f6f4(d, adesc + 2 * kk, bdesc + 2 * kk, IDESC, kk > 0 ? 1u : 0u);
+                        mma_f8f6f4(d, adesc + 2 * kk, bdesc + 2 * kk, C::IDESC, kk > 0 ? 1u : 0u);
                     mma_commit(&empty[s]);
                     mma_commit(&tfull[as]);
                 }
@@ -173,7 +194,7 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             // make sure no MMA is still writing TMEM before teardown
             if (acc_it > 0) {
                 const int j = acc_it - 1;
-                mbar_wait(&tfull[j & 1], (j >> 1) & 1, abort_flag, 200000000ull, false);
+                mbar_wait(&tfull[j % SLABS], (j / SLABS) & 1, abort_flag, 200000000ull, false);
             }
         }
         __syncwarp();
@@ -201,10 +222,10 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 sb0_p = args.b_scale + ((int64_t)e * nblk128 + n_blk) * args.num_kb;
                 sb1_p = args.b_scale + ((int64_t)e * nblk128 + (nblk128 >> 1) + n_blk) * args.num_kb;
             } else {
-                sb0_p = args.b_scale + ((int64_t)e * nblk128 + n_blk * 2 + h) * args.num_kb;
+                sb0_p = args.b_scale + ((int64_t)e * nblk128 + n_blk * (BN_ / 128) + (h * CPT) / 128) * args.num_kb;
                 sb1_p = sb0_p;
             }
-            float acc[128];
+            float acc[CPT];
             float v[64];
             float sa_next = valid ? __ldg(sa_p) : 0.f;
             float sb0_next = __ldg(sb0_p), sb1_next = __ldg(sb1_p);
@@ -216,36 +237,36 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                     sb0_next = __ldg(sb0_p + kb + 1);
                     sb1_next = __ldg(sb1_p + kb + 1);
                 }
-                const int as = acc_it & 1;
-                const uint32_t aph = (acc_it >> 1) & 1;
+                const int as = acc_it % SLABS;
+                const uint32_t aph = (acc_it / SLABS) & 1;
                 if (!__all_sync(0xffffffffu, mbar_wait(&tfull[as], aph, abort_flag))) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t t = lane_base + as * BN;
-                // this thread's 128 columns in two 64-column halves; the slab is
-                // released as soon as the second half is in registers
+                const uint32_t t = lane_base + as * BN_;
+                // this thread's CPT columns in 64-column chunks; the slab is released
+                // as soon as the last chunk is in registers
 #pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    const uint32_t col = STAGE == 1 ? (half == 0 ? 64 * h : 128 + 64 * h) : 128 * h + 64 * half;
-                    const float sc = (STAGE == 1 && half == 1) ? s1 : s0;
+                for (int ch = 0; ch < CPT / 64; ++ch) {
+                    const uint32_t col = STAGE == 1 ? (ch == 0 ? 64 * h : 128 + 64 * h) : CPT * h + 64 * ch;
+                    const float sc = (STAGE == 1 && ch == 1) ? s1 : s0;
                     tmem_ld32(t + col, *reinterpret_cast<float(*)[32]>(&v[0]));
                     tmem_ld32(t + col + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
                     tmem_wait_ld();
-                    if (half == 1) {
+                    if (ch == CPT / 64 - 1) {
                         tc_fence_before();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&tempty[as]);
                     }
                     if (kb == 0) {
 #pragma unroll
-                        for (int j = 0; j < 64; ++j) acc[64 * half + j] = v[j] * sc;
+                        for (int j = 0; j < 64; ++j) acc[64 * ch + j] = v[j] * sc;
                     } else {
 #pragma unroll
-                        for (int j = 0; j < 64; ++j) acc[64 * half + j] = fmaf(v[j], sc, acc[64 * half + j]);
+                        for (int j = 0; j < 64; ++j) acc[64 * ch + j] = fmaf(v[j], sc, acc[64 * ch + j]);
                     }
                 }
             }
             if (!ok) break;
-            if (STAGE == 1) {
+            if constexpr (STAGE == 1) {
                 float amax = 0.f;
 #pragma unroll
                 for (int j = 0; j < 64; ++j) {
@@ -280,9 +301,9 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 const float w = args.sorted_w[srow];
                 if (valid) {
                     __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.out) + (int64_t)tok * args.out_cols +
-                                         n_blk * 256 + 128 * h;
+                                         n_blk * BN_ + CPT * h;
 #pragma unroll
-                    for (int c = 0; c < 16; ++c) {
+                    for (int c = 0; c < CPT / 8; ++c) {
                         const int j = 8 * c;
                         red_add_bf16x8(dst + j, pack_bf16x2(acc[j] * w, acc[j + 1] * w),
                                        pack_bf16x2(acc[j + 2] * w, acc[j + 3] * w),
@@ -374,14 +395,26 @@ void check_sorted_operand(aiter_tensor_t* a, aiter_tensor_t* sc, int rows_pad, c
     AB_CHECK((int64_t)sc->numel_ == (a->shape[1] / 128) * (int64_t)rows_pad, sn, " must be [K/128, rows]");
 }
 
-template <int STAGE>
-void launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& a, int dev, cudaStream_t st) {
+template <int STAGE, int BN_>
+void launch(const CUtensorMap& tmA, const CUtensorMap& tmB, GemmArgs a, int dev, cudaStream_t st) {
+    a.n_tiles = STAGE == 1 ? a.n_tiles : a.N / BN_;
     const int tiles = a.max_m_blocks * a.n_tiles;
     if (tiles == 0) return;
     const int grid = std::min(tiles, ab::num_sms(dev));
-    AB_CUDA(cudaFuncSetAttribute(moe_gemm_fp8_kernel<STAGE>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    moe_gemm_fp8_kernel<STAGE><<<grid, NUM_THREADS, SMEM_BYTES, st>>>(tmA, tmB, a);
+    constexpr int smem = Cfg<BN_>::SMEM_BYTES;
+    AB_CUDA(cudaFuncSetAttribute(moe_gemm_fp8_kernel<STAGE, BN_>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    moe_gemm_fp8_kernel<STAGE, BN_><<<grid, NUM_THREADS, smem, st>>>(tmA, tmB, a);
     ab::check_launch(STAGE == 1 ? "moe_stage1_fp8_blockscale" : "moe_stage2_fp8_blockscale");
+}
+
+// Accumulator width of the stage-2 kernel (AITER_B200_STAGE2_BN=128|256 overrides).
+int stage2_bn() {
+    static int bn = [] {
+        const char* e = getenv("AITER_B200_STAGE2_BN");
+        int v = e ? atoi(e) : 256;
+        return (v == 256) ? 256 : 128;
+    }();
+    return bn;
 }
 
 }  // namespace
@@ -435,7 +468,7 @@ AB_ENTRY(moe_stage1_fp8_blockscale,
     CUtensorMap tmA, tmB;
     make_tmap_2d_u8(&tmA, a1->ptr, (uint64_t)c.rows_pad, D, 128, 128, true);
     make_tmap_2d_u8(&tmB, w1->ptr, (uint64_t)E * N, D, 128, 128, true);
-    launch<1>(tmA, tmB, a, a1->device_id, as_stream(stream));
+    launch<1, 256>(tmA, tmB, a, a1->device_id, as_stream(stream));
 }
 
 AB_ENTRY(moe_stage2_fp8_blockscale,
@@ -478,7 +511,6 @@ AB_ENTRY(moe_stage2_fp8_blockscale,
     a.out = out->ptr;
     a.M = M;
     a.N = D;
-    a.n_tiles = D / 256;
     a.num_kb = I / 128;
     a.max_m_blocks = c.max_m_blocks;
     a.out_cols = D;
@@ -488,7 +520,8 @@ AB_ENTRY(moe_stage2_fp8_blockscale,
     CUtensorMap tmA, tmB;
     make_tmap_2d_u8(&tmA, a2->ptr, (uint64_t)c.rows_pad, I, 128, 128, true);
     make_tmap_2d_u8(&tmB, w2->ptr, (uint64_t)E * D, I, 128, 128, true);
-    launch<2>(tmA, tmB, a, a2->device_id, as_stream(stream));
+    if (stage2_bn() == 256) launch<2, 256>(tmA, tmB, a, a2->device_id, as_stream(stream));
+    else launch<2, 128>(tmA, tmB, a, a2->device_id, as_stream(stream));
 }
 
 extern "C" int aiter_device_error(int clear) {
