@@ -16,7 +16,12 @@
 //   * multi-CTA: kernel 1 writes per-chunk expert histograms to the workspace,
 //     kernel 2 has every chunk-CTA rebuild the expert bases from the histograms and
 //     scatter its chunk.  Extra CTAs of the first kernel zero moe_buf meanwhile.
+#include <mutex>
+
 #include "common.cuh"
+
+// Size of the library-owned sorting scratch of moe_sorting_fwd_static_scratch.
+constexpr int kSortScratchInts = 262144;  // 1 MiB
 
 namespace {
 
@@ -369,4 +374,84 @@ AB_ENTRY(moe_sorting_fwd,
     check_launch("moe_sorting_fwd(count)");
     sort_scatter_kernel<<<a.nchunks, kThreads, smem, st>>>(a);
     check_launch("moe_sorting_fwd(scatter)");
+}
+
+// ---------------------------------------------------------------------------
+// moe_sorting_fwd for callers that cannot allocate device memory.
+//
+// Some callers of this library must not call cudaMalloc (or any allocator) once
+// they are running: a serving engine that carved all free HBM into its KV-cache
+// pool at start-up and treats any later allocation as a fault, or a plain C host
+// program that links this library without a device allocator of its own.  For
+// them the sorting histograms (the only scratch the multi-CTA sort needs) live in
+// this fixed device array.  It is part of the library image, so every GPU that
+// loads the library holds these 1 MiB until the process exits.
+//
+// In host code `g_sort_scratch` is only a stand-in symbol, not a device address:
+// its address on the current device comes from cudaGetSymbolAddress, fetched once
+// per device on that device's first call and cached.  That first call therefore
+// makes a CUDA runtime query; issue it before any stream capture.
+//
+// Every call uses the same array, which keeps whatever the last call wrote.  The
+// count kernel overwrites every histogram entry a call reads, so nothing has to
+// be cleared first.  Two calls whose kernels overlap on the GPU (different streams
+// without ordering between them) race on the array; order them on one stream.
+static __device__ __align__(256) int g_sort_scratch[kSortScratchInts];
+
+namespace {
+
+std::mutex g_scratch_mu;
+int* g_scratch_dev[64] = {nullptr};
+
+int* sort_scratch_on_current_device() {
+    int dev = -1;
+    AB_CUDA(cudaGetDevice(&dev));
+    AB_CHECK(dev >= 0 && dev < 64, "unsupported device id ", dev);
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    if (!g_scratch_dev[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_sort_scratch);
+        if (e != cudaSuccess || p == nullptr)
+            ab::fail("cudaGetSymbolAddress(g_sort_scratch) failed: ", cudaGetErrorString(e));
+        g_scratch_dev[dev] = static_cast<int*>(p);
+    }
+    return g_scratch_dev[dev];
+}
+
+}  // namespace
+
+AB_ENTRY(moe_sorting_fwd_static_scratch,
+         (aiter_tensor_t * topk_ids, aiter_tensor_t* topk_weights, aiter_tensor_t* sorted_token_ids,
+          aiter_tensor_t* sorted_weights, aiter_tensor_t* sorted_expert_ids,
+          aiter_tensor_t* num_valid_ids, aiter_tensor_t* moe_buf, int64_t num_experts,
+          int64_t unit_size, aiter_tensor_t* local_expert_mask, aiter_tensor_t* num_local_tokens,
+          int64_t dispatch_policy, aiter_tensor_t* token_sorted_pos, void* stream),
+         (topk_ids, topk_weights, sorted_token_ids, sorted_weights, sorted_expert_ids,
+          num_valid_ids, moe_buf, num_experts, unit_size, local_expert_mask, num_local_tokens,
+          dispatch_policy, token_sorted_pos, stream)) {
+    using namespace ab;
+    need(topk_ids, "topk_ids");
+    need_ndim(topk_ids, 2, "topk_ids");
+    const int64_t need_bytes = moe_sorting_get_workspace_size(topk_ids->shape[0], num_experts,
+                                                              topk_ids->shape[1], dispatch_policy);
+    const int64_t have = (int64_t)sizeof(int) * kSortScratchInts;
+    AB_CHECK(need_bytes <= have, "this sort needs ", need_bytes, " bytes of scratch but the built-in array holds ",
+             have, " (", kSortScratchInts, " ints = ceil(tokens/tokens_per_chunk) * experts); use moe_sorting_fwd "
+             "with a workspace for larger inputs");
+    aiter_tensor_t ws{};
+    aiter_tensor_t* wsp = nullptr;
+    if (need_bytes > 0) {
+        DeviceGuard dg(topk_ids->device_id);
+        ws.ptr = sort_scratch_on_current_device();
+        ws.numel_ = (size_t)have;
+        ws.ndim = 1;
+        ws.shape[0] = have;
+        ws.strides[0] = 1;
+        ws.dtype_ = AITER_DTYPE_u8;
+        ws.device_id = topk_ids->device_id;
+        wsp = &ws;
+    }
+    moe_sorting_fwd_impl(topk_ids, topk_weights, sorted_token_ids, sorted_weights, sorted_expert_ids,
+                         num_valid_ids, moe_buf, num_experts, unit_size, local_expert_mask, num_local_tokens,
+                         dispatch_policy, wsp, token_sorted_pos, stream);
 }

@@ -118,6 +118,24 @@ int moe_sorting_fwd(aiter_tensor_t* topk_ids, aiter_tensor_t* topk_weights,
                     int64_t dispatch_policy, aiter_tensor_t* workspace,
                     aiter_tensor_t* token_sorted_pos, void* stream);
 
+/* moe_sorting_fwd without a workspace argument, for callers that cannot allocate
+ * device memory while they run (a serving engine that gave all free HBM to its
+ * KV-cache pool at start-up, a C host without its own device allocator).  It has
+ * no counterpart in the reference, whose binding allocates the workspace with
+ * torch.  The histograms use a 1 MiB array inside the library (held on every GPU
+ * that loads it); inputs needing more (moe_sorting_get_workspace_size > 1 MiB,
+ * e.g. more than 262144 = ceil(M*topk/1024) * E) are rejected with an error.  The
+ * first call on a device looks the array up (issue it before any stream capture);
+ * all calls share the array, so calls that overlap on the GPU race.  No
+ * cudaMalloc/cudaFree or other allocation is made. */
+int moe_sorting_fwd_static_scratch(aiter_tensor_t* topk_ids, aiter_tensor_t* topk_weights,
+                                   aiter_tensor_t* sorted_token_ids, aiter_tensor_t* sorted_weights,
+                                   aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids,
+                                   aiter_tensor_t* moe_buf, int64_t num_experts, int64_t unit_size,
+                                   aiter_tensor_t* local_expert_mask, aiter_tensor_t* num_local_tokens,
+                                   int64_t dispatch_policy, aiter_tensor_t* token_sorted_pos,
+                                   void* stream);
+
 /* ---- quantisation -------------------------------------------------------- */
 
 /* Replaces aiter.dynamic_per_token_scaled_quant as per_group_quant_hip drives it
