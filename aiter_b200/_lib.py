@@ -94,6 +94,7 @@ SIGNATURES = {
     "moe_sorting_fwd_static_scratch": [T, T, T, T, T, T, OT, I64, I64, OT, OT, I64, OT],
     "dynamic_per_token_scaled_quant": [T, T, T, OT, B, OT, I64],
     "moe_gather_quant_1x128": [T, OT, T, I64, T, T],
+    "mxfp4_to_fp8_blockscale": [T, T, T, T, OT],
     "moe_stage1_fp8_blockscale": [T, T, T, T, T, T, T, T, T, I64, I64, I64],
     "moe_stage2_fp8_blockscale": [T, T, T, T, T, T, T, T, T, I64],
 }

@@ -136,6 +136,16 @@ def fused_moe(hidden_states, w1, w2, topk_weight, topk_ids, expert_mask: Optiona
     if doweight_stage1:
         raise NotImplementedError("doweight_stage1 is not supported")
     global_E = expert_mask.numel() if expert_mask is not None else E
+    if quant_type == QuantType.per_1x32:
+        # A8W4 as BASELINE defines it: fp8 1x128 activations, MXFP4 weights.  The
+        # MXFP4 weights are expanded exactly into the FP8 block-scale format (do this
+        # once with weights.prepare_a8w4 and call with per_1x128 to skip it per call).
+        from . import weights as _w
+        if w1.dtype not in (dtypes.fp4x2, torch.uint8) or w2.dtype not in (dtypes.fp4x2, torch.uint8):
+            raise TypeError("per_1x32 needs MXFP4 (fp4x2) weights")
+        w1, w1_scale = _w.mxfp4_to_fp8_blockscale(w1, w1_scale)
+        w2, w2_scale = _w.mxfp4_to_fp8_blockscale(w2, w2_scale)
+        quant_type = QuantType.per_1x128
     if quant_type == QuantType.per_1x128:
         if w1.dtype != dtypes.fp8 or w2.dtype != dtypes.fp8:
             raise TypeError("per_1x128 needs fp8 weights")

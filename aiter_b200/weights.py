@@ -91,3 +91,34 @@ def dequant_mxfp4(packed: torch.Tensor, e8m0: torch.Tensor) -> torch.Tensor:
     v = torch.stack([lo, hi], dim=-1).flatten(-2)
     sh = v.shape
     return (v.view(*sh[:-1], sh[-1] // 32, 32) * _e8m0_to_f32(e8m0)[..., None]).view(sh)
+
+
+@torch.no_grad()
+def mxfp4_to_fp8_blockscale(w_fp4: torch.Tensor, w_scale: torch.Tensor, check: bool = True):
+    """MXFP4 weights [E, N, K/2] (fp4x2 or uint8) + e8m0 scales [E, N, K/32] ->
+    (e4m3 [E, N, K], f32 [E, N/128, K/128]) holding exactly the same values, the
+    operand format of the FP8 grouped GEMMs (CUDA kernel `mxfp4_to_fp8_blockscale`).
+    With `check`, raises if a 128x128 block cannot be represented exactly (its
+    non-zero group exponents span more than 14 binades); this synchronises once."""
+    from . import _lib
+    E, N, Kh = w_fp4.shape
+    K = Kh * 2
+    out = torch.empty((E, N, K), dtype=dtypes.fp8, device=w_fp4.device)
+    out_s = torch.empty((E, N // 128, K // 128), dtype=torch.float32, device=w_fp4.device)
+    status = torch.zeros(1, dtype=torch.int32, device=w_fp4.device) if check else None
+    wf = w_fp4.view(torch.uint8) if w_fp4.dtype != torch.uint8 else w_fp4
+    ws = w_scale.view(torch.uint8) if w_scale.dtype != torch.uint8 else w_scale
+    _lib.call("mxfp4_to_fp8_blockscale", wf.contiguous(), ws.contiguous().view(E, N, K // 32), out, out_s, status)
+    if check and int(status.item()) != 0:
+        raise ValueError(f"{int(status.item())} MXFP4 blocks are not exactly representable as e4m3 with one "
+                         "power-of-two scale per 128x128 block")
+    return out, out_s
+
+
+def prepare_a8w4(w1_fp4, w1_scale, w2_fp4, w2_scale):
+    """One-time A8W4 weight preparation (the role of the reference's shuffle_weight):
+    returns (w1_fp8, w1_scale_f32, w2_fp8, w2_scale_f32) for
+    fused_moe(..., quant_type=QuantType.per_1x128)."""
+    w1, s1 = mxfp4_to_fp8_blockscale(w1_fp4, w1_scale)
+    w2, s2 = mxfp4_to_fp8_blockscale(w2_fp4, w2_scale)
+    return w1, s1, w2, s2

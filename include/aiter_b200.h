@@ -163,6 +163,16 @@ int moe_gather_quant_1x128(aiter_tensor_t* hidden, aiter_tensor_t* hidden_scale,
                            aiter_tensor_t* token_sorted_pos, int64_t topk,
                            aiter_tensor_t* out, aiter_tensor_t* out_scale, void* stream);
 
+/* A8W4 weight preparation: MXFP4 weights (e2m1 packed two per byte, low nibble
+ * first, + e8m0 scale per 32 along K; per_1x32_f4_quant, aiter/ops/quant.py:75-106)
+ * -> e4m3 [E, N, K] with a power-of-two f32 scale per 128x128 block, the operand
+ * format of the FP8 grouped GEMMs.  Exact for blocks whose non-zero group
+ * exponents span <= 14 binades; `status` (optional i32 [1], accumulated) counts
+ * blocks that are not.  Runs once per weight, like the reference's shuffle_weight
+ * (aiter/ops/shuffle.py:7-27). */
+int mxfp4_to_fp8_blockscale(aiter_tensor_t* w_fp4, aiter_tensor_t* w_scale, aiter_tensor_t* out,
+                            aiter_tensor_t* out_scale, aiter_tensor_t* status, void* stream);
+
 /* ---- grouped GEMMs (FP8 block-scale, tcgen05) ----------------------------- */
 
 /* Stage 1: replaces ck_moe_stage1_fwd + the intermediate requant
