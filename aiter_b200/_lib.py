@@ -95,6 +95,7 @@ SIGNATURES = {
     "dynamic_per_token_scaled_quant": [T, T, T, OT, B, OT, I64],
     "moe_gather_quant_1x128": [T, OT, T, I64, T, T],
     "mxfp4_to_fp8_blockscale": [T, T, T, T, OT],
+    "gemm_a16w16": [T, T, T],
     "moe_stage1_fp8_blockscale": [T, T, T, T, T, T, T, T, T, I64, I64, I64],
     "moe_stage2_fp8_blockscale": [T, T, T, T, T, T, T, T, T, I64],
 }
@@ -121,6 +122,19 @@ def lib():
         L.moe_sorting_get_workspace_size.argtypes = [ctypes.c_int64] * 4
         L.aiter_device_error.restype = ctypes.c_int
         L.aiter_device_error.argtypes = [ctypes.c_int]
+        c64, vp, p64 = ctypes.c_int64, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64)
+        for name, args in (("custom_ar_init", [c64, c64, c64, c64, p64, vp]),
+                           ("custom_ar_open_peers", [c64, vp]), ("custom_ar_open_loopback", [c64]),
+                           ("custom_ar_next_buffer", [c64, p64, p64]),
+                           ("custom_ar_all_reduce", [c64, ctypes.POINTER(aiter_tensor_t),
+                                                     ctypes.POINTER(aiter_tensor_t), c64, vp]),
+                           ("custom_ar_gemm_all_reduce", [c64, ctypes.POINTER(aiter_tensor_t),
+                                                          ctypes.POINTER(aiter_tensor_t),
+                                                          ctypes.POINTER(aiter_tensor_t), c64, vp]),
+                           ("custom_ar_dispose", [c64]), ("custom_ar_device_error", [ctypes.c_int])):
+            fn = getattr(L, name)
+            fn.restype = ctypes.c_int
+            fn.argtypes = args
         for name, kinds in SIGNATURES.items():
             fn = getattr(L, name)
             fn.restype = ctypes.c_int
@@ -174,6 +188,16 @@ def call(name, *args, stream=None):
         L.aiter_clear_last_error()
         raise RuntimeError(f"{name} failed: {msg}")
     return None
+
+
+def check_status(name, ret):
+    """Raise RuntimeError for a non-zero status of a directly called entry point."""
+    if ret != 0:
+        L = lib()
+        raw = L.aiter_get_last_error()
+        msg = raw.decode(errors="replace") if raw else f"status={ret}"
+        L.aiter_clear_last_error()
+        raise RuntimeError(f"{name} failed: {msg}")
 
 
 def device_error(clear=True):

@@ -1,0 +1,338 @@
+// Custom allreduce over CUDA IPC peer memory (NVLink 5 / NVSwitch): the B200
+// replacement of the reference's HIP-IPC CustomAllreduce
+// (csrc/include/custom_all_reduce.cuh:150-555, aiter/dist/device_communicators/
+// custom_all_reduce.py:243-739).
+//
+// Every rank owns one cudaMalloc'd region, exported with cudaIpcGetMemHandle and
+// opened by every peer:
+//   [ Signal (flags written by peers) | staging buffer 0 | staging buffer 1 ]
+// Call n stages its input in buffer n % 2.  A rank starts call n+1 only after the
+// start barrier of call n+1, which every peer reaches only after finishing call n,
+// so the copy of call n+1 never overwrites data a slow peer is still reading.
+//
+// Barriers are per CTA: CTA b of rank r writes `epoch` into flag[phase][b][r] of
+// every peer (st.release.sys) and waits until its own flag[phase][b][p] == epoch for
+// all peers (ld.acquire.sys, bounded).  All ranks partition the data identically per
+// CTA, so CTA b only ever reads what peer CTAs b wrote before the barrier.
+//   one-shot : copy -> barrier -> out = sum over ranks (rank order 0..W-1)
+//   two-shot : copy -> barrier -> reduce own segment in place -> barrier -> gather
+//              every segment from its owner.
+// Sums accumulate in fp32 in rank order, so every rank gets identical bits.
+// Every wait gives up after 2 s, sets the device error word and returns.
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+
+namespace {
+
+constexpr int kMaxRanks = 8;
+constexpr int kMaxBlocks = 128;
+constexpr int kThreads = 512;
+constexpr size_t kSignalBytes = 2 * kMaxBlocks * kMaxRanks * sizeof(uint32_t);
+constexpr size_t kSignalPad = 64 * 1024;
+
+static __device__ int g_ar_error;
+
+struct Signal {
+    uint32_t flag[2][kMaxBlocks][kMaxRanks];
+};
+
+struct Peers {
+    Signal* sig[kMaxRanks];       // every rank's signal block
+    uint8_t* buf[2][kMaxRanks];   // every rank's staging buffers
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint4 ld_cg(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+
+// Returns false (and sets the error word) when a peer did not arrive in time.
+__device__ bool block_barrier(const Peers& P, int rank, int world, int phase, uint32_t epoch) {
+    __syncthreads();
+    bool ok = true;
+    if (threadIdx.x < world) {
+        // publish: everything this CTA wrote before is visible to peers first
+        __threadfence_system();
+        st_release_sys(&P.sig[threadIdx.x]->flag[phase][blockIdx.x][rank], epoch);
+        const uint32_t* mine = &P.sig[rank]->flag[phase][blockIdx.x][threadIdx.x];
+        const uint64_t t0 = abd::globaltimer_ns();
+        uint32_t n = 0;
+        while (ld_acquire_sys(mine) != epoch) {
+            if ((++n & 255) == 0 && abd::globaltimer_ns() - t0 > 2000000000ull) {
+                atomicExch(&g_ar_error, 1);
+                ok = false;
+                break;
+            }
+        }
+    }
+    return __syncthreads_and(ok ? 1 : 0) != 0;
+}
+
+__device__ __forceinline__ void acc8(float (&a)[8], uint4 v) {
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float2 f = __bfloat1622float2(h[i]);
+        a[2 * i] += f.x;
+        a[2 * i + 1] += f.y;
+    }
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&a)[8]) {
+    uint4 v;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(a[2 * i], a[2 * i + 1]);
+    return v;
+}
+
+// n16: number of 16-byte packs (8 bf16).  `in` may equal the staging buffer
+// (zero-copy producers), then the copy is skipped.
+__global__ void __launch_bounds__(kThreads)
+allreduce_bf16_kernel(Peers P, int rank, int world, int parity, const uint4* __restrict__ in,
+                      uint4* __restrict__ out, int64_t n16, uint32_t epoch, int two_shot) {
+    uint4* mine = reinterpret_cast<uint4*>(P.buf[parity][rank]);
+    const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    // Packs are split into `nseg` segments and pack i of segment s always goes to
+    // thread (i - lo_s) mod stride, in the copy, the reduce and the gather, on every
+    // rank.  A CTA therefore only reads packs that the same CTA index wrote on the
+    // peers before the barrier it waited on.
+    const int nseg = two_shot ? world : 1;
+    const int64_t seg = (n16 + nseg - 1) / nseg;
+    if (in != mine) {
+        for (int s = 0; s < nseg; ++s) {
+            const int64_t lo = (int64_t)s * seg, hi = min(n16, lo + seg);
+            for (int64_t i = lo + tid; i < hi; i += stride) mine[i] = in[i];
+        }
+    }
+    if (!block_barrier(P, rank, world, 0, epoch)) return;
+    if (!two_shot) {
+        for (int64_t i = tid; i < n16; i += stride) {
+            float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            for (int p = 0; p < world; ++p) acc8(a, ld_cg(reinterpret_cast<const uint4*>(P.buf[parity][p]) + i));
+            out[i] = pack8(a);
+        }
+        return;
+    }
+    // rank r reduces segment r in place
+    {
+        const int64_t lo = (int64_t)rank * seg, hi = min(n16, lo + seg);
+        for (int64_t i = lo + tid; i < hi; i += stride) {
+            float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            for (int p = 0; p < world; ++p) acc8(a, ld_cg(reinterpret_cast<const uint4*>(P.buf[parity][p]) + i));
+            mine[i] = pack8(a);
+        }
+    }
+    if (!block_barrier(P, rank, world, 1, epoch)) return;
+    for (int s = 0; s < world; ++s) {
+        const int o = (rank + s) % world;  // start with the own segment, spread peer traffic
+        const int64_t lo = (int64_t)o * seg, hi = min(n16, lo + seg);
+        const uint4* src = reinterpret_cast<const uint4*>(P.buf[parity][o]);
+        for (int64_t i = lo + tid; i < hi; i += stride) out[i] = ld_cg(src + i);
+    }
+}
+
+struct Ctx {
+    int rank = 0, world = 0, device = -1;
+    size_t max_bytes = 0;
+    uint8_t* base = nullptr;               // own region
+    std::vector<void*> opened;             // peer regions opened via IPC
+    Peers peers{};
+    uint32_t epoch = 0;
+    bool ready = false;
+};
+
+std::mutex g_mu;
+
+Ctx* as_ctx(int64_t h) {
+    Ctx* c = reinterpret_cast<Ctx*>(h);
+    AB_CHECK(c != nullptr, "null allreduce context");
+    return c;
+}
+
+}  // namespace
+
+AB_ENTRY(custom_ar_init,
+         (int64_t rank, int64_t world, int64_t max_bytes, int64_t device, int64_t* ctx_out, void* handle_out),
+         (rank, world, max_bytes, device, ctx_out, handle_out)) {
+    using namespace ab;
+    AB_CHECK(world >= 2 && world <= kMaxRanks, "world size must be in [2, ", kMaxRanks, "]");
+    AB_CHECK(rank >= 0 && rank < world, "bad rank");
+    AB_CHECK(max_bytes > 0 && max_bytes % 16 == 0, "max_bytes must be a positive multiple of 16");
+    AB_CHECK(ctx_out && handle_out, "null output pointers");
+    DeviceGuard dg((int)device);
+    Ctx* c = new Ctx();
+    c->rank = (int)rank;
+    c->world = (int)world;
+    c->device = (int)device;
+    c->max_bytes = (size_t)max_bytes;
+    const size_t total = kSignalPad + 2 * (size_t)max_bytes;
+    cudaError_t e = cudaMalloc(&c->base, total);
+    if (e != cudaSuccess) {
+        delete c;
+        fail("cudaMalloc of the IPC region failed: ", cudaGetErrorString(e));
+    }
+    e = cudaMemset(c->base, 0, kSignalPad);
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, c->base);
+    if (e != cudaSuccess) {
+        cudaFree(c->base);
+        delete c;
+        fail("IPC setup failed: ", cudaGetErrorString(e));
+    }
+    memcpy(handle_out, &h, sizeof(h));
+    *ctx_out = reinterpret_cast<int64_t>(c);
+}
+
+AB_ENTRY(custom_ar_open_peers, (int64_t ctx, const void* handles), (ctx, handles)) {
+    using namespace ab;
+    Ctx* c = as_ctx(ctx);
+    AB_CHECK(!c->ready, "peers already opened");
+    DeviceGuard dg(c->device);
+    const cudaIpcMemHandle_t* hs = reinterpret_cast<const cudaIpcMemHandle_t*>(handles);
+    for (int p = 0; p < c->world; ++p) {
+        uint8_t* b = nullptr;
+        if (p == c->rank) {
+            b = c->base;
+        } else {
+            void* q = nullptr;
+            cudaError_t e = cudaIpcOpenMemHandle(&q, hs[p], cudaIpcMemLazyEnablePeerAccess);
+            if (e != cudaSuccess) {
+                for (void* o : c->opened) cudaIpcCloseMemHandle(o);
+                c->opened.clear();
+                fail("cudaIpcOpenMemHandle for rank ", p, " failed: ", cudaGetErrorString(e));
+            }
+            c->opened.push_back(q);
+            b = static_cast<uint8_t*>(q);
+        }
+        c->peers.sig[p] = reinterpret_cast<Signal*>(b);
+        c->peers.buf[0][p] = b + kSignalPad;
+        c->peers.buf[1][p] = b + kSignalPad + c->max_bytes;
+    }
+    c->ready = true;
+}
+
+AB_ENTRY(custom_ar_open_loopback, (int64_t ctx), (ctx)) {
+    Ctx* c = as_ctx(ctx);
+    AB_CHECK(!c->ready, "peers already opened");
+    for (int p = 0; p < c->world; ++p) {
+        c->peers.sig[p] = reinterpret_cast<Signal*>(c->base);
+        c->peers.buf[0][p] = c->base + kSignalPad;
+        c->peers.buf[1][p] = c->base + kSignalPad + c->max_bytes;
+    }
+    c->ready = true;
+}
+
+// Pointer of the staging buffer the next call will use (zero-copy producers write
+// their result there and pass it as `inp`).
+AB_ENTRY(custom_ar_next_buffer, (int64_t ctx, int64_t* ptr_out, int64_t* bytes_out), (ctx, ptr_out, bytes_out)) {
+    Ctx* c = as_ctx(ctx);
+    const int parity = (int)((c->epoch + 1) & 1);
+    *ptr_out = reinterpret_cast<int64_t>(c->base + kSignalPad + parity * c->max_bytes);
+    *bytes_out = (int64_t)c->max_bytes;
+}
+
+AB_ENTRY(custom_ar_all_reduce,
+         (int64_t ctx, aiter_tensor_t* inp, aiter_tensor_t* out, int64_t force_two_shot, void* stream),
+         (ctx, inp, out, force_two_shot, stream)) {
+    using namespace ab;
+    Ctx* c = as_ctx(ctx);
+    AB_CHECK(c->ready, "custom_ar_open_peers has not been called");
+    need(inp, "inp");
+    need(out, "out");
+    need_dtype(inp, AITER_DTYPE_bf16, "inp");
+    need_dtype(out, AITER_DTYPE_bf16, "out");
+    need_contig(inp, "inp");
+    need_contig(out, "out");
+    AB_CHECK(inp->numel_ == out->numel_, "inp and out sizes differ");
+    const size_t bytes = inp->numel_ * 2;
+    AB_CHECK(bytes % 16 == 0, "allreduce size must be a multiple of 16 bytes");
+    AB_CHECK(bytes <= c->max_bytes, "allreduce of ", bytes, " bytes exceeds the registered ", c->max_bytes);
+    AB_CHECK(((uintptr_t)inp->ptr & 15) == 0 && ((uintptr_t)out->ptr & 15) == 0, "buffers must be 16-byte aligned");
+    AB_CHECK(inp->device_id == c->device, "tensor on a different device than the communicator");
+    if (bytes == 0) return;
+    DeviceGuard dg(c->device);
+    c->epoch += 1;
+    const int parity = (int)(c->epoch & 1);
+    const int64_t n16 = (int64_t)(bytes / 16);
+    // force_two_shot: 1 = two-shot, 0 = one-shot, negative = by size (one-shot up
+    // to 256 KiB where latency dominates, two-shot above where bandwidth does)
+    const bool two = force_two_shot > 0 ? true : (force_two_shot == 0 ? false : bytes > 256 * 1024);
+    const int64_t per_block = (int64_t)kThreads * 4;
+    int grid = (int)std::min<int64_t>((n16 + per_block - 1) / per_block, std::min(kMaxBlocks, num_sms(c->device)));
+    grid = std::max(grid, 1);
+    const void* src = inp->ptr;
+    allreduce_bf16_kernel<<<grid, kThreads, 0, as_stream(stream)>>>(c->peers, c->rank, c->world, parity,
+                                                                    (const uint4*)src, (uint4*)out->ptr, n16,
+                                                                    c->epoch, two ? 1 : 0);
+    check_launch("custom_ar_all_reduce");
+}
+
+AB_ENTRY(custom_ar_dispose, (int64_t ctx), (ctx)) {
+    Ctx* c = as_ctx(ctx);
+    {
+        ab::DeviceGuard dg(c->device);
+        cudaDeviceSynchronize();
+        for (void* o : c->opened) cudaIpcCloseMemHandle(o);
+        if (c->base) cudaFree(c->base);
+    }
+    delete c;
+}
+
+extern "C" int custom_ar_device_error(int clear) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_ar_error, sizeof(int)) != cudaSuccess) return -1;
+    if (clear) {
+        int z = 0;
+        cudaMemcpyToSymbol(g_ar_error, &z, sizeof(int));
+    }
+    return v;
+}
+
+// GEMM + allreduce: y = allreduce_over_ranks(A @ W^T).  The bf16 GEMM writes its
+// tile results straight into the staging buffer the allreduce reads next
+// (no copy), then the allreduce runs on the same stream.  The reference has no fused
+// entry; this equals tensor_model_parallel_all_reduce(tgemm.mm(A, W))
+// (aiter/dist/communication_op.py:30-37, aiter/tuned_gemm.py:506-529).
+AB_ENTRY(custom_ar_gemm_all_reduce,
+         (int64_t ctx, aiter_tensor_t* a, aiter_tensor_t* w, aiter_tensor_t* out, int64_t force_two_shot,
+          void* stream),
+         (ctx, a, w, out, force_two_shot, stream)) {
+    using namespace ab;
+    Ctx* c = as_ctx(ctx);
+    AB_CHECK(c->ready, "custom_ar_open_peers has not been called");
+    need(a, "A");
+    need(w, "W");
+    need(out, "out");
+    need_ndim(a, 2, "A");
+    need_ndim(w, 2, "W");
+    const int64_t M = a->shape[0], N = w->shape[0];
+    AB_CHECK(out->ndim == 2 && out->shape[0] == M && out->shape[1] == N, "out must be [M, N]");
+    AB_CHECK((size_t)(M * N * 2) <= c->max_bytes, "GEMM output of ", M * N * 2, " bytes exceeds the registered ",
+             c->max_bytes);
+    const int parity = (int)((c->epoch + 1) & 1);
+    aiter_tensor_t stage{};
+    stage.ptr = c->base + kSignalPad + (size_t)parity * c->max_bytes;
+    stage.numel_ = (size_t)(M * N);
+    stage.ndim = 2;
+    stage.shape[0] = M;
+    stage.shape[1] = N;
+    stage.strides[0] = N;
+    stage.strides[1] = 1;
+    stage.dtype_ = AITER_DTYPE_bf16;
+    stage.device_id = c->device;
+    if (gemm_a16w16(a, w, &stage, stream) != 0) fail(std::string(aiter_get_last_error() ? aiter_get_last_error() : "gemm failed"));
+    custom_ar_all_reduce_impl(ctx, &stage, out, force_two_shot, stream);
+}

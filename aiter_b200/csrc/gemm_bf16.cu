@@ -1,0 +1,220 @@
+// bf16 GEMM y = A @ W^T on tcgen05 (kind::f16, fp32 accumulate in TMEM): the GEMM
+// half of the tensor-parallel GEMM + allreduce (tgemm.mm / gemm_a16w16,
+// aiter/tuned_gemm.py:224-308,506-529; weights [N, K], the F.linear convention).
+//
+// Persistent kernel, one CTA per SM, 384 threads:
+//   warp 0     TMA producer: A box 128 x 64 (128 B rows), W box 128 x 64 twice,
+//              128-byte swizzle, 4-stage ring of 48 KB;
+//   warp 1     TMEM allocator + single-thread MMA issuer (M=128, N=256, K=16 x 4
+//              per 64-wide K block), accumulating the whole K of a tile in one
+//              TMEM slab; two slabs alternate between tiles so the epilogue of
+//              tile t overlaps the MMAs of tile t+1;
+//   warps 4-11 epilogue: TMEM -> registers -> bf16 -> global (rows >= M skipped).
+// The output may be the staging buffer of the IPC allreduce (custom_ar_next_buffer),
+// which then reduces it without an extra copy.
+#include "sm100.cuh"
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_TILE = BM * BK * 2;
+constexpr int B_TILE = BN * BK * 2;
+constexpr int STAGE_BYTES = A_TILE + B_TILE;
+constexpr int NUM_THREADS = 384;
+constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
+// kind::f16 instruction descriptor: D f32, A/B bf16, both K-major
+constexpr uint32_t IDESC_BF16 = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                ((uint32_t)(BM >> 4) << 24);
+
+struct Args {
+    __nv_bfloat16* out;
+    int64_t ldo;
+    int M, N, num_kb, m_tiles, n_tiles;
+};
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(IDESC_BF16), "r"(accumulate));
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Args args) {
+    using namespace sm100;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&tfull[s], 1);
+            mbar_init(&tempty[s], 8);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+        prefetch_tensormap(&tmA);
+        prefetch_tensormap(&tmB);
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int num_tiles = args.m_tiles * args.n_tiles;
+
+    if (warp < 4) {
+        setmaxnreg_dec<40>();
+        if (warp == 0) {
+            int it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+                // n fastest: concurrently running CTAs share the A rows in L2
+                const int m_blk = tile / args.n_tiles, n_blk = tile % args.n_tiles;
+                for (int kb = 0; kb < args.num_kb; ++kb, ++it) {
+                    const int s = it % STAGES;
+                    const uint32_t ph = (it / STAGES) & 1;
+                    ok = __all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1, abort_flag));
+                    if (!ok) break;
+                    if (lane == 0) {
+                        mbar_expect_tx(&full[s], STAGE_BYTES);
+                        uint8_t* a = smem + s * STAGE_BYTES;
+                        uint8_t* b = a + A_TILE;
+                        // the tensor maps address bytes: a 64-element bf16 K block is 128 bytes
+                        const int kx = kb * BK * 2;
+                        tma_load_2d(a, &tmA, &full[s], kx, m_blk * BM);
+                        tma_load_2d(b, &tmB, &full[s], kx, n_blk * BN);
+                        tma_load_2d(b + 128 * BK * 2, &tmB, &full[s], kx, n_blk * BN + 128);
+                    }
+                    __syncwarp();
+                }
+            }
+            if (!ok) {
+                for (int d = 0; d < STAGES && it - 1 - d >= 0; ++d) {
+                    const int j = it - 1 - d;
+                    mbar_wait(&full[j % STAGES], (j / STAGES) & 1, abort_flag, 200000000ull, false);
+                }
+            }
+        } else if (warp == 1) {
+            if (lane == 0) {
+                int it = 0, t = 0;
+                bool ok = true;
+                for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++t) {
+                    const int as = t & 1;
+                    if (!mbar_wait(&tempty[as], ((t >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t d = tmem_base + as * BN;
+                    for (int kb = 0; kb < args.num_kb; ++kb, ++it) {
+                        const int s = it % STAGES;
+                        if (!mbar_wait(&full[s], (it / STAGES) & 1, abort_flag)) { ok = false; break; }
+                        tc_fence_after();
+                        const uint8_t* a = smem + s * STAGE_BYTES;
+                        const uint64_t adesc = smem_desc_sw128(a);
+                        const uint64_t bdesc = smem_desc_sw128(a + A_TILE);
+#pragma unroll
+                        for (int kk = 0; kk < BK / 16; ++kk)
+                            mma_bf16(d, adesc + 2 * kk, bdesc + 2 * kk, (kb > 0 || kk > 0) ? 1u : 0u);
+                        mma_commit(&empty[s]);
+                    }
+                    mma_commit(&tfull[as]);
+                }
+                if (t > 0) {
+                    const int j = t - 1;
+                    mbar_wait(&tfull[j & 1], (j >> 1) & 1, abort_flag, 200000000ull, false);
+                }
+            }
+            __syncwarp();
+        }
+    } else {
+        setmaxnreg_inc<232>();
+        const int q = warp & 3, h = (warp - 4) >> 2;
+        const int row = q * 32 + lane;
+        const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
+        int t = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
+            const int m_blk = tile / args.n_tiles, n_blk = tile % args.n_tiles;
+            const int as = t & 1;
+            if (!__all_sync(0xffffffffu, mbar_wait(&tfull[as], (t >> 1) & 1, abort_flag))) break;
+            tc_fence_after();
+            const int grow = m_blk * BM + row;
+            __nv_bfloat16* dst = args.out + (int64_t)grow * args.ldo + n_blk * BN + 128 * h;
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) {
+                float v[32];
+                tmem_ld32(lane_base + as * BN + 128 * h + 32 * ch, v);
+                tmem_wait_ld();
+                if (ch == 3) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tempty[as]);
+                }
+                if (grow < args.M) {
+                    uint32_t w[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+                        w[i] = *reinterpret_cast<uint32_t*>(&b2);
+                    }
+                    uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * ch);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, 512);
+    }
+}
+
+void make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols) {
+    // bf16 [rows, cols] as a byte matrix of 2*cols bytes per row; box 64 elements x 128 rows
+    ab::make_tmap_2d_u8(map, base, rows, cols * 2, 128, 128, true);
+}
+
+}  // namespace
+
+AB_ENTRY(gemm_a16w16,
+         (aiter_tensor_t * a, aiter_tensor_t* w, aiter_tensor_t* out, void* stream), (a, w, out, stream)) {
+    using namespace ab;
+    need(a, "A");
+    need(w, "W");
+    need(out, "out");
+    need_dtype(a, AITER_DTYPE_bf16, "A");
+    need_dtype(w, AITER_DTYPE_bf16, "W");
+    need_dtype(out, AITER_DTYPE_bf16, "out");
+    need_ndim(a, 2, "A");
+    need_ndim(w, 2, "W");
+    need_contig(a, "A");
+    need_contig(w, "W");
+    AB_CHECK(out->ndim == 2 && out->strides[1] == 1, "out rows must be contiguous");
+    const int M = (int)a->shape[0], K = (int)a->shape[1], N = (int)w->shape[0];
+    AB_CHECK(w->shape[1] == K, "W must be [N, K] with the K of A");
+    AB_CHECK(out->shape[0] == M && out->shape[1] == N, "out must be [M, N]");
+    AB_CHECK(K % BK == 0 && N % BN == 0, "need K % 64 == 0 and N % 256 == 0");
+    AB_CHECK(out->strides[0] % 8 == 0 && ((uintptr_t)out->ptr & 15) == 0, "out rows must be 16-byte aligned");
+    if (M == 0) return;
+    DeviceGuard dg(a->device_id);
+    CUtensorMap tmA, tmB;
+    make_tmap_bf16(&tmA, a->ptr, M, K);
+    make_tmap_bf16(&tmB, w->ptr, N, K);
+    Args args{(__nv_bfloat16*)out->ptr, out->strides[0], M, N, K / BK, (M + BM - 1) / BM, N / BN};
+    const int tiles = args.m_tiles * args.n_tiles;
+    const int grid = std::min(tiles, num_sms(a->device_id));
+    AB_CUDA(cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    gemm_bf16_kernel<<<grid, NUM_THREADS, SMEM_BYTES, as_stream(stream)>>>(tmA, tmB, args);
+    check_launch("gemm_a16w16");
+}

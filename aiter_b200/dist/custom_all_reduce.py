@@ -1,0 +1,116 @@
+"""CustomAllreduce: the CUDA-IPC allreduce of libaiter_b200.so behind the
+reference's interface (aiter/dist/device_communicators/custom_all_reduce.py:243-739).
+
+Each rank allocates one IPC region in the library (signals + two staging buffers of
+`max_size` bytes); the 64-byte IPC handles are exchanged over the CPU (gloo) group,
+as the reference exchanges them over its CPU group / TCP store
+(custom_all_reduce.py:140-153,219-240), and every rank opens all peers' regions.
+"""
+import ctypes
+import logging
+
+import torch
+import torch.distributed as dist
+
+from .. import _lib
+
+logger = logging.getLogger("aiter_b200")
+
+IPC_HANDLE_BYTES = 64
+
+
+def exchange_handles(group, handle: bytes):
+    """All ranks' handles, in rank order, over a CPU process group."""
+    world = dist.get_world_size(group=group)
+    out = [None] * world
+    dist.all_gather_object(out, bytes(handle), group=group)
+    for h in out:
+        if not isinstance(h, (bytes, bytearray)) or len(h) != IPC_HANDLE_BYTES:
+            raise RuntimeError("malformed IPC handle received from a peer")
+    return out
+
+
+class CustomAllreduce:
+    _SUPPORTED_WORLD_SIZES = [2, 4, 6, 8]
+
+    def __init__(self, group, device, max_size=128 * 1024 * 1024):
+        self.disabled = True
+        self._ctx = 0
+        self.group = group
+        assert dist.get_backend(group) != dist.Backend.NCCL, \
+            "CustomAllreduce should be attached to a non-NCCL group."
+        self.rank = dist.get_rank(group=group)
+        self.world_size = dist.get_world_size(group=group)
+        if self.world_size == 1:
+            return
+        if self.world_size not in self._SUPPORTED_WORLD_SIZES:
+            logger.warning("custom allreduce disabled: unsupported world size %d", self.world_size)
+            return
+        if isinstance(device, int):
+            device = torch.device(f"cuda:{device}")
+        elif isinstance(device, str):
+            device = torch.device(device)
+        self.device = device
+        self.max_size = int(max_size)
+        L = _lib.lib()
+        ctx = ctypes.c_int64(0)
+        handle = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+        _lib.check_status("custom_ar_init", L.custom_ar_init(self.rank, self.world_size, self.max_size,
+                                                             device.index, ctypes.byref(ctx), handle))
+        self._ctx = ctx.value
+        try:
+            handles = exchange_handles(group, handle.raw)
+            blob = b"".join(handles)
+            _lib.check_status("custom_ar_open_peers", L.custom_ar_open_peers(self._ctx, blob))
+        except Exception:
+            L.custom_ar_dispose(self._ctx)
+            self._ctx = 0
+            raise
+        self.disabled = False
+
+    def should_custom_ar(self, inp: torch.Tensor) -> bool:
+        """Eligibility (custom_all_reduce.py:423-437): bf16, contiguous, 16-byte
+        multiple, at most the registered size."""
+        if self.disabled:
+            return False
+        nbytes = inp.numel() * inp.element_size()
+        return (inp.dtype == torch.bfloat16 and inp.is_contiguous() and nbytes % 16 == 0
+                and nbytes <= self.max_size and inp.device == self.device)
+
+    def all_reduce(self, inp: torch.Tensor, *, out: torch.Tensor = None, two_shot=None) -> torch.Tensor:
+        if out is None:
+            out = torch.empty_like(inp)
+        force = -1 if two_shot is None else (1 if two_shot else 0)
+        a, b = _lib.to_aiter(inp), _lib.to_aiter(out)
+        st = torch.cuda.current_stream(inp.device).cuda_stream
+        _lib.check_status("custom_ar_all_reduce", _lib.lib().custom_ar_all_reduce(
+            self._ctx, ctypes.byref(a), ctypes.byref(b), force, ctypes.c_void_p(st)))
+        return out
+
+    def custom_all_reduce(self, input: torch.Tensor):
+        if self.disabled or not self.should_custom_ar(input):
+            return None
+        return self.all_reduce(input)
+
+    def gemm_all_reduce(self, a: torch.Tensor, w: torch.Tensor, out: torch.Tensor = None, two_shot=None):
+        """allreduce(a @ w^T) with the GEMM writing into the staging buffer."""
+        if out is None:
+            out = torch.empty((a.shape[0], w.shape[0]), dtype=torch.bfloat16, device=a.device)
+        force = -1 if two_shot is None else (1 if two_shot else 0)
+        ta, tw, to = _lib.to_aiter(a), _lib.to_aiter(w), _lib.to_aiter(out)
+        st = torch.cuda.current_stream(a.device).cuda_stream
+        _lib.check_status("custom_ar_gemm_all_reduce", _lib.lib().custom_ar_gemm_all_reduce(
+            self._ctx, ctypes.byref(ta), ctypes.byref(tw), ctypes.byref(to), force, ctypes.c_void_p(st)))
+        return out
+
+    def close(self):
+        if self._ctx:
+            _lib.lib().custom_ar_dispose(self._ctx)
+            self._ctx = 0
+        self.disabled = True
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

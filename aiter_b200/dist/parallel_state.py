@@ -1,0 +1,116 @@
+"""Process groups for tensor parallelism (the role of aiter/dist/parallel_state.py).
+
+One process per GPU.  `init_distributed_environment` starts torch.distributed
+(nccl) (parallel_state.py:1087-1145); `initialize_model_parallel` builds the TP
+GroupCoordinator (parallel_state.py:1147, get_tp_group :1022).  Like the reference,
+a GroupCoordinator holds an NCCL device group plus a gloo CPU group
+(parallel_state.py:262-270), and attaches the custom allreduce to the CPU group.
+"""
+import datetime
+import os
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from .custom_all_reduce import CustomAllreduce
+
+_TP: Optional["GroupCoordinator"] = None
+
+
+class GroupCoordinator:
+    def __init__(self, ranks, local_rank, backend="nccl", use_custom_allreduce=True,
+                 ca_max_size=128 * 1024 * 1024, timeout_s=120):
+        self.ranks = list(ranks)
+        self.world_size = len(self.ranks)
+        self.rank = dist.get_rank()
+        self.rank_in_group = self.ranks.index(self.rank)
+        self.local_rank = local_rank
+        to = datetime.timedelta(seconds=timeout_s)
+        self.device_group = dist.new_group(self.ranks, backend=backend, timeout=to)
+        self.cpu_group = dist.new_group(self.ranks, backend="gloo", timeout=to)
+        self.device = torch.device(f"cuda:{local_rank}") if torch.cuda.is_available() and backend == "nccl" \
+            else torch.device("cpu")
+        self.ca_comm = None
+        if use_custom_allreduce and self.world_size > 1 and self.device.type == "cuda":
+            self.ca_comm = CustomAllreduce(self.cpu_group, self.device, ca_max_size)
+
+    def all_reduce(self, input_: torch.Tensor, use_new: bool = True, open_fp8_quant: bool = False,
+                   prefill_support: bool = False) -> torch.Tensor:
+        """Out-of-place allreduce (parallel_state.py:376-407): the IPC allreduce for
+        eligible tensors, the NCCL group otherwise."""
+        if self.world_size == 1:
+            return input_
+        if self.ca_comm is not None and not self.ca_comm.disabled:
+            out = self.ca_comm.custom_all_reduce(input_)
+            if out is not None:
+                return out
+        out = input_.clone()
+        dist.all_reduce(out, group=self.device_group)
+        return out
+
+    def gemm_all_reduce(self, a: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        if self.world_size == 1:
+            from ..gemm import gemm_a16w16
+            return gemm_a16w16(a, w)
+        if self.ca_comm is None or self.ca_comm.disabled:
+            raise RuntimeError("GEMM + allreduce needs the custom allreduce (world sizes 2, 4, 6, 8)")
+        return self.ca_comm.gemm_all_reduce(a, w)
+
+    def destroy(self):
+        if self.ca_comm is not None:
+            self.ca_comm.close()
+            self.ca_comm = None
+
+
+def init_distributed_environment(world_size=-1, rank=-1, distributed_init_method="env://", local_rank=-1,
+                                 backend="nccl", timeout_s=120):
+    if not dist.is_initialized():
+        if world_size == -1:
+            world_size = int(os.environ.get("WORLD_SIZE", "1"))
+        if rank == -1:
+            rank = int(os.environ.get("RANK", "0"))
+        dist.init_process_group(backend=backend, init_method=distributed_init_method, world_size=world_size,
+                                rank=rank, timeout=datetime.timedelta(seconds=timeout_s))
+    if local_rank == -1:
+        local_rank = int(os.environ.get("LOCAL_RANK", str(dist.get_rank())))
+    if backend == "nccl" and torch.cuda.is_available():
+        torch.cuda.set_device(local_rank)
+    return local_rank
+
+
+def initialize_model_parallel(tensor_model_parallel_size=1, local_rank=None, backend="nccl",
+                              use_custom_allreduce=True, ca_max_size=128 * 1024 * 1024):
+    global _TP
+    world = dist.get_world_size()
+    assert world % tensor_model_parallel_size == 0
+    if local_rank is None:
+        local_rank = int(os.environ.get("LOCAL_RANK", str(dist.get_rank())))
+    me = dist.get_rank()
+    for g in range(world // tensor_model_parallel_size):
+        ranks = list(range(g * tensor_model_parallel_size, (g + 1) * tensor_model_parallel_size))
+        if me in ranks:
+            # every rank creates every group (torch.distributed requirement): only ours is kept
+            _TP = GroupCoordinator(ranks, local_rank, backend, use_custom_allreduce, ca_max_size)
+        else:
+            dist.new_group(ranks, backend=backend)
+            dist.new_group(ranks, backend="gloo")
+    return _TP
+
+
+def get_tp_group() -> GroupCoordinator:
+    assert _TP is not None, "tensor model parallel group is not initialized"
+    return _TP
+
+
+def destroy_model_parallel():
+    global _TP
+    if _TP is not None:
+        _TP.destroy()
+    _TP = None
+
+
+def destroy_distributed_environment():
+    destroy_model_parallel()
+    if dist.is_initialized():
+        dist.destroy_process_group()

@@ -204,6 +204,47 @@ int moe_stage2_fp8_blockscale(aiter_tensor_t* a2, aiter_tensor_t* a2_scale, aite
                               aiter_tensor_t* sorted_weights, aiter_tensor_t* out, int64_t block_m,
                               void* stream);
 
+/* ---- bf16 GEMM (the GEMM half of GEMM + allreduce) ------------------------ */
+/* out[M, N] = A[M, K] @ W[N, K]^T, bf16 in / fp32 accumulate / bf16 out, on
+ * tcgen05 kind::f16.  Replaces tgemm.mm / gemm_a16w16 (aiter/tuned_gemm.py:224-308,
+ * 506-529; weights in the F.linear [N, K] layout).  Needs K % 64 == 0 and
+ * N % 256 == 0; out may be strided by rows (e.g. an allreduce staging buffer). */
+int gemm_a16w16(aiter_tensor_t* a, aiter_tensor_t* w, aiter_tensor_t* out, void* stream);
+
+/* ---- tensor-parallel allreduce over CUDA IPC ------------------------------ */
+/* Replaces the reference's HIP-IPC custom allreduce (aiter/ops/custom_all_reduce.py:
+ * init_custom_ar / all_reduce / dispose -> csrc/kernels/custom_all_reduce.cu:74-117,
+ * csrc/include/custom_all_reduce.cuh:2243-2420).  One process per GPU.
+ * custom_ar_init allocates this rank's IPC region (signals + 2 staging buffers of
+ * max_bytes) and writes its 64-byte cudaIpcMemHandle to handle_out; the caller
+ * exchanges the handles (the reference uses its CPU group / TCP store,
+ * custom_all_reduce.py:140-153,219-240) and passes all `world` of them, in rank
+ * order, to custom_ar_open_peers. */
+int custom_ar_init(int64_t rank, int64_t world, int64_t max_bytes, int64_t device, int64_t* ctx_out,
+                   void* handle_out);
+int custom_ar_open_peers(int64_t ctx, const void* handles);
+/* Test hook with no reference counterpart: maps every peer slot to this rank's own
+ * region, so barriers wait on flags no peer will ever write (exercises the bounded
+ * waits on one GPU). */
+int custom_ar_open_loopback(int64_t ctx);
+/* Staging buffer the next all_reduce will use: a producer that writes its bf16
+ * result there and passes it as `inp` skips the input copy. */
+int custom_ar_next_buffer(int64_t ctx, int64_t* ptr_out, int64_t* bytes_out);
+/* out = sum over ranks of inp (bf16, accumulated in fp32 in rank order, identical
+ * bits on every rank).  force_two_shot: 1 = two-shot (reduce-scatter + all-gather
+ * over peer memory), 0 = one-shot, negative = one-shot up to 256 KiB, else two-shot. */
+int custom_ar_all_reduce(int64_t ctx, aiter_tensor_t* inp, aiter_tensor_t* out, int64_t force_two_shot,
+                         void* stream);
+/* GEMM + allreduce, out = allreduce(A @ W^T): the GEMM epilogue writes into the
+ * staging buffer the allreduce reads, so the partial product is never copied.
+ * No reference counterpart (the reference calls tgemm.mm then
+ * tensor_model_parallel_all_reduce, aiter/dist/communication_op.py:30-37). */
+int custom_ar_gemm_all_reduce(int64_t ctx, aiter_tensor_t* a, aiter_tensor_t* w, aiter_tensor_t* out,
+                              int64_t force_two_shot, void* stream);
+int custom_ar_dispose(int64_t ctx);
+/* Error word of the allreduce barriers (1 = a peer did not arrive within 2 s). */
+int custom_ar_device_error(int clear);
+
 #ifdef __cplusplus
 }
 #endif
