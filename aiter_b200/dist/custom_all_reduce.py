@@ -103,6 +103,29 @@ class CustomAllreduce:
             self._ctx, ctypes.byref(ta), ctypes.byref(tw), ctypes.byref(to), force, ctypes.c_void_p(st)))
         return out
 
+    def next_buffer_tensor(self, shape, dtype=torch.bfloat16) -> torch.Tensor:
+        """A tensor viewing the staging buffer the next all_reduce will read.  A
+        producer that writes its result there and passes the tensor to all_reduce
+        skips the input copy.  Valid until the call after next."""
+        ptr, nbytes = ctypes.c_int64(0), ctypes.c_int64(0)
+        _lib.check_status("custom_ar_next_buffer",
+                          _lib.lib().custom_ar_next_buffer(self._ctx, ctypes.byref(ptr), ctypes.byref(nbytes)))
+        n = 1
+        for d in shape:
+            n *= int(d)
+        esz = torch.empty((), dtype=dtype).element_size()
+        if n * esz > nbytes.value:
+            raise ValueError(f"{n * esz} bytes exceed the staging buffer ({nbytes.value})")
+        typestr = {1: "|u1", 2: "<i2", 4: "<i4", 8: "<i8"}[esz]
+
+        class _View:
+            pass
+
+        v = _View()
+        v.__cuda_array_interface__ = {"shape": tuple(int(d) for d in shape), "typestr": typestr,
+                                      "data": (ptr.value, False), "version": 3, "strides": None}
+        return torch.as_tensor(v, device=self.device).view(dtype)
+
     def close(self):
         if self._ctx:
             _lib.lib().custom_ar_dispose(self._ctx)

@@ -68,7 +68,7 @@ def get_2stage_cfgs(padded_M, model_dim, inter_dim, expert, topk, dtype, q_dtype
 
 
 def _moe_sorting_ext(topk_ids, topk_weights, num_experts, model_dim, moebuf_dtype, block_size,
-                     expert_mask=None, num_local_tokens=None, dispatch_policy=0, with_pos=False):
+                     expert_mask=None, num_local_tokens=None, dispatch_policy=0, with_pos=False, moe_buf=None):
     device = topk_ids.device
     M, topk = topk_ids.shape
     max_num_tokens_padded = int(topk_ids.numel() + num_experts * block_size - topk)
@@ -77,7 +77,8 @@ def _moe_sorting_ext(topk_ids, topk_weights, num_experts, model_dim, moebuf_dtyp
     sorted_weights = torch.empty(max_num_tokens_padded, dtype=dtypes.fp32, device=device)
     sorted_expert_ids = torch.empty(max_num_m_blocks, dtype=dtypes.i32, device=device)
     num_valid_ids = torch.empty(2, dtype=dtypes.i32, device=device)
-    moe_buf = torch.empty((M, model_dim), dtype=moebuf_dtype, device=device)
+    if moe_buf is None:
+        moe_buf = torch.empty((M, model_dim), dtype=moebuf_dtype, device=device)
     pos = torch.empty(M * topk, dtype=dtypes.i32, device=device) if with_pos else None
     moe_op.moe_sorting_fwd(topk_ids, topk_weights, sorted_ids, sorted_weights, sorted_expert_ids,
                            num_valid_ids, moe_buf, num_experts, int(block_size), expert_mask,
@@ -112,7 +113,10 @@ def fused_moe(hidden_states, w1, w2, topk_weight, topk_ids, expert_mask: Optiona
               a1_scale: Optional[torch.Tensor] = None, a2_scale: Optional[torch.Tensor] = None,
               block_size_M=None, num_local_tokens: Optional[torch.Tensor] = None,
               moe_sorting_dispatch_policy=0, dtype=None, hidden_pad=0, intermediate_pad=0,
-              bias1=None, bias2=None, splitk=0):
+              bias1=None, bias2=None, splitk=0, moe_buf=None):
+    """Reference signature (aiter/fused_moe.py:118-144) plus `moe_buf`: an optional
+    [M, model_dim] bf16 output to write into (e.g. the staging buffer of the
+    tensor-parallel allreduce); it is zeroed and filled like the returned buffer."""
     activation = ActivationType(int(activation))
     quant_type = quant_remap.get(QuantType(int(quant_type)), QuantType(int(quant_type)))
     M, topk = topk_ids.shape
@@ -156,7 +160,7 @@ def fused_moe(hidden_states, w1, w2, topk_weight, topk_ids, expert_mask: Optiona
             raise NotImplementedError(f"block_size_M={block_m}: the grouped GEMM tiles {BLOCK_SIZE_M} rows")
         sorted_ids, sorted_weights, sorted_expert_ids, num_valid_ids, moe_buf, pos = _moe_sorting_ext(
             topk_ids, topk_weight, global_E, model_dim, dtype, block_m, expert_mask, num_local_tokens,
-            moe_sorting_dispatch_policy, with_pos=True)
+            moe_sorting_dispatch_policy, with_pos=True, moe_buf=moe_buf)
         rows = sorted_ids.numel()
         dev = hidden_states.device
         if hidden_states.dtype == dtypes.fp8:

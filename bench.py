@@ -50,6 +50,8 @@ def parse():
     p.add_argument("--E", type=int, default=128, help="experts (profiling cases use fewer)")
     p.add_argument("--cpu-sample", type=int, default=128, help="tokens per CPU-baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--mode", default="moe", choices=["moe", "tp_moe", "gemm_ar"],
+                   help="moe: config 1 (N>1: data-parallel replicas); tp_moe: config 3; gemm_ar: config 4")
     return p.parse_args()
 
 
@@ -308,7 +310,8 @@ def run_b200(args, rank, world, local):
         "data": "synthetic (seeded N(0,1) activations/logits, N(0,1)/sqrt(K) weights)",
         "config": {"workload": "BASELINE config 1: FP8 blockscale fused MoE", "M": M, "hidden": D, "inter": I,
                    "experts": E, "topk": TOPK, "block_m": B, "routing": "uniform softmax top-8 (renormalised)",
-                   "parallelism": "replicas" if world > 1 else "single GPU",
+                   "parallelism": f"dp{world} (independent token batches, no collective)" if world > 1
+                   else "single GPU",
                    "l2": "inputs larger than L2: 2.42 GB of weights per step, no flush"},
         "tflops": round(flops(M) * K * world / (ms * 1e-3) / 1e12, 2),
         "kernel_ms": {k: round(v, 4) for k, v in mean_ms.items()},
@@ -372,10 +375,105 @@ def run_reference(args, rank, world):
     return res
 
 
+def _time_loop(fn, K, W, world, stream=None):
+    """Mean ms per call over K calls after W warm-ups, max over ranks (CUDA events)."""
+    for _ in range(W):
+        fn()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(K):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(e0.elapsed_time(e1) / K, world)
+
+
+def run_tp_moe(args, rank, world, local):
+    """Config 3: tensor-parallel FP8 block-scale MoE, inter_dim/TP of every expert per
+    rank, partial outputs reduced by the IPC allreduce (zero-copy staging), against
+    the same shard MoE followed by an NCCL allreduce."""
+    import aiter_b200 as aiter
+    from aiter_b200.dist import parallel_state as ps
+    from aiter_b200.dist import shard_moe_weights_for_tp, tensor_model_parallel_fused_moe
+    M = args.M
+    if world < 2 or (I // world) % 128 != 0:
+        return {"mode": "tp_moe", "unavailable": f"inter_dim/TP = {I}/{world} is not a multiple of the 128-wide "
+                                                 "FP8 scale blocks (vLLM rejects such shards too)"}
+    tp = ps.initialize_model_parallel(world, local_rank=local, ca_max_size=M * D * 2)
+    x = make_inputs(M, seed=4321, E=E)               # identical on every rank
+    l1, s1, l2, s2 = shard_moe_weights_for_tp(x["w1q"], x["w1s"], x["w2q"], x["w2s"], rank, world)
+    del x["w1q"], x["w2q"]
+    torch.cuda.empty_cache()
+    kw = dict(quant_type=aiter.QuantType.per_1x128, w1_scale=s1, w2_scale=s2)
+    ours = lambda: tensor_model_parallel_fused_moe(x["hidden"], l1, l2, x["tw"], x["tid"], **kw)
+
+    def nccl():
+        y = aiter.fused_moe(x["hidden"], l1, l2, x["tw"], x["tid"], **kw)
+        torch.distributed.all_reduce(y, group=tp.device_group)
+
+    with ClockSampler(local) as clk:
+        ms = _time_loop(ours, args.steps, args.warmup, world)
+    ms_nccl = _time_loop(nccl, args.steps, args.warmup, world)
+    ps.destroy_model_parallel()
+    return {"metric": METRIC, "mode": "tp_moe", "value": round(M / (ms * 1e-3), 1), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp8-e4m3",
+            "data": "synthetic", "tflops": round(flops(M) / (ms * 1e-3) / 1e12, 2),
+            "config": {"workload": "BASELINE config 3: tensor-parallel FP8 blockscale MoE", "M": M, "hidden": D,
+                       "inter": I, "inter_per_rank": I // world, "experts": E, "topk": TOPK,
+                       "parallelism": f"tp{world}"},
+            "nccl_allreduce_arm": {"ms_per_step": round(ms_nccl, 4), "value": round(M / (ms_nccl * 1e-3), 1)},
+            "clocks": clk.summary()}
+
+
+def run_gemm_ar(args, rank, world, local):
+    """Config 4: y = allreduce(A @ B), A [M, 8192/TP], B [8192/TP, 4096] bf16 per rank:
+    the tcgen05 GEMM writing into the IPC allreduce's staging buffer vs cuBLAS
+    (torch.matmul) + NCCL all_reduce.  Latency per call, max over ranks."""
+    from aiter_b200.dist import parallel_state as ps
+    N, Ktot = 4096, 8192
+    K = Ktot // world
+    tp = ps.initialize_model_parallel(world, local_rank=local, ca_max_size=8192 * N * 2)
+    dev = torch.device("cuda", local)
+    g = torch.Generator(device=dev).manual_seed(99 + rank)
+    B = torch.randn(K, N, device=dev, generator=g).to(torch.bfloat16)     # BASELINE layout [K/TP, N]
+    W = B.t().contiguous()                                                 # prepared once: [N, K/TP]
+    rows = []
+    for M in (1, 8, 64, 512, 2048, 8192):
+        A = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+        ours = lambda: tp.gemm_all_reduce(A, W)
+
+        def base():
+            y = torch.matmul(A, B)
+            torch.distributed.all_reduce(y, group=tp.device_group)
+
+        us = 1e3 * _time_loop(ours, args.steps, args.warmup, world)
+        us_b = 1e3 * _time_loop(base, args.steps, args.warmup, world)
+        ar_bytes = 2.0 * (world - 1) / world * M * N * 2
+        rows.append({"M": M, "ours_us": round(us, 2), "cublas_nccl_us": round(us_b, 2),
+                     "speedup": round(us_b / us, 3), "ours_busbw_GBs": round(ar_bytes / (us * 1e-6) / 1e9, 1),
+                     "gemm_tflops": round(2.0 * M * K * N / (us * 1e-6) / 1e12, 2)})
+    ps.destroy_model_parallel()
+    big = rows[-1]
+    return {"metric": "GEMM+allreduce latency (config 4, M=8192)", "mode": "gemm_ar", "value": big["ours_us"],
+            "unit": "us", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic N(0,1)", "config": {"workload": "BASELINE config 4", "N": N, "K": Ktot,
+                                                   "parallelism": f"tp{world}"}, "sweep": rows}
+
+
 def main():
     args = parse()
     rank, world, local = dist_setup(args.gpus)
     try:
+        if args.mode in ("tp_moe", "gemm_ar"):
+            res = (run_tp_moe if args.mode == "tp_moe" else run_gemm_ar)(args, rank, world, local)
+            if rank == 0:
+                print(json.dumps(res), flush=True)
+            return
         if args.impl == "reference":
             res = run_reference(args, rank, world)
             if res is not None:

@@ -84,6 +84,31 @@ def _worker(rank, world, port):
         dist.all_gather(gathered, out, group=tp.device_group)
         for gg in gathered:
             assert torch.equal(gg, out)
+    # tensor-parallel fused MoE vs the single-GPU fused MoE on the full weights
+    import numpy as np
+    import aiter_b200 as aiter
+    from aiter_b200 import weights as W
+    from aiter_b200.dist import shard_moe_weights_for_tp, tensor_model_parallel_fused_moe
+    D, I, E, k, M = 1024, 256 * world, 16, 4, 100
+    g = torch.Generator(device=dev).manual_seed(77)
+    w1q, w1s = W.quant_weight_128x128(torch.randn(E, 2 * I, D, device=dev, generator=g) / D ** 0.5)
+    w2q, w2s = W.quant_weight_128x128(torch.randn(E, D, I, device=dev, generator=g) / I ** 0.5)
+    hidden = torch.randn(M, D, device=dev, generator=g).to(torch.bfloat16)
+    tw, tid = aiter.fused_topk(hidden, torch.randn(M, E, device=dev, generator=g), k, True)
+    full = aiter.fused_moe(hidden, w1q, w2q, tw, tid, quant_type=aiter.QuantType.per_1x128,
+                           w1_scale=w1s, w2_scale=w2s)
+    l1, s1, l2, s2 = shard_moe_weights_for_tp(w1q, w1s, w2q, w2s, rank, world)
+    for _ in range(2):
+        tp_out = tensor_model_parallel_fused_moe(hidden, l1, l2, tw, tid, quant_type=aiter.QuantType.per_1x128,
+                                                 w1_scale=s1, w2_scale=s2)
+        torch.cuda.synchronize()
+        a, b = tp_out.float().cpu().numpy(), full.float().cpu().numpy()
+        np.testing.assert_allclose(a, b, rtol=2e-2, atol=2e-2)
+        assert (np.abs(a - b) > 1e-2 + 1e-2 * np.abs(b)).mean() <= 0.01
+        gathered = [torch.empty_like(tp_out) for _ in range(world)]
+        dist.all_gather(gathered, tp_out, group=tp.device_group)
+        for gg in gathered:
+            assert torch.equal(gg, tp_out)
     ps.destroy_model_parallel()
     dist.destroy_process_group()
 
