@@ -59,6 +59,9 @@ def parse():
 
 
 def dist_setup(n):
+    # keep rank 0's stdout to the one JSON line (NCCL's version banner goes to stdout)
+    if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+        os.environ["NCCL_DEBUG"] = "WARN"
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
