@@ -16,15 +16,24 @@
 
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int BM = 128, BK = 64;
 constexpr int A_TILE = BM * BK * 2;
-constexpr int B_TILE = BN * BK * 2;
-constexpr int STAGE_BYTES = A_TILE + B_TILE;
 constexpr int NUM_THREADS = 384;
-constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
-// kind::f16 instruction descriptor: D f32, A/B bf16, both K-major
-constexpr uint32_t IDESC_BF16 = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                                ((uint32_t)(BM >> 4) << 24);
+
+// Tile width BN (32 .. 256): small M uses narrow tiles so that more SMs stream the
+// weights; large M uses 256-wide tiles for operand reuse.
+template <int BN>
+struct GCfg {
+    static constexpr int B_TILE = BN * BK * 2;
+    static constexpr int STAGE_BYTES = A_TILE + B_TILE;
+    static constexpr int STAGES = (192 * 1024) / STAGE_BYTES > 8 ? 8 : (192 * 1024) / STAGE_BYTES;
+    static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
+    static constexpr int CPT = BN / 2;            // columns per epilogue thread
+    static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+    // kind::f16 instruction descriptor: D f32, A/B bf16, both K-major
+    static constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                      ((uint32_t)(BM >> 4) << 24);
+};
 
 struct Args {
     __nv_bfloat16* out;
@@ -32,17 +41,21 @@ struct Args {
     int M, N, num_kb, m_tiles, n_tiles;
 };
 
-__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(IDESC_BF16), "r"(accumulate));
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
+template <int BN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Args args) {
     using namespace sm100;
+    using C = GCfg<BN>;
+    constexpr int STAGES = C::STAGES, STAGE_BYTES = C::STAGE_BYTES, CPT = C::CPT;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
@@ -66,7 +79,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         prefetch_tensormap(&tmA);
         prefetch_tensormap(&tmB);
     }
-    if (warp == 1) tmem_alloc(tmem_slot, 512);
+    if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -93,8 +106,9 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                         // the tensor maps address bytes: a 64-element bf16 K block is 128 bytes
                         const int kx = kb * BK * 2;
                         tma_load_2d(a, &tmA, &full[s], kx, m_blk * BM);
-                        tma_load_2d(b, &tmB, &full[s], kx, n_blk * BN);
-                        tma_load_2d(b + 128 * BK * 2, &tmB, &full[s], kx, n_blk * BN + 128);
+#pragma unroll
+                        for (int j = 0; j < (BN + 127) / 128; ++j)
+                            tma_load_2d(b + j * 128 * BK * 2, &tmB, &full[s], kx, n_blk * BN + j * 128);
                     }
                     __syncwarp();
                 }
@@ -123,7 +137,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                         const uint64_t bdesc = smem_desc_sw128(a + A_TILE);
 #pragma unroll
                         for (int kk = 0; kk < BK / 16; ++kk)
-                            mma_bf16(d, adesc + 2 * kk, bdesc + 2 * kk, (kb > 0 || kk > 0) ? 1u : 0u);
+                            mma_bf16(d, adesc + 2 * kk, bdesc + 2 * kk, C::IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
                         mma_commit(&empty[s]);
                     }
                     mma_commit(&tfull[as]);
@@ -147,27 +161,27 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             if (!__all_sync(0xffffffffu, mbar_wait(&tfull[as], (t >> 1) & 1, abort_flag))) break;
             tc_fence_after();
             const int grow = m_blk * BM + row;
-            __nv_bfloat16* dst = args.out + (int64_t)grow * args.ldo + n_blk * BN + 128 * h;
+            __nv_bfloat16* dst = args.out + (int64_t)grow * args.ldo + n_blk * BN + CPT * h;
 #pragma unroll
-            for (int ch = 0; ch < 4; ++ch) {
-                float v[32];
-                tmem_ld32(lane_base + as * BN + 128 * h + 32 * ch, v);
+            for (int ch = 0; ch < CPT / 16; ++ch) {
+                float v[16];
+                tmem_ld16(lane_base + as * BN + CPT * h + 16 * ch, v);
                 tmem_wait_ld();
-                if (ch == 3) {
+                if (ch == CPT / 16 - 1) {
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&tempty[as]);
                 }
                 if (grow < args.M) {
-                    uint32_t w[16];
+                    uint32_t w[8];
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
+                    for (int i = 0; i < 8; ++i) {
                         __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
                         w[i] = *reinterpret_cast<uint32_t*>(&b2);
                     }
-                    uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * ch);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+                    uint4* d4 = reinterpret_cast<uint4*>(dst + 16 * ch);
+                    d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                    d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
                 }
             }
         }
@@ -176,13 +190,30 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, 512);
+        tmem_dealloc(tmem_base, C::TMEM_COLS);
     }
 }
 
-void make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols) {
-    // bf16 [rows, cols] as a byte matrix of 2*cols bytes per row; box 64 elements x 128 rows
-    ab::make_tmap_2d_u8(map, base, rows, cols * 2, 128, 128, true);
+template <int BN>
+void launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, Args args, int dev, cudaStream_t st) {
+    args.n_tiles = args.N / BN;
+    const int tiles = args.m_tiles * args.n_tiles;
+    const int grid = std::min(tiles, ab::num_sms(dev));
+    AB_CUDA(cudaFuncSetAttribute(gemm_bf16_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, GCfg<BN>::SMEM_BYTES));
+    gemm_bf16_kernel<BN><<<grid, NUM_THREADS, GCfg<BN>::SMEM_BYTES, st>>>(tmA, tmB, args);
+}
+
+void make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    // bf16 [rows, cols] as a byte matrix of 2*cols bytes per row; box 64 elements x box_rows
+    ab::make_tmap_2d_u8(map, base, rows, cols * 2, 128, box_rows, true);
+}
+
+// Tile width by problem size: enough tiles to cover the SMs when M is small.
+int pick_bn(int M, int N, int sms) {
+    const int m_tiles = (M + BM - 1) / BM;
+    for (int bn : {256, 128, 64, 32})
+        if (N % bn == 0 && m_tiles * (N / bn) >= sms) return bn;
+    return N % 32 == 0 ? 32 : 256;
 }
 
 }  // namespace
@@ -204,17 +235,22 @@ AB_ENTRY(gemm_a16w16,
     const int M = (int)a->shape[0], K = (int)a->shape[1], N = (int)w->shape[0];
     AB_CHECK(w->shape[1] == K, "W must be [N, K] with the K of A");
     AB_CHECK(out->shape[0] == M && out->shape[1] == N, "out must be [M, N]");
-    AB_CHECK(K % BK == 0 && N % BN == 0, "need K % 64 == 0 and N % 256 == 0");
+    AB_CHECK(K % BK == 0 && N % 32 == 0, "need K % 64 == 0 and N % 32 == 0");
     AB_CHECK(out->strides[0] % 8 == 0 && ((uintptr_t)out->ptr & 15) == 0, "out rows must be 16-byte aligned");
     if (M == 0) return;
     DeviceGuard dg(a->device_id);
+    const int dev = a->device_id;
+    const int bn = pick_bn(M, N, num_sms(dev));
     CUtensorMap tmA, tmB;
-    make_tmap_bf16(&tmA, a->ptr, M, K);
-    make_tmap_bf16(&tmB, w->ptr, N, K);
-    Args args{(__nv_bfloat16*)out->ptr, out->strides[0], M, N, K / BK, (M + BM - 1) / BM, N / BN};
-    const int tiles = args.m_tiles * args.n_tiles;
-    const int grid = std::min(tiles, num_sms(a->device_id));
-    AB_CUDA(cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    gemm_bf16_kernel<<<grid, NUM_THREADS, SMEM_BYTES, as_stream(stream)>>>(tmA, tmB, args);
+    make_tmap_bf16(&tmA, a->ptr, M, K, 128);
+    make_tmap_bf16(&tmB, w->ptr, N, K, bn < 128 ? bn : 128);
+    Args args{(__nv_bfloat16*)out->ptr, out->strides[0], M, N, K / BK, (M + BM - 1) / BM, 0};
+    cudaStream_t st = as_stream(stream);
+    switch (bn) {
+        case 256: launch_gemm<256>(tmA, tmB, args, dev, st); break;
+        case 128: launch_gemm<128>(tmA, tmB, args, dev, st); break;
+        case 64: launch_gemm<64>(tmA, tmB, args, dev, st); break;
+        default: launch_gemm<32>(tmA, tmB, args, dev, st); break;
+    }
     check_launch("gemm_a16w16");
 }

@@ -455,10 +455,21 @@ def run_gemm_ar(args, rank, world, local):
 
         us = 1e3 * _time_loop(ours, args.steps, args.warmup, world)
         us_b = 1e3 * _time_loop(base, args.steps, args.warmup, world)
+        # the two halves alone, to show which one sets each total
+        from aiter_b200.gemm import gemm_a16w16
+        y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+        y2 = torch.empty_like(y)
+        parts = {
+            "ours_gemm_us": lambda: gemm_a16w16(A, W, y),
+            "cublas_gemm_us": lambda: torch.matmul(A, B, out=y),
+            "ours_ar_us": lambda: tp.ca_comm.all_reduce(y, out=y2),
+            "nccl_ar_us": lambda: torch.distributed.all_reduce(y, group=tp.device_group),
+        }
+        part_us = {k: round(1e3 * _time_loop(f, args.steps, args.warmup, world), 2) for k, f in parts.items()}
         ar_bytes = 2.0 * (world - 1) / world * M * N * 2
         rows.append({"M": M, "ours_us": round(us, 2), "cublas_nccl_us": round(us_b, 2),
                      "speedup": round(us_b / us, 3), "ours_busbw_GBs": round(ar_bytes / (us * 1e-6) / 1e9, 1),
-                     "gemm_tflops": round(2.0 * M * K * N / (us * 1e-6) / 1e12, 2)})
+                     "gemm_tflops": round(2.0 * M * K * N / (us * 1e-6) / 1e12, 2), **part_us})
     ps.destroy_model_parallel()
     big = rows[-1]
     return {"metric": "GEMM+allreduce latency (config 4, M=8192)", "mode": "gemm_ar", "value": big["ours_us"],

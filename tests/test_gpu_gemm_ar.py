@@ -32,6 +32,22 @@ def test_gemm_a16w16_vs_torch(M, N, K):
     assert bool((err <= tol).all()), float(err.max())
 
 
+# (M, N, K) chosen so that every tile width runs: 32-wide (M=1, N=4096), 64-wide
+# (N=10240), 128-wide (M=200, N=16384), 256-wide (M=2048, N=4096); plus N=96.
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (3, 96, 192), (100, 10240, 256), (200, 16384, 128),
+                                   (2048, 4096, 512)])
+def test_gemm_every_tile_width_vs_torch(M, N, K):
+    g = torch.Generator(device=dev()).manual_seed(M + N + K)
+    A = torch.randn(M, K, device=dev(), generator=g).to(torch.bfloat16)
+    W = torch.randn(N, K, device=dev(), generator=g).to(torch.bfloat16)
+    out = gemm_a16w16(A, W)
+    ref = A.float() @ W.float().t()
+    torch.cuda.synchronize()
+    err = (out.float() - ref).abs()
+    tol = 1e-2 * ref.abs() + 1e-2 * ref.abs().max()
+    assert bool((err <= tol).all()), float(err.max())
+
+
 def test_gemm_writes_only_its_rows_of_a_strided_output():
     A = torch.randn(5, 128, device=dev()).to(torch.bfloat16)
     W = torch.randn(256, 128, device=dev()).to(torch.bfloat16)
