@@ -33,15 +33,15 @@ constexpr int BM = 128, BK = 128;
 constexpr int A_TILE = BM * BK;
 constexpr int NUM_THREADS = 384;
 constexpr int TMEM_COLS = 512;
+constexpr int SRING = 8;            // block-scale ring depth (K blocks ahead)
+constexpr int SRING_FLOATS = 132;   // 128 row scales + 2 column-block scales, padded
 
 // Tile configuration by accumulator width BN.  TMEM (512 fp32 columns x 128 lanes)
 // is split into 512/BN accumulator slabs: the MMA writes one slab per 128-wide K
-// block while the epilogue promotes the previous ones, so more slabs hide more of
-// the MMA -> commit -> epilogue -> MMA turnaround.  The smem ring takes what the
-// operand tiles leave of 192 KB.
+// block while the epilogue promotes the previous ones.  The smem ring takes what
+// the operand tiles leave of 192 KB.
 template <int BN_>
 struct Cfg {
-    static constexpr int BN = BN_;
     static constexpr int SLABS = TMEM_COLS / BN_;
     static constexpr int B_TILE = BN_ * BK;
     static constexpr int STAGE_BYTES = A_TILE + B_TILE;
@@ -49,9 +49,14 @@ struct Cfg {
     static constexpr int CPT = BN_ / 2;  // accumulator columns per epilogue thread
     static constexpr uint32_t IDESC = sm100::idesc_e4m3_f32(BM, BN_);
     static constexpr int BAR_BYTES = 512;
-    static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + BAR_BYTES + 2 * 256 * 4;
+    static constexpr int RED_BYTES = 2 * 256 * 4;                 // stage-1 row amax exchange
+    static constexpr int SRING_BYTES = SRING * SRING_FLOATS * 4;  // block-scale ring
+    static constexpr int OUT_BYTES = BM * 128;                    // stage-1 fp8 output tile
+    static constexpr int SMEM_BYTES =
+        1024 /*align slack*/ + STAGES * STAGE_BYTES + OUT_BYTES + BAR_BYTES + RED_BYTES + SRING_BYTES;
     static_assert(CPT % 64 == 0, "epilogue works in 64-column chunks");
-    static_assert(2 * (STAGES + SLABS) * 8 + 8 <= BAR_BYTES, "barrier area");
+    static_assert(2 * (STAGES + SLABS + SRING) * 8 + 8 <= BAR_BYTES, "barrier area");
+    static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
 };
 
 struct GemmArgs {
@@ -66,9 +71,11 @@ struct GemmArgs {
     int M, N, n_tiles, num_kb, max_m_blocks, act, out_cols, E, rows_pad;
 };
 
+// SiLU with the hardware exp2 and an approximate divide: the result is rounded to
+// bf16 right after, which hides their few-ulp fp32 error.
 __device__ __forceinline__ float act_fn(float g, int act) {
     if (act == AITER_ACT_GELU) return 0.5f * g * (1.0f + erff(g * 0.70710678118654752f));
-    return g / (1.0f + expf(-g));
+    return __fdividef(g, 1.0f + __expf(-g));
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
@@ -84,25 +91,34 @@ __device__ __forceinline__ void red_add_bf16x8(__nv_bfloat16* dst, uint32_t a, u
 }
 
 // STAGE 1: B tile = 128 gate rows + 128 up rows of w1 (BN must be 256), epilogue
-//          act(gate)*up -> 1x128 fp8 requant of the 128 outputs.
+//          act(gate)*up -> 1x128 fp8 requant of the 128 outputs, TMA-stored.
 // STAGE 2: B tile = BN consecutive rows of w2, epilogue weighted scatter-add.
+//
+// Warp roles: 0 TMA producer, 1 TMEM owner + MMA issuer, 2 block-scale prefetcher
+// (cp.async of a_scale[kb][tile rows] and the two w-scales of the tile's column
+// blocks into an SRING-deep smem ring, so the epilogue never waits on a global
+// load), 4..11 epilogue.
 template <int STAGE, int BN_>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const GemmArgs args) {
+                    const __grid_constant__ CUtensorMap tmO, const GemmArgs args) {
     using namespace sm100;
     using C = Cfg<BN_>;
     static_assert(STAGE == 2 || BN_ == 256, "stage 1 pairs 128 gate with 128 up columns");
     constexpr int STAGES = C::STAGES, SLABS = C::SLABS, CPT = C::CPT, STAGE_BYTES = C::STAGE_BYTES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+    uint8_t* out_tile = smem + STAGES * STAGE_BYTES;  // 1024-aligned (swizzled TMA store source)
+    uint64_t* full = reinterpret_cast<uint64_t*>(out_tile + C::OUT_BYTES);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + SLABS;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + SLABS);
+    uint64_t* sfull = tempty + SLABS;
+    uint64_t* sempty = sfull + SRING;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sempty + SRING);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    float* red = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES + C::BAR_BYTES);
+    float* red = reinterpret_cast<float*>(out_tile + C::OUT_BYTES + C::BAR_BYTES);
+    float* sring = red + 2 * 256;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -114,10 +130,15 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             mbar_init(&tfull[s], 1);
             mbar_init(&tempty[s], 8);
         }
+        for (int s = 0; s < SRING; ++s) {
+            mbar_init(&sfull[s], 32);  // one cp.async arrival per prefetcher lane
+            mbar_init(&sempty[s], 8);  // one arrival per epilogue warp
+        }
         *abort_flag = 0;
         fence_mbar_init();
         prefetch_tensormap(&tmA);
         prefetch_tensormap(&tmB);
+        if (STAGE == 1) prefetch_tensormap(&tmO);
     }
     if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
     tc_fence_before();
@@ -127,6 +148,7 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
 
     const int num_m_blocks = min(args.num_valid[0] / BM, args.max_m_blocks);
     const int num_tiles = num_m_blocks * args.n_tiles;
+    const int nblk128 = args.N / 128;
 
     if (warp < 4) {
     setmaxnreg_dec<40>();
@@ -198,6 +220,42 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             }
         }
         __syncwarp();
+    } else if (warp == 2) {
+        // ------------------------------------------------------------ scale prefetcher
+        // ring entry (tile, kb): [0,128) a_scale of the tile's rows, [128] and [129]
+        // the w-scales of the two 128-column blocks the epilogue threads cover
+        // (stage 1: gate block, up block; stage 2: columns [0,128) and [128,256)).
+        int it = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+            const int m_blk = tile / args.n_tiles, n_blk = tile % args.n_tiles;
+            const int e = min(max(args.sorted_eids[m_blk], 0), args.E - 1);
+            const float* sbA;
+            const float* sbB;
+            if (STAGE == 1) {
+                sbA = args.b_scale + ((int64_t)e * nblk128 + n_blk) * args.num_kb;
+                sbB = args.b_scale + ((int64_t)e * nblk128 + (nblk128 >> 1) + n_blk) * args.num_kb;
+            } else {
+                sbA = args.b_scale + ((int64_t)e * nblk128 + n_blk * (BN_ / 128)) * args.num_kb;
+                sbB = BN_ >= 256 ? sbA + args.num_kb : sbA;
+            }
+            const float* sa = args.a_scale + m_blk * BM + lane;
+            for (int kb = 0; kb < args.num_kb; ++kb, ++it) {
+                const int i = it % SRING;
+                ok = __all_sync(0xffffffffu, mbar_wait(&sempty[i], ((it / SRING) & 1) ^ 1, abort_flag));
+                if (!ok) break;
+                float* dst = sring + i * SRING_FLOATS;
+                const float* src = sa + (int64_t)kb * args.rows_pad;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) cp_async4(dst + lane + 32 * j, src + 32 * j);
+                if (lane == 0) {
+                    cp_async4(dst + 128, sbA + kb);
+                    cp_async4(dst + 129, sbB + kb);
+                }
+                cp_async_mbar_arrive(&sfull[i]);
+            }
+        }
+        cp_async_wait_all();
     }
     } else {
         setmaxnreg_inc<232>();
@@ -209,34 +267,24 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         bool ok = true;
         for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++tcount) {
             const int m_blk = tile / args.n_tiles, n_blk = tile % args.n_tiles;
-            const int e = min(max(args.sorted_eids[m_blk], 0), args.E - 1);
-            const int sid = args.sorted_ids[m_blk * BM + row];
-            const int tok = sid & 0xFFFFFF;
-            const bool valid = tok < args.M;
             const int srow = m_blk * BM + row;
-            const float* sa_p = args.a_scale + srow;
-            const int nblk128 = args.N / 128;
-            const float* sb0_p;
-            const float* sb1_p;
-            if (STAGE == 1) {
-                sb0_p = args.b_scale + ((int64_t)e * nblk128 + n_blk) * args.num_kb;
-                sb1_p = args.b_scale + ((int64_t)e * nblk128 + (nblk128 >> 1) + n_blk) * args.num_kb;
-            } else {
-                sb0_p = args.b_scale + ((int64_t)e * nblk128 + n_blk * (BN_ / 128) + (h * CPT) / 128) * args.num_kb;
-                sb1_p = sb0_p;
-            }
+            // needed only after the K loop: issued now, they land meanwhile
+            const int sid = args.sorted_ids[srow];
+            const float wrow = STAGE == 2 ? args.sorted_w[srow] : 0.f;
             float acc[CPT];
             float v[64];
-            float sa_next = valid ? __ldg(sa_p) : 0.f;
-            float sb0_next = __ldg(sb0_p), sb1_next = __ldg(sb1_p);
             for (int kb = 0; kb < args.num_kb; ++kb, ++acc_it) {
-                const float s0 = sa_next * sb0_next;
-                const float s1 = sa_next * sb1_next;
-                if (kb + 1 < args.num_kb) {  // prefetch the next K block's scales
-                    sa_next = valid ? __ldg(sa_p + (int64_t)(kb + 1) * args.rows_pad) : 0.f;
-                    sb0_next = __ldg(sb0_p + kb + 1);
-                    sb1_next = __ldg(sb1_p + kb + 1);
+                const int si = acc_it % SRING;
+                if (!__all_sync(0xffffffffu, mbar_wait(&sfull[si], (acc_it / SRING) & 1, abort_flag))) {
+                    ok = false;
+                    break;
                 }
+                const float* se = sring + si * SRING_FLOATS;
+                const float sa = se[row], sbA = se[128], sbB = se[129];
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sempty[si]);
+                const float s0 = sa * (STAGE == 2 && h * CPT >= 128 ? sbB : sbA);
+                const float s1 = sa * sbB;
                 const int as = acc_it % SLABS;
                 const uint32_t aph = (acc_it / SLABS) & 1;
                 if (!__all_sync(0xffffffffu, mbar_wait(&tfull[as], aph, abort_flag))) { ok = false; break; }
@@ -260,12 +308,15 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
 #pragma unroll
                         for (int j = 0; j < 64; ++j) acc[64 * ch + j] = v[j] * sc;
                     } else {
+                        const uint64_t sc2 = splat2(sc);
 #pragma unroll
-                        for (int j = 0; j < 64; ++j) acc[64 * ch + j] = fmaf(v[j], sc, acc[64 * ch + j]);
+                        for (int j = 0; j < 64; j += 2) fma2(&acc[64 * ch + j], &v[j], sc2);
                     }
                 }
             }
             if (!ok) break;
+            const int tok = sid & 0xFFFFFF;
+            const bool valid = tok < args.M;
             if constexpr (STAGE == 1) {
                 float amax = 0.f;
 #pragma unroll
@@ -277,42 +328,51 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 }
                 float* rb = red + (tcount & 1) * 256;
                 rb[h * 128 + row] = amax;
+                // the previous tile's TMA store must have finished reading out_tile
+                if (threadIdx.x == 128) bulk_wait_read0();
                 named_barrier(1, 256);
                 amax = fmaxf(rb[row], rb[128 + row]);
                 float scale = amax / 448.0f;
                 if (scale == 0.f) scale = 1.0f;
-                if (valid) {
-                    uint8_t* dst = reinterpret_cast<uint8_t*>(args.out) + (int64_t)srow * args.out_cols + n_blk * 128 + 64 * h;
+                const float rs = 1.0f / scale;
+                // row `row` of the 128x128-byte tile, 128-byte swizzle: 16-byte chunk c
+                // of the row sits at chunk c ^ (row & 7)
+                uint8_t* orow = out_tile + row * 128;
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        uint32_t w[4];
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t w[4];
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const int j = 16 * c + 4 * i;
-                            __nv_fp8x4_e4m3 p4(make_float4(acc[j] / scale, acc[j + 1] / scale, acc[j + 2] / scale,
-                                                           acc[j + 3] / scale));
-                            w[i] = *reinterpret_cast<uint32_t*>(&p4);
-                        }
-                        *reinterpret_cast<uint4*>(dst + 16 * c) = make_uint4(w[0], w[1], w[2], w[3]);
+                    for (int i = 0; i < 4; ++i) {
+                        const int j = 16 * c + 4 * i;
+                        __nv_fp8x4_e4m3 p4(make_float4(acc[j] * rs, acc[j + 1] * rs, acc[j + 2] * rs, acc[j + 3] * rs));
+                        w[i] = *reinterpret_cast<uint32_t*>(&p4);
                     }
-                    if (h == 0) args.out_scale[(int64_t)n_blk * args.rows_pad + srow] = scale;
+                    const int chunk = (4 * h + c) ^ (row & 7);
+                    *reinterpret_cast<uint4*>(orow + 16 * chunk) = make_uint4(w[0], w[1], w[2], w[3]);
+                }
+                if (h == 0) args.out_scale[(int64_t)n_blk * args.rows_pad + srow] = scale;
+                fence_proxy_async_smem();
+                named_barrier(1, 256);
+                if (threadIdx.x == 128) {
+                    tma_store_2d(&tmO, out_tile, n_blk * 128, m_blk * BM);
+                    bulk_commit();
                 }
             } else {
-                const float w = args.sorted_w[srow];
                 if (valid) {
                     __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.out) + (int64_t)tok * args.out_cols +
                                          n_blk * BN_ + CPT * h;
 #pragma unroll
                     for (int c = 0; c < CPT / 8; ++c) {
                         const int j = 8 * c;
-                        red_add_bf16x8(dst + j, pack_bf16x2(acc[j] * w, acc[j + 1] * w),
-                                       pack_bf16x2(acc[j + 2] * w, acc[j + 3] * w),
-                                       pack_bf16x2(acc[j + 4] * w, acc[j + 5] * w),
-                                       pack_bf16x2(acc[j + 6] * w, acc[j + 7] * w));
+                        red_add_bf16x8(dst + j, pack_bf16x2(acc[j] * wrow, acc[j + 1] * wrow),
+                                       pack_bf16x2(acc[j + 2] * wrow, acc[j + 3] * wrow),
+                                       pack_bf16x2(acc[j + 4] * wrow, acc[j + 5] * wrow),
+                                       pack_bf16x2(acc[j + 6] * wrow, acc[j + 7] * wrow));
                     }
                 }
             }
         }
+        if (STAGE == 1 && threadIdx.x == 128) bulk_wait0();
     }
     tc_fence_before();
     __syncthreads();
@@ -396,14 +456,15 @@ void check_sorted_operand(aiter_tensor_t* a, aiter_tensor_t* sc, int rows_pad, c
 }
 
 template <int STAGE, int BN_>
-void launch(const CUtensorMap& tmA, const CUtensorMap& tmB, GemmArgs a, int dev, cudaStream_t st) {
+void launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO, GemmArgs a, int dev,
+            cudaStream_t st) {
     a.n_tiles = STAGE == 1 ? a.n_tiles : a.N / BN_;
     const int tiles = a.max_m_blocks * a.n_tiles;
     if (tiles == 0) return;
     const int grid = std::min(tiles, ab::num_sms(dev));
     constexpr int smem = Cfg<BN_>::SMEM_BYTES;
     AB_CUDA(cudaFuncSetAttribute(moe_gemm_fp8_kernel<STAGE, BN_>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    moe_gemm_fp8_kernel<STAGE, BN_><<<grid, NUM_THREADS, smem, st>>>(tmA, tmB, a);
+    moe_gemm_fp8_kernel<STAGE, BN_><<<grid, NUM_THREADS, smem, st>>>(tmA, tmB, tmO, a);
     ab::check_launch(STAGE == 1 ? "moe_stage1_fp8_blockscale" : "moe_stage2_fp8_blockscale");
 }
 
@@ -468,7 +529,9 @@ AB_ENTRY(moe_stage1_fp8_blockscale,
     CUtensorMap tmA, tmB;
     make_tmap_2d_u8(&tmA, a1->ptr, (uint64_t)c.rows_pad, D, 128, 128, true);
     make_tmap_2d_u8(&tmB, w1->ptr, (uint64_t)E * N, D, 128, 128, true);
-    launch<1, 256>(tmA, tmB, a, a1->device_id, as_stream(stream));
+    CUtensorMap tmO;  // output tiles: 128 sorted rows x 128 fp8 columns
+    make_tmap_2d_u8(&tmO, out->ptr, (uint64_t)c.rows_pad, I, 128, 128, true);
+    launch<1, 256>(tmA, tmB, tmO, a, a1->device_id, as_stream(stream));
 }
 
 AB_ENTRY(moe_stage2_fp8_blockscale,
@@ -520,8 +583,8 @@ AB_ENTRY(moe_stage2_fp8_blockscale,
     CUtensorMap tmA, tmB;
     make_tmap_2d_u8(&tmA, a2->ptr, (uint64_t)c.rows_pad, I, 128, 128, true);
     make_tmap_2d_u8(&tmB, w2->ptr, (uint64_t)E * D, I, 128, 128, true);
-    if (stage2_bn() == 256) launch<2, 256>(tmA, tmB, a, a2->device_id, as_stream(stream));
-    else launch<2, 128>(tmA, tmB, a, a2->device_id, as_stream(stream));
+    if (stage2_bn() == 256) launch<2, 256>(tmA, tmB, tmA, a, a2->device_id, as_stream(stream));
+    else launch<2, 128>(tmA, tmB, tmA, a, a2->device_id, as_stream(stream));
 }
 
 extern "C" int aiter_device_error(int clear) {

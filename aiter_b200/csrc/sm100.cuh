@@ -1,5 +1,5 @@
 // sm_100a building blocks written as inline PTX: mbarriers with bounded waits,
-// TMA tile / gather4 loads, tcgen05 MMA, commit, TMEM alloc and loads.
+// TMA tile loads and stores, cp.async, tcgen05 MMA, commit, TMEM alloc and loads.
 #pragma once
 #include <cuda.h>
 #include <stdint.h>
@@ -76,15 +76,41 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
         : "memory");
 }
 
-// Four rows (y0..y3) of `map`'s box (one row high) into dst, dst + row bytes, ...
-__device__ __forceinline__ void tma_gather4(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y0,
-                                            int y1, int y2, int y3) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y0), "r"(y1), "r"(y2),
-        "r"(y3)
-        : "memory");
+// 2-D tiled TMA store of the box at (x, y) from shared memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(smem_u32(src)), "r"(x), "r"(y)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// wait until the committed bulk stores no longer read shared memory
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// generic-proxy shared-memory writes -> visible to the async proxy (TMA store)
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 4-byte asynchronous global -> shared copy (LDGSTS) and the mbarrier arrival that
+// fires once all of this thread's earlier cp.async copies have landed (the barrier's
+// expected count includes it: .noinc).
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// acc[0..1] += v[0..1] * s, as one packed f32x2 FMA (two fma.rn.f32, same bits)
+__device__ __forceinline__ void fma2(float* acc, const float* v, uint64_t s2) {
+    uint64_t& a = *reinterpret_cast<uint64_t*>(acc);
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(a) : "l"(*reinterpret_cast<const uint64_t*>(v)), "l"(s2));
+}
+__device__ __forceinline__ uint64_t splat2(float s) {
+    const uint32_t u = __float_as_uint(s);
+    return ((uint64_t)u << 32) | u;
 }
 
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
