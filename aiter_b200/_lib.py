@@ -11,6 +11,7 @@ There is no fallback: if the library is missing, every op raises.
 """
 import ctypes
 import os
+import struct
 import threading
 
 import torch
@@ -59,19 +60,23 @@ def dtype_code(dt):
         raise TypeError(f"unsupported dtype {dt}") from None
 
 
+_PACK = struct.Struct("<QQi4x8q8qii")  # the 160-byte aiter_tensor_t layout
+_ZEROS = (0,) * 8
+
+
 def to_aiter(t: torch.Tensor) -> aiter_tensor_t:
-    if t.dim() > 8:
+    nd = t.dim()
+    if nd > 8:
         raise ValueError("at most 8 dims")
-    a = aiter_tensor_t()
-    a.ptr = t.data_ptr() if t.numel() > 0 else 0
-    a.numel_ = t.numel()
-    a.ndim = t.dim()
-    for i, (s, st) in enumerate(zip(t.shape, t.stride())):
-        a.shape[i] = s
-        a.strides[i] = st
-    a.dtype_ = dtype_code(t.dtype)
-    a.device_id = t.device.index if t.is_cuda else -1
-    return a
+    n = t.numel()
+    return aiter_tensor_t.from_buffer_copy(_PACK.pack(
+        t.data_ptr() if n > 0 else 0, n, nd, *(tuple(t.shape) + _ZEROS[nd:]), *(t.stride() + _ZEROS[nd:]),
+        dtype_code(t.dtype), t.get_device()))
+
+
+def current_stream_ptr(device_index: int) -> int:
+    """Raw cudaStream_t of the current torch stream of a device."""
+    return torch._C._cuda_getCurrentRawStream(device_index)
 
 
 _lock = threading.Lock()
@@ -164,7 +169,7 @@ def call(name, *args, stream=None):
                 if not isinstance(v, torch.Tensor):
                     raise TypeError(f"{name}: expected a tensor, got {type(v).__name__}")
                 if device is None and v.is_cuda:
-                    device = v.device
+                    device = v.get_device()
                 a = to_aiter(v)
                 keep.append(a)
                 cargs.append(ctypes.byref(a))
@@ -179,8 +184,8 @@ def call(name, *args, stream=None):
         elif k == S:
             cargs.append(None if v is None else v.encode())
     if stream is None:
-        stream = torch.cuda.current_stream(device).cuda_stream if device is not None else 0
-    L.aiter_clear_last_error()
+        stream = current_stream_ptr(device) if device is not None else 0
+    # every entry point clears the thread's last error on entry
     ret = getattr(L, name)(*cargs, ctypes.c_void_p(stream))
     if ret != 0:
         raw = L.aiter_get_last_error()

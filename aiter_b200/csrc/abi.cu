@@ -1,5 +1,7 @@
 // Error bridge and small host utilities of the C ABI
 // (csrc/include/aiter_ctypes_error.h:56-67 in the reference).
+#include <mutex>
+#include <vector>
 #include "common.cuh"
 
 namespace ab {
@@ -18,6 +20,27 @@ int num_sms(int dev) {
         cache[dev] = v;
     }
     return cache[dev];
+}
+
+void set_max_smem_once(const void* kernel, int bytes, int dev) {
+    struct Done {
+        const void* kernel;
+        int bytes, dev;
+    };
+    static std::mutex mu;
+    static std::vector<Done> done;
+    std::lock_guard<std::mutex> g(mu);
+    // the attribute is an upper bound: keep the largest size set per kernel and device
+    for (Done& d : done)
+        if (d.kernel == kernel && d.dev == dev) {
+            if (bytes > d.bytes) {
+                AB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+                d.bytes = bytes;
+            }
+            return;
+        }
+    AB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done.push_back({kernel, bytes, dev});
 }
 
 }  // namespace ab

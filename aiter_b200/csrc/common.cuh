@@ -137,6 +137,11 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 
 int num_sms(int dev);
 
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) costs a driver call; entry points
+// call this instead, which raises the limit only when a launch needs more than any
+// earlier one on that device.
+void set_max_smem_once(const void* kernel, int bytes, int dev);
+
 }  // namespace ab
 
 // ----------------------------------------------------------------- device side

@@ -19,6 +19,7 @@ namespace {
 constexpr int BM = 128, BK = 64;
 constexpr int A_TILE = BM * BK * 2;
 constexpr int NUM_THREADS = 384;
+constexpr int kSwabMaxM = 512;  // up to this many rows: the swap-AB split-K kernel
 
 // Tile width BN (32 .. 256): small M uses narrow tiles so that more SMs stream the
 // weights; large M uses 256-wide tiles for operand reuse.
@@ -199,8 +200,214 @@ void launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, Args args, int 
     args.n_tiles = args.N / BN;
     const int tiles = args.m_tiles * args.n_tiles;
     const int grid = std::min(tiles, ab::num_sms(dev));
-    AB_CUDA(cudaFuncSetAttribute(gemm_bf16_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, GCfg<BN>::SMEM_BYTES));
+    ab::set_max_smem_once((const void*)gemm_bf16_kernel<BN>, GCfg<BN>::SMEM_BYTES, dev);
     gemm_bf16_kernel<BN><<<grid, NUM_THREADS, GCfg<BN>::SMEM_BYTES, st>>>(tmA, tmB, args);
+}
+
+// ---------------------------------------------------------------------------
+// Small-M kernel (swap-AB, split-K over a thread-block cluster).
+//
+// For few activation rows the weights are the stream that matters, so they take
+// the 128-row MMA side: D^T[n, m] = W[n, :] . A[m, :] with M=128 weight rows and
+// N=MT activation rows (MT in 32..256).  A tile of 128 weight rows is split along K
+// over the S CTAs of a cluster (S <= 8) so that tiles x S fills the SMs.  Each CTA
+// leaves its fp32 partial in its own shared memory, [MT][128] (activation row
+// major), and after a cluster barrier CTA r sums rows [r*MT/S, (r+1)*MT/S) of all S
+// partials through distributed shared memory, in rank order (deterministic), and
+// stores them as bf16.  One tile per CTA (not persistent).
+template <int MT>
+struct SCfg {
+    static constexpr int W_TILE = 128 * BK * 2;
+    static constexpr int X_TILE = MT * BK * 2;
+    static constexpr int STAGE_BYTES = W_TILE + X_TILE;
+    static constexpr int STAGES = (192 * 1024) / STAGE_BYTES > 8 ? 8 : (192 * 1024) / STAGE_BYTES;
+    static constexpr int P_BYTES = MT * 128 * 4;
+    static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
+    static constexpr int CPT = MT / 2;  // accumulator columns per epilogue thread
+    static constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(MT >> 3) << 17) |
+                                      ((uint32_t)(128 >> 4) << 24);
+    static_assert(P_BYTES <= STAGES * STAGE_BYTES, "partial tile reuses the operand ring");
+    static_assert(CPT % 16 == 0, "epilogue reads 16-column groups");
+};
+
+struct SArgs {
+    __nv_bfloat16* out;
+    int64_t ldo;
+    int M, N, num_kb, n_tiles, split;
+};
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float4 ld_dsmem_f4(const float* local, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(sm100::smem_u32(local)), "r"(rank));
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(remote)
+                 : "memory");
+    return v;
+}
+
+template <int MT>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+gemm_bf16_swab_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                      const SArgs args) {
+    using namespace sm100;
+    using C = SCfg<MT>;
+    constexpr int STAGES = C::STAGES, STAGE_BYTES = C::STAGE_BYTES, CPT = C::CPT;
+    constexpr int TMEM_COLS = MT;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tdone = empty + STAGES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tdone + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    float* part = reinterpret_cast<float*>(smem);  // [MT][128] fp32, after the K loop
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int S = args.split;
+    const int rank = (int)cluster_ctarank();
+    const int tile = blockIdx.x / S;
+    const int n_blk = tile % args.n_tiles, m_blk = tile / args.n_tiles;
+    const int kb0 = (int)((int64_t)args.num_kb * rank / S), kb1 = (int)((int64_t)args.num_kb * (rank + 1) / S);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(tdone, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+        prefetch_tensormap(&tmW);
+        prefetch_tensormap(&tmX);
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        int it = 0;
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+            const int s = it % STAGES;
+            ok = __all_sync(0xffffffffu, mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, abort_flag));
+            if (!ok) break;
+            if (lane == 0) {
+                mbar_expect_tx(&full[s], STAGE_BYTES);
+                uint8_t* w = smem + s * STAGE_BYTES;
+                tma_load_2d(w, &tmW, &full[s], kb * BK * 2, n_blk * 128);
+                tma_load_2d(w + C::W_TILE, &tmX, &full[s], kb * BK * 2, m_blk * MT);
+            }
+            __syncwarp();
+        }
+        if (!ok) {
+            for (int d = 0; d < STAGES && it - 1 - d >= 0; ++d) {
+                const int j = it - 1 - d;
+                mbar_wait(&full[j % STAGES], (j / STAGES) & 1, abort_flag, 200000000ull, false);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            int it = 0;
+            bool ok = true;
+            for (int kb = kb0; kb < kb1; ++kb, ++it) {
+                const int s = it % STAGES;
+                if (!mbar_wait(&full[s], (it / STAGES) & 1, abort_flag)) { ok = false; break; }
+                tc_fence_after();
+                const uint8_t* w = smem + s * STAGE_BYTES;
+                const uint64_t wdesc = smem_desc_sw128(w);
+                const uint64_t xdesc = smem_desc_sw128(w + C::W_TILE);
+#pragma unroll
+                for (int kk = 0; kk < BK / 16; ++kk)
+                    mma_bf16(tmem_base, wdesc + 2 * kk, xdesc + 2 * kk, C::IDESC, (it > 0 || kk > 0) ? 1u : 0u);
+                mma_commit(&empty[s]);
+            }
+            mma_commit(tdone);  // fires once every MMA above has finished
+            (void)ok;
+        }
+        __syncwarp();
+    } else if (warp >= 4) {
+        // TMEM (lane = weight row n, column = activation row m) -> part[m][n]
+        const int q = warp & 3, h = (warp - 4) >> 2;
+        const int n = q * 32 + lane;
+        const bool have = __all_sync(0xffffffffu, mbar_wait(tdone, 0, abort_flag));
+        tc_fence_after();
+        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + CPT * h;
+#pragma unroll
+        for (int c = 0; c < CPT / 16; ++c) {
+            float v[16];
+            tmem_ld16(taddr + 16 * c, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) part[(CPT * h + 16 * c + j) * 128 + n] = (have && kb1 > kb0) ? v[j] : 0.f;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // every partial of the cluster is in place
+    // rows [r*MT/S, (r+1)*MT/S) of the tile, as 4-column groups
+    const int rows_per = MT / S, rbase = rank * rows_per;
+    for (int idx = threadIdx.x; idx < rows_per * 32; idx += NUM_THREADS) {
+        const int m = rbase + idx / 32, c4 = idx % 32;
+        const float* src = part + m * 128 + 4 * c4;
+        float4 acc = ld_dsmem_f4(src, 0);
+        for (int r = 1; r < S; ++r) {
+            const float4 v = ld_dsmem_f4(src, (uint32_t)r);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        const int gm = m_blk * MT + m;
+        if (gm < args.M) {
+            __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+            uint2 pk = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+            *reinterpret_cast<uint2*>(args.out + (int64_t)gm * args.ldo + n_blk * 128 + 4 * c4) = pk;
+        }
+    }
+    cluster_sync();  // peers are done reading this CTA's partial
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+// Split of K over a cluster so that tiles x split covers the SMs once.
+int pick_split(int tiles, int num_kb, int sms) {
+    int s = sms / std::max(tiles, 1);
+    s = std::min(s, 8);
+    s = std::min(s, num_kb);
+    return std::max(s, 1);
+}
+
+template <int MT>
+void launch_swab(const CUtensorMap& tmW, const CUtensorMap& tmX, SArgs args, int dev, cudaStream_t st) {
+    const int tiles = args.n_tiles * ((args.M + MT - 1) / MT);
+    args.split = pick_split(tiles, args.num_kb, ab::num_sms(dev));
+    ab::set_max_smem_once((const void*)gemm_bf16_swab_kernel<MT>, SCfg<MT>::SMEM_BYTES, dev);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(tiles * args.split);
+    cfg.blockDim = dim3(NUM_THREADS);
+    cfg.dynamicSmemBytes = SCfg<MT>::SMEM_BYTES;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = args.split;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    AB_CUDA(cudaLaunchKernelEx(&cfg, gemm_bf16_swab_kernel<MT>, tmW, tmX, args));
 }
 
 void make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
@@ -240,12 +447,27 @@ AB_ENTRY(gemm_a16w16,
     if (M == 0) return;
     DeviceGuard dg(a->device_id);
     const int dev = a->device_id;
+    cudaStream_t st = as_stream(stream);
+    if (M <= kSwabMaxM && N % 128 == 0) {
+        const int mt = M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
+        CUtensorMap tmW, tmX;
+        make_tmap_bf16(&tmW, w->ptr, N, K, 128);
+        make_tmap_bf16(&tmX, a->ptr, M, K, mt);
+        SArgs sa{(__nv_bfloat16*)out->ptr, out->strides[0], M, N, K / BK, N / 128, 1};
+        switch (mt) {
+            case 32: launch_swab<32>(tmW, tmX, sa, dev, st); break;
+            case 64: launch_swab<64>(tmW, tmX, sa, dev, st); break;
+            case 128: launch_swab<128>(tmW, tmX, sa, dev, st); break;
+            default: launch_swab<256>(tmW, tmX, sa, dev, st); break;
+        }
+        check_launch("gemm_a16w16");
+        return;
+    }
     const int bn = pick_bn(M, N, num_sms(dev));
     CUtensorMap tmA, tmB;
     make_tmap_bf16(&tmA, a->ptr, M, K, 128);
     make_tmap_bf16(&tmB, w->ptr, N, K, bn < 128 ? bn : 128);
     Args args{(__nv_bfloat16*)out->ptr, out->strides[0], M, N, K / BK, (M + BM - 1) / BM, 0};
-    cudaStream_t st = as_stream(stream);
     switch (bn) {
         case 256: launch_gemm<256>(tmA, tmB, args, dev, st); break;
         case 128: launch_gemm<128>(tmA, tmB, args, dev, st); break;

@@ -405,6 +405,24 @@ void make_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t
                      uint32_t box_rows, bool swizzle128) {
     AB_CHECK(((uintptr_t)base & 15) == 0, "TMA base address must be 16-byte aligned");
     AB_CHECK(cols % 16 == 0, "TMA row pitch must be a multiple of 16 bytes");
+    // Encoded maps depend only on these values: a small per-thread cache saves the
+    // driver call for operands seen again (weights, reused activation buffers).
+    struct Entry {
+        const void* base;
+        uint64_t rows, cols;
+        uint32_t box_cols, box_rows;
+        bool swz, used;
+        CUtensorMap map;
+    };
+    constexpr int kEntries = 32;
+    thread_local Entry cache[kEntries] = {};
+    thread_local int next = 0;
+    for (Entry& e : cache)
+        if (e.used && e.base == base && e.rows == rows && e.cols == cols && e.box_cols == box_cols &&
+            e.box_rows == box_rows && e.swz == swizzle128) {
+            *map = e.map;
+            return;
+        }
     cuuint64_t dims[2] = {cols, rows};
     cuuint64_t strides[1] = {cols};
     cuuint32_t box[2] = {box_cols, box_rows};
@@ -414,6 +432,9 @@ void make_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t
                               swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) fail("cuTensorMapEncodeTiled failed with code ", (int)r);
+    Entry& e = cache[next];
+    next = (next + 1) % kEntries;
+    e = Entry{base, rows, cols, box_cols, box_rows, swizzle128, true, *map};
 }
 }  // namespace ab
 
@@ -463,7 +484,7 @@ void launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& t
     if (tiles == 0) return;
     const int grid = std::min(tiles, ab::num_sms(dev));
     constexpr int smem = Cfg<BN_>::SMEM_BYTES;
-    AB_CUDA(cudaFuncSetAttribute(moe_gemm_fp8_kernel<STAGE, BN_>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    ab::set_max_smem_once((const void*)moe_gemm_fp8_kernel<STAGE, BN_>, smem, dev);
     moe_gemm_fp8_kernel<STAGE, BN_><<<grid, NUM_THREADS, smem, st>>>(tmA, tmB, tmO, a);
     ab::check_launch(STAGE == 1 ? "moe_stage1_fp8_blockscale" : "moe_stage2_fp8_blockscale");
 }

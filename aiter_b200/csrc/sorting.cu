@@ -359,7 +359,7 @@ AB_ENTRY(moe_sorting_fwd,
         return;
     }
     if (use_oneshot(M, K, dispatch_policy)) {
-        AB_CUDA(cudaFuncSetAttribute(sort_oneshot_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        ab::set_max_smem_once((const void*)sort_oneshot_kernel, (int)smem, dev);
         sort_oneshot_kernel<<<1 + zero_ctas, kThreads, smem, st>>>(a);
         check_launch("moe_sorting_fwd(one-shot)");
         return;
@@ -368,8 +368,8 @@ AB_ENTRY(moe_sorting_fwd,
     AB_CHECK(workspace && workspace->ptr && (int64_t)(workspace->numel_ * elem_size(workspace->dtype_)) >= ws_need,
              "workspace of at least ", ws_need, " bytes required (moe_sorting_get_workspace_size)");
     a.counts = (int*)workspace->ptr;
-    AB_CUDA(cudaFuncSetAttribute(sort_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    AB_CUDA(cudaFuncSetAttribute(sort_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    ab::set_max_smem_once((const void*)sort_count_kernel, (int)smem, dev);
+    ab::set_max_smem_once((const void*)sort_scatter_kernel, (int)smem, dev);
     sort_count_kernel<<<a.nchunks + zero_ctas, kThreads, a.E * sizeof(int), st>>>(a);
     check_launch("moe_sorting_fwd(count)");
     sort_scatter_kernel<<<a.nchunks, kThreads, smem, st>>>(a);

@@ -53,6 +53,7 @@ class CustomAllreduce:
         self.device = device
         self.max_size = int(max_size)
         L = _lib.lib()
+        self._L = L
         ctx = ctypes.c_int64(0)
         handle = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
         _lib.check_status("custom_ar_init", L.custom_ar_init(self.rank, self.world_size, self.max_size,
@@ -82,9 +83,10 @@ class CustomAllreduce:
             out = torch.empty_like(inp)
         force = -1 if two_shot is None else (1 if two_shot else 0)
         a, b = _lib.to_aiter(inp), _lib.to_aiter(out)
-        st = torch.cuda.current_stream(inp.device).cuda_stream
-        _lib.check_status("custom_ar_all_reduce", _lib.lib().custom_ar_all_reduce(
-            self._ctx, ctypes.byref(a), ctypes.byref(b), force, ctypes.c_void_p(st)))
+        st = _lib.current_stream_ptr(self.device.index)
+        ret = self._L.custom_ar_all_reduce(self._ctx, ctypes.byref(a), ctypes.byref(b), force, st)
+        if ret:
+            _lib.check_status("custom_ar_all_reduce", ret)
         return out
 
     def custom_all_reduce(self, input: torch.Tensor):
@@ -98,9 +100,11 @@ class CustomAllreduce:
             out = torch.empty((a.shape[0], w.shape[0]), dtype=torch.bfloat16, device=a.device)
         force = -1 if two_shot is None else (1 if two_shot else 0)
         ta, tw, to = _lib.to_aiter(a), _lib.to_aiter(w), _lib.to_aiter(out)
-        st = torch.cuda.current_stream(a.device).cuda_stream
-        _lib.check_status("custom_ar_gemm_all_reduce", _lib.lib().custom_ar_gemm_all_reduce(
-            self._ctx, ctypes.byref(ta), ctypes.byref(tw), ctypes.byref(to), force, ctypes.c_void_p(st)))
+        st = _lib.current_stream_ptr(self.device.index)
+        ret = self._L.custom_ar_gemm_all_reduce(self._ctx, ctypes.byref(ta), ctypes.byref(tw), ctypes.byref(to),
+                                                force, st)
+        if ret:
+            _lib.check_status("custom_ar_gemm_all_reduce", ret)
         return out
 
     def next_buffer_tensor(self, shape, dtype=torch.bfloat16) -> torch.Tensor:
