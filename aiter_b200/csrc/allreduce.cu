@@ -98,49 +98,84 @@ __device__ __forceinline__ uint4 pack8(const float (&a)[8]) {
 }
 
 // n16: number of 16-byte packs (8 bf16).  `in` may equal the staging buffer
-// (zero-copy producers), then the copy is skipped.
+// (zero-copy producers), then the copy is skipped.  W (the world size) is a
+// template parameter so that the peer loops unroll and every thread keeps
+// U * W independent 16-byte loads in flight (U packs per thread per step).
+template <int W>
 __global__ void __launch_bounds__(kThreads)
-allreduce_bf16_kernel(Peers P, int rank, int world, int parity, const uint4* __restrict__ in,
-                      uint4* __restrict__ out, int64_t n16, uint32_t epoch, int two_shot) {
+allreduce_bf16_kernel(Peers P, int rank, int parity, const uint4* __restrict__ in, uint4* __restrict__ out,
+                      int64_t n16, uint32_t epoch, int two_shot) {
+    constexpr int U = W >= 8 ? 1 : 8 / W;
     uint4* mine = reinterpret_cast<uint4*>(P.buf[parity][rank]);
+    const uint4* bufs[W];
+#pragma unroll
+    for (int p = 0; p < W; ++p) bufs[p] = reinterpret_cast<const uint4*>(P.buf[parity][p]);
     const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     // Packs are split into `nseg` segments and pack i of segment s always goes to
     // thread (i - lo_s) mod stride, in the copy, the reduce and the gather, on every
     // rank.  A CTA therefore only reads packs that the same CTA index wrote on the
     // peers before the barrier it waited on.
-    const int nseg = two_shot ? world : 1;
+    const int nseg = two_shot ? W : 1;
     const int64_t seg = (n16 + nseg - 1) / nseg;
     if (in != mine) {
         for (int s = 0; s < nseg; ++s) {
             const int64_t lo = (int64_t)s * seg, hi = min(n16, lo + seg);
-            for (int64_t i = lo + tid; i < hi; i += stride) mine[i] = in[i];
+            for (int64_t i = lo + tid; i < hi; i += 4 * stride) {
+                uint4 v[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    if (i + u * stride < hi) v[u] = in[i + u * stride];
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    if (i + u * stride < hi) mine[i + u * stride] = v[u];
+            }
         }
     }
-    if (!block_barrier(P, rank, world, 0, epoch)) return;
-    if (!two_shot) {
-        for (int64_t i = tid; i < n16; i += stride) {
-            float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-            for (int p = 0; p < world; ++p) acc8(a, ld_cg(reinterpret_cast<const uint4*>(P.buf[parity][p]) + i));
-            out[i] = pack8(a);
+    if (!block_barrier(P, rank, W, 0, epoch)) return;
+    // sum of packs [lo, hi) over ranks in rank order -> dst
+    auto reduce_range = [&](int64_t lo, int64_t hi, uint4* dst) {
+        for (int64_t i = lo + tid; i < hi; i += U * stride) {
+            uint4 v[U][W];
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+#pragma unroll
+                for (int p = 0; p < W; ++p)
+                    if (i + u * stride < hi) v[u][p] = ld_cg(bufs[p] + i + u * stride);
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                if (i + u * stride < hi) {
+                    float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+                    for (int p = 0; p < W; ++p) acc8(a, v[u][p]);
+                    dst[i + u * stride] = pack8(a);
+                }
+            }
         }
+    };
+    if (!two_shot) {
+        reduce_range(0, n16, out);
         return;
     }
     // rank r reduces segment r in place
-    {
-        const int64_t lo = (int64_t)rank * seg, hi = min(n16, lo + seg);
-        for (int64_t i = lo + tid; i < hi; i += stride) {
-            float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-            for (int p = 0; p < world; ++p) acc8(a, ld_cg(reinterpret_cast<const uint4*>(P.buf[parity][p]) + i));
-            mine[i] = pack8(a);
-        }
-    }
-    if (!block_barrier(P, rank, world, 1, epoch)) return;
-    for (int s = 0; s < world; ++s) {
-        const int o = (rank + s) % world;  // start with the own segment, spread peer traffic
+    reduce_range((int64_t)rank * seg, min(n16, (int64_t)(rank + 1) * seg), mine);
+    if (!block_barrier(P, rank, W, 1, epoch)) return;
+    for (int s = 0; s < W; ++s) {
+        const int o = (rank + s) % W;  // start with the own segment, spread peer traffic
         const int64_t lo = (int64_t)o * seg, hi = min(n16, lo + seg);
-        const uint4* src = reinterpret_cast<const uint4*>(P.buf[parity][o]);
-        for (int64_t i = lo + tid; i < hi; i += stride) out[i] = ld_cg(src + i);
+        const uint4* src = bufs[0];
+#pragma unroll
+        for (int p = 1; p < W; ++p)
+            if (p == o) src = bufs[p];  // select, keeps bufs[] in registers
+        for (int64_t i = lo + tid; i < hi; i += 8 * stride) {
+            uint4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (i + u * stride < hi) v[u] = ld_cg(src + i + u * stride);
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (i + u * stride < hi) out[i + u * stride] = v[u];
+        }
     }
 }
 
@@ -267,16 +302,28 @@ AB_ENTRY(custom_ar_all_reduce,
     c->epoch += 1;
     const int parity = (int)(c->epoch & 1);
     const int64_t n16 = (int64_t)(bytes / 16);
-    // force_two_shot: 1 = two-shot, 0 = one-shot, negative = by size (one-shot up
-    // to 256 KiB where latency dominates, two-shot above where bandwidth does)
-    const bool two = force_two_shot > 0 ? true : (force_two_shot == 0 ? false : bytes > 256 * 1024);
-    const int64_t per_block = (int64_t)kThreads * 4;
+    // force_two_shot: 1 = two-shot, 0 = one-shot, negative = by size.  One-shot reads
+    // (W-1) x the data over NVLink, two-shot 2 (W-1)/W x plus one more barrier: with
+    // two ranks one-shot always wins, with more it wins while latency dominates.
+    const int64_t one_shot_max = c->world == 2 ? INT64_MAX : (c->world == 4 ? (1 << 20) : (256 << 10));
+    const bool two = force_two_shot > 0 ? true : (force_two_shot == 0 ? false : (int64_t)bytes > one_shot_max);
+    // about two packs per thread per CTA: small messages still spread over CTAs
+    const int64_t per_block = (int64_t)kThreads * 2;
     int grid = (int)std::min<int64_t>((n16 + per_block - 1) / per_block, std::min(kMaxBlocks, num_sms(c->device)));
     grid = std::max(grid, 1);
-    const void* src = inp->ptr;
-    allreduce_bf16_kernel<<<grid, kThreads, 0, as_stream(stream)>>>(c->peers, c->rank, c->world, parity,
-                                                                    (const uint4*)src, (uint4*)out->ptr, n16,
-                                                                    c->epoch, two ? 1 : 0);
+    const uint4* src = (const uint4*)inp->ptr;
+    uint4* dst = (uint4*)out->ptr;
+    cudaStream_t st = as_stream(stream);
+    const int tw = two ? 1 : 0;
+    switch (c->world) {
+        case 2: allreduce_bf16_kernel<2><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, c->epoch, tw); break;
+        case 3: allreduce_bf16_kernel<3><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, c->epoch, tw); break;
+        case 4: allreduce_bf16_kernel<4><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, c->epoch, tw); break;
+        case 5: allreduce_bf16_kernel<5><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, c->epoch, tw); break;
+        case 6: allreduce_bf16_kernel<6><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, c->epoch, tw); break;
+        case 7: allreduce_bf16_kernel<7><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, c->epoch, tw); break;
+        default: allreduce_bf16_kernel<8><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, c->epoch, tw); break;
+    }
     check_launch("custom_ar_all_reduce");
 }
 
