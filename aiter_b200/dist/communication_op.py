@@ -17,21 +17,47 @@ def tensor_model_parallel_gemm_all_reduce(a: torch.Tensor, w: torch.Tensor) -> t
     return get_tp_group().gemm_all_reduce(a, w)
 
 
-def shard_moe_weights_for_tp(w1, w1_scale, w2, w2_scale, rank, tp):
+def shard_moe_weights_for_tp(w1, w1_scale, w2, w2_scale, rank, tp, chunk=8):
     """Rank `rank`'s share of FP8 block-scale MoE weights under tensor parallelism:
     inter_dim/tp columns of the gate and of the up half of w1 and the matching rows of
-    w2's K, for every expert (the MoE TP layout of the reference's callers).  Needs
-    inter_dim/tp to be a multiple of the 128-wide scale blocks."""
+    w2's K, for every expert (the MoE TP layout of the reference's callers).
+
+    When inter_dim/tp is a multiple of the 128-wide scale blocks the shard is a plain
+    slice (bit-exact).  Otherwise (e.g. 1536/8 = 192) the shard cuts through scale
+    blocks, so it is dequantised, zero-padded to the next multiple of 128 and
+    re-quantised into shard-local 128x128 blocks.  The padded gate/up rows give
+    act(0) * 0 = 0 in the intermediate and meet zero columns of w2, so they add
+    nothing; the re-quantisation rounds the shard's weights once more to fp8."""
     E, two_i, D = w1.shape
     I = two_i // 2
-    assert I % tp == 0 and (I // tp) % 128 == 0, "inter_dim / tp must be a multiple of 128"
+    assert I % tp == 0, "inter_dim must divide by tp"
     il = I // tp
-    b0, b1 = rank * il // 128, (rank + 1) * il // 128
-    w1l = torch.cat([w1[:, rank * il:(rank + 1) * il], w1[:, I + rank * il:I + (rank + 1) * il]], dim=1)
-    s1l = torch.cat([w1_scale[:, b0:b1], w1_scale[:, I // 128 + b0:I // 128 + b1]], dim=1)
-    w2l = w2[:, :, rank * il:(rank + 1) * il]
-    s2l = w2_scale[:, :, b0:b1]
-    return w1l.contiguous(), s1l.contiguous(), w2l.contiguous(), s2l.contiguous()
+    if il % 128 == 0:
+        b0, b1 = rank * il // 128, (rank + 1) * il // 128
+        w1l = torch.cat([w1[:, rank * il:(rank + 1) * il], w1[:, I + rank * il:I + (rank + 1) * il]], dim=1)
+        s1l = torch.cat([w1_scale[:, b0:b1], w1_scale[:, I // 128 + b0:I // 128 + b1]], dim=1)
+        w2l = w2[:, :, rank * il:(rank + 1) * il]
+        s2l = w2_scale[:, :, b0:b1]
+        return w1l.contiguous(), s1l.contiguous(), w2l.contiguous(), s2l.contiguous()
+    from ..weights import dequant_128x128, quant_weight_128x128
+    ilp = (il + 127) // 128 * 128
+    lo, hi = rank * il, (rank + 1) * il
+    q1, q1s, q2, q2s = [], [], [], []
+    for e0 in range(0, E, chunk):
+        e1 = min(E, e0 + chunk)
+        f1 = dequant_128x128(w1[e0:e1], w1_scale[e0:e1])
+        pad1 = torch.zeros((e1 - e0, ilp - il, D), dtype=f1.dtype, device=f1.device)
+        q, sc = quant_weight_128x128(torch.cat([f1[:, lo:hi], pad1, f1[:, I + lo:I + hi], pad1], dim=1))
+        q1.append(q)
+        q1s.append(sc)
+        del f1
+        f2 = dequant_128x128(w2[e0:e1], w2_scale[e0:e1])
+        pad2 = torch.zeros((e1 - e0, D, ilp - il), dtype=f2.dtype, device=f2.device)
+        q, sc = quant_weight_128x128(torch.cat([f2[:, :, lo:hi], pad2], dim=2))
+        q2.append(q)
+        q2s.append(sc)
+        del f2
+    return torch.cat(q1), torch.cat(q1s), torch.cat(q2), torch.cat(q2s)
 
 
 def tensor_model_parallel_fused_moe(hidden_states, w1, w2, topk_weight, topk_ids, **kwargs):

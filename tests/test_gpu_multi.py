@@ -56,9 +56,12 @@ def _worker(rank, world, port):
         assert _lib.lib().custom_ar_device_error(1) == 0
         exp = _expected(xs)
         assert torch.equal(y.cpu(), exp), f"call {i}: n={n} two_shot={two}"
+        # NCCL sums in bf16 along its ring, rounding every partial sum, so it drifts
+        # from the exact sum by up to ~world bf16 ulps of the partials: a sanity
+        # check only (the bit-exact check above is the real one)
         ref = x.clone()
         dist.all_reduce(ref, group=tp.device_group)
-        assert torch.allclose(y.float(), ref.float(), rtol=2e-2, atol=2e-2)
+        assert torch.allclose(y.float(), ref.float(), rtol=2e-2, atol=2e-2 * world)
         # identical bits on every rank
         gathered = [torch.empty_like(y) for _ in range(world)]
         dist.all_gather(gathered, y, group=tp.device_group)
@@ -85,11 +88,18 @@ def _worker(rank, world, port):
         for gg in gathered:
             assert torch.equal(gg, out)
     # tensor-parallel fused MoE vs the single-GPU fused MoE on the full weights
+    for i_per_rank in (256, 192):  # 192: shards re-blocked to 256 (inter_dim / tp not 128-aligned)
+        _tp_moe_case(rank, world, dev, tp, i_per_rank)
+    ps.destroy_model_parallel()
+    dist.destroy_process_group()
+
+
+def _tp_moe_case(rank, world, dev, tp, i_per_rank):
     import numpy as np
     import aiter_b200 as aiter
     from aiter_b200 import weights as W
     from aiter_b200.dist import shard_moe_weights_for_tp, tensor_model_parallel_fused_moe
-    D, I, E, k, M = 1024, 256 * world, 16, 4, 100
+    D, I, E, k, M = 1024, i_per_rank * world, 16, 4, 100
     g = torch.Generator(device=dev).manual_seed(77)
     w1q, w1s = W.quant_weight_128x128(torch.randn(E, 2 * I, D, device=dev, generator=g) / D ** 0.5)
     w2q, w2s = W.quant_weight_128x128(torch.randn(E, D, I, device=dev, generator=g) / I ** 0.5)
@@ -109,8 +119,6 @@ def _worker(rank, world, port):
         dist.all_gather(gathered, tp_out, group=tp.device_group)
         for gg in gathered:
             assert torch.equal(gg, tp_out)
-    ps.destroy_model_parallel()
-    dist.destroy_process_group()
 
 
 def test_ipc_allreduce_and_gemm_allreduce_multi_gpu():
