@@ -105,16 +105,29 @@ def _tp_moe_case(rank, world, dev, tp, i_per_rank):
     w2q, w2s = W.quant_weight_128x128(torch.randn(E, D, I, device=dev, generator=g) / I ** 0.5)
     hidden = torch.randn(M, D, device=dev, generator=g).to(torch.bfloat16)
     tw, tid = aiter.fused_topk(hidden, torch.randn(M, E, device=dev, generator=g), k, True)
-    full = aiter.fused_moe(hidden, w1q, w2q, tw, tid, quant_type=aiter.QuantType.per_1x128,
-                           w1_scale=w1s, w2_scale=w2s)
+    kw = dict(quant_type=aiter.QuantType.per_1x128)
+    full = aiter.fused_moe(hidden, w1q, w2q, tw, tid, w1_scale=w1s, w2_scale=w2s, **kw)
     l1, s1, l2, s2 = shard_moe_weights_for_tp(w1q, w1s, w2q, w2s, rank, world)
+    # every rank's shard output, summed in fp32: what the TP path must reproduce
+    part = aiter.fused_moe(hidden, l1, l2, tw, tid, w1_scale=s1, w2_scale=s2, **kw)
+    parts = [torch.empty_like(part) for _ in range(world)]
+    dist.all_gather(parts, part, group=tp.device_group)
+    shard_sum = sum(p.float() for p in parts).cpu().numpy()
     for _ in range(2):
-        tp_out = tensor_model_parallel_fused_moe(hidden, l1, l2, tw, tid, quant_type=aiter.QuantType.per_1x128,
-                                                 w1_scale=s1, w2_scale=s2)
+        tp_out = tensor_model_parallel_fused_moe(hidden, l1, l2, tw, tid, w1_scale=s1, w2_scale=s2, **kw)
         torch.cuda.synchronize()
         a, b = tp_out.float().cpu().numpy(), full.float().cpu().numpy()
-        np.testing.assert_allclose(a, b, rtol=2e-2, atol=2e-2)
-        assert (np.abs(a - b) > 1e-2 + 1e-2 * np.abs(b)).mean() <= 0.01
+        # the stage-2 scatter-add is bf16 atomics, so the partials may differ in order
+        np.testing.assert_allclose(a, shard_sum, rtol=1e-2, atol=1e-2, err_msg=f"inter/rank {i_per_rank}")
+        if i_per_rank % 128 == 0:
+            # plain slices: the same weights as the single-GPU run
+            np.testing.assert_allclose(a, b, rtol=2e-2, atol=2e-2, err_msg=f"inter/rank {i_per_rank}")
+            assert (np.abs(a - b) > 1e-2 + 1e-2 * np.abs(b)).mean() <= 0.01
+        else:
+            # re-blocked shards round the weights to fp8 once more (e4m3: up to 2^-4
+            # relative per weight), which moves outputs by a few percent
+            np.testing.assert_allclose(a, b, rtol=0.1, atol=0.1, err_msg=f"inter/rank {i_per_rank}")
+            assert (np.abs(a - b) > 2e-2 + 2e-2 * np.abs(b)).mean() <= 0.1
         gathered = [torch.empty_like(tp_out) for _ in range(world)]
         dist.all_gather(gathered, tp_out, group=tp.device_group)
         for gg in gathered:
