@@ -305,7 +305,7 @@ AB_ENTRY(custom_ar_all_reduce,
     // force_two_shot: 1 = two-shot, 0 = one-shot, negative = by size.  One-shot reads
     // (W-1) x the data over NVLink, two-shot 2 (W-1)/W x plus one more barrier: with
     // two ranks one-shot always wins, with more it wins while latency dominates.
-    const int64_t one_shot_max = c->world == 2 ? INT64_MAX : (c->world == 4 ? (1 << 20) : (256 << 10));
+    const int64_t one_shot_max = c->world == 2 ? INT64_MAX : (c->world <= 4 ? (2 << 20) : (1 << 20));
     const bool two = force_two_shot > 0 ? true : (force_two_shot == 0 ? false : (int64_t)bytes > one_shot_max);
     // about two packs per thread per CTA: small messages still spread over CTAs
     const int64_t per_block = (int64_t)kThreads * 2;

@@ -355,24 +355,43 @@ gemm_bf16_swab_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_cons
     tc_fence_before();
     __syncthreads();
     cluster_sync();  // every partial of the cluster is in place
-    // rows [r*MT/S, (r+1)*MT/S) of the tile, as 4-column groups
+    // rows [r*MT/S, (r+1)*MT/S) of the tile, as 4-column groups; rows past M are
+    // skipped.  Each thread first issues the loads of R groups from all S ranks,
+    // then sums: the remote reads overlap instead of paying one latency each.
+    constexpr int R = 4;
     const int rows_per = MT / S, rbase = rank * rows_per;
-    for (int idx = threadIdx.x; idx < rows_per * 32; idx += NUM_THREADS) {
-        const int m = rbase + idx / 32, c4 = idx % 32;
-        const float* src = part + m * 128 + 4 * c4;
-        float4 acc = ld_dsmem_f4(src, 0);
-        for (int r = 1; r < S; ++r) {
-            const float4 v = ld_dsmem_f4(src, (uint32_t)r);
-            acc.x += v.x;
-            acc.y += v.y;
-            acc.z += v.z;
-            acc.w += v.w;
+    const int rows_live = max(0, min(rows_per, args.M - m_blk * MT - rbase));
+    const int groups = rows_live * 32;
+    for (int g0 = threadIdx.x; g0 < groups; g0 += R * NUM_THREADS) {
+        float4 v[R][8];
+#pragma unroll
+        for (int j = 0; j < R; ++j) {
+            const int g = g0 + j * NUM_THREADS;
+            if (g < groups) {
+                const float* src = part + (rbase + g / 32) * 128 + 4 * (g % 32);
+#pragma unroll
+                for (int r = 0; r < 8; ++r)
+                    if (r < S) v[j][r] = ld_dsmem_f4(src, (uint32_t)r);
+            }
         }
-        const int gm = m_blk * MT + m;
-        if (gm < args.M) {
-            __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
-            uint2 pk = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
-            *reinterpret_cast<uint2*>(args.out + (int64_t)gm * args.ldo + n_blk * 128 + 4 * c4) = pk;
+#pragma unroll
+        for (int j = 0; j < R; ++j) {
+            const int g = g0 + j * NUM_THREADS;
+            if (g < groups) {
+                float4 acc = v[j][0];
+#pragma unroll
+                for (int r = 1; r < 8; ++r)
+                    if (r < S) {  // rank order: identical bits for any thread layout
+                        acc.x += v[j][r].x;
+                        acc.y += v[j][r].y;
+                        acc.z += v[j][r].z;
+                        acc.w += v[j][r].w;
+                    }
+                const int gm = m_blk * MT + rbase + g / 32;
+                __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+                uint2 pk = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+                *reinterpret_cast<uint2*>(args.out + (int64_t)gm * args.ldo + n_blk * 128 + 4 * (g % 32)) = pk;
+            }
         }
     }
     cluster_sync();  // peers are done reading this CTA's partial

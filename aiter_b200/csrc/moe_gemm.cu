@@ -55,7 +55,7 @@ struct Cfg {
     static constexpr int SMEM_BYTES =
         1024 /*align slack*/ + STAGES * STAGE_BYTES + OUT_BYTES + BAR_BYTES + RED_BYTES + SRING_BYTES;
     static_assert(CPT % 64 == 0, "epilogue works in 64-column chunks");
-    static_assert(2 * (STAGES + SLABS + SRING) * 8 + 8 <= BAR_BYTES, "barrier area");
+    static_assert(2 * (STAGES + SLABS + SRING) * 8 + 2 * 8 + 8 <= BAR_BYTES, "barrier area");
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
 };
 
@@ -76,6 +76,14 @@ struct GemmArgs {
 __device__ __forceinline__ float act_fn(float g, int act) {
     if (act == AITER_ACT_GELU) return 0.5f * g * (1.0f + erff(g * 0.70710678118654752f));
     return __fdividef(g, 1.0f + __expf(-g));
+}
+
+// Barrier of the 8 epilogue warps: lane 0 of each warp arrives after the warp's
+// shared-memory writes, then every lane waits (bounded) for the phase.
+__device__ __forceinline__ bool epi_sync(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) sm100::mbar_arrive(bar);
+    return __all_sync(0xffffffffu, sm100::mbar_wait(bar, parity, abort_flag));
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
@@ -115,7 +123,8 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     uint64_t* tempty = tfull + SLABS;
     uint64_t* sfull = tempty + SLABS;
     uint64_t* sempty = sfull + SRING;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sempty + SRING);
+    uint64_t* ebar = sempty + SRING;  // [0] row amax exchange, [1] output tile complete
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ebar + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     float* red = reinterpret_cast<float*>(out_tile + C::OUT_BYTES + C::BAR_BYTES);
     float* sring = red + 2 * 256;
@@ -134,6 +143,8 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             mbar_init(&sfull[s], 32);  // one cp.async arrival per prefetcher lane
             mbar_init(&sempty[s], 8);  // one arrival per epilogue warp
         }
+        mbar_init(&ebar[0], 8);
+        mbar_init(&ebar[1], 8);
         *abort_flag = 0;
         fence_mbar_init();
         prefetch_tensormap(&tmA);
@@ -330,7 +341,9 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 rb[h * 128 + row] = amax;
                 // the previous tile's TMA store must have finished reading out_tile
                 if (threadIdx.x == 128) bulk_wait_read0();
-                named_barrier(1, 256);
+                // barriers among the epilogue warps are mbarriers with bounded waits:
+                // a warp that gave up earlier never strands the others here
+                if (!epi_sync(&ebar[0], tcount & 1, abort_flag)) break;
                 amax = fmaxf(rb[row], rb[128 + row]);
                 float scale = amax / 448.0f;
                 if (scale == 0.f) scale = 1.0f;
@@ -352,10 +365,15 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 }
                 if (h == 0) args.out_scale[(int64_t)n_blk * args.rows_pad + srow] = scale;
                 fence_proxy_async_smem();
-                named_barrier(1, 256);
-                if (threadIdx.x == 128) {
-                    tma_store_2d(&tmO, out_tile, n_blk * 128, m_blk * BM);
-                    bulk_commit();
+                // only the storing warp waits for the whole tile; the others move on
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ebar[1]);
+                if (warp == 4) {
+                    if (!__all_sync(0xffffffffu, mbar_wait(&ebar[1], tcount & 1, abort_flag))) break;
+                    if (lane == 0) {
+                        tma_store_2d(&tmO, out_tile, n_blk * 128, m_blk * BM);
+                        bulk_commit();
+                    }
                 }
             } else {
                 if (valid) {

@@ -117,8 +117,10 @@ def _tp_moe_case(rank, world, dev, tp, i_per_rank):
         tp_out = tensor_model_parallel_fused_moe(hidden, l1, l2, tw, tid, w1_scale=s1, w2_scale=s2, **kw)
         torch.cuda.synchronize()
         a, b = tp_out.float().cpu().numpy(), full.float().cpu().numpy()
-        # the stage-2 scatter-add is bf16 atomics, so the partials may differ in order
-        np.testing.assert_allclose(a, shard_sum, rtol=1e-2, atol=1e-2, err_msg=f"inter/rank {i_per_rank}")
+        # the stage-2 scatter-add is bf16 atomics in no fixed order: each of the k adds
+        # rounds a running sum that can be ~1 before it cancels, so two runs differ by
+        # a few bf16 ulps of that sum (~1e-2), not of the result
+        np.testing.assert_allclose(a, shard_sum, rtol=1e-2, atol=2e-2, err_msg=f"inter/rank {i_per_rank}")
         if i_per_rank % 128 == 0:
             # plain slices: the same weights as the single-GPU run
             np.testing.assert_allclose(a, b, rtol=2e-2, atol=2e-2, err_msg=f"inter/rank {i_per_rank}")
