@@ -175,6 +175,7 @@ def make_inputs(M, seed=1234, E=E):
     w2 = torch.randn(E, D, I, device=dev, generator=g) / I ** 0.5
     w2q, w2s = W.quant_weight_128x128(w2)
     del w2
+    torch.cuda.empty_cache()  # drop the fp32 originals: ~2.6 GB stay on the device
     hidden = torch.randn(M, D, device=dev, generator=g).to(torch.bfloat16)
     logits = torch.randn(M, E, device=dev, generator=g)
     tw, tid = aiter.fused_topk(hidden, logits, TOPK, True)
