@@ -5,15 +5,23 @@
 //
 // Every rank owns one cudaMalloc'd region, exported with cudaIpcGetMemHandle and
 // opened by every peer:
-//   [ Signal (flags written by peers) | staging buffer 0 | staging buffer 1 ]
-// Call n stages its input in buffer n % 2.  A rank starts call n+1 only after the
-// start barrier of call n+1, which every peer reaches only after finishing call n,
-// so the copy of call n+1 never overwrites data a slow peer is still reading.
+//   [ Signal (flags written by peers, own call counters) | staging 0 | staging 1 ]
+// Call n stages its input in buffer n % 2 (host-side count).  Eagerly, a rank starts
+// call n+2 (same buffer) only after the start barrier of call n+1, which every peer
+// reaches only after finishing call n, so nothing a slow peer still reads is
+// overwritten.  Under CUDA-graph capture the buffer of each captured call is fixed
+// for every replay, so captured calls end with a third barrier: no rank leaves the
+// call before every peer has finished reading its buffer.
 //
-// Barriers are per CTA: CTA b of rank r writes `epoch` into flag[phase][b][r] of
-// every peer (st.release.sys) and waits until its own flag[phase][b][p] == epoch for
-// all peers (ld.acquire.sys, bounded).  All ranks partition the data identically per
-// CTA, so CTA b only ever reads what peer CTAs b wrote before the barrier.
+// Epochs live in device memory: CTA b of a call increments its own counter[b]
+// (only CTA b of this rank touches it, launches are stream-ordered), so replayed
+// graphs and eager calls share one monotonic sequence per CTA index, identical on
+// all ranks because all ranks launch the same grid for the same call.
+// Barriers are per CTA: CTA b of rank r writes its epoch into flag[phase][b][r] of
+// every peer (st.release.sys) and waits until its own flag[phase][b][p] has reached
+// that epoch for all peers (ld.acquire.sys, wrap-safe >=, bounded).  All ranks
+// partition the data identically per CTA, so CTA b only ever reads what peer CTAs b
+// wrote before the barrier.
 //   one-shot : copy -> barrier -> out = sum over ranks (rank order 0..W-1)
 //   two-shot : copy -> barrier -> reduce own segment in place -> barrier -> gather
 //              every segment from its owner.
@@ -29,14 +37,16 @@ namespace {
 constexpr int kMaxRanks = 8;
 constexpr int kMaxBlocks = 128;
 constexpr int kThreads = 512;
-constexpr size_t kSignalBytes = 2 * kMaxBlocks * kMaxRanks * sizeof(uint32_t);
+constexpr size_t kSignalBytes = (3 * kMaxBlocks * kMaxRanks + kMaxBlocks) * sizeof(uint32_t);
 constexpr size_t kSignalPad = 64 * 1024;
 
 static __device__ int g_ar_error;
 
 struct Signal {
-    uint32_t flag[2][kMaxBlocks][kMaxRanks];
+    uint32_t flag[3][kMaxBlocks][kMaxRanks];  // [start | mid (two-shot) | end (captured)]
+    uint32_t counter[kMaxBlocks];            // own calls per CTA index (never read by peers)
 };
+static_assert(sizeof(Signal) == kSignalBytes, "signal layout");
 
 struct Peers {
     Signal* sig[kMaxRanks];       // every rank's signal block
@@ -68,7 +78,8 @@ __device__ bool block_barrier(const Peers& P, int rank, int world, int phase, ui
         const uint32_t* mine = &P.sig[rank]->flag[phase][blockIdx.x][threadIdx.x];
         const uint64_t t0 = abd::globaltimer_ns();
         uint32_t n = 0;
-        while (ld_acquire_sys(mine) != epoch) {
+        // >=, not ==: a fast peer may already have moved on to its next call
+        while ((int32_t)(ld_acquire_sys(mine) - epoch) < 0) {
             if ((++n & 255) == 0 && abd::globaltimer_ns() - t0 > 2000000000ull) {
                 atomicExch(&g_ar_error, 1);
                 ok = false;
@@ -104,7 +115,15 @@ __device__ __forceinline__ uint4 pack8(const float (&a)[8]) {
 template <int W>
 __global__ void __launch_bounds__(kThreads)
 allreduce_bf16_kernel(Peers P, int rank, int parity, const uint4* __restrict__ in, uint4* __restrict__ out,
-                      int64_t n16, uint32_t epoch, int two_shot) {
+                      int64_t n16, int two_shot, int end_barrier) {
+    __shared__ uint32_t s_epoch;
+    if (threadIdx.x == 0) {
+        uint32_t* ctr = &P.sig[rank]->counter[blockIdx.x];
+        s_epoch = *ctr + 1;
+        *ctr = s_epoch;
+    }
+    __syncthreads();
+    const uint32_t epoch = s_epoch;
     constexpr int U = W >= 8 ? 1 : 8 / W;
     uint4* mine = reinterpret_cast<uint4*>(P.buf[parity][rank]);
     const uint4* bufs[W];
@@ -155,6 +174,7 @@ allreduce_bf16_kernel(Peers P, int rank, int parity, const uint4* __restrict__ i
     };
     if (!two_shot) {
         reduce_range(0, n16, out);
+        if (end_barrier) block_barrier(P, rank, W, 2, epoch);
         return;
     }
     // rank r reduces segment r in place
@@ -177,6 +197,7 @@ allreduce_bf16_kernel(Peers P, int rank, int parity, const uint4* __restrict__ i
                 if (i + u * stride < hi) out[i + u * stride] = v[u];
         }
     }
+    if (end_barrier) block_barrier(P, rank, W, 2, epoch);
 }
 
 struct Ctx {
@@ -315,14 +336,17 @@ AB_ENTRY(custom_ar_all_reduce,
     uint4* dst = (uint4*)out->ptr;
     cudaStream_t st = as_stream(stream);
     const int tw = two ? 1 : 0;
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    AB_CUDA(cudaStreamIsCapturing(st, &cap));
+    const int endb = cap == cudaStreamCaptureStatusNone ? 0 : 1;  // captured: buffers are reused per replay
     switch (c->world) {
-        case 2: allreduce_bf16_kernel<2><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, c->epoch, tw); break;
-        case 3: allreduce_bf16_kernel<3><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, c->epoch, tw); break;
-        case 4: allreduce_bf16_kernel<4><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, c->epoch, tw); break;
-        case 5: allreduce_bf16_kernel<5><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, c->epoch, tw); break;
-        case 6: allreduce_bf16_kernel<6><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, c->epoch, tw); break;
-        case 7: allreduce_bf16_kernel<7><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, c->epoch, tw); break;
-        default: allreduce_bf16_kernel<8><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, c->epoch, tw); break;
+        case 2: allreduce_bf16_kernel<2><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, tw, endb); break;
+        case 3: allreduce_bf16_kernel<3><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, tw, endb); break;
+        case 4: allreduce_bf16_kernel<4><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, tw, endb); break;
+        case 5: allreduce_bf16_kernel<5><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, tw, endb); break;
+        case 6: allreduce_bf16_kernel<6><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, tw, endb); break;
+        case 7: allreduce_bf16_kernel<7><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, tw, endb); break;
+        default: allreduce_bf16_kernel<8><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, tw, endb); break;
     }
     check_launch("custom_ar_all_reduce");
 }

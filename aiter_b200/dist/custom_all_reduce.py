@@ -6,6 +6,7 @@ Each rank allocates one IPC region in the library (signals + two staging buffers
 as the reference exchanges them over its CPU group / TCP store
 (custom_all_reduce.py:140-153,219-240), and every rank opens all peers' regions.
 """
+import contextlib
 import ctypes
 import logging
 
@@ -35,6 +36,7 @@ class CustomAllreduce:
 
     def __init__(self, group, device, max_size=128 * 1024 * 1024):
         self.disabled = True
+        self._IS_CAPTURING = False
         self._ctx = 0
         self.group = group
         assert dist.get_backend(group) != dist.Backend.NCCL, \
@@ -68,6 +70,24 @@ class CustomAllreduce:
             self._ctx = 0
             raise
         self.disabled = False
+
+    @contextlib.contextmanager
+    def capture(self):
+        """Context for CUDA-graph capture (custom_all_reduce.py:391-403 in the
+        reference).  Nothing needs registering afterwards: the staging buffers are
+        IPC-shared at construction, call epochs are counted on the device, and a call
+        made while its stream is capturing ends with an extra barrier because every
+        replay reuses the same staging buffer.  `is_capturing` mirrors the reference's
+        `_IS_CAPTURING`."""
+        try:
+            self._IS_CAPTURING = True
+            yield
+        finally:
+            self._IS_CAPTURING = False
+
+    @property
+    def is_capturing(self) -> bool:
+        return self._IS_CAPTURING
 
     def should_custom_ar(self, inp: torch.Tensor) -> bool:
         """Eligibility (custom_all_reduce.py:423-437): bf16, contiguous, 16-byte

@@ -6,6 +6,8 @@ GroupCoordinator (parallel_state.py:1147, get_tp_group :1022).  Like the referen
 a GroupCoordinator holds an NCCL device group plus a gloo CPU group
 (parallel_state.py:262-270), and attaches the custom allreduce to the CPU group.
 """
+import contextlib
+import dataclasses
 import datetime
 import os
 from typing import Optional
@@ -16,6 +18,11 @@ import torch.distributed as dist
 from .custom_all_reduce import CustomAllreduce
 
 _TP: Optional["GroupCoordinator"] = None
+
+
+@dataclasses.dataclass
+class GraphCaptureContext:
+    stream: torch.cuda.Stream
 
 
 class GroupCoordinator:
@@ -56,6 +63,21 @@ class GroupCoordinator:
         if self.ca_comm is None or self.ca_comm.disabled:
             raise RuntimeError("GEMM + allreduce needs the custom allreduce (world sizes 2, 4, 6, 8)")
         return self.ca_comm.gemm_all_reduce(a, w)
+
+    @contextlib.contextmanager
+    def graph_capture(self, graph_capture_context: Optional["GraphCaptureContext"] = None):
+        """Run the body on a side stream inside the allreduce's capture context
+        (parallel_state.py:345-374 in the reference)."""
+        if graph_capture_context is None:
+            graph_capture_context = GraphCaptureContext(torch.cuda.Stream(device=self.device))
+        stream = graph_capture_context.stream
+        curr = torch.cuda.current_stream(self.device)
+        if curr != stream:
+            stream.wait_stream(curr)
+        ca = self.ca_comm.capture() if self.ca_comm is not None and not self.ca_comm.disabled \
+            else contextlib.nullcontext()
+        with torch.cuda.stream(stream), ca:
+            yield graph_capture_context
 
     def destroy(self):
         if self.ca_comm is not None:
@@ -101,6 +123,15 @@ def initialize_model_parallel(tensor_model_parallel_size=1, local_rank=None, bac
 def get_tp_group() -> GroupCoordinator:
     assert _TP is not None, "tensor model parallel group is not initialized"
     return _TP
+
+
+@contextlib.contextmanager
+def graph_capture():
+    """Context around CUDA-graph capture of tensor-parallel code
+    (parallel_state.py:1058-1074 in the reference): yields a GraphCaptureContext
+    whose stream the graph should be captured on."""
+    with get_tp_group().graph_capture() as ctx:
+        yield ctx
 
 
 def destroy_model_parallel():

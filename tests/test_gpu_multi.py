@@ -87,11 +87,53 @@ def _worker(rank, world, port):
         dist.all_gather(gathered, out, group=tp.device_group)
         for gg in gathered:
             assert torch.equal(gg, out)
+    # CUDA-graph capture: each replay reuses the captured buffers and counts its
+    # epochs on the device; results must follow the inputs copied in before replay,
+    # also when eager calls are interleaved with replays
+    _graph_case(rank, world, dev, tp, ca)
     # tensor-parallel fused MoE vs the single-GPU fused MoE on the full weights
     for i_per_rank in (256, 192):  # 192: shards re-blocked to 256 (inter_dim / tp not 128-aligned)
         _tp_moe_case(rank, world, dev, tp, i_per_rank)
     ps.destroy_model_parallel()
     dist.destroy_process_group()
+
+
+def _graph_case(rank, world, dev, tp, ca):
+    from aiter_b200 import _lib
+    from aiter_b200.dist import parallel_state as ps
+    n, M, K, N = 64 * 1024, 8, 8192 // world, 4096
+    x_static = torch.zeros(n, dtype=torch.bfloat16, device=dev)
+    a_static = torch.zeros(M, K, dtype=torch.bfloat16, device=dev)
+    w = torch.randn(N, K, generator=torch.Generator().manual_seed(5 + rank)).to(torch.bfloat16).to(dev)
+    ca.all_reduce(x_static)  # warm: kernels loaded before capture
+    tp.gemm_all_reduce(a_static, w)
+    torch.cuda.synchronize()
+    with ps.graph_capture() as ctx:
+        assert ca.is_capturing
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=ctx.stream):
+            y_static = ca.all_reduce(x_static)
+            z_static = tp.gemm_all_reduce(a_static, w)
+    assert not ca.is_capturing
+    ws = [torch.randn(N, K, generator=torch.Generator().manual_seed(5 + r)).to(torch.bfloat16) for r in range(world)]
+    for it in range(6):
+        xs = _inputs(n, world, 300 + it)
+        g_ = torch.Generator().manual_seed(700 + it)
+        As = [torch.randn(M, K, generator=g_).to(torch.bfloat16) for _ in range(world)]
+        x_static.copy_(xs[rank].to(dev))
+        a_static.copy_(As[rank].to(dev))
+        g.replay()
+        if it % 2 == 1:  # an eager call between replays
+            e = ca.all_reduce(xs[rank].to(dev))
+            torch.cuda.synchronize()
+            assert torch.equal(e.cpu(), _expected(xs)), f"eager call after replay {it}"
+        torch.cuda.synchronize()
+        assert _lib.lib().custom_ar_device_error(1) == 0
+        assert torch.equal(y_static.cpu(), _expected(xs)), f"replay {it}"
+        ref = sum((As[r].float() @ ws[r].float().t()) for r in range(world))
+        err = (z_static.float().cpu() - ref).abs()
+        assert bool((err <= 2e-2 * ref.abs() + 2e-2 * ref.abs().max()).all()), (it, float(err.max()))
+    del g
 
 
 def _tp_moe_case(rank, world, dev, tp, i_per_rank):
