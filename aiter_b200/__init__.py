@@ -17,6 +17,7 @@ from .moe_op import (biased_grouped_topk, biased_grouped_topk_hip, dynamic_per_t
                      topk_softmax)
 from .fused_moe import fused_moe, fused_topk, moe_sorting, get_inter_dim
 from ._lib import device_error
+from . import torch_ops  # registers torch.ops.aiter_b200.* (fake impls for torch.compile)
 
 __all__ = [
     "dtypes", "ActivationType", "QuantType", "topk_softmax", "grouped_topk", "biased_grouped_topk",

@@ -116,7 +116,29 @@ def fused_moe(hidden_states, w1, w2, topk_weight, topk_ids, expert_mask: Optiona
               bias1=None, bias2=None, splitk=0, moe_buf=None):
     """Reference signature (aiter/fused_moe.py:118-144) plus `moe_buf`: an optional
     [M, model_dim] bf16 output to write into (e.g. the staging buffer of the
-    tensor-parallel allreduce); it is zeroed and filled like the returned buffer."""
+    tensor-parallel allreduce); it is zeroed and filled like the returned buffer.
+
+    While torch is compiling, the call goes through the custom op
+    `torch.ops.aiter_b200.fused_moe_` (fake implementation in torch_ops.py), as
+    the reference's `fused_moe` goes through `fused_moe_`."""
+    plain = (block_size_M is None and dtype is None and not hidden_pad and not intermediate_pad and bias1 is None
+             and bias2 is None and not splitk and moe_buf is None)
+    if plain and torch.compiler.is_compiling():
+        from . import torch_ops  # noqa: F401  (registers the ops)
+        return torch.ops.aiter_b200.fused_moe_(hidden_states, w1, w2, topk_weight, topk_ids, expert_mask,
+                                               int(activation), int(quant_type), bool(doweight_stage1), w1_scale,
+                                               w2_scale, a1_scale, a2_scale, num_local_tokens,
+                                               int(moe_sorting_dispatch_policy))
+    return _fused_moe_impl(hidden_states, w1, w2, topk_weight, topk_ids, expert_mask, activation, quant_type,
+                           doweight_stage1, w1_scale, w2_scale, a1_scale, a2_scale, block_size_M, num_local_tokens,
+                           moe_sorting_dispatch_policy, dtype, hidden_pad, intermediate_pad, bias1, bias2, splitk,
+                           moe_buf)
+
+
+def _fused_moe_impl(hidden_states, w1, w2, topk_weight, topk_ids, expert_mask=None, activation=ActivationType.Silu,
+                    quant_type=QuantType.No, doweight_stage1=False, w1_scale=None, w2_scale=None, a1_scale=None,
+                    a2_scale=None, block_size_M=None, num_local_tokens=None, moe_sorting_dispatch_policy=0,
+                    dtype=None, hidden_pad=0, intermediate_pad=0, bias1=None, bias2=None, splitk=0, moe_buf=None):
     activation = ActivationType(int(activation))
     quant_type = quant_remap.get(QuantType(int(quant_type)), QuantType(int(quant_type)))
     M, topk = topk_ids.shape
