@@ -50,8 +50,9 @@ def parse():
     p.add_argument("--E", type=int, default=128, help="experts (profiling cases use fewer)")
     p.add_argument("--cpu-sample", type=int, default=128, help="tokens per CPU-baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--mode", default="moe", choices=["moe", "tp_moe", "gemm_ar"],
-                   help="moe: config 1 (N>1: data-parallel replicas); tp_moe: config 3; gemm_ar: config 4")
+    p.add_argument("--mode", default="moe", choices=["moe", "moe_sweep", "tp_moe", "gemm_ar"],
+                   help="moe: config 1 at --M (N>1: data-parallel replicas); moe_sweep: config 1 token sweep "
+                        "on one GPU; tp_moe: config 3; gemm_ar: config 4")
     return p.parse_args()
 
 
@@ -433,6 +434,60 @@ def run_tp_moe(args, rank, world, local):
             "clocks": clk.summary()}
 
 
+def run_moe_sweep(args, rank, world, local):
+    """Config 1 token sweep M in {1, 16, 128, 1024, 4096, 16384} on one GPU: device-
+    resident fused-MoE step time (sort -> gather-quant -> stage 1 -> stage 2) with
+    both roofline fractions, since small M is weight-bandwidth bound and large M
+    tensor bound.  Algorithmic bytes per step: fp8 weights (+ scales) of the experts
+    the batch routes to, bf16 input, fp8 intermediate (+ scales), bf16 output and the
+    output zeroing; FLOPs 6 M k D I."""
+    from aiter_b200 import moe_op, dtypes
+    pk, src = peaks()
+    fp8_peak = 2.0 * pk["bf16_tflops"]
+    rows = []
+    x = make_inputs(16384, seed=1234, E=E)
+    B = 128
+    for M in (1, 16, 128, 1024, 4096, 16384):
+        tid, tw, hid = x["tid"][:M].contiguous(), x["tw"][:M].contiguous(), x["hidden"][:M].contiguous()
+        dev = hid.device
+        max_pad = M * TOPK + E * B - TOPK
+        sid = torch.empty(max_pad, dtype=torch.int32, device=dev)
+        sw = torch.empty(max_pad, dtype=torch.float32, device=dev)
+        seid = torch.empty((max_pad + B - 1) // B, dtype=torch.int32, device=dev)
+        nv = torch.empty(2, dtype=torch.int32, device=dev)
+        pos = torch.empty(M * TOPK, dtype=torch.int32, device=dev)
+        out = torch.empty(M, D, dtype=torch.bfloat16, device=dev)
+        ws_n = moe_op.moe_sorting_get_workspace_size(M, E, TOPK, 0)
+        ws = torch.empty(max(ws_n, 1), dtype=torch.uint8, device=dev)
+        a1 = torch.empty(max_pad, D, dtype=dtypes.fp8, device=dev)
+        a1s = torch.empty(D // 128, max_pad, dtype=torch.float32, device=dev)
+        a2 = torch.empty(max_pad, I, dtype=dtypes.fp8, device=dev)
+        a2s = torch.empty(I // 128, max_pad, dtype=torch.float32, device=dev)
+
+        def step():
+            moe_op.moe_sorting_fwd(tid, tw, sid, sw, seid, nv, out, E, B, None, None, 0, ws if ws_n else None, pos)
+            moe_op.moe_gather_quant_1x128(hid, pos, TOPK, max_pad, out=a1, out_scale=a1s)
+            moe_op.moe_stage1_fp8_blockscale(a1, a1s, x["w1q"], x["w1s"], sid, seid, nv, a2, a2s, M, B)
+            moe_op.moe_stage2_fp8_blockscale(a2, a2s, x["w2q"], x["w2s"], sid, seid, nv, sw, out, B)
+
+        ms = _time_loop(step, args.steps, args.warmup, world)
+        active = int(torch.unique(tid).numel())
+        w_bytes = active * 3 * D * I + active * (3 * D * I // (128 * 128)) * 4
+        bytes_ = w_bytes + M * D * 2 + 2 * M * TOPK * I + M * TOPK * (I // 128) * 4 + M * D * 2 * 2
+        tfl = flops(M) / (ms * 1e-3) / 1e12
+        gbs = bytes_ / (ms * 1e-3) / 1e9
+        rows.append({"M": M, "ms_per_step": round(ms, 4), "tokens_per_s": round(M / (ms * 1e-3), 1),
+                     "tflops": round(tfl, 2), "active_experts": active,
+                     "tensor_frac": round(tfl / fp8_peak, 4), "hbm_GBs": round(gbs, 1),
+                     "hbm_frac": round(gbs / pk["hbm_gbs"], 4),
+                     "bound": "hbm" if gbs / pk["hbm_gbs"] > tfl / fp8_peak else "tensor"})
+    return {"metric": METRIC, "mode": "moe_sweep", "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "dtype": "fp8-e4m3", "data": "synthetic",
+            "config": {"workload": "BASELINE config 1 token sweep", "hidden": D, "inter": I, "experts": E,
+                       "topk": TOPK}, "peaks": {"fp8_tflops": fp8_peak, "hbm_gbs": pk["hbm_gbs"], "source": src},
+            "sweep": rows}
+
+
 def run_gemm_ar(args, rank, world, local):
     """Config 4: y = allreduce(A @ B), A [M, 8192/TP], B [8192/TP, 4096] bf16 per rank:
     the tcgen05 GEMM writing into the IPC allreduce's staging buffer vs cuBLAS
@@ -484,8 +539,9 @@ def main():
     args = parse()
     rank, world, local = dist_setup(args.gpus)
     try:
-        if args.mode in ("tp_moe", "gemm_ar"):
-            res = (run_tp_moe if args.mode == "tp_moe" else run_gemm_ar)(args, rank, world, local)
+        if args.mode in ("tp_moe", "gemm_ar", "moe_sweep"):
+            res = {"tp_moe": run_tp_moe, "gemm_ar": run_gemm_ar, "moe_sweep": run_moe_sweep}[args.mode](
+                args, rank, world, local)
             if rank == 0:
                 print(json.dumps(res), flush=True)
             return

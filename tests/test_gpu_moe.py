@@ -221,3 +221,31 @@ def test_fused_moe_traces_under_torch_compile():
     assert out_c.shape == out_e.shape and out_c.dtype == torch.bfloat16
     # the stage-2 scatter-add is bf16 atomics in no fixed order
     assert torch.allclose(out_c.float(), out_e.float(), rtol=1e-2, atol=1e-2)
+
+
+def test_fused_moe_expert_parallel_partials_sum_to_full():
+    """Expert parallelism through `expert_mask` (the EP path of fused_moe,
+    aiter/fused_moe.py:118-144 with op_tests/test_moe_ep.py): each of two simulated
+    ranks holds half of the experts' weights; the masked sort maps global expert ids
+    to local ones and drops tokens routed elsewhere, so the two partial outputs add up
+    to the full MoE."""
+    M, D, I, E, k = 64, 1024, 512, 16, 4
+    c = inputs.make_moe_case(11, M, D, I, E, k)
+    hidden = to_dev(c["hidden"], torch.bfloat16)
+    w1, w2 = fp8_from_codes(c["w1_q"]), fp8_from_codes(c["w2_q"])
+    w1s, w2s = to_dev(c["w1_s"]), to_dev(c["w2_s"])
+    tw, tid = to_dev(c["topk_weights"]), to_dev(c["topk_ids"])
+    kw = dict(quant_type=aiter.QuantType.per_1x128)
+    full = aiter.fused_moe(hidden, w1, w2, tw, tid, w1_scale=w1s, w2_scale=w2s, **kw)
+    total = torch.zeros_like(full, dtype=torch.float32)
+    for r in range(2):
+        lo, hi = r * E // 2, (r + 1) * E // 2
+        mask = torch.zeros(E, dtype=torch.int32, device=dev())
+        mask[lo:hi] = 1
+        part = aiter.fused_moe(hidden, w1[lo:hi].contiguous(), w2[lo:hi].contiguous(), tw, tid, expert_mask=mask,
+                               w1_scale=w1s[lo:hi].contiguous(), w2_scale=w2s[lo:hi].contiguous(), **kw)
+        total += part.float()
+    torch.cuda.synchronize()
+    check_no_device_error()
+    # the partials are bf16-rounded before the sum
+    assert_moe_close(total.cpu().numpy(), full.float().cpu().numpy())
