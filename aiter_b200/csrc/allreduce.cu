@@ -200,6 +200,124 @@ allreduce_bf16_kernel(Peers P, int rank, int parity, const uint4* __restrict__ i
     if (end_barrier) block_barrier(P, rank, W, 2, epoch);
 }
 
+// ---------------------------------------------------------------------------
+// Allreduce fused with the residual add and RMSNorm that follow it in a TP layer
+// (fused_allreduce_rmsnorm / _quant, csrc/include/custom_all_reduce.cuh:1187-1250,
+// 1420-1500 in the reference).  One-shot over rows: CTA b stages and later reduces
+// rows b, b + grid, ..., so it only reads rows the same CTA index of every peer
+// staged before the barrier.  Per row, in fp32:
+//   ar      = bf16(sum over ranks in rank order)      (the plain allreduce result)
+//   x       = ar + res_inp;  res_out = bf16(x)
+//   r       = rsqrt(mean(x^2) + eps)
+//   out     = bf16(x * w * r)                         (QUANT: y = x * w * r, then
+//             per-row fp8: scale = amax(|y|) / 448 (0 -> 1), q = fp8(y / scale))
+template <int W, bool QUANT>
+__global__ void __launch_bounds__(kThreads)
+allreduce_rmsnorm_kernel(Peers P, int rank, int parity, const uint4* __restrict__ in,
+                         const uint4* __restrict__ res_in, uint4* __restrict__ res_out, void* __restrict__ out,
+                         float* __restrict__ scale_out, const uint4* __restrict__ weight, int64_t rows, int ppr,
+                         float eps, int end_barrier) {
+    constexpr int MAXP = 4;  // packs of 8 per thread: hidden <= 4 * 8 * kThreads
+    __shared__ uint32_t s_epoch;
+    __shared__ float s_red[kThreads / 32];
+    if (threadIdx.x == 0) {
+        uint32_t* ctr = &P.sig[rank]->counter[blockIdx.x];
+        s_epoch = *ctr + 1;
+        *ctr = s_epoch;
+    }
+    __syncthreads();
+    const uint32_t epoch = s_epoch;
+    uint4* mine = reinterpret_cast<uint4*>(P.buf[parity][rank]);
+    const uint4* bufs[W];
+#pragma unroll
+    for (int p = 0; p < W; ++p) bufs[p] = reinterpret_cast<const uint4*>(P.buf[parity][p]);
+    if (in != mine)
+        for (int64_t row = blockIdx.x; row < rows; row += gridDim.x)
+            for (int p = threadIdx.x; p < ppr; p += blockDim.x) mine[row * ppr + p] = in[row * ppr + p];
+    if (!block_barrier(P, rank, W, 0, epoch)) return;
+    const float inv_n = 1.0f / (float)(ppr * 8);
+    auto block_sum = [&](float v, bool is_max) -> float {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float t = __shfl_xor_sync(0xffffffffu, v, o);
+            v = is_max ? fmaxf(v, t) : v + t;
+        }
+        if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = v;
+        __syncthreads();
+        float r = is_max ? 0.f : 0.f;
+        for (int i = 0; i < (int)(blockDim.x >> 5); ++i) r = is_max ? fmaxf(r, s_red[i]) : r + s_red[i];
+        __syncthreads();  // s_red is reused by the next reduction
+        return r;
+    };
+    for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+        float x[MAXP][8];
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < MAXP; ++j) {
+            const int p = threadIdx.x + j * blockDim.x;
+            if (p < ppr) {
+                const int64_t i = row * ppr + p;
+                uint4 v[W];
+#pragma unroll
+                for (int r = 0; r < W; ++r) v[r] = ld_cg(bufs[r] + i);
+                float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+                for (int r = 0; r < W; ++r) acc8(a, v[r]);
+                const uint4 ar = pack8(a);  // the allreduce result, rounded to bf16
+                const uint4 rs = res_in[i];
+                const __nv_bfloat162* ah = reinterpret_cast<const __nv_bfloat162*>(&ar);
+                const __nv_bfloat162* rh = reinterpret_cast<const __nv_bfloat162*>(&rs);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 fa = __bfloat1622float2(ah[e]), fr = __bfloat1622float2(rh[e]);
+                    x[j][2 * e] = fa.x + fr.x;
+                    x[j][2 * e + 1] = fa.y + fr.y;
+                    ss += x[j][2 * e] * x[j][2 * e] + x[j][2 * e + 1] * x[j][2 * e + 1];
+                }
+                res_out[i] = pack8(x[j]);
+            }
+        }
+        const float rinv = rsqrtf(block_sum(ss, false) * inv_n + eps);
+        float amax = 0.f;
+#pragma unroll
+        for (int j = 0; j < MAXP; ++j) {
+            const int p = threadIdx.x + j * blockDim.x;
+            if (p < ppr) {
+                const uint4 wv = weight[p];
+                const __nv_bfloat162* wh = reinterpret_cast<const __nv_bfloat162*>(&wv);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 fw = __bfloat1622float2(wh[e]);
+                    x[j][2 * e] = x[j][2 * e] * fw.x * rinv;
+                    x[j][2 * e + 1] = x[j][2 * e + 1] * fw.y * rinv;
+                    amax = fmaxf(amax, fmaxf(fabsf(x[j][2 * e]), fabsf(x[j][2 * e + 1])));
+                }
+                if (!QUANT) reinterpret_cast<uint4*>(out)[row * ppr + p] = pack8(x[j]);
+            }
+        }
+        if (QUANT) {
+            amax = block_sum(amax, true);
+            const float scale = amax == 0.f ? 1.f : amax / 448.0f;
+#pragma unroll
+            for (int j = 0; j < MAXP; ++j) {
+                const int p = threadIdx.x + j * blockDim.x;
+                if (p < ppr) {
+                    uint32_t q[2];
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        __nv_fp8x4_e4m3 f4(make_float4(x[j][4 * h] / scale, x[j][4 * h + 1] / scale,
+                                                       x[j][4 * h + 2] / scale, x[j][4 * h + 3] / scale));
+                        q[h] = *reinterpret_cast<uint32_t*>(&f4);
+                    }
+                    reinterpret_cast<uint2*>(out)[row * ppr + p] = make_uint2(q[0], q[1]);
+                }
+            }
+            if (threadIdx.x == 0) scale_out[row] = scale;
+        }
+    }
+    if (end_barrier) block_barrier(P, rank, W, 2, epoch);
+}
+
 struct Ctx {
     int rank = 0, world = 0, device = -1;
     size_t max_bytes = 0;
@@ -406,4 +524,71 @@ AB_ENTRY(custom_ar_gemm_all_reduce,
     stage.device_id = c->device;
     if (gemm_a16w16(a, w, &stage, stream) != 0) fail(std::string(aiter_get_last_error() ? aiter_get_last_error() : "gemm failed"));
     custom_ar_all_reduce_impl(ctx, &stage, out, force_two_shot, stream);
+}
+
+// allreduce(inp) + res_inp -> res_out, RMSNorm(res_out) * w -> out (bf16), or with
+// `out` fp8 and `scale_out` [rows] f32: the per-row fp8 quant of the normalised row.
+AB_ENTRY(custom_ar_allreduce_rmsnorm,
+         (int64_t ctx, aiter_tensor_t* inp, aiter_tensor_t* res_inp, aiter_tensor_t* res_out, aiter_tensor_t* out,
+          aiter_tensor_t* weight, float eps, aiter_tensor_t* scale_out, void* stream),
+         (ctx, inp, res_inp, res_out, out, weight, eps, scale_out, stream)) {
+    using namespace ab;
+    Ctx* c = as_ctx(ctx);
+    AB_CHECK(c->ready, "custom_ar_open_peers has not been called");
+    for (aiter_tensor_t* t : {inp, res_inp, res_out, out, weight}) need(t, "tensor");
+    for (aiter_tensor_t* t : {inp, res_inp, res_out, weight}) need_dtype(t, AITER_DTYPE_bf16, "bf16 operand");
+    for (aiter_tensor_t* t : {inp, res_inp, res_out, out, weight}) need_contig(t, "operand");
+    const bool quant = scale_out != nullptr;
+    need_dtype(out, quant ? AITER_DTYPE_fp8 : AITER_DTYPE_bf16, "out");
+    AB_CHECK(inp->ndim >= 1, "inp must have a hidden dimension");
+    const int64_t hidden = inp->shape[inp->ndim - 1];
+    const int64_t rows = hidden > 0 ? (int64_t)inp->numel_ / hidden : 0;
+    AB_CHECK(hidden % 8 == 0 && hidden <= 4 * 8 * kThreads, "hidden size must be a multiple of 8 and at most ",
+             4 * 8 * kThreads);
+    AB_CHECK((int64_t)weight->numel_ == hidden, "weight must have `hidden` elements");
+    for (aiter_tensor_t* t : {res_inp, res_out, out})
+        AB_CHECK(t->numel_ == inp->numel_, "inp, res_inp, res_out and out must have the same number of elements");
+    if (quant) {
+        need_dtype(scale_out, AITER_DTYPE_fp32, "scale_out");
+        need_contig(scale_out, "scale_out");
+        AB_CHECK((int64_t)scale_out->numel_ == rows, "scale_out must hold one scale per row");
+    }
+    const size_t bytes = inp->numel_ * 2;
+    AB_CHECK(bytes <= c->max_bytes, "allreduce of ", bytes, " bytes exceeds the registered ", c->max_bytes);
+    for (aiter_tensor_t* t : {inp, res_inp, res_out, out, weight})
+        AB_CHECK(((uintptr_t)t->ptr & 15) == 0, "buffers must be 16-byte aligned");
+    AB_CHECK(inp->device_id == c->device, "tensor on a different device than the communicator");
+    if (rows == 0) return;
+    DeviceGuard dg(c->device);
+    c->epoch += 1;
+    const int parity = (int)(c->epoch & 1);
+    const int ppr = (int)(hidden / 8);
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(rows, std::min(kMaxBlocks, num_sms(c->device))));
+    cudaStream_t st = as_stream(stream);
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    AB_CUDA(cudaStreamIsCapturing(st, &cap));
+    const int endb = cap == cudaStreamCaptureStatusNone ? 0 : 1;
+    const uint4* src = (const uint4*)inp->ptr;
+#define AB_ARRMS(WW)                                                                                              \
+    do {                                                                                                          \
+        if (quant)                                                                                                \
+            allreduce_rmsnorm_kernel<WW, true><<<grid, kThreads, 0, st>>>(                                        \
+                c->peers, c->rank, parity, src, (const uint4*)res_inp->ptr, (uint4*)res_out->ptr, out->ptr,       \
+                (float*)scale_out->ptr, (const uint4*)weight->ptr, rows, ppr, eps, endb);                         \
+        else                                                                                                      \
+            allreduce_rmsnorm_kernel<WW, false><<<grid, kThreads, 0, st>>>(                                       \
+                c->peers, c->rank, parity, src, (const uint4*)res_inp->ptr, (uint4*)res_out->ptr, out->ptr,       \
+                nullptr, (const uint4*)weight->ptr, rows, ppr, eps, endb);                                        \
+    } while (0)
+    switch (c->world) {
+        case 2: AB_ARRMS(2); break;
+        case 3: AB_ARRMS(3); break;
+        case 4: AB_ARRMS(4); break;
+        case 5: AB_ARRMS(5); break;
+        case 6: AB_ARRMS(6); break;
+        case 7: AB_ARRMS(7); break;
+        default: AB_ARRMS(8); break;
+    }
+#undef AB_ARRMS
+    check_launch("custom_ar_allreduce_rmsnorm");
 }

@@ -60,6 +60,19 @@ def shard_moe_weights_for_tp(w1, w1_scale, w2, w2_scale, rank, tp, chunk=8):
     return torch.cat(q1), torch.cat(q1s), torch.cat(q2), torch.cat(q2s)
 
 
+def tensor_model_parallel_fused_allreduce_rmsnorm(input_, residual_inp_, weight_, eps, prefill_support=False):
+    """(RMSNorm(allreduce(x) + residual) * w, allreduce(x) + residual)
+    (aiter/dist/communication_op.py:40-49)."""
+    return get_tp_group().fused_allreduce_rmsnorm(input_, residual_inp_, weight_, eps, prefill_support)
+
+
+def tensor_model_parallel_fused_allreduce_rmsnorm_quant(input_, residual_inp_, weight_, eps,
+                                                        prefill_support=False):
+    """fp8 per-row-quantised variant: (out_fp8, residual_out, scale)
+    (aiter/dist/communication_op.py:52-65)."""
+    return get_tp_group().fused_allreduce_rmsnorm_quant(input_, residual_inp_, weight_, eps, prefill_support)
+
+
 def tensor_model_parallel_fused_moe(hidden_states, w1, w2, topk_weight, topk_ids, **kwargs):
     """Tensor-parallel fused MoE: each rank holds inter_dim/tp of every expert
     (`shard_moe_weights_for_tp`), runs the fused MoE on its shard with the stage-2

@@ -127,6 +127,49 @@ class CustomAllreduce:
             _lib.check_status("custom_ar_gemm_all_reduce", ret)
         return out
 
+    def fused_ar_rms(self, inp: torch.Tensor, res_inp: torch.Tensor, *, res_out: torch.Tensor = None,
+                     out: torch.Tensor = None, scale_out: torch.Tensor = None, w: torch.Tensor, eps: float,
+                     registered: bool = False, use_1stage: bool = False, post_per_token_quant: bool = False):
+        """allreduce(inp) + res_inp -> res_out and RMSNorm(res_out) * w -> out in one
+        kernel (custom_all_reduce.py:603-660 in the reference).  With
+        `post_per_token_quant` the output is fp8 with one fp32 scale per row.
+        Returns (out, res_out) or (out, res_out, scale_out).  `registered` and
+        `use_1stage` are accepted for the reference's signature; the kernel is one-shot."""
+        if res_out is None:
+            res_out = torch.empty_like(inp)
+        if post_per_token_quant:
+            if out is None:
+                out = torch.empty(inp.shape, dtype=torch.float8_e4m3fn, device=inp.device)
+            if scale_out is None:
+                scale_out = torch.empty(inp.shape[:-1] + (1,), dtype=torch.float32, device=inp.device)
+        elif out is None:
+            out = torch.empty_like(inp)
+        ts = [_lib.to_aiter(t) for t in (inp, res_inp, res_out, out, w)]
+        sc = _lib.to_aiter(scale_out) if post_per_token_quant else None
+        st = _lib.current_stream_ptr(self.device.index)
+        ret = self._L.custom_ar_allreduce_rmsnorm(self._ctx, *[ctypes.byref(t) for t in ts], float(eps),
+                                                  ctypes.byref(sc) if sc is not None else None, st)
+        if ret:
+            _lib.check_status("custom_ar_allreduce_rmsnorm", ret)
+        return (out, res_out, scale_out) if post_per_token_quant else (out, res_out)
+
+    def _fused_eligible(self, inp: torch.Tensor) -> bool:
+        h = inp.shape[-1] if inp.dim() else 0
+        return self.should_custom_ar(inp) and h % 8 == 0 and 0 < h <= 16384
+
+    def custom_fused_ar_rms(self, input: torch.Tensor, residual_inp: torch.Tensor, weight: torch.Tensor,
+                            eps: float, use_1stage: bool = False):
+        if self.disabled or not self._fused_eligible(input):
+            return None
+        return self.fused_ar_rms(input, residual_inp, w=weight, eps=eps, use_1stage=use_1stage)
+
+    def custom_fused_ar_rms_quant(self, input: torch.Tensor, residual_inp: torch.Tensor, weight: torch.Tensor,
+                                  eps: float, use_1stage: bool = False):
+        if self.disabled or not self._fused_eligible(input):
+            return None
+        return self.fused_ar_rms(input, residual_inp, w=weight, eps=eps, use_1stage=use_1stage,
+                                 post_per_token_quant=True)
+
     def next_buffer_tensor(self, shape, dtype=torch.bfloat16) -> torch.Tensor:
         """A tensor viewing the staging buffer the next all_reduce will read.  A
         producer that writes its result there and passes the tensor to all_reduce

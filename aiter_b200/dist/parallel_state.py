@@ -20,6 +20,20 @@ from .custom_all_reduce import CustomAllreduce
 _TP: Optional["GroupCoordinator"] = None
 
 
+def _rmsnorm_after(ar: torch.Tensor, res: torch.Tensor, w: torch.Tensor, eps: float, quant: bool):
+    """The math of the fused kernel on an already reduced tensor (used when the IPC
+    allreduce does not take the tensor): x = ar + res in fp32, res_out = bf16(x),
+    y = x * w * rsqrt(mean(x^2) + eps)."""
+    x = ar.float() + res.float()
+    res_out = x.to(ar.dtype)
+    y = x * w.float() * torch.rsqrt(x.pow(2).mean(dim=-1, keepdim=True) + eps)
+    if not quant:
+        return y.to(ar.dtype), res_out
+    amax = y.abs().amax(dim=-1, keepdim=True)
+    scale = torch.where(amax == 0, torch.ones_like(amax), amax / 448.0)
+    return (y / scale).to(torch.float8_e4m3fn), res_out, scale
+
+
 @dataclasses.dataclass
 class GraphCaptureContext:
     stream: torch.cuda.Stream
@@ -55,6 +69,28 @@ class GroupCoordinator:
         out = input_.clone()
         dist.all_reduce(out, group=self.device_group)
         return out
+
+    def fused_allreduce_rmsnorm(self, input_: torch.Tensor, residual_inp_: torch.Tensor, weight_: torch.Tensor,
+                                eps: float, prefill_support: bool = False):
+        """(out, residual_out) = (RMSNorm(allreduce(input_) + residual_inp_) * weight_,
+        allreduce(input_) + residual_inp_) -- the fused kernel when the IPC allreduce
+        takes the tensor, else the allreduce followed by the same math in torch
+        (communicator_cuda.py:207-255 in the reference)."""
+        if self.world_size > 1 and self.ca_comm is not None:
+            r = self.ca_comm.custom_fused_ar_rms(input_, residual_inp_, weight_, eps)
+            if r is not None:
+                return r
+        return _rmsnorm_after(self.all_reduce(input_), residual_inp_, weight_, eps, quant=False)
+
+    def fused_allreduce_rmsnorm_quant(self, input_: torch.Tensor, residual_inp_: torch.Tensor,
+                                      weight_: torch.Tensor, eps: float, prefill_support: bool = False):
+        """As fused_allreduce_rmsnorm with the normalised rows quantised to fp8 e4m3,
+        one scale per row: (out_fp8, residual_out, scale [.., 1])."""
+        if self.world_size > 1 and self.ca_comm is not None:
+            r = self.ca_comm.custom_fused_ar_rms_quant(input_, residual_inp_, weight_, eps)
+            if r is not None:
+                return r
+        return _rmsnorm_after(self.all_reduce(input_), residual_inp_, weight_, eps, quant=True)
 
     def gemm_all_reduce(self, a: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         if self.world_size == 1:

@@ -241,6 +241,15 @@ int custom_ar_all_reduce(int64_t ctx, aiter_tensor_t* inp, aiter_tensor_t* out, 
  * tensor_model_parallel_all_reduce, aiter/dist/communication_op.py:30-37). */
 int custom_ar_gemm_all_reduce(int64_t ctx, aiter_tensor_t* a, aiter_tensor_t* w, aiter_tensor_t* out,
                               int64_t force_two_shot, void* stream);
+/* Allreduce fused with the residual add and RMSNorm that follow it: res_out =
+ * bf16(allreduce(inp) + res_inp), out = bf16(res * weight * rsqrt(mean(res^2) + eps))
+ * row by row over the last dimension (hidden <= 16384).  With scale_out given
+ * ([rows] f32) `out` is fp8 e4m3 with one scale per row (amax / 448).  Replaces
+ * fused_allreduce_rmsnorm / fused_allreduce_rmsnorm_quant
+ * (aiter/ops/custom_all_reduce.py:65-94; csrc/include/custom_all_reduce.cuh:1187-1500). */
+int custom_ar_allreduce_rmsnorm(int64_t ctx, aiter_tensor_t* inp, aiter_tensor_t* res_inp, aiter_tensor_t* res_out,
+                                aiter_tensor_t* out, aiter_tensor_t* weight, float eps, aiter_tensor_t* scale_out,
+                                void* stream);
 int custom_ar_dispose(int64_t ctx);
 /* Error word of the allreduce barriers (1 = a peer did not arrive within 2 s). */
 int custom_ar_device_error(int clear);

@@ -62,6 +62,35 @@ def test_group_coordinator_allreduce_fallback_path():
     run_ranks(_group_allreduce, 2)
 
 
+def _group_fused_rmsnorm(rank, world, port):
+    """fused_allreduce_rmsnorm(_quant) through the non-custom path: allreduce, then
+    x = ar + residual (fp32), residual_out = bf16(x), out = x * w * rsqrt(mean x^2 + eps)."""
+    _init(rank, world, port)
+    from aiter_b200.dist import parallel_state as ps
+    from aiter_b200.dist import (tensor_model_parallel_fused_allreduce_rmsnorm,
+                                 tensor_model_parallel_fused_allreduce_rmsnorm_quant)
+    ps.initialize_model_parallel(world, local_rank=rank, backend="gloo", use_custom_allreduce=False)
+    g = torch.Generator().manual_seed(3)
+    xs = [torch.randn(5, 64, generator=g).to(torch.bfloat16) for _ in range(world)]
+    res = torch.randn(5, 64, generator=g).to(torch.bfloat16)
+    w = (torch.rand(64, generator=g) + 0.5).to(torch.bfloat16)
+    out, res_out = tensor_model_parallel_fused_allreduce_rmsnorm(xs[rank].clone(), res, w, 1e-6)
+    ar = sum(x.float() for x in xs).to(torch.bfloat16)  # gloo sums bf16 in rank order too
+    x = ar.float() + res.float()
+    assert torch.equal(res_out, x.to(torch.bfloat16))
+    ref = x * w.float() / torch.sqrt((x * x).mean(-1, keepdim=True) + 1e-6)
+    assert torch.allclose(out.float(), ref, rtol=1e-2, atol=1e-2)
+    q, res_out2, scale = tensor_model_parallel_fused_allreduce_rmsnorm_quant(xs[rank].clone(), res, w, 1e-6)
+    assert q.dtype == torch.float8_e4m3fn and scale.shape == (5, 1) and torch.equal(res_out2, res_out)
+    assert torch.allclose(q.float() * scale, ref, rtol=0.07, atol=0.02 * float(ref.abs().max()))
+    ps.destroy_model_parallel()
+    dist.destroy_process_group()
+
+
+def test_group_coordinator_fused_allreduce_rmsnorm_fallback_path():
+    run_ranks(_group_fused_rmsnorm, 2)
+
+
 def _unsupported_world(rank, world, port):
     _init(rank, world, port)
     from aiter_b200.dist.custom_all_reduce import CustomAllreduce

@@ -87,6 +87,8 @@ def _worker(rank, world, port):
         dist.all_gather(gathered, out, group=tp.device_group)
         for gg in gathered:
             assert torch.equal(gg, out)
+    # allreduce fused with the residual add and RMSNorm (and the fp8 per-row quant)
+    _fused_rmsnorm_case(rank, world, dev, ca)
     # CUDA-graph capture: each replay reuses the captured buffers and counts its
     # epochs on the device; results must follow the inputs copied in before replay,
     # also when eager calls are interleaved with replays
@@ -96,6 +98,35 @@ def _worker(rank, world, port):
         _tp_moe_case(rank, world, dev, tp, i_per_rank)
     ps.destroy_model_parallel()
     dist.destroy_process_group()
+
+
+def _fused_rmsnorm_case(rank, world, dev, ca):
+    from aiter_b200 import _lib
+    for rows, hidden in ((1, 4096), (7, 7168), (300, 8192), (64, 16384)):
+        g = torch.Generator().manual_seed(rows + hidden)
+        xs = [torch.randn(rows, hidden, generator=g).to(torch.bfloat16) for _ in range(world)]
+        res = torch.randn(rows, hidden, generator=g).to(torch.bfloat16)
+        w = (torch.rand(hidden, generator=g) + 0.5).to(torch.bfloat16)
+        out, res_out = ca.custom_fused_ar_rms(xs[rank].to(dev), res.to(dev), w.to(dev), 1e-6)
+        q, res_out2, scale = ca.custom_fused_ar_rms_quant(xs[rank].to(dev), res.to(dev), w.to(dev), 1e-6)
+        torch.cuda.synchronize()
+        assert _lib.lib().custom_ar_device_error(1) == 0
+        ar = _expected([x.reshape(-1) for x in xs]).reshape(rows, hidden)  # bf16 of the rank-ordered fp32 sum
+        x = ar.float() + res.float()
+        assert torch.equal(res_out.cpu(), x.to(torch.bfloat16)), (rows, hidden)
+        assert torch.equal(res_out2.cpu(), x.to(torch.bfloat16))
+        ref = x * w.float() / torch.sqrt((x * x).mean(-1, keepdim=True) + 1e-6)
+        assert torch.allclose(out.float().cpu(), ref, rtol=1e-2, atol=1e-2), (rows, hidden)
+        sc = scale.cpu()
+        assert sc.shape == (rows, 1)
+        assert torch.allclose(sc, ref.abs().amax(-1, keepdim=True) / 448.0, rtol=1e-2)
+        deq = q.float().cpu() * sc
+        assert torch.allclose(deq, ref, rtol=0.07, atol=0.02 * float(ref.abs().max())), (rows, hidden)
+        for t in (out, res_out, q.view(torch.uint8), scale):
+            gathered = [torch.empty_like(t) for _ in range(world)]
+            dist.all_gather(gathered, t)
+            for gg in gathered:
+                assert torch.equal(gg, t)
 
 
 def _graph_case(rank, world, dev, tp, ca):
