@@ -23,8 +23,6 @@
 // Stage 2 epilogue: multiply by the row's top-k weight and add into the bf16
 // output row of its token with vector red.global.add (the output is zeroed by
 // moe_sorting_fwd), i.e. the scatter-reduce over the k slots.
-#include <cstdlib>
-
 #include "sm100.cuh"
 
 namespace {
@@ -507,16 +505,6 @@ void launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& t
     ab::check_launch(STAGE == 1 ? "moe_stage1_fp8_blockscale" : "moe_stage2_fp8_blockscale");
 }
 
-// Accumulator width of the stage-2 kernel (AITER_B200_STAGE2_BN=128|256 overrides).
-int stage2_bn() {
-    static int bn = [] {
-        const char* e = getenv("AITER_B200_STAGE2_BN");
-        int v = e ? atoi(e) : 256;
-        return (v == 256) ? 256 : 128;
-    }();
-    return bn;
-}
-
 }  // namespace
 
 AB_ENTRY(moe_stage1_fp8_blockscale,
@@ -622,8 +610,7 @@ AB_ENTRY(moe_stage2_fp8_blockscale,
     CUtensorMap tmA, tmB;
     make_tmap_2d_u8(&tmA, a2->ptr, (uint64_t)c.rows_pad, I, 128, 128, true);
     make_tmap_2d_u8(&tmB, w2->ptr, (uint64_t)E * D, I, 128, 128, true);
-    if (stage2_bn() == 256) launch<2, 256>(tmA, tmB, tmA, a, a2->device_id, as_stream(stream));
-    else launch<2, 128>(tmA, tmB, tmA, a, a2->device_id, as_stream(stream));
+    launch<2, 256>(tmA, tmB, tmA, a, a2->device_id, as_stream(stream));
 }
 
 extern "C" int aiter_device_error(int clear) {

@@ -28,6 +28,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -99,7 +100,9 @@ class ClockSampler:
     def __init__(self, gpu_index):
         self.idx = gpu_index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{gpu_index}.csv")
+        # raw samples (the JSON line carries their summary); BENCH_CLOCKS_DIR keeps them
+        out_dir = os.environ.get("BENCH_CLOCKS_DIR") or tempfile.gettempdir()
+        self.path = os.path.join(out_dir, f"clocks_gpu{gpu_index}.csv")
 
     def __enter__(self):
         try:

@@ -241,4 +241,6 @@ def moe_reference_a8w4(ref, seed, M, D, I, E, k):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <reference checkout>")
+    main(sys.argv[1])
