@@ -51,9 +51,9 @@ def parse():
     p.add_argument("--E", type=int, default=128, help="experts (profiling cases use fewer)")
     p.add_argument("--cpu-sample", type=int, default=128, help="tokens per CPU-baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--mode", default="moe", choices=["moe", "moe_sweep", "tp_moe", "gemm_ar"],
+    p.add_argument("--mode", default="moe", choices=["moe", "moe_sweep", "a8w4", "tp_moe", "gemm_ar"],
                    help="moe: config 1 at --M (N>1: data-parallel replicas); moe_sweep: config 1 token sweep "
-                        "on one GPU; tp_moe: config 3; gemm_ar: config 4")
+                        "on one GPU; a8w4: config 2 on one GPU; tp_moe: config 3; gemm_ar: config 4")
     return p.parse_args()
 
 
@@ -191,6 +191,14 @@ def flops(M):
     return 6.0 * M * TOPK * D * I
 
 
+def config1(M, world):
+    """The `config` of a config-1 line (both arms report the same one)."""
+    return {"workload": "BASELINE config 1: FP8 blockscale fused MoE", "M": M, "hidden": D, "inter": I,
+            "experts": E, "topk": TOPK, "block_m": 128, "routing": "uniform softmax top-8 (renormalised)",
+            "parallelism": f"dp{world} (independent token batches, no collective)" if world > 1 else "single GPU",
+            "l2": "inputs larger than L2: 2.42 GB of weights per step, no flush"}
+
+
 def run_b200(args, rank, world, local):
     import aiter_b200 as aiter
     from aiter_b200 import dtypes, moe_op
@@ -316,11 +324,7 @@ def run_b200(args, rank, world, local):
         "vs_baseline": None,
         "dtype": "fp8-e4m3 (fp32 accumulate, bf16 out)",
         "data": "synthetic (seeded N(0,1) activations/logits, N(0,1)/sqrt(K) weights)",
-        "config": {"workload": "BASELINE config 1: FP8 blockscale fused MoE", "M": M, "hidden": D, "inter": I,
-                   "experts": E, "topk": TOPK, "block_m": B, "routing": "uniform softmax top-8 (renormalised)",
-                   "parallelism": f"dp{world} (independent token batches, no collective)" if world > 1
-                   else "single GPU",
-                   "l2": "inputs larger than L2: 2.42 GB of weights per step, no flush"},
+        "config": config1(M, world),
         "tflops": round(flops(M) * K * world / (ms * 1e-3) / 1e12, 2),
         "kernel_ms": {k: round(v, 4) for k, v in mean_ms.items()},
         "roofline": {"bound": "tensor", "kernel": "moe_stage1_fp8_blockscale (tcgen05 kind::f8f6f4)",
@@ -374,8 +378,7 @@ def run_reference(args, rank, world):
         "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * total / args.steps, 2),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (dequantised fp8)",
-        "data": "synthetic", "config": {"workload": "BASELINE config 1: FP8 blockscale fused MoE",
-                                        "M": args.cpu_sample, "hidden": D, "inter": I, "experts": E, "topk": TOPK},
+        "data": "synthetic", "config": config1(args.M, world),
         "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
                          "sample": f"{args.cpu_sample} tokens per step (bounded sample of the M=4096 workload)"},
         "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -491,6 +494,97 @@ def run_moe_sweep(args, rank, world, local):
             "sweep": rows}
 
 
+def run_a8w4(args, rank, world, local):
+    """Config 2 (A8W4) on one GPU: hidden 4096, inter 2048, E = 256, top-8, MXFP4
+    weights (e2m1 + ue8m0 per 32 along K, quantised from N(0,1)/sqrt(K)), fp8 1x128
+    activations, skewed routing: N(0,1) logits plus log p_e with p Zipf(s=1.1) over a
+    random expert order.  The MXFP4 weights are expanded once into the fp8
+    block-scale format (`prepare_a8w4`, timed separately); each step is then the
+    device-resident fused MoE.  The HBM fraction uses the algorithmic bytes of the
+    MXFP4 weights (0.5 B + 1/32 B per element) of the experts the batch routes to."""
+    import aiter_b200 as aiter
+    from aiter_b200 import moe_op, dtypes
+    from aiter_b200 import weights as Wt
+    De, Ie, Ee = 4096, 2048, 256
+    dev = torch.device("cuda", local)
+    g = torch.Generator(device=dev).manual_seed(2024)
+
+    def mxfp4(N, K, chunk=16):
+        packed = torch.empty((Ee, N, K // 2), dtype=torch.uint8, device=dev)
+        scales = torch.empty((Ee, N, K // 32), dtype=torch.uint8, device=dev)
+        for e0 in range(0, Ee, chunk):
+            w = torch.randn(chunk, N, K, device=dev, generator=g) / K ** 0.5
+            packed[e0:e0 + chunk], scales[e0:e0 + chunk] = Wt.quant_weight_mxfp4(w)
+            del w
+        return packed, scales
+
+    w1p, w1e = mxfp4(2 * Ie, De)
+    w2p, w2e = mxfp4(De, Ie)
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    w1q, w1s, w2q, w2s = Wt.prepare_a8w4(w1p, w1e, w2p, w2e)
+    t1.record()
+    torch.cuda.synchronize()
+    prep_ms = t0.elapsed_time(t1)
+    torch.cuda.empty_cache()
+    pk, src = peaks()
+    fp8_peak = 2.0 * pk["bf16_tflops"]
+    perm = torch.randperm(Ee, generator=torch.Generator().manual_seed(7)) + 1
+    bias = torch.log((1.0 / perm.double() ** 1.1) / (1.0 / perm.double() ** 1.1).sum()).float().to(dev)
+    rows = []
+    B = 128
+    for M in (64, 2048, 8192):
+        hid = torch.randn(M, De, device=dev, generator=g).to(torch.bfloat16)
+        logits = torch.randn(M, Ee, device=dev, generator=g) + bias
+        tw, tid = aiter.fused_topk(hid, logits, TOPK, True)
+        max_pad = M * TOPK + Ee * B - TOPK
+        sid = torch.empty(max_pad, dtype=torch.int32, device=dev)
+        sw = torch.empty(max_pad, dtype=torch.float32, device=dev)
+        seid = torch.empty((max_pad + B - 1) // B, dtype=torch.int32, device=dev)
+        nv = torch.empty(2, dtype=torch.int32, device=dev)
+        pos = torch.empty(M * TOPK, dtype=torch.int32, device=dev)
+        out = torch.empty(M, De, dtype=torch.bfloat16, device=dev)
+        ws_n = moe_op.moe_sorting_get_workspace_size(M, Ee, TOPK, 0)
+        ws = torch.empty(max(ws_n, 1), dtype=torch.uint8, device=dev)
+        a1 = torch.empty(max_pad, De, dtype=dtypes.fp8, device=dev)
+        a1s = torch.empty(De // 128, max_pad, dtype=torch.float32, device=dev)
+        a2 = torch.empty(max_pad, Ie, dtype=dtypes.fp8, device=dev)
+        a2s = torch.empty(Ie // 128, max_pad, dtype=torch.float32, device=dev)
+
+        def step():
+            moe_op.moe_sorting_fwd(tid, tw, sid, sw, seid, nv, out, Ee, B, None, None, 0, ws if ws_n else None, pos)
+            moe_op.moe_gather_quant_1x128(hid, pos, TOPK, max_pad, out=a1, out_scale=a1s)
+            moe_op.moe_stage1_fp8_blockscale(a1, a1s, w1q, w1s, sid, seid, nv, a2, a2s, M, B)
+            moe_op.moe_stage2_fp8_blockscale(a2, a2s, w2q, w2s, sid, seid, nv, sw, out, B)
+
+        ms = _time_loop(step, args.steps, args.warmup, world)
+        # the same step through the public A8W4 call (per-call MXFP4 expansion included)
+        ref = aiter.fused_moe(hid, w1p.view(dtypes.fp4x2), w2p.view(dtypes.fp4x2), tw, tid,
+                              quant_type=aiter.QuantType.per_1x32, w1_scale=w1e.view(dtypes.fp8_e8m0),
+                              w2_scale=w2e.view(dtypes.fp8_e8m0))
+        torch.cuda.synchronize()
+        assert torch.allclose(ref.float(), out.float(), rtol=2e-2, atol=2e-2)
+        active = int(torch.unique(tid).numel())
+        fl = 6.0 * M * TOPK * De * Ie
+        w_bytes = active * 3 * De * Ie * (0.5 + 1.0 / 32)
+        bytes_ = w_bytes + M * De * 2 + 2 * M * TOPK * Ie + M * De * 2 * 2
+        tfl = fl / (ms * 1e-3) / 1e12
+        gbs = bytes_ / (ms * 1e-3) / 1e9
+        rows.append({"M": M, "ms_per_step": round(ms, 4), "tokens_per_s": round(M / (ms * 1e-3), 1),
+                     "tflops": round(tfl, 2), "active_experts": active, "tensor_frac": round(tfl / fp8_peak, 4),
+                     "hbm_GBs_algorithmic": round(gbs, 1), "hbm_frac": round(gbs / pk["hbm_gbs"], 4)})
+    return {"metric": METRIC.replace("E=128", "E=256").replace("inter 1536", "inter 2048").replace(
+                "FP8 blockscale", "A8W4: fp8 activations, MXFP4 weights"),
+            "mode": "a8w4", "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "dtype": "fp8-e4m3 x (MXFP4 expanded to fp8 block-scale)",
+            "data": "synthetic", "config": {"workload": "BASELINE config 2: A8W4 fused MoE", "hidden": De,
+                                            "inter": Ie, "experts": Ee, "topk": TOPK, "routing": "zipf s=1.1 bias"},
+            "weight_prep_ms": round(prep_ms, 2),
+            "peaks": {"fp8_tflops": fp8_peak, "hbm_gbs": pk["hbm_gbs"], "source": src}, "sweep": rows}
+
+
 def run_gemm_ar(args, rank, world, local):
     """Config 4: y = allreduce(A @ B), A [M, 8192/TP], B [8192/TP, 4096] bf16 per rank:
     the tcgen05 GEMM writing into the IPC allreduce's staging buffer vs cuBLAS
@@ -542,8 +636,9 @@ def main():
     args = parse()
     rank, world, local = dist_setup(args.gpus)
     try:
-        if args.mode in ("tp_moe", "gemm_ar", "moe_sweep"):
-            res = {"tp_moe": run_tp_moe, "gemm_ar": run_gemm_ar, "moe_sweep": run_moe_sweep}[args.mode](
+        if args.mode in ("tp_moe", "gemm_ar", "moe_sweep", "a8w4"):
+            res = {"tp_moe": run_tp_moe, "gemm_ar": run_gemm_ar, "moe_sweep": run_moe_sweep,
+                   "a8w4": run_a8w4}[args.mode](
                 args, rank, world, local)
             if rank == 0:
                 print(json.dumps(res), flush=True)
