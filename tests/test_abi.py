@@ -61,3 +61,39 @@ def test_gather_quant_rejects_fp8_without_scale():
     with pytest.raises(RuntimeError, match="hidden_scale must not be None"):
         _lib.call("moe_gather_quant_1x128", torch.empty(4, 128, dtype=f8), None, torch.empty(8, dtype=torch.int32),
                   2, torch.empty(8, 128, dtype=f8), torch.empty(1, 8))
+
+
+def test_tensor_descriptor_packing():
+    """to_aiter packs the 160-byte aiter_tensor_t (aiter_tensor.h:8-18) field by field."""
+    x = torch.empty(3, 5, 7, dtype=torch.bfloat16)[:, 1:4]          # strided view
+    a = _lib.to_aiter(x)
+    assert a.ptr == x.data_ptr() and a.numel_ == x.numel() and a.ndim == 3
+    assert list(a.shape)[:3] == [3, 3, 7] and list(a.strides)[:3] == list(x.stride())
+    assert list(a.shape)[3:] == [0] * 5 and a.dtype_ == 3 and a.device_id == -1
+    e = _lib.to_aiter(torch.empty(0, 4, dtype=torch.int32))
+    assert e.ptr is None and e.numel_ == 0 and e.dtype_ == 8
+    with pytest.raises(ValueError):
+        _lib.to_aiter(torch.empty([1] * 9))
+
+
+def test_gemm_rejects_bad_shapes():
+    a = torch.empty(4, 96, dtype=torch.bfloat16)                   # K not a multiple of 64
+    w = torch.empty(256, 96, dtype=torch.bfloat16)
+    o = torch.empty(4, 256, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="K % 64"):
+        _lib.call("gemm_a16w16", a, w, o)
+    with pytest.raises(RuntimeError, match="W must be"):
+        _lib.call("gemm_a16w16", torch.empty(4, 128, dtype=torch.bfloat16), w, o)
+
+
+def test_allreduce_entries_reject_bad_context_and_world():
+    L = _lib.lib()
+    ctx = ctypes.c_int64(0)
+    handle = ctypes.create_string_buffer(64)
+    assert L.custom_ar_init(0, 9, 1 << 20, 0, ctypes.byref(ctx), handle) != 0
+    assert b"world size" in L.aiter_get_last_error()
+    x = _lib.to_aiter(torch.empty(8, dtype=torch.bfloat16))
+    assert L.custom_ar_all_reduce(0, ctypes.byref(x), ctypes.byref(x), -1, None) != 0
+    assert b"null allreduce context" in L.aiter_get_last_error()
+    assert L.custom_ar_allreduce_rmsnorm(0, *([ctypes.byref(x)] * 5), 1e-6, None, None) != 0
+    assert b"null allreduce context" in L.aiter_get_last_error()
