@@ -386,6 +386,30 @@ def run_reference(args, rank, world):
     return res
 
 
+def _graph_time(fn, K):
+    """Mean ms per call of `fn` replayed from a CUDA graph that holds K calls
+    (one process, CUDA events around the replay)."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        fn()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(K):
+            fn()
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    del g
+    return e0.elapsed_time(e1) / K
+
+
 def _time_loop(fn, K, W, world, stream=None):
     """Mean ms per call over K calls after W warm-ups, max over ranks (CUDA events)."""
     for _ in range(W):
@@ -442,9 +466,10 @@ def run_tp_moe(args, rank, world, local):
 
 def run_moe_sweep(args, rank, world, local):
     """Config 1 token sweep M in {1, 16, 128, 1024, 4096, 16384} on one GPU: device-
-    resident fused-MoE step time (sort -> gather-quant -> stage 1 -> stage 2) with
-    both roofline fractions, since small M is weight-bandwidth bound and large M
-    tensor bound.  Algorithmic bytes per step: fp8 weights (+ scales) of the experts
+    resident fused-MoE step time (sort -> gather-quant -> stage 1 -> stage 2), replayed
+    from a CUDA graph (`ms_per_step`; eager calls in `ms_per_step_eager`, which small M
+    spends in host overhead), with both roofline fractions, since small M is
+    weight-bandwidth bound and large M tensor bound.  Algorithmic bytes per step: fp8 weights (+ scales) of the experts
     the batch routes to, bf16 input, fp8 intermediate (+ scales), bf16 output and the
     output zeroing; FLOPs 6 M k D I."""
     from aiter_b200 import moe_op, dtypes
@@ -476,14 +501,15 @@ def run_moe_sweep(args, rank, world, local):
             moe_op.moe_stage1_fp8_blockscale(a1, a1s, x["w1q"], x["w1s"], sid, seid, nv, a2, a2s, M, B)
             moe_op.moe_stage2_fp8_blockscale(a2, a2s, x["w2q"], x["w2s"], sid, seid, nv, sw, out, B)
 
-        ms = _time_loop(step, args.steps, args.warmup, world)
+        ms_eager = _time_loop(step, args.steps, args.warmup, world)
+        ms = _graph_time(step, args.steps)  # what a serving engine sees: no per-call host overhead
         active = int(torch.unique(tid).numel())
         w_bytes = active * 3 * D * I + active * (3 * D * I // (128 * 128)) * 4
         bytes_ = w_bytes + M * D * 2 + 2 * M * TOPK * I + M * TOPK * (I // 128) * 4 + M * D * 2 * 2
         tfl = flops(M) / (ms * 1e-3) / 1e12
         gbs = bytes_ / (ms * 1e-3) / 1e9
-        rows.append({"M": M, "ms_per_step": round(ms, 4), "tokens_per_s": round(M / (ms * 1e-3), 1),
-                     "tflops": round(tfl, 2), "active_experts": active,
+        rows.append({"M": M, "ms_per_step": round(ms, 4), "ms_per_step_eager": round(ms_eager, 4),
+                     "tokens_per_s": round(M / (ms * 1e-3), 1), "tflops": round(tfl, 2), "active_experts": active,
                      "tensor_frac": round(tfl / fp8_peak, 4), "hbm_GBs": round(gbs, 1),
                      "hbm_frac": round(gbs / pk["hbm_gbs"], 4),
                      "bound": "hbm" if gbs / pk["hbm_gbs"] > tfl / fp8_peak else "tensor"})
