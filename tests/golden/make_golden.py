@@ -55,11 +55,15 @@ SORT_CASES = [
     ("m2000_e128_k8_b128", 2000, 128, 8, 128, None, None),
     ("mask_m64_e16_k4_b32", 64, 16, 4, 32, "mask", None),
     ("local_m80_e16_k4_b16", 80, 16, 4, 16, None, 50),
+    # config 1 at full size, and config-2 routing (Zipf(1.1)-skewed experts)
+    ("m4096_e128_k8_b128", 4096, 128, 8, 128, None, None),
+    ("zipf_m2048_e256_k8_b128", 2048, 256, 8, 128, None, None),
 ]
 
 TOPK_CASES = [
     ("m64_e8_k2", 64, 8, 2), ("m64_e128_k8", 64, 128, 8), ("m33_e256_k8", 33, 256, 8),
     ("m17_e64_k6", 17, 64, 6), ("m9_e512_k8", 9, 512, 8),
+    ("zipf_m64_e256_k8", 64, 256, 8),
 ]
 
 
@@ -71,6 +75,10 @@ def main(root):
         rng = np.random.default_rng(1000 + i)
         if name == "kat_doc":
             ids = np.array([[0, 3, 5], [2, 3, 5], [1, 3, 5], [1, 2, 3], [1, 3, 5]], dtype=np.int32)
+        elif name.startswith("zipf"):
+            # the k largest of N(0,1) + log p_e logits, p Zipf(1.1) over a random expert order
+            lg = inputs.make_logits(rng, M, E, zipf_s=1.1)
+            ids = np.argsort(-lg, axis=1, kind="stable")[:, :k].astype(np.int32)
         else:
             ids = np.stack([rng.permutation(E)[:k] for _ in range(M)]).astype(np.int32)
         w = rng.random((M, k), dtype=np.float32)
@@ -97,7 +105,8 @@ def main(root):
     # ---------------------------------------------------------------- topk softmax
     for i, (name, M, E, k) in enumerate(TOPK_CASES):
         rng = np.random.default_rng(2000 + i)
-        g = rng.standard_normal((M, E), dtype=np.float32)
+        g = inputs.make_logits(rng, M, E, zipf_s=1.1) if name.startswith("zipf") else \
+            rng.standard_normal((M, E), dtype=np.float32)
         for renorm in (True, False):
             w, ids = ref.test_nofuse(torch.from_numpy(g), k, renorm)
             p = f"topk/{name}_r{int(renorm)}/"
