@@ -136,6 +136,9 @@ def lib():
                            ("custom_ar_gemm_all_reduce", [c64, ctypes.POINTER(aiter_tensor_t),
                                                           ctypes.POINTER(aiter_tensor_t),
                                                           ctypes.POINTER(aiter_tensor_t), c64, vp]),
+                           ("custom_ar_gemm_all_reduce_fused", [c64, ctypes.POINTER(aiter_tensor_t),
+                                                                ctypes.POINTER(aiter_tensor_t),
+                                                                ctypes.POINTER(aiter_tensor_t), c64, vp]),
                            ("custom_ar_allreduce_rmsnorm", [c64] + [ctypes.POINTER(aiter_tensor_t)] * 5 +
                             [ctypes.c_float, ctypes.POINTER(aiter_tensor_t), vp]),
                            ("custom_ar_dispose", [c64]), ("custom_ar_device_error", [ctypes.c_int])):

@@ -30,83 +30,15 @@
 #include <mutex>
 #include <vector>
 
-#include "common.cuh"
+#include "gemm_bf16.cuh"
 
 namespace {
 
-constexpr int kMaxRanks = 8;
-constexpr int kMaxBlocks = 128;
+using namespace ipc;
+
+constexpr int kMaxBlocks = 128;  // grid cap of the allreduce kernels
 constexpr int kThreads = 512;
-constexpr size_t kSignalBytes = (3 * kMaxBlocks * kMaxRanks + kMaxBlocks) * sizeof(uint32_t);
-constexpr size_t kSignalPad = 64 * 1024;
-
-static __device__ int g_ar_error;
-
-struct Signal {
-    uint32_t flag[3][kMaxBlocks][kMaxRanks];  // [start | mid (two-shot) | end (captured)]
-    uint32_t counter[kMaxBlocks];            // own calls per CTA index (never read by peers)
-};
-static_assert(sizeof(Signal) == kSignalBytes, "signal layout");
-
-struct Peers {
-    Signal* sig[kMaxRanks];       // every rank's signal block
-    uint8_t* buf[2][kMaxRanks];   // every rank's staging buffers
-};
-
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ uint4 ld_cg(const void* p) {
-    uint4 v;
-    asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
-    return v;
-}
-
-// Returns false (and sets the error word) when a peer did not arrive in time.
-__device__ bool block_barrier(const Peers& P, int rank, int world, int phase, uint32_t epoch) {
-    __syncthreads();
-    bool ok = true;
-    if (threadIdx.x < world) {
-        // publish: everything this CTA wrote before is visible to peers first
-        __threadfence_system();
-        st_release_sys(&P.sig[threadIdx.x]->flag[phase][blockIdx.x][rank], epoch);
-        const uint32_t* mine = &P.sig[rank]->flag[phase][blockIdx.x][threadIdx.x];
-        const uint64_t t0 = abd::globaltimer_ns();
-        uint32_t n = 0;
-        // >=, not ==: a fast peer may already have moved on to its next call
-        while ((int32_t)(ld_acquire_sys(mine) - epoch) < 0) {
-            if ((++n & 255) == 0 && abd::globaltimer_ns() - t0 > 2000000000ull) {
-                atomicExch(&g_ar_error, 1);
-                ok = false;
-                break;
-            }
-        }
-    }
-    return __syncthreads_and(ok ? 1 : 0) != 0;
-}
-
-__device__ __forceinline__ void acc8(float (&a)[8], uint4 v) {
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        float2 f = __bfloat1622float2(h[i]);
-        a[2 * i] += f.x;
-        a[2 * i + 1] += f.y;
-    }
-}
-
-__device__ __forceinline__ uint4 pack8(const float (&a)[8]) {
-    uint4 v;
-    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&v);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(a[2 * i], a[2 * i + 1]);
-    return v;
-}
+static_assert(kMaxBlocks <= kFlagBlocks, "allreduce CTAs need their own flags");
 
 // n16: number of 16-byte packs (8 bf16).  `in` may equal the staging buffer
 // (zero-copy producers), then the copy is skipped.  W (the world size) is a
@@ -480,14 +412,18 @@ AB_ENTRY(custom_ar_dispose, (int64_t ctx), (ctx)) {
     delete c;
 }
 
+// Error word of the allreduce context: peer waits of every IPC kernel, folded with
+// the mbarrier waits of the fused GEMM + allreduce kernels (this unit's copy).
 extern "C" int custom_ar_device_error(int clear) {
-    int v = 0;
+    int v = 0, m = 0;
     if (cudaMemcpyFromSymbol(&v, g_ar_error, sizeof(int)) != cudaSuccess) return -1;
+    if (cudaMemcpyFromSymbol(&m, sm100::g_device_error, sizeof(int)) != cudaSuccess) return -1;
     if (clear) {
         int z = 0;
         cudaMemcpyToSymbol(g_ar_error, &z, sizeof(int));
+        cudaMemcpyToSymbol(sm100::g_device_error, &z, sizeof(int));
     }
-    return v;
+    return v ? v : m;
 }
 
 // GEMM + allreduce: y = allreduce_over_ranks(A @ W^T).  The bf16 GEMM writes its
@@ -591,4 +527,75 @@ AB_ENTRY(custom_ar_allreduce_rmsnorm,
     }
 #undef AB_ARRMS
     check_launch("custom_ar_allreduce_rmsnorm");
+}
+
+// GEMM + allreduce in one kernel: y = allreduce_over_ranks(A @ W^T) with the GEMM
+// pushing its output over NVLink into the peers' staging buffers while its MMAs run
+// (gemm_bf16.cuh): one-shot (every rank gets every rank's rows, then sums them) for
+// small messages, two-shot (owner rank sums each piece, every rank pulls it) above
+// the same size cut-over as custom_ar_all_reduce.  Same result bits as
+// custom_ar_gemm_all_reduce.  Falls back to that two-kernel path when the pushed
+// images do not fit one staging buffer or the grid exceeds the per-CTA flags.
+AB_ENTRY(custom_ar_gemm_all_reduce_fused,
+         (int64_t ctx, aiter_tensor_t* a, aiter_tensor_t* w, aiter_tensor_t* out, int64_t force_two_shot,
+          void* stream),
+         (ctx, a, w, out, force_two_shot, stream)) {
+    using namespace ab;
+    Ctx* c = as_ctx(ctx);
+    AB_CHECK(c->ready, "custom_ar_open_peers has not been called");
+    need(a, "A");
+    need(w, "W");
+    need(out, "out");
+    need_dtype(a, AITER_DTYPE_bf16, "A");
+    need_dtype(w, AITER_DTYPE_bf16, "W");
+    need_dtype(out, AITER_DTYPE_bf16, "out");
+    need_ndim(a, 2, "A");
+    need_ndim(w, 2, "W");
+    need_contig(a, "A");
+    need_contig(w, "W");
+    const int64_t M = a->shape[0], K = a->shape[1], N = w->shape[0];
+    AB_CHECK(w->shape[1] == K, "W must be [N, K] with the K of A");
+    AB_CHECK(out->ndim == 2 && out->shape[0] == M && out->shape[1] == N && out->strides[1] == 1,
+             "out must be [M, N] with contiguous rows");
+    AB_CHECK(K % g16::BK == 0 && N % 32 == 0, "need K % 64 == 0 and N % 32 == 0");
+    AB_CHECK(out->strides[0] % 8 == 0 && ((uintptr_t)out->ptr & 15) == 0, "out rows must be 16-byte aligned");
+    AB_CHECK(a->device_id == c->device && w->device_id == c->device && out->device_id == c->device,
+             "tensor on a different device than the communicator");
+    const int64_t n_bytes = M * N * 2;
+    AB_CHECK(n_bytes <= (int64_t)c->max_bytes, "GEMM output of ", n_bytes, " bytes exceeds the registered ",
+             c->max_bytes);
+    if (M == 0) return;
+    const int sms = num_sms(c->device);
+    int mode = g16::kTwoShot;
+    int64_t slot = 0;
+    bool eligible = false;
+    if (M <= g16::kSwabMaxM && N % 128 == 0) {
+        const int grid = g16::swab_grid((int)M, (int)N, (int)(K / g16::BK), sms);
+        const int64_t one_shot_max = c->world == 2 ? INT64_MAX : (c->world <= 4 ? (2 << 20) : (1 << 20));
+        const bool two = force_two_shot > 0 ? true : (force_two_shot == 0 ? false : n_bytes > one_shot_max);
+        mode = two ? g16::kTwoShot : g16::kOneShot;
+        slot = n_bytes;  // every slot is an [M, N] image
+        eligible = grid <= kFlagBlocks && (int64_t)c->world * slot <= (int64_t)c->max_bytes;
+    } else {
+        int tiles = 0;
+        slot = g16::twoshot_slot_bytes((int)M, (int)N, c->world, sms, &tiles);
+        eligible = force_two_shot != 0 && std::min(tiles, sms) <= kFlagBlocks &&
+                   (int64_t)c->world * slot <= (int64_t)c->max_bytes;
+    }
+    if (!eligible) {
+        custom_ar_gemm_all_reduce_impl(ctx, a, w, out, force_two_shot, stream);
+        return;
+    }
+    DeviceGuard dg(c->device);
+    cudaStream_t st = as_stream(stream);
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    AB_CUDA(cudaStreamIsCapturing(st, &cap));
+    c->epoch += 1;
+    g16::FuseArgs F{c->peers, c->rank, c->world, (int)(c->epoch & 1),
+                    cap == cudaStreamCaptureStatusNone ? 0 : 1, slot};
+    if (mode == g16::kOneShot)
+        g16::run<g16::kOneShot>(a, w, (__nv_bfloat16*)out->ptr, out->strides[0], F, c->device, st);
+    else
+        g16::run<g16::kTwoShot>(a, w, (__nv_bfloat16*)out->ptr, out->strides[0], F, c->device, st);
+    check_launch("custom_ar_gemm_all_reduce_fused");
 }

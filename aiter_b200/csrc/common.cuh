@@ -142,6 +142,9 @@ int num_sms(int dev);
 // earlier one on that device.
 void set_max_smem_once(const void* kernel, int bytes, int dev);
 
+// Error word of the mbarrier waits in the bf16 GEMM unit (0 = none, -1 = read failed).
+int gemm_bf16_device_error(int clear);
+
 }  // namespace ab
 
 // ----------------------------------------------------------------- device side

@@ -613,6 +613,8 @@ AB_ENTRY(moe_stage2_fp8_blockscale,
     launch<2, 256>(tmA, tmB, tmA, a, a2->device_id, as_stream(stream));
 }
 
+// Error word of every mbarrier wait outside the allreduce context: this unit's
+// (the grouped GEMMs) folded with the bf16 GEMM unit's.
 extern "C" int aiter_device_error(int clear) {
     int v = 0;
     if (cudaMemcpyFromSymbol(&v, sm100::g_device_error, sizeof(int)) != cudaSuccess) return -1;
@@ -620,5 +622,7 @@ extern "C" int aiter_device_error(int clear) {
         int z = 0;
         cudaMemcpyToSymbol(sm100::g_device_error, &z, sizeof(int));
     }
-    return v;
+    const int g = ab::gemm_bf16_device_error(clear);
+    if (g < 0) return -1;
+    return v ? v : g;
 }

@@ -10,11 +10,12 @@ def tensor_model_parallel_all_reduce(input_: torch.Tensor, use_new: bool = True,
     return get_tp_group().all_reduce(input_, use_new, open_fp8_quant, prefill_support)
 
 
-def tensor_model_parallel_gemm_all_reduce(a: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+def tensor_model_parallel_gemm_all_reduce(a: torch.Tensor, w: torch.Tensor, fused: bool = False) -> torch.Tensor:
     """allreduce(a @ w^T) over the TP group, GEMM and allreduce sharing the IPC
-    staging buffer.  Equals tensor_model_parallel_all_reduce(tgemm.mm(a, w)); the
-    reference has no fused entry, this one is new."""
-    return get_tp_group().gemm_all_reduce(a, w)
+    staging buffer (`fused=True`: one kernel, the GEMM pushing its tiles to the
+    peers).  Equals tensor_model_parallel_all_reduce(tgemm.mm(a, w)); the reference
+    has no fused entry, this one is new."""
+    return get_tp_group().gemm_all_reduce(a, w, fused=fused)
 
 
 def shard_moe_weights_for_tp(w1, w1_scale, w2, w2_scale, rank, tp, chunk=8):

@@ -114,17 +114,21 @@ class CustomAllreduce:
             return None
         return self.all_reduce(input)
 
-    def gemm_all_reduce(self, a: torch.Tensor, w: torch.Tensor, out: torch.Tensor = None, two_shot=None):
-        """allreduce(a @ w^T) with the GEMM writing into the staging buffer."""
+    def gemm_all_reduce(self, a: torch.Tensor, w: torch.Tensor, out: torch.Tensor = None, two_shot=None,
+                        fused: bool = False):
+        """allreduce(a @ w^T).  Default: the GEMM writes into the staging buffer and
+        the allreduce kernel reduces it (two launches, no copy).  `fused=True`: one
+        kernel whose GEMM epilogue pushes its tiles to the peers over NVLink while the
+        MMAs of the next tiles run, then sums them (same result bits)."""
         if out is None:
             out = torch.empty((a.shape[0], w.shape[0]), dtype=torch.bfloat16, device=a.device)
         force = -1 if two_shot is None else (1 if two_shot else 0)
         ta, tw, to = _lib.to_aiter(a), _lib.to_aiter(w), _lib.to_aiter(out)
         st = _lib.current_stream_ptr(self.device.index)
-        ret = self._L.custom_ar_gemm_all_reduce(self._ctx, ctypes.byref(ta), ctypes.byref(tw), ctypes.byref(to),
-                                                force, st)
+        name = "custom_ar_gemm_all_reduce_fused" if fused else "custom_ar_gemm_all_reduce"
+        ret = getattr(self._L, name)(self._ctx, ctypes.byref(ta), ctypes.byref(tw), ctypes.byref(to), force, st)
         if ret:
-            _lib.check_status("custom_ar_gemm_all_reduce", ret)
+            _lib.check_status(name, ret)
         return out
 
     def fused_ar_rms(self, inp: torch.Tensor, res_inp: torch.Tensor, *, res_out: torch.Tensor = None,

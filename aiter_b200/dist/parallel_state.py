@@ -92,13 +92,13 @@ class GroupCoordinator:
                 return r
         return _rmsnorm_after(self.all_reduce(input_), residual_inp_, weight_, eps, quant=True)
 
-    def gemm_all_reduce(self, a: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    def gemm_all_reduce(self, a: torch.Tensor, w: torch.Tensor, fused: bool = False) -> torch.Tensor:
         if self.world_size == 1:
             from ..gemm import gemm_a16w16
             return gemm_a16w16(a, w)
         if self.ca_comm is None or self.ca_comm.disabled:
             raise RuntimeError("GEMM + allreduce needs the custom allreduce (world sizes 2, 4, 6, 8)")
-        return self.ca_comm.gemm_all_reduce(a, w)
+        return self.ca_comm.gemm_all_reduce(a, w, fused=fused)
 
     @contextlib.contextmanager
     def graph_capture(self, graph_capture_context: Optional["GraphCaptureContext"] = None):

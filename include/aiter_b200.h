@@ -232,7 +232,8 @@ int custom_ar_open_loopback(int64_t ctx);
 int custom_ar_next_buffer(int64_t ctx, int64_t* ptr_out, int64_t* bytes_out);
 /* out = sum over ranks of inp (bf16, accumulated in fp32 in rank order, identical
  * bits on every rank).  force_two_shot: 1 = two-shot (reduce-scatter + all-gather
- * over peer memory), 0 = one-shot, negative = one-shot up to 256 KiB, else two-shot. */
+ * over peer memory), 0 = one-shot, negative = by size (one-shot always at 2 ranks, up to
+ * 2 MiB at 3-4 ranks, up to 1 MiB above). */
 int custom_ar_all_reduce(int64_t ctx, aiter_tensor_t* inp, aiter_tensor_t* out, int64_t force_two_shot,
                          void* stream);
 /* GEMM + allreduce, out = allreduce(A @ W^T): the GEMM epilogue writes into the
@@ -241,6 +242,16 @@ int custom_ar_all_reduce(int64_t ctx, aiter_tensor_t* inp, aiter_tensor_t* out, 
  * tensor_model_parallel_all_reduce, aiter/dist/communication_op.py:30-37). */
 int custom_ar_gemm_all_reduce(int64_t ctx, aiter_tensor_t* a, aiter_tensor_t* w, aiter_tensor_t* out,
                               int64_t force_two_shot, void* stream);
+/* The same GEMM + allreduce as one kernel: the GEMM epilogue pushes its output tiles
+ * over NVLink into the peers' staging buffers while later tiles are multiplied
+ * (one-shot: to every rank, which then sums all images; two-shot: to the tile's
+ * owner rank, which sums and publishes it for every rank to pull).  Same result
+ * bits as custom_ar_gemm_all_reduce, which it falls back to when the pushed images
+ * do not fit one staging buffer.  Replaces, with custom_ar_gemm_all_reduce, the
+ * reference's tgemm.mm + tensor_model_parallel_all_reduce pair
+ * (aiter/tuned_gemm.py:506-529, aiter/dist/communication_op.py:30-37). */
+int custom_ar_gemm_all_reduce_fused(int64_t ctx, aiter_tensor_t* a, aiter_tensor_t* w, aiter_tensor_t* out,
+                                    int64_t force_two_shot, void* stream);
 /* Allreduce fused with the residual add and RMSNorm that follow it: res_out =
  * bf16(allreduce(inp) + res_inp), out = bf16(res * weight * rsqrt(mean(res^2) + eps))
  * row by row over the last dimension (hidden <= 16384).  With scale_out given
