@@ -133,6 +133,8 @@ def lib():
                            ("custom_ar_next_buffer", [c64, p64, p64]),
                            ("custom_ar_all_reduce", [c64, ctypes.POINTER(aiter_tensor_t),
                                                      ctypes.POINTER(aiter_tensor_t), c64, vp]),
+                           ("custom_ar_all_reduce_fp8", [c64, ctypes.POINTER(aiter_tensor_t),
+                                                         ctypes.POINTER(aiter_tensor_t), vp]),
                            ("custom_ar_gemm_all_reduce", [c64, ctypes.POINTER(aiter_tensor_t),
                                                           ctypes.POINTER(aiter_tensor_t),
                                                           ctypes.POINTER(aiter_tensor_t), c64, vp]),

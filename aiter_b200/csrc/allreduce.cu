@@ -40,13 +40,54 @@ constexpr int kMaxBlocks = 128;  // grid cap of the allreduce kernels
 constexpr int kThreads = 512;
 static_assert(kMaxBlocks <= kFlagBlocks, "allreduce CTAs need their own flags");
 
-// n16: number of 16-byte packs (8 bf16).  `in` may equal the staging buffer
+// 16-byte packs of each element type: bf16 and fp16 carry 8 values, fp32 4; sums
+// accumulate in fp32 and round once to the element type.
+template <typename T>
+struct Elem;
+template <>
+struct Elem<__nv_bfloat16> {
+    __device__ static void acc(float (&a)[8], uint4 v) { acc8(a, v); }
+    __device__ static uint4 pack(const float (&a)[8]) { return pack8(a); }
+};
+template <>
+struct Elem<__half> {
+    __device__ static void acc(float (&a)[8], uint4 v) {
+        const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(h[i]);
+            a[2 * i] += f.x;
+            a[2 * i + 1] += f.y;
+        }
+    }
+    __device__ static uint4 pack(const float (&a)[8]) {
+        uint4 v;
+        __half2* h = reinterpret_cast<__half2*>(&v);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(a[2 * i], a[2 * i + 1]);
+        return v;
+    }
+};
+template <>
+struct Elem<float> {
+    __device__ static void acc(float (&a)[8], uint4 v) {
+        a[0] += __uint_as_float(v.x);
+        a[1] += __uint_as_float(v.y);
+        a[2] += __uint_as_float(v.z);
+        a[3] += __uint_as_float(v.w);
+    }
+    __device__ static uint4 pack(const float (&a)[8]) {
+        return make_uint4(__float_as_uint(a[0]), __float_as_uint(a[1]), __float_as_uint(a[2]), __float_as_uint(a[3]));
+    }
+};
+
+// n16: number of 16-byte packs (8 bf16 / fp16, 4 fp32).  `in` may equal the staging buffer
 // (zero-copy producers), then the copy is skipped.  W (the world size) is a
 // template parameter so that the peer loops unroll and every thread keeps
 // U * W independent 16-byte loads in flight (U packs per thread per step).
-template <int W>
+template <typename T, int W>
 __global__ void __launch_bounds__(kThreads)
-allreduce_bf16_kernel(Peers P, int rank, int parity, const uint4* __restrict__ in, uint4* __restrict__ out,
+allreduce_kernel(Peers P, int rank, int parity, const uint4* __restrict__ in, uint4* __restrict__ out,
                       int64_t n16, int two_shot, int end_barrier) {
     __shared__ uint32_t s_epoch;
     if (threadIdx.x == 0) {
@@ -98,8 +139,8 @@ allreduce_bf16_kernel(Peers P, int rank, int parity, const uint4* __restrict__ i
                 if (i + u * stride < hi) {
                     float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
-                    for (int p = 0; p < W; ++p) acc8(a, v[u][p]);
-                    dst[i + u * stride] = pack8(a);
+                    for (int p = 0; p < W; ++p) Elem<T>::acc(a, v[u][p]);
+                    dst[i + u * stride] = Elem<T>::pack(a);
                 }
             }
         }
@@ -127,6 +168,107 @@ allreduce_bf16_kernel(Peers P, int rank, int parity, const uint4* __restrict__ i
 #pragma unroll
             for (int u = 0; u < 8; ++u)
                 if (i + u * stride < hi) out[i + u * stride] = v[u];
+        }
+    }
+    if (end_barrier) block_barrier(P, rank, W, 2, epoch);
+}
+
+// ---------------------------------------------------------------------------
+// fp8-quantised two-shot allreduce of fp16 data: the reference's allReduceQuantFp8
+// (csrc/include/custom_all_reduce.cuh:1018-1088), used with open_fp8_quant for fp16
+// messages of at least 128 * 2048 elements (csrc/kernels/custom_all_reduce.cu:90-96).
+// The n8 packs (8 halves) are cut into W segments of n8 / W packs, the last rank
+// taking the remainder.  Owner rank r sums segment r over the ranks in the rotated
+// order r, r+1, ..., r-1 in fp32, rounds to fp16 and writes that to its own output;
+// then it quantises the sum in groups of G = 8 * gp elements aligned to the segment
+// start, scale = fp16(amax / 448), code = e4m3(x / scale) (a zero scale gives zero
+// codes; the reference would produce NaN), into its staging buffer after the input
+// (codes at q_off, fp16 scales at s_off).  After a barrier every rank decodes the
+// other segments, fp16(code * scale).  Only the all-gather half moves fp8 (half the
+// bytes); each rank's own segment is exact, the others carry the fp8 rounding.
+// Pack i of segment s is handled by thread (i - lo_s) mod stride on every rank, so
+// a CTA reads only what the same CTA index of each peer wrote before the barrier;
+// the gp lanes of a group are consecutive lanes of one warp.
+template <int W>
+__global__ void __launch_bounds__(kThreads)
+allreduce_fp8q_kernel(Peers P, int rank, int parity, const uint4* __restrict__ in, uint4* __restrict__ out,
+                      int64_t n8, int gp, int64_t q_off, int64_t s_off, int end_barrier) {
+    __shared__ uint32_t s_epoch;
+    if (threadIdx.x == 0) s_epoch = next_epoch(P, rank);
+    __syncthreads();
+    const uint32_t epoch = s_epoch;
+    uint4* mine = reinterpret_cast<uint4*>(P.buf[parity][rank]);
+    const int lane = threadIdx.x & 31;
+    const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t part = n8 / W;
+    auto seg_lo = [&](int s) -> int64_t { return (int64_t)s * part; };
+    auto seg_hi = [&](int s) -> int64_t { return s == W - 1 ? n8 : (int64_t)(s + 1) * part; };
+    if (in != mine)
+        for (int s = 0; s < W; ++s)
+            for (int64_t i = seg_lo(s) + tid; i < seg_hi(s); i += stride) mine[i] = in[i];
+    if (!block_barrier(P, rank, W, 0, epoch)) return;
+    {
+        const int64_t lo = seg_lo(rank), hi = seg_hi(rank);
+        uint8_t* qbase = P.buf[parity][rank] + q_off;
+        __half* sbase = reinterpret_cast<__half*>(P.buf[parity][rank] + s_off);
+        // warp-uniform trip count: every lane takes part in the group shuffles
+        for (int64_t i0 = lo + tid - lane; i0 < hi; i0 += stride) {
+            const int64_t i = i0 + lane;
+            const bool active = i < hi;
+            float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            if (active) {
+#pragma unroll
+                for (int j = 0; j < W; ++j)
+                    Elem<__half>::acc(a, ld_cg(reinterpret_cast<const uint4*>(P.buf[parity][(rank + j) % W]) + i));
+            }
+            const uint4 h = Elem<__half>::pack(a);
+            const __half* hv = reinterpret_cast<const __half*>(&h);
+            float amax = 0.f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(__half2float(hv[e])));
+            for (int o = gp >> 1; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            const __half sh = __float2half_rn(amax / 448.0f);
+            const float sf = __half2float(sh);
+            if (active) {
+                out[i] = h;
+                uint32_t q[2];
+#pragma unroll
+                for (int k = 0; k < 2; ++k) {
+                    float4 f;
+                    f.x = sf == 0.f ? 0.f : __half2float(hv[4 * k]) / sf;
+                    f.y = sf == 0.f ? 0.f : __half2float(hv[4 * k + 1]) / sf;
+                    f.z = sf == 0.f ? 0.f : __half2float(hv[4 * k + 2]) / sf;
+                    f.w = sf == 0.f ? 0.f : __half2float(hv[4 * k + 3]) / sf;
+                    __nv_fp8x4_e4m3 f4(f);
+                    q[k] = *reinterpret_cast<uint32_t*>(&f4);
+                }
+                *reinterpret_cast<uint2*>(qbase + (i - lo) * 8) = make_uint2(q[0], q[1]);
+                if ((i - lo) % gp == 0) sbase[(i - lo) / gp] = sh;
+            }
+        }
+    }
+    if (!block_barrier(P, rank, W, 1, epoch)) return;
+    for (int d = 1; d < W; ++d) {
+        const int s = (rank + d) % W;
+        const int64_t lo = seg_lo(s), hi = seg_hi(s);
+        const uint8_t* qsrc = P.buf[parity][s] + q_off;
+        const uint8_t* ssrc = P.buf[parity][s] + s_off;
+        for (int64_t i = lo + tid; i < hi; i += stride) {
+            const uint2 qv = ld_cg8(qsrc + (i - lo) * 8);
+            const unsigned short sb = *reinterpret_cast<const volatile unsigned short*>(ssrc + ((i - lo) / gp) * 2);
+            const float sf = __half2float(__ushort_as_half(sb));
+            const __nv_fp8x4_e4m3* q4 = reinterpret_cast<const __nv_fp8x4_e4m3*>(&qv);
+            float a[8];
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                const float4 f = static_cast<float4>(q4[k]);
+                a[4 * k] = f.x * sf;
+                a[4 * k + 1] = f.y * sf;
+                a[4 * k + 2] = f.z * sf;
+                a[4 * k + 3] = f.w * sf;
+            }
+            out[i] = Elem<__half>::pack(a);
         }
     }
     if (end_barrier) block_barrier(P, rank, W, 2, epoch);
@@ -358,12 +500,13 @@ AB_ENTRY(custom_ar_all_reduce,
     AB_CHECK(c->ready, "custom_ar_open_peers has not been called");
     need(inp, "inp");
     need(out, "out");
-    need_dtype(inp, AITER_DTYPE_bf16, "inp");
-    need_dtype(out, AITER_DTYPE_bf16, "out");
+    AB_CHECK(inp->dtype_ == AITER_DTYPE_bf16 || inp->dtype_ == AITER_DTYPE_fp16 || inp->dtype_ == AITER_DTYPE_fp32,
+             "allreduce supports bf16, fp16 and fp32, got ", dtype_name(inp->dtype_));
+    need_dtype(out, inp->dtype_, "out");
     need_contig(inp, "inp");
     need_contig(out, "out");
     AB_CHECK(inp->numel_ == out->numel_, "inp and out sizes differ");
-    const size_t bytes = inp->numel_ * 2;
+    const size_t bytes = inp->numel_ * elem_size(inp->dtype_);
     AB_CHECK(bytes % 16 == 0, "allreduce size must be a multiple of 16 bytes");
     AB_CHECK(bytes <= c->max_bytes, "allreduce of ", bytes, " bytes exceeds the registered ", c->max_bytes);
     AB_CHECK(((uintptr_t)inp->ptr & 15) == 0 && ((uintptr_t)out->ptr & 15) == 0, "buffers must be 16-byte aligned");
@@ -389,16 +532,85 @@ AB_ENTRY(custom_ar_all_reduce,
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
     AB_CUDA(cudaStreamIsCapturing(st, &cap));
     const int endb = cap == cudaStreamCaptureStatusNone ? 0 : 1;  // captured: buffers are reused per replay
-    switch (c->world) {
-        case 2: allreduce_bf16_kernel<2><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, tw, endb); break;
-        case 3: allreduce_bf16_kernel<3><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, tw, endb); break;
-        case 4: allreduce_bf16_kernel<4><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, tw, endb); break;
-        case 5: allreduce_bf16_kernel<5><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, tw, endb); break;
-        case 6: allreduce_bf16_kernel<6><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, tw, endb); break;
-        case 7: allreduce_bf16_kernel<7><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, tw, endb); break;
-        default: allreduce_bf16_kernel<8><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, tw, endb); break;
+#define AB_AR(TT)                                                                                               \
+    switch (c->world) {                                                                                         \
+        case 2: allreduce_kernel<TT, 2><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, tw, endb); break; \
+        case 3: allreduce_kernel<TT, 3><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, tw, endb); break; \
+        case 4: allreduce_kernel<TT, 4><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, tw, endb); break; \
+        case 5: allreduce_kernel<TT, 5><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, tw, endb); break; \
+        case 6: allreduce_kernel<TT, 6><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, tw, endb); break; \
+        case 7: allreduce_kernel<TT, 7><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, tw, endb); break; \
+        default: allreduce_kernel<TT, 8><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, tw, endb); break; \
     }
+    if (inp->dtype_ == AITER_DTYPE_bf16) {
+        AB_AR(__nv_bfloat16)
+    } else if (inp->dtype_ == AITER_DTYPE_fp16) {
+        AB_AR(__half)
+    } else {
+        AB_AR(float)
+    }
+#undef AB_AR
     check_launch("custom_ar_all_reduce");
+}
+
+// allreduce with open_fp8_quant (the reference's all_reduce(..., open_fp8_quant=True),
+// csrc/kernels/custom_all_reduce.cu:76-115): fp16 messages of at least 128 * 2048
+// elements take the fp8-quantised two-shot kernel; every other message, and one whose
+// codes and scales do not fit the staging buffer after the input, the plain
+// allreduce (bf16 ignores the flag in the reference too).
+AB_ENTRY(custom_ar_all_reduce_fp8, (int64_t ctx, aiter_tensor_t* inp, aiter_tensor_t* out, void* stream),
+         (ctx, inp, out, stream)) {
+    using namespace ab;
+    Ctx* c = as_ctx(ctx);
+    AB_CHECK(c->ready, "custom_ar_open_peers has not been called");
+    need(inp, "inp");
+    need(out, "out");
+    const int64_t numel = (int64_t)inp->numel_;
+    const int64_t n8 = numel / 8;
+    int gp = 1;  // packs per quant group: the largest of 16, 8, 4, 2 dividing numel / W / 8
+    for (int g : {16, 8, 4, 2})
+        if ((numel / c->world) % (8 * g) == 0) {
+            gp = g;
+            break;
+        }
+    const int64_t largest = n8 / c->world + n8 % c->world;
+    const int64_t q_off = (numel * 2 + 255) / 256 * 256;
+    const int64_t s_off = q_off + (largest * 8 + 255) / 256 * 256;
+    const int64_t need_bytes = s_off + (largest / gp + 1) * 2;
+    const bool quant = inp->dtype_ == AITER_DTYPE_fp16 && numel >= 128 * 2048 && numel % 8 == 0 &&
+                       need_bytes <= (int64_t)c->max_bytes;
+    if (!quant) {
+        custom_ar_all_reduce_impl(ctx, inp, out, -1, stream);
+        return;
+    }
+    need_dtype(out, AITER_DTYPE_fp16, "out");
+    need_contig(inp, "inp");
+    need_contig(out, "out");
+    AB_CHECK(inp->numel_ == out->numel_, "inp and out sizes differ");
+    AB_CHECK(((uintptr_t)inp->ptr & 15) == 0 && ((uintptr_t)out->ptr & 15) == 0, "buffers must be 16-byte aligned");
+    AB_CHECK(inp->device_id == c->device, "tensor on a different device than the communicator");
+    DeviceGuard dg(c->device);
+    c->epoch += 1;
+    const int parity = (int)(c->epoch & 1);
+    const int64_t per_block = (int64_t)kThreads * 2;
+    int grid = (int)std::min<int64_t>((n8 + per_block - 1) / per_block, std::min(kMaxBlocks, num_sms(c->device)));
+    grid = std::max(grid, 1);
+    cudaStream_t st = as_stream(stream);
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    AB_CUDA(cudaStreamIsCapturing(st, &cap));
+    const int endb = cap == cudaStreamCaptureStatusNone ? 0 : 1;
+    const uint4* src = (const uint4*)inp->ptr;
+    uint4* dst = (uint4*)out->ptr;
+    switch (c->world) {
+        case 2: allreduce_fp8q_kernel<2><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n8, gp, q_off, s_off, endb); break;
+        case 3: allreduce_fp8q_kernel<3><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n8, gp, q_off, s_off, endb); break;
+        case 4: allreduce_fp8q_kernel<4><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n8, gp, q_off, s_off, endb); break;
+        case 5: allreduce_fp8q_kernel<5><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n8, gp, q_off, s_off, endb); break;
+        case 6: allreduce_fp8q_kernel<6><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n8, gp, q_off, s_off, endb); break;
+        case 7: allreduce_fp8q_kernel<7><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n8, gp, q_off, s_off, endb); break;
+        default: allreduce_fp8q_kernel<8><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n8, gp, q_off, s_off, endb); break;
+    }
+    check_launch("custom_ar_all_reduce_fp8");
 }
 
 AB_ENTRY(custom_ar_dispose, (int64_t ctx), (ctx)) {

@@ -89,30 +89,44 @@ class CustomAllreduce:
     def is_capturing(self) -> bool:
         return self._IS_CAPTURING
 
+    _DTYPES = (torch.bfloat16, torch.float16, torch.float32)
+
     def should_custom_ar(self, inp: torch.Tensor) -> bool:
-        """Eligibility (custom_all_reduce.py:423-437): bf16, contiguous, 16-byte
-        multiple, at most the registered size."""
+        """Eligibility (custom_all_reduce.py:423-437): bf16, fp16 or fp32, contiguous,
+        16-byte multiple, at most the registered size."""
         if self.disabled:
             return False
         nbytes = inp.numel() * inp.element_size()
-        return (inp.dtype == torch.bfloat16 and inp.is_contiguous() and nbytes % 16 == 0
+        return (inp.dtype in self._DTYPES and inp.is_contiguous() and nbytes % 16 == 0
                 and nbytes <= self.max_size and inp.device == self.device)
 
-    def all_reduce(self, inp: torch.Tensor, *, out: torch.Tensor = None, two_shot=None) -> torch.Tensor:
+    def all_reduce(self, inp: torch.Tensor, *, out: torch.Tensor = None, two_shot=None,
+                   open_fp8_quant: bool = False) -> torch.Tensor:
+        """out = sum over ranks of inp, accumulated in fp32 in rank order (identical
+        bits on every rank).  `open_fp8_quant` (custom_all_reduce.py:453-482): fp16
+        messages of at least 128 * 2048 elements take the two-shot allreduce whose
+        all-gather half moves fp8 codes with one fp16 scale per group, as the
+        reference does; each rank's own segment is then exact and the others carry
+        the fp8 rounding.  Other messages ignore the flag."""
         if out is None:
             out = torch.empty_like(inp)
-        force = -1 if two_shot is None else (1 if two_shot else 0)
         a, b = _lib.to_aiter(inp), _lib.to_aiter(out)
         st = _lib.current_stream_ptr(self.device.index)
-        ret = self._L.custom_ar_all_reduce(self._ctx, ctypes.byref(a), ctypes.byref(b), force, st)
+        if open_fp8_quant:
+            ret = self._L.custom_ar_all_reduce_fp8(self._ctx, ctypes.byref(a), ctypes.byref(b), st)
+            name = "custom_ar_all_reduce_fp8"
+        else:
+            force = -1 if two_shot is None else (1 if two_shot else 0)
+            ret = self._L.custom_ar_all_reduce(self._ctx, ctypes.byref(a), ctypes.byref(b), force, st)
+            name = "custom_ar_all_reduce"
         if ret:
-            _lib.check_status("custom_ar_all_reduce", ret)
+            _lib.check_status(name, ret)
         return out
 
-    def custom_all_reduce(self, input: torch.Tensor):
+    def custom_all_reduce(self, input: torch.Tensor, use_new: bool = True, open_fp8_quant: bool = False):
         if self.disabled or not self.should_custom_ar(input):
             return None
-        return self.all_reduce(input)
+        return self.all_reduce(input, open_fp8_quant=open_fp8_quant)
 
     def gemm_all_reduce(self, a: torch.Tensor, w: torch.Tensor, out: torch.Tensor = None, two_shot=None,
                         fused: bool = False):

@@ -63,7 +63,7 @@ class GroupCoordinator:
         if self.world_size == 1:
             return input_
         if self.ca_comm is not None and not self.ca_comm.disabled:
-            out = self.ca_comm.custom_all_reduce(input_)
+            out = self.ca_comm.custom_all_reduce(input_, use_new, open_fp8_quant)
             if out is not None:
                 return out
         out = input_.clone()

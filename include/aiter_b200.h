@@ -230,12 +230,19 @@ int custom_ar_open_loopback(int64_t ctx);
 /* Staging buffer the next all_reduce will use: a producer that writes its bf16
  * result there and passes it as `inp` skips the input copy. */
 int custom_ar_next_buffer(int64_t ctx, int64_t* ptr_out, int64_t* bytes_out);
-/* out = sum over ranks of inp (bf16, accumulated in fp32 in rank order, identical
+/* out = sum over ranks of inp (bf16, fp16 or fp32, accumulated in fp32 in rank order, identical
  * bits on every rank).  force_two_shot: 1 = two-shot (reduce-scatter + all-gather
  * over peer memory), 0 = one-shot, negative = by size (one-shot always at 2 ranks, up to
  * 2 MiB at 3-4 ranks, up to 1 MiB above). */
 int custom_ar_all_reduce(int64_t ctx, aiter_tensor_t* inp, aiter_tensor_t* out, int64_t force_two_shot,
                          void* stream);
+/* all_reduce with open_fp8_quant (csrc/kernels/custom_all_reduce.cu:76-115 and
+ * allReduceQuantFp8, csrc/include/custom_all_reduce.cuh:1018-1088): fp16 messages of
+ * at least 128 * 2048 elements take a two-shot allreduce whose all-gather moves fp8
+ * e4m3 codes with one fp16 scale per group of 128 (or 64, 32, 16, 8) elements; each
+ * rank's own segment is exact, the others carry the fp8 rounding.  Every other
+ * message takes custom_ar_all_reduce's path. */
+int custom_ar_all_reduce_fp8(int64_t ctx, aiter_tensor_t* inp, aiter_tensor_t* out, void* stream);
 /* GEMM + allreduce, out = allreduce(A @ W^T): the GEMM epilogue writes into the
  * staging buffer the allreduce reads, so the partial product is never copied.
  * No reference counterpart (the reference calls tgemm.mm then

@@ -1,0 +1,83 @@
+"""Multi-GPU parity of the IPC allreduce for fp16 and fp32 and of the fp8-quantised
+allreduce (custom_ar_all_reduce_fp8), one process per GPU.  Skipped with fewer than
+2 GPUs, and until these kernels have been run on a multi-GPU box, unless
+AITER_B200_TEST_UNRUN_MULTI=1.
+
+* fp16 / fp32: bit-exact against the fp32 rank-order sum (oracle), one- and two-shot;
+* open_fp8_quant with fp16: every rank's output bit-exact against the restatement of
+  the reference's allReduceQuantFp8 (oracle/allreduce.py), including group sizes
+  below 128 and a message whose pack count leaves a remainder for the last rank;
+  bf16 and small fp16 messages ignore the flag (plain allreduce bits).
+"""
+import os
+import sys
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+
+from dist_util import run_ranks
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+pytestmark = [
+    pytest.mark.gpu,
+    pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs"),
+    pytest.mark.skipif(os.environ.get("AITER_B200_TEST_UNRUN_MULTI") != "1",
+                       reason="fp16/fp32 and fp8-quantised allreduce not yet run on a multi-GPU box"),
+]
+
+
+def _inputs(n, world, seed, dtype):
+    out = []
+    for r in range(world):
+        g = torch.Generator().manual_seed(seed * 100 + r)
+        out.append(torch.randn(n, generator=g).to(dtype))
+    return out
+
+
+def _worker(rank, world, port):
+    sys.path.insert(0, ROOT)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    from aiter_b200 import _lib
+    from aiter_b200.dist import parallel_state as ps
+    from oracle.allreduce import allreduce_fp8_quant, allreduce_rank_order
+    ps.init_distributed_environment(world, rank, f"tcp://127.0.0.1:{port}", rank, "nccl", timeout_s=60)
+    tp = ps.initialize_model_parallel(world, local_rank=rank, ca_max_size=64 * 1024 * 1024)
+    ca = tp.ca_comm
+    dev = torch.device("cuda", rank)
+    for i, (dtype, n, two) in enumerate([(torch.float16, 4096, None), (torch.float16, 1 << 20, True),
+                                         (torch.float32, 4096, False), (torch.float32, 3 << 18, True),
+                                         (torch.float16, 8, None), (torch.float32, 4, None)]):
+        xs = _inputs(n, world, 10 + i, dtype)
+        y = ca.all_reduce(xs[rank].to(dev), two_shot=two)
+        torch.cuda.synchronize()
+        assert _lib.lib().custom_ar_device_error(1) == 0
+        want = allreduce_rank_order([x.numpy() for x in xs], xs[0].numpy().dtype)
+        assert np.array_equal(y.cpu().numpy(), want), (dtype, n, two)
+    # open_fp8_quant: 128-element groups; 64-element groups; a pack remainder
+    npd = np.float16
+    for j, n in enumerate([128 * 2048, 128 * 2048 * 3, world * 64 * 4097, 128 * 2048 + 8 * 3]):
+        xs = _inputs(n, world, 50 + j, torch.float16)
+        y = tp.all_reduce(xs[rank].to(dev), open_fp8_quant=True)
+        torch.cuda.synchronize()
+        assert _lib.lib().custom_ar_device_error(1) == 0
+        want = allreduce_fp8_quant([x.numpy() for x in xs])[rank]
+        got = y.cpu().numpy()
+        assert got.dtype == npd and np.array_equal(got, want), (n, int((got != want).sum()))
+    # the flag is ignored for bf16 and for fp16 below 128 * 2048 elements
+    for dtype, n in ((torch.bfloat16, 128 * 2048), (torch.float16, 4096)):
+        xs = _inputs(n, world, 70, dtype)
+        y = tp.all_reduce(xs[rank].to(dev), open_fp8_quant=True)
+        z = ca.all_reduce(xs[rank].to(dev))
+        torch.cuda.synchronize()
+        assert torch.equal(y, z), (dtype, n)
+    ps.destroy_model_parallel()
+    dist.destroy_process_group()
+
+
+def test_allreduce_dtypes_and_fp8_quant_multi_gpu():
+    world = min(torch.cuda.device_count(), 8)
+    world = 2 if world < 4 else (4 if world < 8 else 8)
+    run_ranks(_worker, world)
