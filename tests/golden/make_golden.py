@@ -17,6 +17,8 @@ reference locations:
 * f32_to_e8m0 / e8m0_to_f32 / mxfp4_to_f32  aiter/utility/fp4_utils.py:19-69
 * weight_per_128x128_quant op_tests/test_moe_2stage.py:84-110
 * torch_moe_stage1/2       aiter/fused_moe.py:1483-1666
+* e8m0_shuffle             aiter/utility/fp4_utils.py:72-92
+* run_torch (sorted MXFP4 scale layout)  op_tests/test_moe_sorting_mxfp4.py:20-43
 """
 import hashlib
 import os
@@ -64,6 +66,15 @@ TOPK_CASES = [
     ("m64_e8_k2", 64, 8, 2), ("m64_e128_k8", 64, 128, 8), ("m33_e256_k8", 33, 256, 8),
     ("m17_e64_k6", 17, 64, 6), ("m9_e512_k8", 9, 512, 8),
     ("zipf_m64_e256_k8", 64, 256, 8),
+]
+
+
+MXFP4_SORT_CASES = [
+    # name, tokens, model_dim, E, topk, block, stage (1: scales per token, 2: per token and slot)
+    ("s1_t37_d512_e8_k2_b32", 37, 512, 8, 2, 32, 1),
+    ("s2_t37_d512_e8_k2_b32", 37, 512, 8, 2, 32, 2),
+    ("s1_t300_d1024_e16_k4_b128", 300, 1024, 16, 4, 128, 1),
+    ("s2_t64_d256_e32_k8_b64", 64, 256, 32, 8, 64, 2),
 ]
 
 
@@ -169,6 +180,29 @@ def main(root):
                             np.array([2.0 ** -10, 2.0 ** -9 * 1.5, 2.0 ** -7 * 1.0625, 464.0, 448.0], np.float32)])
     out["codec/fp8_in"] = fp8in
     out["codec/fp8_out"] = t2n(torch.from_numpy(fp8in).to(torch.float8_e4m3fn))
+    # ---------------------------------------------------------------- MXFP4 activation quant + MoE scale sort
+    for i, (name, T, D, E, k, B, stage) in enumerate(MXFP4_SORT_CASES):
+        rng = np.random.default_rng(5000 + i)
+        ids = np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.int32)
+        w = rng.random((T, k), dtype=np.float32)
+        sid, _, _, nv = ref.moe_sorting_native(torch.from_numpy(ids), torch.from_numpy(w), E, B, None, None)
+        rows = T if stage == 1 else T * k
+        x = torch.from_numpy((rng.standard_normal((rows, D)) * 2).astype(np.float32)).to(torch.bfloat16)
+        x[1, :32] = 0                          # an all-zero group
+        x[2, 40] = 300.0                       # a dominant outlier
+        q, sc = ref.per_1x32_f4_quant(x)
+        sc8 = sc.view(torch.uint8)
+        scale_in = sc8 if stage == 1 else sc8.view(T, k, D // 32)
+        srt = ref.moe_mxfp4_sort_torch(scale_in.clone(), sid.clone(), nv[0], T)
+        p = f"mxfp4sort/{name}/"
+        out[p + "meta"] = np.array([T, D, E, k, B, stage], dtype=np.int64)
+        out[p + "x"] = t2n(x)
+        out[p + "sorted_ids"] = t2n(sid)
+        out[p + "num_valid_ids"] = t2n(nv)
+        out[p + "q"] = t2n(q)
+        out[p + "scale"] = t2n(sc8)
+        out[p + "sorted_scale"] = t2n(srt)
+        out[p + "shuffled_scale"] = t2n(ref.e8m0_shuffle(sc8.clone()))
     # ---------------------------------------------------------------- MoE config 0 (fp8 blockscale)
     for tag, (seed, M, D, I, E, k) in {"cfg0": (0, 32, 1024, 512, 8, 2),
                                         "cfg0_m7": (7, 7, 1024, 256, 8, 2)}.items():

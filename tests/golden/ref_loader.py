@@ -91,7 +91,7 @@ class Reference:
         # fp4 codecs first: quant and the stage functions use them
         fp4 = self._load(ns, "aiter/utility/fp4_utils.py",
                          ["_n_ones", "EBITS_F32", "F32_EXP_BIAS", "_f32_to_floatx_unpacked", "down_size", "pack_uint4",
-                          "f32_to_mxfp4", "mxfp4_to_f32", "f32_to_e8m0", "e8m0_to_f32"])
+                          "f32_to_mxfp4", "mxfp4_to_f32", "f32_to_e8m0", "e8m0_to_f32", "e8m0_shuffle"])
         fp4_mod = types.ModuleType("fp4_utils")
         for k in fp4 + ["MBITS_F32"]:
             setattr(fp4_mod, k, ns[k])
@@ -106,6 +106,10 @@ class Reference:
                     "torch_moe_stage1", "torch_moe_stage2"])
         self._load(ns, "aiter/ops/topk.py", ["biased_grouped_topk_torch", "grouped_topk_torch"])
         self._load(ns, "op_tests/test_moe_sorting.py", ["moe_sorting_native"])
+        # the torch reference of the sorted MXFP4 scale layout, kept under its own name
+        run_torch = dict(torch=torch)
+        self._load(run_torch, "op_tests/test_moe_sorting_mxfp4.py", ["run_torch"])
+        ns["moe_mxfp4_sort_torch"] = run_torch["run_torch"]
         self._load(ns, "op_tests/test_moeTopkSoftmax.py", ["test_nofuse"])
         self._load(ns, "op_tests/test_moe_2stage.py", ["weight_per_128x128_quant"],
                    nested_in="test_fmoe")

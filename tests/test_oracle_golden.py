@@ -173,3 +173,24 @@ def test_moe_a8w4_matches_reference(golden):
                                  c["topk_weights"], c["topk_ids"], return_intermediate=True)
     np.testing.assert_allclose(st["out1"], g["out1"], rtol=1e-2, atol=1e-3)
     np.testing.assert_allclose(out, g["out"], rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("case", ["s1_t37_d512_e8_k2_b32", "s2_t37_d512_e8_k2_b32", "s1_t300_d1024_e16_k4_b128",
+                                  "s2_t64_d256_e32_k8_b64"])
+def test_mxfp4_quant_and_moe_scale_sort_match_reference(golden, case):
+    from oracle import mxfp4_sort
+    g = golden_group(golden, "mxfp4sort")[case]
+    T, D, E, k, B, stage = (int(v) for v in g["meta"])
+    q, s = quant.per_1x32_f4_quant(g["x"])
+    assert np.array_equal(q, g["q"])
+    assert np.array_equal(s, g["scale"])
+    scale_in = s if stage == 1 else s.reshape(T, k, D // 32)
+    srt = mxfp4_sort.moe_mxfp4_sort(scale_in, g["sorted_ids"], int(g["num_valid_ids"][0]), T)
+    assert srt.shape == g["sorted_scale"].shape
+    assert np.array_equal(srt, g["sorted_scale"])
+    # e8m0_shuffle pads with uninitialised memory: compare where the source is real
+    sh = mxfp4_sort.e8m0_shuffle(s)
+    rows, cols = sh.shape
+    r, c = mxfp4_sort.shuffle_index(rows, cols)
+    real = ((r < s.shape[0]) & (c < s.shape[1])).reshape(rows, cols)
+    assert np.array_equal(sh[real], g["shuffled_scale"][real])
