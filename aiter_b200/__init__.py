@@ -11,10 +11,12 @@ include/aiter_b200.h), called through ctypes; there is no CPU fallback.
 """
 from . import dtypes
 from .enums import ActivationType, QuantType
-from .moe_op import (biased_grouped_topk, biased_grouped_topk_hip, dynamic_per_token_scaled_quant,
-                     grouped_topk, moe_gather_quant_1x128, moe_sorting_fwd, moe_sorting_get_workspace_size,
-                     moe_stage1_fp8_blockscale, moe_stage2_fp8_blockscale, per_group_quant_hip,
-                     topk_softmax)
+from .moe_op import (biased_grouped_topk, biased_grouped_topk_hip, dynamic_per_group_scaled_quant_fp4,
+                     dynamic_per_token_scaled_quant, fused_dynamic_mxfp4_quant_moe_sort,
+                     fused_dynamic_mxfp4_quant_moe_sort_hip, grouped_topk, moe_gather_quant_1x128,
+                     moe_sorting_fwd, moe_sorting_get_workspace_size, moe_stage1_fp8_blockscale,
+                     moe_stage2_fp8_blockscale, mxfp4_moe_sort_fwd, mxfp4_moe_sort_hip, per_1x32_f4_quant_hip,
+                     per_group_quant_hip, topk_softmax)
 from .fused_moe import fused_moe, fused_topk, moe_sorting, get_inter_dim
 from ._lib import device_error
 from . import torch_ops  # registers torch.ops.aiter_b200.* (fake impls for torch.compile)
@@ -24,5 +26,6 @@ __all__ = [
     "biased_grouped_topk_hip", "moe_gather_quant_1x128", "moe_sorting_fwd", "moe_sorting_get_workspace_size",
     "dynamic_per_token_scaled_quant", "per_group_quant_hip", "moe_stage1_fp8_blockscale",
     "moe_stage2_fp8_blockscale", "fused_moe", "fused_topk", "moe_sorting", "get_inter_dim",
-    "device_error",
+    "device_error", "dynamic_per_group_scaled_quant_fp4", "per_1x32_f4_quant_hip", "mxfp4_moe_sort_hip",
+    "mxfp4_moe_sort_fwd", "fused_dynamic_mxfp4_quant_moe_sort_hip", "fused_dynamic_mxfp4_quant_moe_sort",
 ]

@@ -101,6 +101,9 @@ SIGNATURES = {
     "moe_gather_quant_1x128": [T, OT, T, I64, T, T],
     "mxfp4_to_fp8_blockscale": [T, T, T, T, OT],
     "gemm_a16w16": [T, T, T],
+    "dynamic_per_group_scaled_quant_fp4": [T, T, T, I64, B, OT, I64],
+    "mxfp4_moe_sort_hip": [T, T, T, T, I64, I64],
+    "fused_dynamic_mxfp4_quant_moe_sort_hip": [T, T, T, T, T, I64, I64, I64],
     "moe_stage1_fp8_blockscale": [T, T, T, T, T, T, T, T, T, I64, I64, I64],
     "moe_stage2_fp8_blockscale": [T, T, T, T, T, T, T, T, T, I64],
 }

@@ -94,6 +94,81 @@ def per_group_quant_hip(x: Tensor, scale: Optional[Tensor] = None, quant_dtype=d
     return y, scale
 
 
+def dynamic_per_group_scaled_quant_fp4(out: Tensor, input: Tensor, scales: Tensor, group_size: int = 32,
+                                       shuffle_scale: bool = True, num_rows: Optional[Tensor] = None,
+                                       num_rows_factor: int = 1) -> None:
+    """MXFP4 quant of `input` rows (aiter/ops/quant.py:485-497): fp4x2 codes into `out`,
+    one e8m0 scale per 32 elements into `scales` (row order, or the e8m0_shuffle layout
+    when `shuffle_scale`).  Rows from num_rows[0] * num_rows_factor on are skipped."""
+    _lib.call("dynamic_per_group_scaled_quant_fp4", out, input, scales, group_size, shuffle_scale, num_rows,
+              num_rows_factor)
+
+
+def per_1x32_f4_quant_hip(x: Tensor, scale: Optional[Tensor] = None, quant_dtype=dtypes.fp4x2, shuffle: bool = False,
+                          num_rows: Optional[Tensor] = None, num_rows_factor: int = 1) -> Tuple[Tensor, Tensor]:
+    """(fp4x2 [m, n/2], e8m0 scales) of x [m, n] (aiter/ops/quant.py:295-343)."""
+    m, n = x.shape
+    assert quant_dtype == dtypes.fp4x2
+    assert n % 2 == 0
+    if scale is not None:
+        raise ValueError("unsupported: static per token quant")
+    if shuffle:
+        scale = torch.empty(((m + 255) // 256 * 256, ((n + 31) // 32 + 7) // 8 * 8), dtype=torch.uint8,
+                            device=x.device).view(dtypes.fp8_e8m0)
+    else:
+        scale = torch.empty((m, (n + 31) // 32), dtype=torch.uint8, device=x.device).view(dtypes.fp8_e8m0)
+    y = torch.empty(m, n // 2, dtype=quant_dtype, device=x.device)
+    dynamic_per_group_scaled_quant_fp4(y, x, scale, 32, shuffle_scale=shuffle, num_rows=num_rows,
+                                       num_rows_factor=num_rows_factor)
+    return y, scale
+
+
+def mxfp4_moe_sort_hip(out_scale: Tensor, scale: Tensor, sorted_ids: Tensor, num_valid_ids: Tensor, token_num: int,
+                       cols: int) -> None:
+    """e8m0 scales gathered into moe_sorting order and shuffled (aiter/ops/quant.py:552-563)."""
+    _lib.call("mxfp4_moe_sort_hip", out_scale, scale, sorted_ids, num_valid_ids, token_num, cols)
+
+
+def mxfp4_moe_sort_fwd(scale: Tensor, sorted_ids: Tensor, num_valid_ids: Tensor, token_num: int,
+                       cols: int) -> Tensor:
+    """aiter/ops/quant.py:566-580."""
+    out_scale = torch.empty(((sorted_ids.shape[0] + 31) // 32 * 32, (cols + 31) // 32), dtype=dtypes.fp8_e8m0,
+                            device=scale.device)
+    mxfp4_moe_sort_hip(out_scale, scale, sorted_ids, num_valid_ids, token_num, cols)
+    return out_scale
+
+
+def fused_dynamic_mxfp4_quant_moe_sort_hip(out: Tensor, scales: Tensor, input: Tensor, sorted_ids: Tensor,
+                                           num_valid_ids: Tensor, token_num: int, block_m: int,
+                                           group_size: int = 32) -> None:
+    """MXFP4 quant of every input row and its scales in sorted, shuffled order, one
+    launch (aiter/ops/quant.py:584-597)."""
+    _lib.call("fused_dynamic_mxfp4_quant_moe_sort_hip", out, scales, input, sorted_ids, num_valid_ids, token_num,
+              block_m, group_size)
+
+
+def fused_dynamic_mxfp4_quant_moe_sort(input: Tensor, sorted_ids: Tensor, num_valid_ids: Tensor, token_num: int,
+                                       topk: int, block_size: int, num_rows: Optional[Tensor] = None,
+                                       group_size: int = 32) -> Tuple[Tensor, Tensor]:
+    """(fp4x2 [M, N/2] in row order, sorted shuffled e8m0 scales), with the reference's
+    choice between the one-launch kernel (few tokens) and quant then sort
+    (aiter/ops/quant.py:600-652); both give the same bytes."""
+    switch = [8 * 384 / topk, 8 * 1024 / topk]
+    M, N = input.view(-1, input.shape[-1]).shape
+    is_stage1 = M == token_num
+    topk = 1 if is_stage1 else topk
+    scale = torch.empty(((sorted_ids.shape[0] + 31) // 32 * 32, (N + 31) // 32), dtype=dtypes.fp8_e8m0,
+                        device=input.device)
+    if (is_stage1 and M <= switch[0]) or (not is_stage1 and M <= switch[1] * topk) or group_size != 32:
+        out = torch.empty(M, N // 2, dtype=dtypes.fp4x2, device=input.device)
+        fused_dynamic_mxfp4_quant_moe_sort_hip(out, scale, input, sorted_ids, num_valid_ids, token_num, block_size,
+                                               group_size)
+    else:
+        out, scale_ = per_1x32_f4_quant_hip(input, None, dtypes.fp4x2, num_rows=num_rows, num_rows_factor=topk)
+        mxfp4_moe_sort_hip(scale, scale_, sorted_ids, num_valid_ids, token_num, N)
+    return out, scale
+
+
 def moe_gather_quant_1x128(hidden_states: Tensor, token_sorted_pos: Tensor, topk: int, rows: int,
                            hidden_scale: Optional[Tensor] = None, out: Optional[Tensor] = None,
                            out_scale: Optional[Tensor] = None) -> Tuple[Tensor, Tensor]:

@@ -163,6 +163,29 @@ int moe_gather_quant_1x128(aiter_tensor_t* hidden, aiter_tensor_t* hidden_scale,
                            aiter_tensor_t* token_sorted_pos, int64_t topk,
                            aiter_tensor_t* out, aiter_tensor_t* out_scale, void* stream);
 
+/* MXFP4 activation quant: per 32-element group e = e8m0(amax / 4) (the reference's
+ * round-half-up rule), codes e2m1(x / 2^(e-127)) round-to-nearest-even saturating at
+ * 6, packed two per byte low nibble first; scales in row order [rows, cols/32] or, with
+ * shuffle_scale, in the e8m0_shuffle layout of a [rows padded to 32, cols/32 padded
+ * to 8] matrix.  Rows from num_rows[0] * num_rows_factor on are skipped.  group_size
+ * must be 32.  Replaces dynamic_per_group_scaled_quant_fp4 (aiter/ops/quant.py:485-497;
+ * semantics of per_1x32_f4_quant, :75-106). */
+int dynamic_per_group_scaled_quant_fp4(aiter_tensor_t* out, aiter_tensor_t* input, aiter_tensor_t* scales,
+                                       int64_t group_size, int shuffle_scale, aiter_tensor_t* num_rows,
+                                       int64_t num_rows_factor, void* stream);
+/* e8m0 scales [token_num or token_num * topk, cols/32] gathered into moe_sorting order
+ * and shuffled: out_scale [ceil(len(sorted_ids)/32)*32, cols/32]; padding slots and
+ * rows from num_valid_ids[0] on are 0.  Replaces mxfp4_moe_sort_hip
+ * (aiter/ops/quant.py:552-563; layout of op_tests/test_moe_sorting_mxfp4.py:20-43). */
+int mxfp4_moe_sort_hip(aiter_tensor_t* out_scale, aiter_tensor_t* scale, aiter_tensor_t* sorted_ids,
+                       aiter_tensor_t* num_valid_ids, int64_t token_num, int64_t cols, void* stream);
+/* Both in one launch: out [rows, cols/2] fp4x2 of every input row (rows = token_num,
+ * or token_num * topk), scales sorted and shuffled as mxfp4_moe_sort_hip writes them.
+ * Replaces fused_dynamic_mxfp4_quant_moe_sort_hip (aiter/ops/quant.py:584-597). */
+int fused_dynamic_mxfp4_quant_moe_sort_hip(aiter_tensor_t* out, aiter_tensor_t* scales, aiter_tensor_t* input,
+                                           aiter_tensor_t* sorted_ids, aiter_tensor_t* num_valid_ids,
+                                           int64_t token_num, int64_t block_m, int64_t group_size, void* stream);
+
 /* A8W4 weight preparation: MXFP4 weights (e2m1 packed two per byte, low nibble
  * first, + e8m0 scale per 32 along K; per_1x32_f4_quant, aiter/ops/quant.py:75-106)
  * -> e4m3 [E, N, K] with a power-of-two f32 scale per 128x128 block, the operand

@@ -1,7 +1,7 @@
 """Multi-GPU parity of the IPC allreduce for fp16 and fp32 and of the fp8-quantised
 allreduce (custom_ar_all_reduce_fp8), one process per GPU.  Skipped with fewer than
 2 GPUs, and until these kernels have been run on a multi-GPU box, unless
-AITER_B200_TEST_UNRUN_MULTI=1.
+AITER_B200_TEST_UNRUN=1.
 
 * fp16 / fp32: bit-exact against the fp32 rank-order sum (oracle), one- and two-shot;
 * open_fp8_quant with fp16: every rank's output bit-exact against the restatement of
@@ -23,7 +23,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 pytestmark = [
     pytest.mark.gpu,
     pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs"),
-    pytest.mark.skipif(os.environ.get("AITER_B200_TEST_UNRUN_MULTI") != "1",
+    pytest.mark.skipif(os.environ.get("AITER_B200_TEST_UNRUN") != "1",
                        reason="fp16/fp32 and fp8-quantised allreduce not yet run on a multi-GPU box"),
 ]
 
