@@ -24,7 +24,7 @@ def max_num_tokens_padded(M, topk, num_experts, block_size):
 
 def moe_sorting(topk_ids, topk_weights, num_experts, block_size,
                 expert_mask=None, num_local_tokens=None):
-    """Returns (sorted_ids, sorted_weights, sorted_expert_ids, num_valid_ids, valid_len)."""
+    """Returns (sorted_ids, sorted_weights, sorted_expert_ids, num_valid_ids)."""
     topk_ids = np.asarray(topk_ids, dtype=np.int32)
     topk_weights = np.asarray(topk_weights, dtype=np.float32)
     M, topk = topk_ids.shape

@@ -85,7 +85,7 @@ def test_config2_size_against_oracle(stage):
     lg = inputs.make_logits(rng, M, E, zipf_s=1.1)
     ids = np.argsort(-lg, axis=1, kind="stable")[:, :k].astype(np.int32)
     w = rng.random((M, k), dtype=np.float32)
-    sid, _, _, nv, _ = sorting.moe_sorting(ids, w, E, B)
+    sid, _, _, nv = sorting.moe_sorting(ids, w, E, B)
     rows = M if stage == 1 else M * k
     xb = torch.from_numpy((rng.standard_normal((rows, D)) * 3).astype(np.float32)).to(torch.bfloat16)
     out, sc = aiter.fused_dynamic_mxfp4_quant_moe_sort(xb.to(dev()), to_dev(sid), to_dev(nv), M, k, B)
