@@ -51,6 +51,8 @@ def parse():
     p.add_argument("--E", type=int, default=128, help="experts (profiling cases use fewer)")
     p.add_argument("--cpu-sample", type=int, default=128, help="tokens per CPU-baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--fused-gemm-ar", action="store_true",
+                   help="gemm_ar mode: also time the one-kernel GEMM + allreduce (custom_ar_gemm_all_reduce_fused)")
     p.add_argument("--mode", default="moe", choices=["moe", "moe_sweep", "a8w4", "tp_moe", "gemm_ar"],
                    help="moe: config 1 at --M (N>1: data-parallel replicas); moe_sweep: config 1 token sweep "
                         "on one GPU; a8w4: config 2 on one GPU; tp_moe: config 3; gemm_ar: config 4")
@@ -503,6 +505,24 @@ def run_moe_sweep(args, rank, world, local):
 
         ms_eager = _time_loop(step, args.steps, args.warmup, world)
         ms = _graph_time(step, args.steps)  # what a serving engine sees: no per-call host overhead
+        # per-kernel CUDA-event times of the eager step (launch gaps fall between them)
+        names = ["moe_sorting", "gather_quant_1x128", "stage1_gemm", "stage2_gemm"]
+        calls = [
+            lambda: moe_op.moe_sorting_fwd(tid, tw, sid, sw, seid, nv, out, E, B, None, None, 0,
+                                           ws if ws_n else None, pos),
+            lambda: moe_op.moe_gather_quant_1x128(hid, pos, TOPK, max_pad, out=a1, out_scale=a1s),
+            lambda: moe_op.moe_stage1_fp8_blockscale(a1, a1s, x["w1q"], x["w1s"], sid, seid, nv, a2, a2s, M, B),
+            lambda: moe_op.moe_stage2_fp8_blockscale(a2, a2s, x["w2q"], x["w2s"], sid, seid, nv, sw, out, B),
+        ]
+        kev = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+        for i in range(args.steps):
+            for j, fn in enumerate(calls):
+                kev[i][j].record()
+                fn()
+            kev[i][4].record()
+        torch.cuda.synchronize()
+        kernel_ms = {n: round(sum(kev[i][j].elapsed_time(kev[i][j + 1]) for i in range(args.steps)) / args.steps, 4)
+                     for j, n in enumerate(names)}
         active = int(torch.unique(tid).numel())
         w_bytes = active * 3 * D * I + active * (3 * D * I // (128 * 128)) * 4
         bytes_ = w_bytes + M * D * 2 + 2 * M * TOPK * I + M * TOPK * (I // 128) * 4 + M * D * 2 * 2
@@ -512,7 +532,8 @@ def run_moe_sweep(args, rank, world, local):
                      "tokens_per_s": round(M / (ms * 1e-3), 1), "tflops": round(tfl, 2), "active_experts": active,
                      "tensor_frac": round(tfl / fp8_peak, 4), "hbm_GBs": round(gbs, 1),
                      "hbm_frac": round(gbs / pk["hbm_gbs"], 4),
-                     "bound": "hbm" if gbs / pk["hbm_gbs"] > tfl / fp8_peak else "tensor"})
+                     "bound": "hbm" if gbs / pk["hbm_gbs"] > tfl / fp8_peak else "tensor",
+                     "kernel_ms_eager": kernel_ms})
     return {"metric": METRIC, "mode": "moe_sweep", "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
             "warmup": args.warmup, "higher_is_better": True, "dtype": "fp8-e4m3", "data": "synthetic",
             "config": {"workload": "BASELINE config 1 token sweep", "hidden": D, "inter": I, "experts": E,
@@ -634,6 +655,10 @@ def run_gemm_ar(args, rank, world, local):
 
         us = 1e3 * _time_loop(ours, args.steps, args.warmup, world)
         us_b = 1e3 * _time_loop(base, args.steps, args.warmup, world)
+        fused = {}
+        if args.fused_gemm_ar:
+            us_f = 1e3 * _time_loop(lambda: tp.gemm_all_reduce(A, W, fused=True), args.steps, args.warmup, world)
+            fused = {"ours_fused_us": round(us_f, 2), "fused_speedup_vs_cublas_nccl": round(us_b / us_f, 3)}
         # the two halves alone, to show which one sets each total
         from aiter_b200.gemm import gemm_a16w16
         y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
@@ -648,7 +673,7 @@ def run_gemm_ar(args, rank, world, local):
         ar_bytes = 2.0 * (world - 1) / world * M * N * 2
         rows.append({"M": M, "ours_us": round(us, 2), "cublas_nccl_us": round(us_b, 2),
                      "speedup": round(us_b / us, 3), "ours_busbw_GBs": round(ar_bytes / (us * 1e-6) / 1e9, 1),
-                     "gemm_tflops": round(2.0 * M * K * N / (us * 1e-6) / 1e12, 2), **part_us})
+                     "gemm_tflops": round(2.0 * M * K * N / (us * 1e-6) / 1e12, 2), **fused, **part_us})
     ps.destroy_model_parallel()
     big = rows[-1]
     return {"metric": "GEMM+allreduce latency (config 4, M=8192)", "mode": "gemm_ar", "value": big["ours_us"],
