@@ -14,7 +14,10 @@ flush is needed between steps.
            the launching stream, max over ranks; N > 1 runs independent replicas.
 * e2e    : the same metric through the public `aiter_b200.fused_moe` call with
            pinned host buffers: H2D of hidden/topk_weights/topk_ids and D2H of the
-           output inside the timed region.
+           output of every step inside the timed region, the copies of neighbouring
+           steps overlapping the compute on two copy streams (double-buffered device
+           inputs), as a serving loop runs it; `serial_value` is the same loop with
+           every copy and call in one stream.
 * roofline: stage-1 grouped GEMM (the dominant kernel): algorithmic FP8 FLOPs per
            launch / its mean CUDA-event duration, against the FP8 dense peak (2x
            the measured bf16 cuBLAS burst of MEASURED_PEAKS.json).
@@ -298,12 +301,23 @@ def run_b200(args, rank, world, local):
     e1.record(stream)
     torch.cuda.synchronize()
     barrier(world)
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    e2e_serial_ms = max_over_ranks(e0.elapsed_time(e1), world)
     # the e2e output must match the device-resident run
     ref_out = out.float()
     assert torch.allclose(h_out.to(dev).float(), ref_out, atol=2e-2, rtol=2e-2)
     h2d = h_hidden.numel() * 2 + h_tw.numel() * 4 + h_tid.numel() * 4
     d2h = h_out.numel() * 2
+    # The same K calls with the copies of neighbouring steps overlapping the compute,
+    # as a serving loop runs them: every step still copies its own inputs in and its
+    # result out inside the timed region.  Falls back to the serial loop's time if the
+    # pipelined loop fails for any reason.
+    e2e_mode = "pipelined: H2D of step i+1 and D2H of step i-1 on their own streams overlap step i"
+    try:
+        e2e_ms = max_over_ranks(_e2e_pipelined(aiter, x, h_hidden, h_tw, h_tid, ref_out, K, args.warmup, world),
+                                world)
+    except Exception as exc:  # keep the line: report the serial measurement instead
+        e2e_ms = e2e_serial_ms
+        e2e_mode = f"serial (pipelined loop failed: {type(exc).__name__}: {exc})"[:300]
 
     pk, src = peaks()
     fp8_peak_tflops = 2.0 * pk["bf16_tflops"]
@@ -336,10 +350,69 @@ def run_b200(args, rank, world, local):
                      "traffic": traffic},
         "gpu_launches": launches_per_step * K,
         "e2e": {"value": round(M * K * world / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "api": "aiter_b200.fused_moe"},
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "api": "aiter_b200.fused_moe",
+                "copies": e2e_mode, "serial_value": round(M * K * world / (e2e_serial_ms * 1e-3), 1)},
         "clocks": clk.summary(),
     }
     return res, x
+
+
+def _e2e_pipelined(aiter, x, h_hidden, h_tw, h_tid, ref_out, K, W, world):
+    """ms of K fused_moe calls from pinned host buffers with double-buffered device
+    inputs: step i's H2D (copy stream) overlaps step i-1's compute and step i-2's
+    D2H (second copy stream).  Events order each buffer's reuse; the last step's
+    output is checked against the device-resident result."""
+    dev = x["hidden"].device
+    cmp = torch.cuda.current_stream()
+    s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    d_in = [(torch.empty_like(x["hidden"]), torch.empty_like(x["tw"]), torch.empty_like(x["tid"])) for _ in range(2)]
+    h_out = [torch.empty(ref_out.shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    done_cmp = [torch.cuda.Event() for _ in range(2)]
+    done_in = [torch.cuda.Event() for _ in range(2)]
+    done_out = [torch.cuda.Event() for _ in range(2)]
+    used = [False, False]
+
+    def run(n, start_event=None):
+        if start_event is not None:
+            s_in.wait_event(start_event)
+        for i in range(n):
+            b = i & 1
+            with torch.cuda.stream(s_in):
+                if used[b]:
+                    s_in.wait_event(done_cmp[b])      # step i-2 has finished reading d_in[b]
+                for d, h in zip(d_in[b], (h_hidden, h_tw, h_tid)):
+                    d.copy_(h, non_blocking=True)
+                done_in[b].record(s_in)
+            cmp.wait_event(done_in[b])
+            if used[b]:
+                cmp.wait_event(done_out[b])           # h_out[b] of step i-2 has been read out
+            o = aiter.fused_moe(d_in[b][0], x["w1q"], x["w2q"], d_in[b][1], d_in[b][2],
+                                quant_type=aiter.QuantType.per_1x128, activation=aiter.ActivationType.Silu,
+                                w1_scale=x["w1s"], w2_scale=x["w2s"])
+            done_cmp[b].record(cmp)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(done_cmp[b])
+                h_out[b].copy_(o, non_blocking=True)
+                o.record_stream(s_out)
+                done_out[b].record(s_out)
+            used[b] = True
+        cmp.wait_stream(s_in)
+        cmp.wait_stream(s_out)
+        return (n - 1) & 1
+
+    run(W)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(cmp)
+    last = run(K, start_event=e0)
+    e1.record(cmp)
+    torch.cuda.synchronize()
+    barrier(world)
+    if not torch.allclose(h_out[last].to(dev).float(), ref_out, atol=2e-2, rtol=2e-2):
+        raise RuntimeError("pipelined e2e output differs from the device-resident result")
+    return e0.elapsed_time(e1)
 
 
 def cpu_baseline(x, sample, threads=None):
