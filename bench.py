@@ -160,6 +160,16 @@ def peaks():
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
+def tmem_peak_from_profile():
+    """Measured TMEM -> register read throughput of a B200 (TB/s over all SMs) from the
+    committed probe summary, or None when it has not been measured."""
+    path = os.path.join(ROOT, "profiles", "tmem_ld_throughput.json")
+    try:
+        return json.load(open(path)).get("tmem_read_TBs")
+    except Exception:
+        return None
+
+
 def traffic_from_profile():
     """Per-launch DRAM bytes of the stage-1 kernel from the committed ncu summary."""
     path = os.path.join(ROOT, "profiles", "moe_stage1_fp8_cfg1_traffic.json")
@@ -325,6 +335,12 @@ def run_b200(args, rank, world, local):
     s1_ms = mean_ms["stage1_gemm"]
     achieved = s1_flops / (s1_ms * 1e-3) / 1e12
     traffic, _ = traffic_from_profile()
+    # block-scale promotion: every sorted row's 2I fp32 accumulators are read from TMEM
+    # once per 128-wide K block (D/128 times) -- the second bound of this kernel
+    rows_padded = int(nv[0].item())
+    promoted = float(rows_padded) * 2 * I * (D // 128) * 4
+    tmem_tbs = promoted / (s1_ms * 1e-3) / 1e12
+    tmem_peak = tmem_peak_from_profile()
     total_tokens = M * K * world
     value = total_tokens / (ms * 1e-3)
     res = {
@@ -347,7 +363,12 @@ def run_b200(args, rank, world, local):
                      "achieved": round(achieved, 1), "peak": round(fp8_peak_tflops, 1), "unit": "TFLOP/s",
                      "frac": round(achieved / fp8_peak_tflops, 4),
                      "peak_source": f"2 x bf16_tflops of MEASURED_PEAKS.json ({src}); fp8 dense runs at 2x bf16",
-                     "traffic": traffic},
+                     "traffic": traffic,
+                     "promotion": {"bound": "tmem", "bytes_per_launch": promoted, "rows_padded": rows_padded,
+                                   "achieved": round(tmem_tbs, 2), "unit": "TB/s",
+                                   "peak": tmem_peak, "frac": round(tmem_tbs / tmem_peak, 4) if tmem_peak else None,
+                                   "peak_source": "profiles/tmem_ld_throughput.json" if tmem_peak else
+                                   "not measured yet"}},
         "gpu_launches": launches_per_step * K,
         "e2e": {"value": round(M * K * world / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "api": "aiter_b200.fused_moe",
