@@ -146,7 +146,8 @@ def _fused_moe_impl(hidden_states, w1, w2, topk_weight, topk_ids, expert_mask=No
     assert w1.shape[1] in (inter_dim, inter_dim * 2), f"Invalid MoE weight: {w1.shape=} {w2.shape=}"
     is_g1u1 = w1.shape[1] == 2 * inter_dim
     if getattr(w1, "is_shuffled", False) or getattr(w2, "is_shuffled", False):
-        raise ValueError("pre-shuffled (AMD MFMA layout) weights are not accepted; pass [E, N, K] weights")
+        raise ValueError("pre-shuffled (AMD MFMA layout) weights are not accepted; pass [E, N, K] weights "
+                         "(aiter_b200.weights.unshuffle_weight undoes shuffle_weight once)")
     dtype = hidden_states.dtype if dtype is None else dtype
     if dtype == dtypes.fp8:          # pre-quantised input: output defaults to bf16
         dtype = dtypes.bf16

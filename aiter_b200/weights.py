@@ -4,6 +4,8 @@
   the quantiser of op_tests/test_moe_2stage.py:84-110 (amax / 448, 0 -> 1).
 * `quant_weight_mxfp4`    e2m1 values packed two per byte (low nibble first) with
   e8m0 scales per 32 along K, the quantiser of aiter/ops/quant.py:75-106.
+* `unshuffle_weight`      the inverse of the reference's `shuffle_weight`
+  (aiter/ops/shuffle.py:7-27), for weights prepared for AMD's MFMA kernels.
 Weights are [E, N, K] with K contiguous (no AMD pre-shuffle).
 """
 import torch
@@ -122,3 +124,26 @@ def prepare_a8w4(w1_fp4, w1_scale, w2_fp4, w2_scale):
     w1, s1 = mxfp4_to_fp8_blockscale(w1_fp4, w1_scale)
     w2, s2 = mxfp4_to_fp8_blockscale(w2_fp4, w2_scale)
     return w1, s1, w2, s2
+
+
+@torch.no_grad()
+def unshuffle_weight(x: torch.Tensor, layout=(16, 16), use_int4: bool = False) -> torch.Tensor:
+    """[.., N, K] weights back from the AMD MFMA tile order of `shuffle_weight`
+    (aiter/ops/shuffle.py:7-27), which views the weights as
+    [-1, N/BN, BN, K/BK, BK/P, P] (BN = layout[0], BK = 2 * layout[1], P = 16 bytes
+    of elements, 32 for int4) and stores them permuted to (0, 1, 3, 4, 2, 5); this
+    applies the inverse permutation.  The result is the [E, N, K], K-contiguous layout
+    the B200 kernels take; the `is_shuffled` mark is not carried over."""
+    x_type = x.dtype
+    if x_type == dtypes.fp4x2:
+        x = x.view(torch.uint8)
+    IN, IK = layout
+    BK = IK * 2
+    P = 16 // x.element_size() if not use_int4 else 32
+    BN = IN
+    N, K = x.shape[-2], x.shape[-1]
+    if N % BN or K % BK:
+        raise ValueError(f"weights [{N}, {K}] are not a whole number of {BN} x {BK} shuffle tiles")
+    y = x.contiguous().view(-1, N // BN, K // BK, BK // P, BN, P)
+    y = y.permute(0, 1, 4, 2, 3, 5).contiguous().view(*x.shape)
+    return y.view(x_type)

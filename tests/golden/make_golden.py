@@ -18,6 +18,7 @@ reference locations:
 * weight_per_128x128_quant op_tests/test_moe_2stage.py:84-110
 * torch_moe_stage1/2       aiter/fused_moe.py:1483-1666
 * e8m0_shuffle             aiter/utility/fp4_utils.py:72-92
+* shuffle_weight           aiter/ops/shuffle.py:7-27
 * run_torch (sorted MXFP4 scale layout)  op_tests/test_moe_sorting_mxfp4.py:20-43
 """
 import hashlib
@@ -32,7 +33,7 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 sys.path.insert(0, HERE)
 
 from ref_loader import Reference, QuantType, ActivationType  # noqa: E402
-from oracle import inputs  # noqa: E402
+from oracle import inputs, mxfp4_sort  # noqa: E402
 
 
 def sha(a):
@@ -202,7 +203,19 @@ def main(root):
         out[p + "q"] = t2n(q)
         out[p + "scale"] = t2n(sc8)
         out[p + "sorted_scale"] = t2n(srt)
-        out[p + "shuffled_scale"] = t2n(ref.e8m0_shuffle(sc8.clone()))
+        # e8m0_shuffle pads with torch.empty: keep only elements whose source is real
+        shf = t2n(ref.e8m0_shuffle(sc8.clone()))
+        r_, c_ = mxfp4_sort.shuffle_index(*shf.shape)
+        real = ((r_ < sc8.shape[0]) & (c_ < sc8.shape[1])).reshape(shf.shape)
+        out[p + "shuffled_scale"] = np.where(real, shf, 0).astype(np.uint8)
+    # ---------------------------------------------------------------- AMD weight pre-shuffle (to undo)
+    rng = np.random.default_rng(6000)
+    ws = rng.integers(0, 256, (2, 64, 128), dtype=np.uint8)
+    out["shuffle/w_u8"] = ws
+    out["shuffle/shuffled_fp8"] = t2n(ref.shuffle_weight(torch.from_numpy(ws.copy()).view(torch.float8_e4m3fn)))
+    wb = rng.standard_normal((2, 32, 64)).astype(np.float32)
+    out["shuffle/w_bf16"] = t2n(torch.from_numpy(wb).to(torch.bfloat16))
+    out["shuffle/shuffled_bf16"] = t2n(ref.shuffle_weight(torch.from_numpy(wb).to(torch.bfloat16)))
     # ---------------------------------------------------------------- MoE config 0 (fp8 blockscale)
     for tag, (seed, M, D, I, E, k) in {"cfg0": (0, 32, 1024, 512, 8, 2),
                                         "cfg0_m7": (7, 7, 1024, 256, 8, 2)}.items():

@@ -106,6 +106,7 @@ class Reference:
                     "torch_moe_stage1", "torch_moe_stage2"])
         self._load(ns, "aiter/ops/topk.py", ["biased_grouped_topk_torch", "grouped_topk_torch"])
         self._load(ns, "op_tests/test_moe_sorting.py", ["moe_sorting_native"])
+        self._load(ns, "aiter/ops/shuffle.py", ["shuffle_weight"])
         # the torch reference of the sorted MXFP4 scale layout, kept under its own name
         run_torch = dict(torch=torch)
         self._load(run_torch, "op_tests/test_moe_sorting_mxfp4.py", ["run_torch"])

@@ -194,3 +194,17 @@ def test_mxfp4_quant_and_moe_scale_sort_match_reference(golden, case):
     r, c = mxfp4_sort.shuffle_index(rows, cols)
     real = ((r < s.shape[0]) & (c < s.shape[1])).reshape(rows, cols)
     assert np.array_equal(sh[real], g["shuffled_scale"][real])
+
+
+def test_unshuffle_weight_inverts_the_reference_shuffle(golden):
+    """aiter_b200.weights.unshuffle_weight undoes the reference's shuffle_weight
+    (aiter/ops/shuffle.py:7-27) for 1-byte (fp8) and 2-byte (bf16) weights."""
+    import torch
+    from aiter_b200.weights import unshuffle_weight
+    sh = torch.from_numpy(golden["shuffle/shuffled_fp8"]).view(torch.float8_e4m3fn)
+    back = unshuffle_weight(sh).view(torch.uint8).numpy()
+    assert np.array_equal(back, golden["shuffle/w_u8"])
+    shb = torch.from_numpy(golden["shuffle/shuffled_bf16"]).to(torch.bfloat16)
+    backb = unshuffle_weight(shb).float().numpy()
+    assert np.array_equal(backb, golden["shuffle/w_bf16"])
+    assert not np.array_equal(golden["shuffle/shuffled_fp8"], golden["shuffle/w_u8"])
