@@ -23,6 +23,8 @@
 // Stage 2 epilogue: multiply by the row's top-k weight and add into the bf16
 // output row of its token with vector red.global.add (the output is zeroed by
 // moe_sorting_fwd), i.e. the scatter-reduce over the k slots.
+#include <cstdlib>
+
 #include "sm100.cuh"
 
 namespace {
@@ -46,6 +48,7 @@ struct Cfg {
     static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
     static constexpr int CPT = BN_ / 2;  // accumulator columns per epilogue thread
     static constexpr uint32_t IDESC = sm100::idesc_e4m3_f32(BM, BN_);
+    static constexpr uint32_t IDESC64 = sm100::idesc_e4m3_f32(64, BN_);  // half tiles
     static constexpr int BAR_BYTES = 512;
     static constexpr int RED_BYTES = 2 * 256 * 4;                 // stage-1 row amax exchange
     static constexpr int SRING_BYTES = SRING * SRING_FLOATS * 4;  // block-scale ring
@@ -67,7 +70,17 @@ struct GemmArgs {
     void* out;              // stage 1: fp8 [rows_pad, I] sorted; stage 2: bf16 [M, D]
     float* out_scale;       // stage 1: [I/128][rows_pad]
     int M, N, n_tiles, num_kb, max_m_blocks, act, out_cols, E, rows_pad;
+    int half_tiles;  // 1: blocks whose rows 64.. are all padding run as M=64 tiles
 };
+
+// Half tile: sorted row 64 of the block is padding.  Within an expert's segment the
+// real rows come first and padding fills the block, so rows 64..127 are then all
+// padding and an M=64 MMA covers every real row.  The M=64 accumulator occupies the
+// lower 16 lanes of each TMEM subpartition (rows 16q..16q+15 -> lanes 32q..32q+15),
+// so the epilogue reads half the TMEM bytes of a full tile.
+__device__ __forceinline__ bool half_block(const GemmArgs& a, int m_blk) {
+    return a.half_tiles && (a.sorted_ids[m_blk * 128 + 64] & 0xFFFFFF) >= a.M;
+}
 
 // SiLU with the hardware exp2 and an approximate divide: the result is rounded to
 // bf16 right after, which hides their few-ulp fp32 error.
@@ -203,6 +216,7 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             int it = 0, acc_it = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+                const uint32_t idesc = half_block(args, tile / args.n_tiles) ? C::IDESC64 : C::IDESC;
                 for (int kb = 0; kb < args.num_kb; ++kb, ++it, ++acc_it) {
                     const int s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1;
@@ -217,7 +231,7 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                     const uint32_t d = tmem_base + as * BN_;
 #pragma unroll
                     for (int kk = 0; kk < BK / 32; ++kk)
-                        mma_f8f6f4(d, adesc + 2 * kk, bdesc + 2 * kk, C::IDESC, kk > 0 ? 1u : 0u);
+                        mma_f8f6f4(d, adesc + 2 * kk, bdesc + 2 * kk, idesc, kk > 0 ? 1u : 0u);
                     mma_commit(&empty[s]);
                     mma_commit(&tfull[as]);
                 }
@@ -276,7 +290,12 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         bool ok = true;
         for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++tcount) {
             const int m_blk = tile / args.n_tiles, n_blk = tile % args.n_tiles;
-            const int srow = m_blk * BM + row;
+            // half tile: this thread holds row 16q + lane%16 and the column half lane/16
+            // of its warp's columns (16x32bx2 loads); full tile: row 32q + lane
+            const bool half = half_block(args, m_blk);
+            const int hh = lane >> 4;
+            const int erow = half ? q * 16 + (lane & 15) : row;
+            const int srow = m_blk * BM + erow;
             // needed only after the K loop: issued now, they land meanwhile
             const int sid = args.sorted_ids[srow];
             const float wrow = STAGE == 2 ? args.sorted_w[srow] : 0.f;
@@ -289,7 +308,7 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                     break;
                 }
                 const float* se = sring + si * SRING_FLOATS;
-                const float sa = se[row], sbA = se[128], sbB = se[129];
+                const float sa = se[erow], sbA = se[128], sbB = se[129];
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&sempty[si]);
                 const float s0 = sa * (STAGE == 2 && h * CPT >= 128 ? sbB : sbA);
@@ -299,6 +318,34 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 if (!__all_sync(0xffffffffu, mbar_wait(&tfull[as], aph, abort_flag))) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t t = lane_base + as * BN_;
+                if (half) {
+                    // stage 1: gate columns 64h.. and up columns 128 + 64h..; stage 2:
+                    // columns 128h.. and 128h + 64..; 32 of each per thread half
+                    const uint32_t c0 = STAGE == 1 ? 64 * h : 128 * h;
+                    const uint32_t c1 = STAGE == 1 ? 128 + 64 * h : 128 * h + 64;
+                    tmem_ld16x32bx2_32(t + c0, &v[0]);
+                    tmem_ld16x32bx2_32(t + c1, &v[32]);
+                    tmem_wait_ld();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tempty[as]);
+                    const float sc1 = STAGE == 1 ? s1 : s0;
+                    if (kb == 0) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            acc[j] = v[j] * s0;
+                            acc[32 + j] = v[32 + j] * sc1;
+                        }
+                    } else {
+                        const uint64_t a2 = splat2(s0), b2 = splat2(sc1);
+#pragma unroll
+                        for (int j = 0; j < 32; j += 2) {
+                            fma2(&acc[j], &v[j], a2);
+                            fma2(&acc[32 + j], &v[32 + j], b2);
+                        }
+                    }
+                    continue;
+                }
                 // this thread's CPT columns in 64-column chunks; the slab is released
                 // as soon as the last chunk is in registers
 #pragma unroll
@@ -326,7 +373,66 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             if (!ok) break;
             const int tok = sid & 0xFFFFFF;
             const bool valid = tok < args.M;
-            if constexpr (STAGE == 1) {
+            if (STAGE == 1 && half) {
+                // 32 gate / up pairs -> 32 outputs: columns 64h + 32hh .. of the tile
+                float amax = 0.f;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const float y = act_fn(acc[j], args.act) * acc[32 + j];
+                    const float yb = __bfloat162float(__float2bfloat16_rn(y));
+                    acc[j] = yb;
+                    amax = fmaxf(amax, fabsf(yb));
+                }
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 16));  // the row's other half
+                float* rb = red + (tcount & 1) * 256;
+                if (hh == 0) rb[h * 128 + erow] = amax;
+                if (threadIdx.x == 128) bulk_wait_read0();
+                if (!epi_sync(&ebar[0], tcount & 1, abort_flag)) break;
+                amax = fmaxf(rb[erow], rb[128 + erow]);
+                float scale = amax / 448.0f;
+                if (scale == 0.f) scale = 1.0f;
+                const float rs = 1.0f / scale;
+                uint8_t* orow = out_tile + erow * 128;
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    uint32_t w[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int j = 16 * c + 4 * i;
+                        __nv_fp8x4_e4m3 p4(make_float4(acc[j] * rs, acc[j + 1] * rs, acc[j + 2] * rs, acc[j + 3] * rs));
+                        w[i] = *reinterpret_cast<uint32_t*>(&p4);
+                    }
+                    const int chunk = (4 * h + 2 * hh + c) ^ (erow & 7);
+                    *reinterpret_cast<uint4*>(orow + 16 * chunk) = make_uint4(w[0], w[1], w[2], w[3]);
+                }
+                if (h == 0 && hh == 0) args.out_scale[(int64_t)n_blk * args.rows_pad + srow] = scale;
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ebar[1]);
+                if (warp == 4) {
+                    if (!__all_sync(0xffffffffu, mbar_wait(&ebar[1], tcount & 1, abort_flag))) break;
+                    if (lane == 0) {
+                        tma_store_2d(&tmO, out_tile, n_blk * 128, m_blk * BM);
+                        bulk_commit();
+                    }
+                }
+            } else if (STAGE == 2 && half) {
+                if (valid) {
+                    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.out) + (int64_t)tok * args.out_cols +
+                                         n_blk * BN_ + 128 * h + 32 * hh;
+#pragma unroll
+                    for (int r = 0; r < 2; ++r) {
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            const int j = 32 * r + 8 * c;
+                            red_add_bf16x8(dst + 64 * r + 8 * c, pack_bf16x2(acc[j] * wrow, acc[j + 1] * wrow),
+                                           pack_bf16x2(acc[j + 2] * wrow, acc[j + 3] * wrow),
+                                           pack_bf16x2(acc[j + 4] * wrow, acc[j + 5] * wrow),
+                                           pack_bf16x2(acc[j + 6] * wrow, acc[j + 7] * wrow));
+                        }
+                    }
+                }
+            } else if constexpr (STAGE == 1) {
                 float amax = 0.f;
 #pragma unroll
                 for (int j = 0; j < 64; ++j) {
@@ -492,9 +598,20 @@ void check_sorted_operand(aiter_tensor_t* a, aiter_tensor_t* sc, int rows_pad, c
     AB_CHECK((int64_t)sc->numel_ == (a->shape[1] / 128) * (int64_t)rows_pad, sn, " must be [K/128, rows]");
 }
 
+// M=64 tiles for blocks whose rows 64.. are padding (half_block): on when
+// AITER_B200_MOE_HALF_TILES=1.  Off by default until timed on a B200.
+int half_tiles_enabled() {
+    static const int on = [] {
+        const char* e = std::getenv("AITER_B200_MOE_HALF_TILES");
+        return e != nullptr && e[0] == '1' ? 1 : 0;
+    }();
+    return on;
+}
+
 template <int STAGE, int BN_>
 void launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO, GemmArgs a, int dev,
             cudaStream_t st) {
+    a.half_tiles = half_tiles_enabled();
     a.n_tiles = STAGE == 1 ? a.n_tiles : a.N / BN_;
     const int tiles = a.max_m_blocks * a.n_tiles;
     if (tiles == 0) return;
