@@ -35,9 +35,26 @@ def gelu(x):
     return (0.5 * x * (1.0 + erf(x / sqrt(2.0)))).astype(F32)
 
 
-def stage1(a_deq, w1_deq, topk_ids, activation="silu", expert_list=None):
+def swiglu(gate, up, alpha=1.702, limit=7.0):
+    """`swiglu` (aiter/fused_moe.py:1473-1480): clamp(gate, max=7) * sigmoid(1.702 *
+    that) * (clamp(up, -7, 7) + 1), in fp32."""
+    g = np.minimum(np.asarray(gate, dtype=F32), F32(limit))
+    u = np.clip(np.asarray(up, dtype=F32), F32(-limit), F32(limit))
+    return (g * (F32(1.0) / (F32(1.0) + np.exp(-F32(alpha) * g))) * (u + F32(1.0))).astype(F32)
+
+
+def round_to(x, dtype):
+    """Round f32 values to bf16 or fp16 (RNE), returned as f32."""
+    if dtype == "fp16":
+        return np.asarray(x, dtype=F32).astype(np.float16).astype(F32)
+    return codecs.round_bf16(x)
+
+
+def stage1(a_deq, w1_deq, topk_ids, activation="silu", expert_list=None, topk_weights=None, dtype="bf16"):
     """a_deq: [M, D] f32, w1_deq: callable e -> [2I, D] f32 (or array [E,2I,D]).
-    Returns bf16-rounded f32 [M, k, I]."""
+    With `topk_weights` the GEMM output is multiplied by the token's top-k weight
+    before the activation (doweight, aiter/fused_moe.py:1569-1570).  Returns f32 [M, k, I]
+    rounded to `dtype` (bf16 or fp16)."""
     M, k = topk_ids.shape
     get_w = w1_deq if callable(w1_deq) else (lambda e: w1_deq[e])
     E = int(topk_ids.max()) + 1 if expert_list is None else None
@@ -49,6 +66,8 @@ def stage1(a_deq, w1_deq, topk_ids, activation="silu", expert_list=None):
             continue
         w = get_w(int(e))
         h = a_deq[tok] @ w.T
+        if topk_weights is not None:
+            h = (h * np.asarray(topk_weights, dtype=F32)[tok, slot][:, None]).astype(F32)
         if out is None:
             out = np.zeros((M, k, w.shape[0]), dtype=F32)
         out[tok, slot] = h
@@ -56,13 +75,17 @@ def stage1(a_deq, w1_deq, topk_ids, activation="silu", expert_list=None):
         raise ValueError("no routed tokens")
     inter = out.shape[-1] // 2
     gate, up = out[..., :inter], out[..., inter:]
-    act = silu(gate) if activation == "silu" else gelu(gate)
-    return codecs.round_bf16((act * up).astype(F32))
+    if activation == "swiglu":
+        y = swiglu(gate, up)
+    else:
+        y = (silu(gate) if activation == "silu" else gelu(gate)) * up
+    return round_to(np.asarray(y, dtype=F32), dtype)
 
 
-def stage2(a2_deq, w2_deq, topk_weights, topk_ids, expert_list=None):
+def stage2(a2_deq, w2_deq, topk_weights, topk_ids, expert_list=None, doweight=True, dtype="bf16"):
     """a2_deq: [M, k, I] f32; w2_deq: callable e -> [D, I] or array [E, D, I].
-    Returns bf16-rounded f32 [M, D]."""
+    Returns f32 [M, D] rounded to `dtype`; `doweight=False` when stage 1 applied the
+    top-k weights."""
     M, k = topk_ids.shape
     get_w = w2_deq if callable(w2_deq) else (lambda e: w2_deq[e])
     experts = np.unique(topk_ids) if expert_list is None else expert_list
@@ -76,21 +99,24 @@ def stage2(a2_deq, w2_deq, topk_weights, topk_ids, expert_list=None):
         if out is None:
             out = np.zeros((M, k, w.shape[0]), dtype=F32)
         out[tok, slot] = y
-    out = out * np.asarray(topk_weights, dtype=F32)[:, :, None]
-    return codecs.round_bf16(out.sum(axis=1, dtype=F32))
+    if doweight:
+        out = out * np.asarray(topk_weights, dtype=F32)[:, :, None]
+    return round_to(out.sum(axis=1, dtype=F32), dtype)
 
 
 def fused_moe_fp8_blockscale(hidden, w1_q, w1_s, w2_q, w2_s, topk_weights, topk_ids,
-                             activation="silu", return_intermediate=False):
-    """QuantType.per_1x128 end to end. hidden: [M, D] bf16 values (f32 array)."""
+                             activation="silu", return_intermediate=False, doweight_stage1=False, dtype="bf16"):
+    """QuantType.per_1x128 end to end. hidden: [M, D] bf16 (or fp16) values (f32 array);
+    `dtype` is the activation / intermediate / output type."""
     a1_q, a1_s = quant.per_1x128_quant(hidden)
     a1 = quant.dequant_1x128(a1_q, a1_s)
     w1 = lambda e: quant.dequant_128x128(w1_q[e:e + 1], w1_s[e:e + 1])[0]
     w2 = lambda e: quant.dequant_128x128(w2_q[e:e + 1], w2_s[e:e + 1])[0]
-    out1 = stage1(a1, w1, topk_ids, activation)
+    out1 = stage1(a1, w1, topk_ids, activation, topk_weights=topk_weights if doweight_stage1 else None,
+                  dtype=dtype)
     a2_q, a2_s = quant.per_1x128_quant(out1)
     a2 = quant.dequant_1x128(a2_q, a2_s)
-    out = stage2(a2, w2, topk_weights, topk_ids)
+    out = stage2(a2, w2, topk_weights, topk_ids, doweight=not doweight_stage1, dtype=dtype)
     if return_intermediate:
         return out, dict(a1_q=a1_q, a1_s=a1_s, out1=out1, a2_q=a2_q, a2_s=a2_s)
     return out
@@ -150,5 +176,6 @@ def fused_moe_fp8_blockscale_threaded(hidden, w1_q, w1_s, w2_q, w2_s, topk_weigh
 
     with ThreadPoolExecutor(threads) as ex:
         list(ex.map(s2, experts))
-    out = out * np.asarray(topk_weights, dtype=F32)[:, :, None]
-    return codecs.round_bf16(out.sum(axis=1, dtype=F32))
+    if doweight:
+        out = out * np.asarray(topk_weights, dtype=F32)[:, :, None]
+    return round_to(out.sum(axis=1, dtype=F32), dtype)

@@ -222,6 +222,12 @@ def main(root):
         case = moe_reference_fp8(ref, seed, M, D, I, E, k)
         for kk, v in case.items():
             out[f"moe_fp8/{tag}/{kk}"] = v
+    for tag, (seed, opts) in {"swiglu": (21, dict(activation=ActivationType.Swiglu)),
+                              "doweight": (22, dict(doweight_stage1=True)),
+                              "fp16": (23, dict(dtype=torch.float16))}.items():
+        case = moe_reference_fp8(ref, seed, 32, 1024, 512, 8, 2, **opts)
+        for kk, v in case.items():
+            out[f"moe_fp8_opts/{tag}/{kk}"] = v
     for tag, (seed, M, D, I, E, k) in {"cfg0": (11, 32, 1024, 512, 8, 2)}.items():
         case = moe_reference_a8w4(ref, seed, M, D, I, E, k)
         for kk, v in case.items():
@@ -242,23 +248,28 @@ def _float_case(seed, M, D, I, E, k, zipf=None):
     return hidden, tw, tid, w1, w2
 
 
-def moe_reference_fp8(ref, seed, M, D, I, E, k):
+def moe_reference_fp8(ref, seed, M, D, I, E, k, activation=ActivationType.Silu, doweight_stage1=False,
+                      dtype=torch.bfloat16):
+    """The reference's 2-stage pipeline (op_tests/test_moe_2stage.py:187-231) with its
+    options: activation, doweight_stage1 (top-k weight applied to the stage-1 GEMM output,
+    not in stage 2) and the activation / output dtype (bf16 or fp16)."""
     hidden, tw, tid, w1, w2 = _float_case(seed, M, D, I, E, k)
     fp8 = torch.float8_e4m3fn
     w1q, w1s = ref.weight_per_128x128_quant(torch.from_numpy(w1), fp8)
     w2q, w2s = ref.weight_per_128x128_quant(torch.from_numpy(w2), fp8)
-    h = torch.from_numpy(hidden).to(torch.bfloat16)
+    h = torch.from_numpy(hidden).to(dtype)
     a1q, a1s = ref.pertoken_quant(h.view(M, -1, 128), quant_dtype=fp8)
     a1q = a1q.view(M, D)
     a1s = a1s.squeeze(-1)
     tw_t, tid_t = torch.from_numpy(tw), torch.from_numpy(tid)
-    out1 = ref.torch_moe_stage1(a1q, w1q, w2q, tw_t, tid_t, dtype=torch.bfloat16,
-                                activation=ActivationType.Silu, quant_type=QuantType.per_128x128,
-                                a1_scale=a1s, w1_scale=w1s)
+    out1 = ref.torch_moe_stage1(a1q, w1q, w2q, tw_t, tid_t, dtype=dtype,
+                                activation=activation, quant_type=QuantType.per_128x128,
+                                a1_scale=a1s, w1_scale=w1s, doweight=doweight_stage1)
     a2q, a2s = ref.pertoken_quant(out1.view(M, -1, 128), quant_dtype=fp8)
     a2s = a2s.view(M, k, -1)
-    out2 = ref.torch_moe_stage2(a2q.view(M, k, -1), w1q, w2q, tw_t, tid_t, dtype=torch.bfloat16,
-                                quant_type=QuantType.per_128x128, w2_scale=w2s, a2_scale=a2s)
+    out2 = ref.torch_moe_stage2(a2q.view(M, k, -1), w1q, w2q, tw_t, tid_t, dtype=dtype,
+                                quant_type=QuantType.per_128x128, w2_scale=w2s, a2_scale=a2s,
+                                doweight=not doweight_stage1)
     return dict(w1q_sha=np.frombuffer(sha(t2n(w1q)).encode(), dtype=np.uint8),
                 w2q_sha=np.frombuffer(sha(t2n(w2q)).encode(), dtype=np.uint8),
                 w1s=t2n(w1s), w2s=t2n(w2s), a1q=t2n(a1q), a1s=t2n(a1s),

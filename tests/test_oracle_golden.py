@@ -208,3 +208,25 @@ def test_unshuffle_weight_inverts_the_reference_shuffle(golden):
     backb = unshuffle_weight(shb).float().numpy()
     assert np.array_equal(backb, golden["shuffle/w_bf16"])
     assert not np.array_equal(golden["shuffle/shuffled_fp8"], golden["shuffle/w_u8"])
+
+
+@pytest.mark.parametrize("tag,opts", [("swiglu", dict(activation="swiglu")),
+                                      ("doweight", dict(doweight_stage1=True)),
+                                      ("fp16", dict(dtype="fp16"))])
+def test_moe_fp8_options_match_reference(golden, tag, opts):
+    """fused_moe options of the reference pipeline: Swiglu (aiter/fused_moe.py:1473-1480),
+    doweight_stage1 (top-k weight on the stage-1 GEMM output, none in stage 2), and fp16
+    activations / intermediate / output."""
+    g = golden_group(golden, "moe_fp8_opts")[tag]
+    seed = {"swiglu": 21, "doweight": 22, "fp16": 23}[tag]
+    c = inputs.make_moe_case(seed, 32, 1024, 512, 8, 2)
+    assert np.array_equal(c["topk_ids"], g["topk_ids"])
+    hidden = c["hidden"]
+    if opts.get("dtype") == "fp16":
+        hidden = hidden.astype(np.float16).astype(np.float32)
+    out, st = moe.fused_moe_fp8_blockscale(hidden, c["w1_q"], c["w1_s"], c["w2_q"], c["w2_s"],
+                                           c["topk_weights"], c["topk_ids"], return_intermediate=True, **opts)
+    assert np.array_equal(st["a1_q"], g["a1q"])
+    np.testing.assert_allclose(st["out1"], g["out1"], rtol=1e-2, atol=1e-3)
+    np.testing.assert_allclose(out, g["out"], rtol=2e-2, atol=2e-2)
+    assert np.mean(np.abs(out - g["out"]) > 1e-3) < 0.02
