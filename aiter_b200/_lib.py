@@ -105,7 +105,8 @@ SIGNATURES = {
     "mxfp4_moe_sort_hip": [T, T, T, T, I64, I64],
     "fused_dynamic_mxfp4_quant_moe_sort_hip": [T, T, T, T, T, I64, I64, I64],
     "moe_stage1_fp8_blockscale": [T, T, T, T, T, T, T, T, T, I64, I64, I64],
-    "moe_stage2_fp8_blockscale": [T, T, T, T, T, T, T, T, T, I64],
+    "moe_stage1_fp8_blockscale_ex": [T, T, T, T, T, T, T, T, T, I64, I64, I64, OT, I64],
+    "moe_stage2_fp8_blockscale": [T, T, T, T, T, T, T, OT, T, I64],
 }
 
 _CT = {T: ctypes.POINTER(aiter_tensor_t), OT: ctypes.POINTER(aiter_tensor_t), I64: ctypes.c_int64,

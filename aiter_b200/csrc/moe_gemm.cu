@@ -71,6 +71,9 @@ struct GemmArgs {
     float* out_scale;       // stage 1: [I/128][rows_pad]
     int M, N, n_tiles, num_kb, max_m_blocks, act, out_cols, E, rows_pad;
     int half_tiles;  // 1: blocks whose rows 64.. are all padding run as M=64 tiles
+    int doweight;    // stage 1: multiply gate/up by the row's top-k weight (doweight_stage1)
+    int inter_f16;   // stage 1: round the intermediate to fp16 (else bf16) before the requant
+    int out_f16;     // stage 2: fp16 output (else bf16); sorted_w == nullptr: weight 1
 };
 
 // Half tile: sorted row 64 of the block is padding.  Within an expert's segment the
@@ -87,6 +90,24 @@ __device__ __forceinline__ bool half_block(const GemmArgs& a, int m_blk) {
 __device__ __forceinline__ float act_fn(float g, int act) {
     if (act == AITER_ACT_GELU) return 0.5f * g * (1.0f + erff(g * 0.70710678118654752f));
     return __fdividef(g, 1.0f + __expf(-g));
+}
+
+// Gated activation of a (gate, up) pair: act(gate) * up, or Swiglu
+// (aiter/fused_moe.py:1473-1480): min(gate, 7) * sigmoid(1.702 min(gate, 7)) *
+// (clamp(up, -7, 7) + 1).
+__device__ __forceinline__ float act_pair(float g, float u, int act) {
+    if (act == AITER_ACT_SWIGLU) {
+        g = fminf(g, 7.0f);
+        u = fminf(fmaxf(u, -7.0f), 7.0f);
+        return __fdividef(g, 1.0f + __expf(-1.702f * g)) * (u + 1.0f);
+    }
+    return act_fn(g, act) * u;
+}
+
+// The stage-1 intermediate is rounded to the activation dtype (bf16 or fp16) before
+// its fp8 requant, as the reference casts it (aiter/fused_moe.py:1585).
+__device__ __forceinline__ float round_inter(float y, int f16) {
+    return f16 ? __half2float(__float2half_rn(y)) : __bfloat162float(__float2bfloat16_rn(y));
 }
 
 // Barrier of the 8 epilogue warps: lane 0 of each warp arrives after the warp's
@@ -107,6 +128,29 @@ __device__ __forceinline__ void red_add_bf16x8(__nv_bfloat16* dst, uint32_t a, u
     asm volatile("red.global.add.noftz.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(dst), "r"(a), "r"(b), "r"(c),
                  "r"(d)
                  : "memory");
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ void red_add_f16x8(__half* dst, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("red.global.add.noftz.v4.f16x2 [%0], {%1, %2, %3, %4};" ::"l"(dst), "r"(a), "r"(b), "r"(c),
+                 "r"(d)
+                 : "memory");
+}
+
+// out[off .. off+8) += a[0..8) * w, as bf16 (default) or fp16 vector atomics.
+__device__ __forceinline__ void scatter_add8(void* out, int64_t off, const float* a, float w, int f16) {
+    if (f16) {
+        red_add_f16x8(reinterpret_cast<__half*>(out) + off, pack_f16x2(a[0] * w, a[1] * w),
+                      pack_f16x2(a[2] * w, a[3] * w), pack_f16x2(a[4] * w, a[5] * w), pack_f16x2(a[6] * w, a[7] * w));
+    } else {
+        red_add_bf16x8(reinterpret_cast<__nv_bfloat16*>(out) + off, pack_bf16x2(a[0] * w, a[1] * w),
+                       pack_bf16x2(a[2] * w, a[3] * w), pack_bf16x2(a[4] * w, a[5] * w),
+                       pack_bf16x2(a[6] * w, a[7] * w));
+    }
 }
 
 // STAGE 1: B tile = 128 gate rows + 128 up rows of w1 (BN must be 256), epilogue
@@ -298,7 +342,7 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             const int srow = m_blk * BM + erow;
             // needed only after the K loop: issued now, they land meanwhile
             const int sid = args.sorted_ids[srow];
-            const float wrow = STAGE == 2 ? args.sorted_w[srow] : 0.f;
+            const float wrow = (STAGE == 2 || args.doweight) && args.sorted_w != nullptr ? args.sorted_w[srow] : 1.f;
             float acc[CPT];
             float v[64];
             for (int kb = 0; kb < args.num_kb; ++kb, ++acc_it) {
@@ -378,8 +422,9 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 float amax = 0.f;
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
-                    const float y = act_fn(acc[j], args.act) * acc[32 + j];
-                    const float yb = __bfloat162float(__float2bfloat16_rn(y));
+                    const float g = args.doweight ? acc[j] * wrow : acc[j];
+                    const float u = args.doweight ? acc[32 + j] * wrow : acc[32 + j];
+                    const float yb = round_inter(act_pair(g, u, args.act), args.inter_f16);
                     acc[j] = yb;
                     amax = fmaxf(amax, fabsf(yb));
                 }
@@ -418,26 +463,21 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 }
             } else if (STAGE == 2 && half) {
                 if (valid) {
-                    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.out) + (int64_t)tok * args.out_cols +
-                                         n_blk * BN_ + 128 * h + 32 * hh;
+                    const int64_t base = (int64_t)tok * args.out_cols + n_blk * BN_ + 128 * h + 32 * hh;
 #pragma unroll
                     for (int r = 0; r < 2; ++r) {
 #pragma unroll
-                        for (int c = 0; c < 4; ++c) {
-                            const int j = 32 * r + 8 * c;
-                            red_add_bf16x8(dst + 64 * r + 8 * c, pack_bf16x2(acc[j] * wrow, acc[j + 1] * wrow),
-                                           pack_bf16x2(acc[j + 2] * wrow, acc[j + 3] * wrow),
-                                           pack_bf16x2(acc[j + 4] * wrow, acc[j + 5] * wrow),
-                                           pack_bf16x2(acc[j + 6] * wrow, acc[j + 7] * wrow));
-                        }
+                        for (int c = 0; c < 4; ++c)
+                            scatter_add8(args.out, base + 64 * r + 8 * c, &acc[32 * r + 8 * c], wrow, args.out_f16);
                     }
                 }
             } else if constexpr (STAGE == 1) {
                 float amax = 0.f;
 #pragma unroll
                 for (int j = 0; j < 64; ++j) {
-                    const float y = act_fn(acc[j], args.act) * acc[64 + j];
-                    const float yb = __bfloat162float(__float2bfloat16_rn(y));
+                    const float g = args.doweight ? acc[j] * wrow : acc[j];
+                    const float u = args.doweight ? acc[64 + j] * wrow : acc[64 + j];
+                    const float yb = round_inter(act_pair(g, u, args.act), args.inter_f16);
                     acc[j] = yb;
                     amax = fmaxf(amax, fabsf(yb));
                 }
@@ -481,16 +521,9 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 }
             } else {
                 if (valid) {
-                    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.out) + (int64_t)tok * args.out_cols +
-                                         n_blk * BN_ + CPT * h;
+                    const int64_t base = (int64_t)tok * args.out_cols + n_blk * BN_ + CPT * h;
 #pragma unroll
-                    for (int c = 0; c < CPT / 8; ++c) {
-                        const int j = 8 * c;
-                        red_add_bf16x8(dst + j, pack_bf16x2(acc[j] * wrow, acc[j + 1] * wrow),
-                                       pack_bf16x2(acc[j + 2] * wrow, acc[j + 3] * wrow),
-                                       pack_bf16x2(acc[j + 4] * wrow, acc[j + 5] * wrow),
-                                       pack_bf16x2(acc[j + 6] * wrow, acc[j + 7] * wrow));
-                    }
+                    for (int c = 0; c < CPT / 8; ++c) scatter_add8(args.out, base + 8 * c, &acc[8 * c], wrow, args.out_f16);
                 }
             }
         }
@@ -624,13 +657,14 @@ void launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& t
 
 }  // namespace
 
-AB_ENTRY(moe_stage1_fp8_blockscale,
-         (aiter_tensor_t * a1, aiter_tensor_t* a1_scale, aiter_tensor_t* w1, aiter_tensor_t* w1_scale,
-          aiter_tensor_t* sorted_token_ids, aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids,
-          aiter_tensor_t* out, aiter_tensor_t* out_scale, int64_t num_tokens, int64_t block_m, int64_t activation,
-          void* stream),
-         (a1, a1_scale, w1, w1_scale, sorted_token_ids, sorted_expert_ids, num_valid_ids, out, out_scale, num_tokens,
-          block_m, activation, stream)) {
+namespace {
+// Stage 1 with its options: sorted_weights given = doweight_stage1 (gate and up
+// multiplied by the row's top-k weight before the activation); inter_dtype = the
+// dtype the intermediate is rounded to before its fp8 requant (bf16 or fp16).
+void run_stage1(aiter_tensor_t* a1, aiter_tensor_t* a1_scale, aiter_tensor_t* w1, aiter_tensor_t* w1_scale,
+                aiter_tensor_t* sorted_token_ids, aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids,
+                aiter_tensor_t* out, aiter_tensor_t* out_scale, int64_t num_tokens, int64_t block_m,
+                int64_t activation, aiter_tensor_t* sorted_weights, int64_t inter_dtype, void* stream) {
     using namespace ab;
     Sorted c = check_sorting(sorted_token_ids, sorted_expert_ids, num_valid_ids, block_m);
     check_sorted_operand(a1, a1_scale, c.rows_pad, "a1", "a1_scale");
@@ -641,7 +675,9 @@ AB_ENTRY(moe_stage1_fp8_blockscale,
     need_contig(w1, "w1");
     need_contig(w1_scale, "w1_scale");
     need_ndim(w1, 3, "w1");
-    AB_CHECK(activation == AITER_ACT_SILU || activation == AITER_ACT_GELU, "activation must be Silu or Gelu");
+    AB_CHECK(activation == AITER_ACT_SILU || activation == AITER_ACT_GELU || activation == AITER_ACT_SWIGLU,
+             "activation must be Silu, Gelu or Swiglu");
+    AB_CHECK(inter_dtype == AITER_DTYPE_bf16 || inter_dtype == AITER_DTYPE_fp16, "inter_dtype must be bf16 or fp16");
     const int D = (int)a1->shape[1];
     const int E = (int)w1->shape[0], N = (int)w1->shape[1];
     AB_CHECK(w1->shape[2] == D, "w1 K dim must equal the activation width");
@@ -669,6 +705,13 @@ AB_ENTRY(moe_stage1_fp8_blockscale,
     a.out_cols = I;
     a.E = E;
     a.rows_pad = c.rows_pad;
+    if (sorted_weights) {
+        need_dtype(sorted_weights, AITER_DTYPE_fp32, "sorted_weights");
+        AB_CHECK(!sorted_weights || (int64_t)sorted_weights->numel_ >= c.rows_pad, "sorted_weights too small");
+        a.sorted_w = (const float*)sorted_weights->ptr;
+        a.doweight = 1;
+    }
+    a.inter_f16 = inter_dtype == AITER_DTYPE_fp16 ? 1 : 0;
     DeviceGuard dg(a1->device_id);
     CUtensorMap tmA, tmB;
     make_tmap_2d_u8(&tmA, a1->ptr, (uint64_t)c.rows_pad, D, 128, 128, true);
@@ -676,6 +719,29 @@ AB_ENTRY(moe_stage1_fp8_blockscale,
     CUtensorMap tmO;  // output tiles: 128 sorted rows x 128 fp8 columns
     make_tmap_2d_u8(&tmO, out->ptr, (uint64_t)c.rows_pad, I, 128, 128, true);
     launch<1, 256>(tmA, tmB, tmO, a, a1->device_id, as_stream(stream));
+}
+}  // namespace
+
+AB_ENTRY(moe_stage1_fp8_blockscale,
+         (aiter_tensor_t * a1, aiter_tensor_t* a1_scale, aiter_tensor_t* w1, aiter_tensor_t* w1_scale,
+          aiter_tensor_t* sorted_token_ids, aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids,
+          aiter_tensor_t* out, aiter_tensor_t* out_scale, int64_t num_tokens, int64_t block_m, int64_t activation,
+          void* stream),
+         (a1, a1_scale, w1, w1_scale, sorted_token_ids, sorted_expert_ids, num_valid_ids, out, out_scale, num_tokens,
+          block_m, activation, stream)) {
+    run_stage1(a1, a1_scale, w1, w1_scale, sorted_token_ids, sorted_expert_ids, num_valid_ids, out, out_scale,
+               num_tokens, block_m, activation, nullptr, AITER_DTYPE_bf16, stream);
+}
+
+AB_ENTRY(moe_stage1_fp8_blockscale_ex,
+         (aiter_tensor_t * a1, aiter_tensor_t* a1_scale, aiter_tensor_t* w1, aiter_tensor_t* w1_scale,
+          aiter_tensor_t* sorted_token_ids, aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids,
+          aiter_tensor_t* out, aiter_tensor_t* out_scale, int64_t num_tokens, int64_t block_m, int64_t activation,
+          aiter_tensor_t* sorted_weights, int64_t inter_dtype, void* stream),
+         (a1, a1_scale, w1, w1_scale, sorted_token_ids, sorted_expert_ids, num_valid_ids, out, out_scale, num_tokens,
+          block_m, activation, sorted_weights, inter_dtype, stream)) {
+    run_stage1(a1, a1_scale, w1, w1_scale, sorted_token_ids, sorted_expert_ids, num_valid_ids, out, out_scale,
+               num_tokens, block_m, activation, sorted_weights, inter_dtype, stream);
 }
 
 AB_ENTRY(moe_stage2_fp8_blockscale,
@@ -690,15 +756,14 @@ AB_ENTRY(moe_stage2_fp8_blockscale,
     need(w2, "w2");
     need(w2_scale, "w2_scale");
     need(out, "out");
-    need(sorted_weights, "sorted_weights");
     need_dtype(w2, AITER_DTYPE_fp8, "w2");
     need_dtype(w2_scale, AITER_DTYPE_fp32, "w2_scale");
-    need_dtype(out, AITER_DTYPE_bf16, "out");
-    need_dtype(sorted_weights, AITER_DTYPE_fp32, "sorted_weights");
+    AB_CHECK(out->dtype_ == AITER_DTYPE_bf16 || out->dtype_ == AITER_DTYPE_fp16, "out must be bf16 or fp16");
+    if (sorted_weights) need_dtype(sorted_weights, AITER_DTYPE_fp32, "sorted_weights");
     for (auto* t : {w2, w2_scale, out}) need_contig(t, "operand");
     need_ndim(w2, 3, "w2");
     need_ndim(out, 2, "out");
-    AB_CHECK((int64_t)sorted_weights->numel_ >= c.rows_pad, "sorted_weights too small");
+    AB_CHECK(!sorted_weights || (int64_t)sorted_weights->numel_ >= c.rows_pad, "sorted_weights too small");
     const int I = (int)a2->shape[1];
     const int E = (int)w2->shape[0], D = (int)w2->shape[1];
     const int M = (int)out->shape[0];
@@ -714,7 +779,8 @@ AB_ENTRY(moe_stage2_fp8_blockscale,
     a.num_valid = (const int*)num_valid_ids->ptr;
     a.a_scale = (const float*)a2_scale->ptr;
     a.b_scale = (const float*)w2_scale->ptr;
-    a.sorted_w = (const float*)sorted_weights->ptr;
+    a.sorted_w = sorted_weights ? (const float*)sorted_weights->ptr : nullptr;  // none: weight 1
+    a.out_f16 = out->dtype_ == AITER_DTYPE_fp16 ? 1 : 0;
     a.out = out->ptr;
     a.M = M;
     a.N = D;

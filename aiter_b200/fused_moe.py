@@ -10,7 +10,8 @@ libaiter_b200.so on the current stream (five launches when sorting takes its
 multi-CTA form), with no host synchronisation: moe_sorting_fwd (also zeroes the
 output) -> gather + 1x128 fp8 activation quant into sorted-row order -> stage-1
 grouped GEMM (gate/up, act, fp8 requant fused; sorted rows out) -> stage-2
-grouped GEMM (top-k weighted scatter-add into the output).  Weights are taken unshuffled
+grouped GEMM (top-k weighted scatter-add into the output).  Options: Silu / Gelu /
+Swiglu, doweight_stage1, bf16 or fp16 activations and output.  Weights are taken unshuffled
 ([E, 2I, D] / [E, D, I], K contiguous); AMD pre-shuffled weights
 (`is_shuffled=True`, aiter/ops/shuffle.py:7-27) are rejected.
 """
@@ -152,16 +153,12 @@ def _fused_moe_impl(hidden_states, w1, w2, topk_weight, topk_ids, expert_mask=No
     if dtype == dtypes.fp8:          # pre-quantised input: output defaults to bf16
         dtype = dtypes.bf16
     assert dtype in (dtypes.bf16, dtypes.fp16), f"Fused_moe unsupported out dtype: {dtype}"
-    if dtype != dtypes.bf16:
-        raise NotImplementedError("the B200 path writes bf16 outputs")
     if not is_g1u1:
         raise NotImplementedError("only gate+up (g1u1) MoE weights are supported")
-    if activation not in (ActivationType.Silu, ActivationType.Gelu):
+    if activation not in (ActivationType.Silu, ActivationType.Gelu, ActivationType.Swiglu):
         raise NotImplementedError(f"activation {activation} not supported")
     if bias1 is not None or bias2 is not None or hidden_pad or intermediate_pad:
         raise NotImplementedError("bias / padding variants are not supported")
-    if doweight_stage1:
-        raise NotImplementedError("doweight_stage1 is not supported")
     global_E = expert_mask.numel() if expert_mask is not None else E
     if quant_type == QuantType.per_1x32:
         # A8W4 as BASELINE defines it: fp8 1x128 activations, MXFP4 weights.  The
@@ -194,9 +191,13 @@ def _fused_moe_impl(hidden_states, w1, w2, topk_weight, topk_ids, expert_mask=No
             a1, a1s = moe_op.moe_gather_quant_1x128(hidden_states, pos, topk, rows)
         a2 = torch.empty((rows, inter_dim), dtype=dtypes.fp8, device=dev)
         a2s = torch.empty((inter_dim // 128, rows), dtype=dtypes.fp32, device=dev)
+        # doweight_stage1: the top-k weight scales the stage-1 GEMM output (before the
+        # activation) and stage 2 adds unweighted rows (torch_moe_stage1/2 `doweight`)
         moe_op.moe_stage1_fp8_blockscale(a1, a1s, w1, w1_scale, sorted_ids, sorted_expert_ids, num_valid_ids,
-                                         a2, a2s, M, block_m, activation)
+                                         a2, a2s, M, block_m, activation,
+                                         sorted_weights=sorted_weights if doweight_stage1 else None,
+                                         inter_dtype=dtype)
         moe_op.moe_stage2_fp8_blockscale(a2, a2s, w2, w2_scale, sorted_ids, sorted_expert_ids, num_valid_ids,
-                                         sorted_weights, moe_buf, block_m)
+                                         None if doweight_stage1 else sorted_weights, moe_buf, block_m)
         return moe_buf
     raise NotImplementedError(f"quant_type {quant_type} is not supported by the B200 path")

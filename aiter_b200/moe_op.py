@@ -186,17 +186,26 @@ def moe_gather_quant_1x128(hidden_states: Tensor, token_sorted_pos: Tensor, topk
 def moe_stage1_fp8_blockscale(a1: Tensor, a1_scale: Tensor, w1: Tensor, w1_scale: Tensor,
                               sorted_token_ids: Tensor, sorted_expert_ids: Tensor, num_valid_ids: Tensor,
                               out: Tensor, out_scale: Tensor, num_tokens: int, block_m: int = 128,
-                              activation=ActivationType.Silu) -> Tuple[Tensor, Tensor]:
-    """Gate/up grouped GEMM with fused act and 1x128 fp8 requant; sorted-row in and out."""
-    _lib.call("moe_stage1_fp8_blockscale", a1, a1_scale, w1, w1_scale, sorted_token_ids, sorted_expert_ids,
-              num_valid_ids, out, out_scale, num_tokens, block_m, int(activation))
+                              activation=ActivationType.Silu, sorted_weights: Optional[Tensor] = None,
+                              inter_dtype=dtypes.bf16) -> Tuple[Tensor, Tensor]:
+    """Gate/up grouped GEMM with fused act and 1x128 fp8 requant; sorted-row in and out.
+    `sorted_weights` given: doweight_stage1 (gate/up scaled by the top-k weight before
+    the activation); `inter_dtype`: bf16 or fp16 rounding of the intermediate."""
+    if sorted_weights is None and inter_dtype == dtypes.bf16:
+        _lib.call("moe_stage1_fp8_blockscale", a1, a1_scale, w1, w1_scale, sorted_token_ids, sorted_expert_ids,
+                  num_valid_ids, out, out_scale, num_tokens, block_m, int(activation))
+    else:
+        _lib.call("moe_stage1_fp8_blockscale_ex", a1, a1_scale, w1, w1_scale, sorted_token_ids,
+                  sorted_expert_ids, num_valid_ids, out, out_scale, num_tokens, block_m, int(activation),
+                  sorted_weights, _lib.dtype_code(inter_dtype))
     return out, out_scale
 
 
 def moe_stage2_fp8_blockscale(a2: Tensor, a2_scale: Tensor, w2: Tensor, w2_scale: Tensor,
                               sorted_token_ids: Tensor, sorted_expert_ids: Tensor, num_valid_ids: Tensor,
-                              sorted_weights: Tensor, out: Tensor, block_m: int = 128) -> Tensor:
-    """Down grouped GEMM; adds the top-k weighted rows into out [M, D] (bf16)."""
+                              sorted_weights: Optional[Tensor], out: Tensor, block_m: int = 128) -> Tensor:
+    """Down grouped GEMM; adds the top-k weighted rows into out [M, D] (bf16 or fp16);
+    `sorted_weights` None: unweighted (the weights were applied in stage 1)."""
     _lib.call("moe_stage2_fp8_blockscale", a2, a2_scale, w2, w2_scale, sorted_token_ids, sorted_expert_ids,
               num_valid_ids, sorted_weights, out, block_m)
     return out

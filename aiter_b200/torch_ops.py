@@ -35,8 +35,10 @@ def fused_moe_(hidden_states: Tensor, w1: Tensor, w2: Tensor, topk_weight: Tenso
 def _fused_moe_fake(hidden_states, w1, w2, topk_weight, topk_ids, expert_mask=None, activation=0, quant_type=0,
                     doweight_stage1=False, w1_scale=None, w2_scale=None, a1_scale=None, a2_scale=None,
                     num_local_tokens=None, moe_sorting_dispatch_policy=0):
-    # output [M, model_dim] bf16 (w2 is [E, model_dim, inter_dim] or its fp4x2 packing)
-    return hidden_states.new_empty((topk_ids.shape[0], w2.shape[1]), dtype=torch.bfloat16)
+    # output [M, model_dim] in the activation dtype: fp16 for fp16 inputs, else bf16
+    # (w2 is [E, model_dim, inter_dim] or its fp4x2 packing)
+    out_dtype = torch.float16 if hidden_states.dtype == torch.float16 else torch.bfloat16
+    return hidden_states.new_empty((topk_ids.shape[0], w2.shape[1]), dtype=out_dtype)
 
 
 @torch.library.custom_op(f"{NS}::topk_softmax",

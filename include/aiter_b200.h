@@ -206,21 +206,35 @@ int mxfp4_to_fp8_blockscale(aiter_tensor_t* w_fp4, aiter_tensor_t* w_scale, aite
  * num_valid_ids from moe_sorting_fwd with unit_size == block_m (128).
  * Writes, for every real sorted row r, out[r, :] = fp8(act(gate) * up / s) and
  * out_scale[:, r] = s per 128 columns (1x128 requant, s = amax/448); padding rows
- * are not written.  num_tokens = M (the padding id).  activation: AITER_ACT_SILU
- * or AITER_ACT_GELU. */
+ * are not written.  num_tokens = M (the padding id).  activation: AITER_ACT_SILU,
+ * AITER_ACT_GELU or AITER_ACT_SWIGLU (aiter/fused_moe.py:1473-1480).  The
+ * intermediate is rounded to bf16 before the requant. */
 int moe_stage1_fp8_blockscale(aiter_tensor_t* a1, aiter_tensor_t* a1_scale, aiter_tensor_t* w1,
                               aiter_tensor_t* w1_scale, aiter_tensor_t* sorted_token_ids,
                               aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids,
                               aiter_tensor_t* out, aiter_tensor_t* out_scale, int64_t num_tokens,
                               int64_t block_m, int64_t activation, void* stream);
+/* Stage 1 with the fused_moe options of the reference's stage-1 path
+ * (torch_moe_stage1, aiter/fused_moe.py:1483-1585): sorted_weights non-NULL =
+ * doweight_stage1 (gate and up of row r multiplied by sorted_weights[r] before the
+ * activation; pass NULL weights to stage 2 then); inter_dtype = AITER_DTYPE_bf16 or
+ * AITER_DTYPE_fp16, the dtype the intermediate is rounded to before its fp8 requant
+ * (the activation dtype of the call). */
+int moe_stage1_fp8_blockscale_ex(aiter_tensor_t* a1, aiter_tensor_t* a1_scale, aiter_tensor_t* w1,
+                                 aiter_tensor_t* w1_scale, aiter_tensor_t* sorted_token_ids,
+                                 aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids,
+                                 aiter_tensor_t* out, aiter_tensor_t* out_scale, int64_t num_tokens,
+                                 int64_t block_m, int64_t activation, aiter_tensor_t* sorted_weights,
+                                 int64_t inter_dtype, void* stream);
 
 /* Stage 2: replaces ck_moe_stage2_fwd (aiter/ops/moe_op.py:578-615; CK template
  * gemm_moe_ck2stages_common_blockscale.cuh:330-470).
  * a2 [rows, I] fp8 + a2_scale [I/128, rows] f32 (stage-1 output, sorted rows);
  * w2 [E, D, I] fp8 + w2_scale [E, D/128, I/128] f32.  Adds
  * sorted_weights[r] * (a2[r] @ w2[e]^T) of every real sorted row r into
- * out[token(r)] (bf16 [M, D], zeroed by moe_sorting_fwd): the top-k weighted
- * scatter-reduce back to token order. */
+ * out[token(r)] (bf16 or fp16 [M, D], zeroed by moe_sorting_fwd): the top-k weighted
+ * scatter-reduce back to token order.  sorted_weights NULL: weight 1 (after
+ * doweight_stage1). */
 int moe_stage2_fp8_blockscale(aiter_tensor_t* a2, aiter_tensor_t* a2_scale, aiter_tensor_t* w2,
                               aiter_tensor_t* w2_scale, aiter_tensor_t* sorted_token_ids,
                               aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids,
