@@ -147,6 +147,8 @@ def lib():
                                                                 ctypes.POINTER(aiter_tensor_t), c64, vp]),
                            ("custom_ar_allreduce_rmsnorm", [c64] + [ctypes.POINTER(aiter_tensor_t)] * 5 +
                             [ctypes.c_float, ctypes.POINTER(aiter_tensor_t), vp]),
+                           ("custom_ar_allreduce_rmsnorm_ex", [c64] + [ctypes.POINTER(aiter_tensor_t)] * 5 +
+                            [ctypes.c_float, ctypes.POINTER(aiter_tensor_t), c64, vp]),
                            ("custom_ar_dispose", [c64]), ("custom_ar_device_error", [ctypes.c_int])):
             fn = getattr(L, name)
             fn.restype = ctypes.c_int

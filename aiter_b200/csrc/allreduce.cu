@@ -290,7 +290,7 @@ __global__ void __launch_bounds__(kThreads)
 allreduce_rmsnorm_kernel(Peers P, int rank, int parity, const uint4* __restrict__ in,
                          const uint4* __restrict__ res_in, uint4* __restrict__ res_out, void* __restrict__ out,
                          float* __restrict__ scale_out, const uint4* __restrict__ weight, int64_t rows, int ppr,
-                         float eps, int end_barrier) {
+                         float eps, int end_barrier, int two_shot) {
     constexpr int MAXP = 4;  // packs of 8 per thread: hidden <= 4 * 8 * kThreads
     __shared__ uint32_t s_epoch;
     __shared__ float s_red[kThreads / 32];
@@ -309,6 +309,26 @@ allreduce_rmsnorm_kernel(Peers P, int rank, int parity, const uint4* __restrict_
         for (int64_t row = blockIdx.x; row < rows; row += gridDim.x)
             for (int p = threadIdx.x; p < ppr; p += blockDim.x) mine[row * ppr + p] = in[row * ppr + p];
     if (!block_barrier(P, rank, W, 0, epoch)) return;
+    // the allreduce of pack i: every rank's staged pack summed in rank order, bf16
+    auto sum_pack = [&](int64_t i) -> uint4 {
+        uint4 v[W];
+#pragma unroll
+        for (int r = 0; r < W; ++r) v[r] = ld_cg(bufs[r] + i);
+        float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+        for (int r = 0; r < W; ++r) acc8(a, v[r]);
+        return pack8(a);
+    };
+    // two-shot: row b + k * grid belongs to rank k % W, which reduces it in place in its
+    // staging buffer (only it reads that row of its buffer before the next barrier);
+    // after the barrier every rank takes the reduced row from its owner
+    if (two_shot) {
+        for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+            if ((row / gridDim.x) % W != rank) continue;
+            for (int p = threadIdx.x; p < ppr; p += blockDim.x) mine[row * ppr + p] = sum_pack(row * ppr + p);
+        }
+        if (!block_barrier(P, rank, W, 1, epoch)) return;
+    }
     const float inv_n = 1.0f / (float)(ppr * 8);
     auto block_sum = [&](float v, bool is_max) -> float {
 #pragma unroll
@@ -331,13 +351,8 @@ allreduce_rmsnorm_kernel(Peers P, int rank, int parity, const uint4* __restrict_
             const int p = threadIdx.x + j * blockDim.x;
             if (p < ppr) {
                 const int64_t i = row * ppr + p;
-                uint4 v[W];
-#pragma unroll
-                for (int r = 0; r < W; ++r) v[r] = ld_cg(bufs[r] + i);
-                float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-#pragma unroll
-                for (int r = 0; r < W; ++r) acc8(a, v[r]);
-                const uint4 ar = pack8(a);  // the allreduce result, rounded to bf16
+                // the allreduce result, rounded to bf16
+                const uint4 ar = two_shot ? ld_cg(bufs[(row / gridDim.x) % W] + i) : sum_pack(i);
                 const uint4 rs = res_in[i];
                 const __nv_bfloat162* ah = reinterpret_cast<const __nv_bfloat162*>(&ar);
                 const __nv_bfloat162* rh = reinterpret_cast<const __nv_bfloat162*>(&rs);
@@ -676,10 +691,10 @@ AB_ENTRY(custom_ar_gemm_all_reduce,
 
 // allreduce(inp) + res_inp -> res_out, RMSNorm(res_out) * w -> out (bf16), or with
 // `out` fp8 and `scale_out` [rows] f32: the per-row fp8 quant of the normalised row.
-AB_ENTRY(custom_ar_allreduce_rmsnorm,
-         (int64_t ctx, aiter_tensor_t* inp, aiter_tensor_t* res_inp, aiter_tensor_t* res_out, aiter_tensor_t* out,
-          aiter_tensor_t* weight, float eps, aiter_tensor_t* scale_out, void* stream),
-         (ctx, inp, res_inp, res_out, out, weight, eps, scale_out, stream)) {
+namespace {
+void run_allreduce_rmsnorm(int64_t ctx, aiter_tensor_t* inp, aiter_tensor_t* res_inp, aiter_tensor_t* res_out,
+                           aiter_tensor_t* out, aiter_tensor_t* weight, float eps, aiter_tensor_t* scale_out,
+                           int64_t force_two_shot, void* stream) {
     using namespace ab;
     Ctx* c = as_ctx(ctx);
     AB_CHECK(c->ready, "custom_ar_open_peers has not been called");
@@ -717,16 +732,20 @@ AB_ENTRY(custom_ar_allreduce_rmsnorm,
     AB_CUDA(cudaStreamIsCapturing(st, &cap));
     const int endb = cap == cudaStreamCaptureStatusNone ? 0 : 1;
     const uint4* src = (const uint4*)inp->ptr;
+    // one-shot reads (W-1) x the rows over NVLink, two-shot 2 (W-1)/W x plus a barrier:
+    // the size cut-over of the plain allreduce
+    const int64_t one_shot_max = c->world == 2 ? INT64_MAX : (c->world <= 4 ? (2 << 20) : (1 << 20));
+    const int tw = force_two_shot > 0 ? 1 : (force_two_shot == 0 ? 0 : ((int64_t)bytes > one_shot_max ? 1 : 0));
 #define AB_ARRMS(WW)                                                                                              \
     do {                                                                                                          \
         if (quant)                                                                                                \
             allreduce_rmsnorm_kernel<WW, true><<<grid, kThreads, 0, st>>>(                                        \
                 c->peers, c->rank, parity, src, (const uint4*)res_inp->ptr, (uint4*)res_out->ptr, out->ptr,       \
-                (float*)scale_out->ptr, (const uint4*)weight->ptr, rows, ppr, eps, endb);                         \
+                (float*)scale_out->ptr, (const uint4*)weight->ptr, rows, ppr, eps, endb, tw);                     \
         else                                                                                                      \
             allreduce_rmsnorm_kernel<WW, false><<<grid, kThreads, 0, st>>>(                                       \
                 c->peers, c->rank, parity, src, (const uint4*)res_inp->ptr, (uint4*)res_out->ptr, out->ptr,       \
-                nullptr, (const uint4*)weight->ptr, rows, ppr, eps, endb);                                        \
+                nullptr, (const uint4*)weight->ptr, rows, ppr, eps, endb, tw);                                    \
     } while (0)
     switch (c->world) {
         case 2: AB_ARRMS(2); break;
@@ -739,6 +758,24 @@ AB_ENTRY(custom_ar_allreduce_rmsnorm,
     }
 #undef AB_ARRMS
     check_launch("custom_ar_allreduce_rmsnorm");
+}
+}  // namespace
+
+AB_ENTRY(custom_ar_allreduce_rmsnorm,
+         (int64_t ctx, aiter_tensor_t* inp, aiter_tensor_t* res_inp, aiter_tensor_t* res_out, aiter_tensor_t* out,
+          aiter_tensor_t* weight, float eps, aiter_tensor_t* scale_out, void* stream),
+         (ctx, inp, res_inp, res_out, out, weight, eps, scale_out, stream)) {
+    run_allreduce_rmsnorm(ctx, inp, res_inp, res_out, out, weight, eps, scale_out, 0, stream);
+}
+
+// The same with the one-/two-shot choice: force_two_shot 1 = two-shot (rows reduced
+// by an owner rank, every rank takes them from it and normalises locally), 0 =
+// one-shot, negative = by size as custom_ar_all_reduce.  Both give the same bits.
+AB_ENTRY(custom_ar_allreduce_rmsnorm_ex,
+         (int64_t ctx, aiter_tensor_t* inp, aiter_tensor_t* res_inp, aiter_tensor_t* res_out, aiter_tensor_t* out,
+          aiter_tensor_t* weight, float eps, aiter_tensor_t* scale_out, int64_t force_two_shot, void* stream),
+         (ctx, inp, res_inp, res_out, out, weight, eps, scale_out, force_two_shot, stream)) {
+    run_allreduce_rmsnorm(ctx, inp, res_inp, res_out, out, weight, eps, scale_out, force_two_shot, stream);
 }
 
 // GEMM + allreduce in one kernel: y = allreduce_over_ranks(A @ W^T) with the GEMM

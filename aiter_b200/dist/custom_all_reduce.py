@@ -147,12 +147,15 @@ class CustomAllreduce:
 
     def fused_ar_rms(self, inp: torch.Tensor, res_inp: torch.Tensor, *, res_out: torch.Tensor = None,
                      out: torch.Tensor = None, scale_out: torch.Tensor = None, w: torch.Tensor, eps: float,
-                     registered: bool = False, use_1stage: bool = False, post_per_token_quant: bool = False):
+                     registered: bool = False, use_1stage: bool = False, post_per_token_quant: bool = False,
+                     two_shot=None):
         """allreduce(inp) + res_inp -> res_out and RMSNorm(res_out) * w -> out in one
         kernel (custom_all_reduce.py:603-660 in the reference).  With
         `post_per_token_quant` the output is fp8 with one fp32 scale per row.
-        Returns (out, res_out) or (out, res_out, scale_out).  `registered` and
-        `use_1stage` are accepted for the reference's signature; the kernel is one-shot."""
+        Returns (out, res_out) or (out, res_out, scale_out).  `registered` is accepted
+        for the reference's signature.  The kernel is one-shot unless `two_shot` is
+        True (owner ranks reduce the rows, every rank normalises them locally; same bits)
+        or False/True is chosen by size with two_shot="auto"."""
         if res_out is None:
             res_out = torch.empty_like(inp)
         if post_per_token_quant:
@@ -165,8 +168,13 @@ class CustomAllreduce:
         ts = [_lib.to_aiter(t) for t in (inp, res_inp, res_out, out, w)]
         sc = _lib.to_aiter(scale_out) if post_per_token_quant else None
         st = _lib.current_stream_ptr(self.device.index)
-        ret = self._L.custom_ar_allreduce_rmsnorm(self._ctx, *[ctypes.byref(t) for t in ts], float(eps),
-                                                  ctypes.byref(sc) if sc is not None else None, st)
+        scp = ctypes.byref(sc) if sc is not None else None
+        if two_shot is None or use_1stage:
+            ret = self._L.custom_ar_allreduce_rmsnorm(self._ctx, *[ctypes.byref(t) for t in ts], float(eps), scp, st)
+        else:
+            force = -1 if two_shot == "auto" else (1 if two_shot else 0)
+            ret = self._L.custom_ar_allreduce_rmsnorm_ex(self._ctx, *[ctypes.byref(t) for t in ts], float(eps), scp,
+                                                         force, st)
         if ret:
             _lib.check_status("custom_ar_allreduce_rmsnorm", ret)
         return (out, res_out, scale_out) if post_per_token_quant else (out, res_out)

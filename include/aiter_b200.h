@@ -305,6 +305,14 @@ int custom_ar_gemm_all_reduce_fused(int64_t ctx, aiter_tensor_t* a, aiter_tensor
 int custom_ar_allreduce_rmsnorm(int64_t ctx, aiter_tensor_t* inp, aiter_tensor_t* res_inp, aiter_tensor_t* res_out,
                                 aiter_tensor_t* out, aiter_tensor_t* weight, float eps, aiter_tensor_t* scale_out,
                                 void* stream);
+/* The same with the one-/two-shot choice (the reference's use_1stage): force_two_shot
+ * 1 = two-shot (each row reduced by one owner rank, every rank takes the reduced bf16
+ * row from it and adds the residual and normalises locally, as the reference's
+ * two-stage kernels do, csrc/include/custom_all_reduce.cuh:1187-1250), 0 = one-shot,
+ * negative = by size.  Same bits either way. */
+int custom_ar_allreduce_rmsnorm_ex(int64_t ctx, aiter_tensor_t* inp, aiter_tensor_t* res_inp,
+                                   aiter_tensor_t* res_out, aiter_tensor_t* out, aiter_tensor_t* weight,
+                                   float eps, aiter_tensor_t* scale_out, int64_t force_two_shot, void* stream);
 int custom_ar_dispose(int64_t ctx);
 /* Error word of the allreduce barriers (1 = a peer did not arrive within 2 s). */
 int custom_ar_device_error(int clear);

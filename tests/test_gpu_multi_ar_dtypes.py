@@ -4,6 +4,7 @@ allreduce (custom_ar_all_reduce_fp8), one process per GPU.  Skipped with fewer t
 AITER_B200_TEST_UNRUN=1.
 
 * fp16 / fp32: bit-exact against the fp32 rank-order sum (oracle), one- and two-shot;
+* fused allreduce + RMSNorm (+ fp8 quant): the two-shot form returns the one-shot bits;
 * open_fp8_quant with fp16: every rank's output bit-exact against the restatement of
   the reference's allReduceQuantFp8 (oracle/allreduce.py), including group sizes
   below 128 and a message whose pack count leaves a remainder for the last rank;
@@ -66,6 +67,22 @@ def _worker(rank, world, port):
         want = allreduce_fp8_quant([x.numpy() for x in xs])[rank]
         got = y.cpu().numpy()
         assert got.dtype == npd and np.array_equal(got, want), (n, int((got != want).sum()))
+    # fused allreduce + residual + RMSNorm: two-shot (owner ranks reduce the rows, every
+    # rank normalises locally) returns the one-shot kernel's bits
+    for rows, hidden in ((1024, 4096), (333, 7168), (8, 16384)):
+        g = torch.Generator().manual_seed(rows)
+        xs = [torch.randn(rows, hidden, generator=g).to(torch.bfloat16) for _ in range(world)]
+        res = torch.randn(rows, hidden, generator=g).to(torch.bfloat16).to(dev)
+        wt = (torch.rand(hidden, generator=g) + 0.5).to(torch.bfloat16).to(dev)
+        x = xs[rank].to(dev)
+        o1, r1 = ca.fused_ar_rms(x, res, w=wt, eps=1e-6)
+        o2, r2 = ca.fused_ar_rms(x, res, w=wt, eps=1e-6, two_shot=True)
+        q1, _, s1 = ca.fused_ar_rms(x, res, w=wt, eps=1e-6, post_per_token_quant=True)
+        q2, _, s2 = ca.fused_ar_rms(x, res, w=wt, eps=1e-6, post_per_token_quant=True, two_shot=True)
+        torch.cuda.synchronize()
+        assert _lib.lib().custom_ar_device_error(1) == 0
+        assert torch.equal(r1, r2) and torch.equal(o1, o2), (rows, hidden)
+        assert torch.equal(q1.view(torch.uint8), q2.view(torch.uint8)) and torch.equal(s1, s2), (rows, hidden)
     # the flag is ignored for bf16 and for fp16 below 128 * 2048 elements
     for dtype, n in ((torch.bfloat16, 128 * 2048), (torch.float16, 4096)):
         xs = _inputs(n, world, 70, dtype)
