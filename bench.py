@@ -56,9 +56,10 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--fused-gemm-ar", action="store_true",
                    help="gemm_ar mode: also time the one-kernel GEMM + allreduce (custom_ar_gemm_all_reduce_fused)")
-    p.add_argument("--mode", default="moe", choices=["moe", "moe_sweep", "a8w4", "tp_moe", "gemm_ar"],
+    p.add_argument("--mode", default="moe", choices=["moe", "moe_sweep", "a8w4", "tp_moe", "gemm_ar", "routing"],
                    help="moe: config 1 at --M (N>1: data-parallel replicas); moe_sweep: config 1 token sweep "
-                        "on one GPU; a8w4: config 2 on one GPU; tp_moe: config 3; gemm_ar: config 4")
+                        "on one GPU; a8w4: config 2 on one GPU; tp_moe: config 3; gemm_ar: config 4; "
+                        "routing: topk_softmax and moe_sorting alone (achieved HBM GB/s)")
     return p.parse_args()
 
 
@@ -726,6 +727,61 @@ def run_a8w4(args, rank, world, local):
             "peaks": {"fp8_tflops": fp8_peak, "hbm_gbs": pk["hbm_gbs"], "source": src}, "sweep": rows}
 
 
+def run_routing(args, rank, world, local):
+    """topk_softmax and moe_sorting_fwd alone at the config-1 (E=128) and config-2 (E=256,
+    Zipf-skewed) routing shapes over the token sweep: CUDA-event time per call (inputs
+    and outputs far smaller than L2 except the zeroed output, so the figures are
+    launch- and latency-bound at small M) and achieved bytes / s against the measured HBM
+    peak.  Algorithmic bytes: topk_softmax M*E*4 (fp32 logits) + M*k*12 (weights, ids,
+    token-expert indices); sorting M*k*8 read + rows*8 written (ids, weights) + block ids
+    + M*D*2 of output zeroing."""
+    from aiter_b200 import moe_op
+    pk, src = peaks()
+    dev = torch.device("cuda", local)
+    g = torch.Generator(device=dev).manual_seed(5)
+    rows_out = []
+    for E_, zipf in ((128, False), (256, True)):
+        bias = None
+        if zipf:
+            perm = torch.randperm(E_, generator=torch.Generator().manual_seed(7)) + 1
+            bias = torch.log((1.0 / perm.double() ** 1.1) / (1.0 / perm.double() ** 1.1).sum()).float().to(dev)
+        for M in (1, 16, 128, 1024, 4096, 16384):
+            logits = torch.randn(M, E_, device=dev, generator=g)
+            if bias is not None:
+                logits = logits + bias
+            tw = torch.empty(M, TOPK, dtype=torch.float32, device=dev)
+            tid = torch.empty(M, TOPK, dtype=torch.int32, device=dev)
+            tei = torch.empty(M, TOPK, dtype=torch.int32, device=dev)
+            B = 128
+            max_pad = M * TOPK + E_ * B - TOPK
+            sid = torch.empty(max_pad, dtype=torch.int32, device=dev)
+            sw = torch.empty(max_pad, dtype=torch.float32, device=dev)
+            seid = torch.empty((max_pad + B - 1) // B, dtype=torch.int32, device=dev)
+            nv = torch.empty(2, dtype=torch.int32, device=dev)
+            out = torch.empty(M, D, dtype=torch.bfloat16, device=dev)
+            ws_n = moe_op.moe_sorting_get_workspace_size(M, E_, TOPK, 0)
+            ws = torch.empty(max(ws_n, 1), dtype=torch.uint8, device=dev)
+            topk = lambda: moe_op.topk_softmax(tw, tid, tei, logits, True)
+            sort = lambda: moe_op.moe_sorting_fwd(tid, tw, sid, sw, seid, nv, out, E_, B, None, None, 0,
+                                                  ws if ws_n else None, None)
+            us_t = 1e3 * _time_loop(topk, args.steps, args.warmup, world)
+            us_s = 1e3 * _time_loop(sort, args.steps, args.warmup, world)
+            bytes_t = M * E_ * 4 + M * TOPK * 12
+            bytes_s = M * TOPK * 8 + max_pad * 8 + seid.numel() * 4 + M * D * 2
+            gbs_t, gbs_s = bytes_t / (us_t * 1e-6) / 1e9, bytes_s / (us_s * 1e-6) / 1e9
+            rows_out.append({"E": E_, "routing": "zipf s=1.1" if zipf else "uniform", "M": M,
+                             "topk_softmax_us": round(us_t, 2), "topk_softmax_GBs": round(gbs_t, 1),
+                             "topk_softmax_hbm_frac": round(gbs_t / pk["hbm_gbs"], 4),
+                             "sorting_us": round(us_s, 2), "sorting_GBs": round(gbs_s, 1),
+                             "sorting_hbm_frac": round(gbs_s / pk["hbm_gbs"], 4),
+                             "sorting_launches": 1 if ws_n == 0 else 2})
+    return {"metric": "routing and sorting kernel time and HBM GB/s", "mode": "routing", "unit": "us",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": False,
+            "dtype": "fp32 logits, i32 ids", "data": "synthetic N(0,1) logits (+ Zipf(1.1) bias for E=256)",
+            "config": {"workload": "routing of BASELINE configs 1 and 2", "topk": TOPK, "block_m": 128,
+                       "hidden_zeroed": D}, "peaks": {"hbm_gbs": pk["hbm_gbs"], "source": src}, "sweep": rows_out}
+
+
 def run_gemm_ar(args, rank, world, local):
     """Config 4: y = allreduce(A @ B), A [M, 8192/TP], B [8192/TP, 4096] bf16 per rank:
     the tcgen05 GEMM writing into the IPC allreduce's staging buffer vs cuBLAS
@@ -781,9 +837,9 @@ def main():
     args = parse()
     rank, world, local = dist_setup(args.gpus)
     try:
-        if args.mode in ("tp_moe", "gemm_ar", "moe_sweep", "a8w4"):
+        if args.mode in ("tp_moe", "gemm_ar", "moe_sweep", "a8w4", "routing"):
             res = {"tp_moe": run_tp_moe, "gemm_ar": run_gemm_ar, "moe_sweep": run_moe_sweep,
-                   "a8w4": run_a8w4}[args.mode](
+                   "a8w4": run_a8w4, "routing": run_routing}[args.mode](
                 args, rank, world, local)
             if rank == 0:
                 print(json.dumps(res), flush=True)
