@@ -408,7 +408,8 @@ void launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, Args args, cons
 // leaves its fp32 partial in its own shared memory, [MT][128] (activation row
 // major), and after a cluster barrier CTA r sums rows [r*MT/S, (r+1)*MT/S) of all S
 // partials through distributed shared memory, in rank order (deterministic), and
-// stores them as bf16.  One tile per CTA (not persistent).
+// stores them as bf16 (S need not divide MT: shares of ceil(MT/S) rows, the last one
+// shorter).  One tile per CTA (not persistent).
 // Fused: CTA b's rows go, as a [M, N] image in slot [this rank], to every rank
 // (kOneShot) or to rank b % W (kTwoShot) instead of `out`; then the per-CTA
 // cross-rank barriers of the allreduce (phase 0 after the push, phase 1 after the
@@ -560,8 +561,9 @@ gemm_bf16_swab_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_cons
     // skipped.  Each thread first issues the loads of R groups from all S ranks,
     // then sums: the remote reads overlap instead of paying one latency each.
     constexpr int R = 4;
-    const int rows_per = MT / S, rbase = rank * rows_per;
-    const int rows_live = max(0, min(rows_per, args.M - m_blk * MT - rbase));
+    // ceil: S need not divide MT (S = 3, 5, 6, 7 leave a shorter last share)
+    const int rows_per = (MT + S - 1) / S, rbase = rank * rows_per;
+    const int rows_live = max(0, min(min(rows_per, MT - rbase), args.M - m_blk * MT - rbase));
     const int groups = rows_live * 32;
     // fused: where this CTA's rows go, and the byte offset of group g's 4 columns
     const int owner = FUSE == kTwoShot ? (int)(blockIdx.x % F.world) : F.rank;
