@@ -323,12 +323,14 @@ def run_b200(args, rank, world, local):
     # result out inside the timed region.  Falls back to the serial loop's time if the
     # pipelined loop fails for any reason.
     e2e_mode = "pipelined: H2D of step i+1 and D2H of step i-1 on their own streams overlap step i"
-    try:
-        e2e_ms = max_over_ranks(_e2e_pipelined(aiter, x, h_hidden, h_tw, h_tid, ref_out, K, args.warmup, world),
-                                world)
-    except Exception as exc:  # keep the line: report the serial measurement instead
+    pip_ms, pip_err = _e2e_pipelined(aiter, x, h_hidden, h_tw, h_tid, ref_out, K, args.warmup, world)
+    # every rank takes the same collective steps whether or not its loop failed
+    if max_over_ranks(0.0 if pip_err is None else 1.0, world) > 0:
         e2e_ms = e2e_serial_ms
-        e2e_mode = f"serial (pipelined loop failed: {type(exc).__name__}: {exc})"[:300]
+        why = f"{type(pip_err).__name__}: {pip_err}" if pip_err is not None else "on another rank"
+        e2e_mode = f"serial (pipelined loop failed: {why})"[:300]
+    else:
+        e2e_ms = max_over_ranks(pip_ms, world)
 
     pk, src = peaks()
     fp8_peak_tflops = 2.0 * pk["bf16_tflops"]
@@ -422,19 +424,30 @@ def _e2e_pipelined(aiter, x, h_hidden, h_tw, h_tid, ref_out, K, W, world):
         cmp.wait_stream(s_out)
         return (n - 1) & 1
 
-    run(W)
-    torch.cuda.synchronize()
+    # (ms, None) or (None, the exception); both barriers run on every path so that
+    # ranks stay in step when one of them fails
+    err, ms = None, None
+    try:
+        run(W)
+        torch.cuda.synchronize()
+    except Exception as exc:
+        err = exc
     barrier(world)
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(cmp)
-    last = run(K, start_event=e0)
-    e1.record(cmp)
-    torch.cuda.synchronize()
+    if err is None:
+        try:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(cmp)
+            last = run(K, start_event=e0)
+            e1.record(cmp)
+            torch.cuda.synchronize()
+            if not torch.allclose(h_out[last].to(dev).float(), ref_out, atol=2e-2, rtol=2e-2):
+                raise RuntimeError("pipelined e2e output differs from the device-resident result")
+            ms = e0.elapsed_time(e1)
+        except Exception as exc:
+            err = exc
     barrier(world)
-    if not torch.allclose(h_out[last].to(dev).float(), ref_out, atol=2e-2, rtol=2e-2):
-        raise RuntimeError("pipelined e2e output differs from the device-resident result")
-    return e0.elapsed_time(e1)
+    return ms, err
 
 
 def cpu_baseline(x, sample, threads=None):
