@@ -39,3 +39,41 @@ def test_gemm_fake_shape_and_mutating_ops_trace():
         ti = torch.empty(5, 4, dtype=torch.int32, device="cuda")
         tei = torch.empty(5, 4, dtype=torch.int32, device="cuda")
         assert torch.ops.aiter_b200.topk_softmax(tw, ti, tei, g, True) is None
+
+
+def test_fused_moe_fake_dtype_follows_fp16_activations():
+    M, D, I, E, k = 3, 512, 256, 4, 2
+    with FakeTensorMode():
+        x = torch.empty(M, D, dtype=torch.float16, device="cuda")
+        w1 = torch.empty(E, 2 * I, D, dtype=dtypes.fp8, device="cuda")
+        w2 = torch.empty(E, D, I, dtype=dtypes.fp8, device="cuda")
+        tw = torch.empty(M, k, device="cuda")
+        ti = torch.empty(M, k, dtype=torch.int32, device="cuda")
+        y = torch.ops.aiter_b200.fused_moe_(x, w1, w2, tw, ti, None, 2, 4, True)
+        assert y.dtype == torch.float16 and y.shape == (M, D)
+
+
+def test_fused_moe_rejects_what_the_b200_path_does_not_run():
+    """Unsupported combinations raise before any kernel launch, as the reference
+    raises for combinations it has no kernel for (aiter/fused_moe.py:251-254)."""
+    import pytest
+    from aiter_b200 import ActivationType, QuantType
+    from aiter_b200.fused_moe import fused_moe
+    M, D, I, E, k = 2, 256, 128, 4, 2
+    x = torch.zeros(M, D, dtype=torch.bfloat16)
+    w1 = torch.zeros(E, 2 * I, D, dtype=dtypes.fp8)
+    w2 = torch.zeros(E, D, I, dtype=dtypes.fp8)
+    tw = torch.zeros(M, k)
+    ti = torch.zeros(M, k, dtype=torch.int32)
+    sh = w1.clone()
+    sh.is_shuffled = True
+    with pytest.raises(ValueError, match="pre-shuffled"):
+        fused_moe(x, sh, w2, tw, ti, quant_type=QuantType.per_1x128)
+    with pytest.raises(NotImplementedError, match="bias"):
+        fused_moe(x, w1, w2, tw, ti, quant_type=QuantType.per_1x128, bias1=torch.zeros(E, 2 * I))
+    with pytest.raises(NotImplementedError, match="g1u1"):
+        fused_moe(x, w1[:, :I], w2, tw, ti, quant_type=QuantType.per_1x128)
+    with pytest.raises(NotImplementedError, match="quant_type"):
+        fused_moe(x, w1, w2, tw, ti, quant_type=QuantType.per_Token)
+    with pytest.raises(NotImplementedError, match="activation"):
+        fused_moe(x, w1, w2, tw, ti, quant_type=QuantType.per_1x128, activation=ActivationType.No)
