@@ -135,6 +135,7 @@ def lib():
         for name, args in (("custom_ar_init", [c64, c64, c64, c64, p64, vp]),
                            ("custom_ar_open_peers", [c64, vp]), ("custom_ar_open_loopback", [c64]),
                            ("custom_ar_next_buffer", [c64, p64, p64]),
+                           ("custom_ar_next_buffer_ex", [c64, c64, p64, p64]),
                            ("custom_ar_all_reduce", [c64, ctypes.POINTER(aiter_tensor_t),
                                                      ctypes.POINTER(aiter_tensor_t), c64, vp]),
                            ("custom_ar_all_reduce_fp8", [c64, ctypes.POINTER(aiter_tensor_t),

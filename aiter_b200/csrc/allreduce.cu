@@ -87,7 +87,7 @@ struct Elem<float> {
 // U * W independent 16-byte loads in flight (U packs per thread per step).
 template <typename T, int W>
 __global__ void __launch_bounds__(kThreads)
-allreduce_kernel(Peers P, int rank, int parity, const uint4* __restrict__ in, uint4* __restrict__ out,
+allreduce_kernel(Peers P, int rank, int buffer, const uint4* __restrict__ in, uint4* __restrict__ out,
                       int64_t n16, int two_shot, int end_barrier) {
     __shared__ uint32_t s_epoch;
     if (threadIdx.x == 0) {
@@ -98,10 +98,10 @@ allreduce_kernel(Peers P, int rank, int parity, const uint4* __restrict__ in, ui
     __syncthreads();
     const uint32_t epoch = s_epoch;
     constexpr int U = W >= 8 ? 1 : 8 / W;
-    uint4* mine = reinterpret_cast<uint4*>(P.buf[parity][rank]);
+    uint4* mine = reinterpret_cast<uint4*>(P.buf[buffer][rank]);
     const uint4* bufs[W];
 #pragma unroll
-    for (int p = 0; p < W; ++p) bufs[p] = reinterpret_cast<const uint4*>(P.buf[parity][p]);
+    for (int p = 0; p < W; ++p) bufs[p] = reinterpret_cast<const uint4*>(P.buf[buffer][p]);
     const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     // Packs are split into `nseg` segments and pack i of segment s always goes to
@@ -191,13 +191,13 @@ allreduce_kernel(Peers P, int rank, int parity, const uint4* __restrict__ in, ui
 // the gp lanes of a group are consecutive lanes of one warp.
 template <int W>
 __global__ void __launch_bounds__(kThreads)
-allreduce_fp8q_kernel(Peers P, int rank, int parity, const uint4* __restrict__ in, uint4* __restrict__ out,
+allreduce_fp8q_kernel(Peers P, int rank, int buffer, const uint4* __restrict__ in, uint4* __restrict__ out,
                       int64_t n8, int gp, int64_t q_off, int64_t s_off, int end_barrier) {
     __shared__ uint32_t s_epoch;
     if (threadIdx.x == 0) s_epoch = next_epoch(P, rank);
     __syncthreads();
     const uint32_t epoch = s_epoch;
-    uint4* mine = reinterpret_cast<uint4*>(P.buf[parity][rank]);
+    uint4* mine = reinterpret_cast<uint4*>(P.buf[buffer][rank]);
     const int lane = threadIdx.x & 31;
     const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -210,8 +210,8 @@ allreduce_fp8q_kernel(Peers P, int rank, int parity, const uint4* __restrict__ i
     if (!block_barrier(P, rank, W, 0, epoch)) return;
     {
         const int64_t lo = seg_lo(rank), hi = seg_hi(rank);
-        uint8_t* qbase = P.buf[parity][rank] + q_off;
-        __half* sbase = reinterpret_cast<__half*>(P.buf[parity][rank] + s_off);
+        uint8_t* qbase = P.buf[buffer][rank] + q_off;
+        __half* sbase = reinterpret_cast<__half*>(P.buf[buffer][rank] + s_off);
         // warp-uniform trip count: every lane takes part in the group shuffles
         for (int64_t i0 = lo + tid - lane; i0 < hi; i0 += stride) {
             const int64_t i = i0 + lane;
@@ -220,7 +220,7 @@ allreduce_fp8q_kernel(Peers P, int rank, int parity, const uint4* __restrict__ i
             if (active) {
 #pragma unroll
                 for (int j = 0; j < W; ++j)
-                    Elem<__half>::acc(a, ld_cg(reinterpret_cast<const uint4*>(P.buf[parity][(rank + j) % W]) + i));
+                    Elem<__half>::acc(a, ld_cg(reinterpret_cast<const uint4*>(P.buf[buffer][(rank + j) % W]) + i));
             }
             const uint4 h = Elem<__half>::pack(a);
             const __half* hv = reinterpret_cast<const __half*>(&h);
@@ -252,8 +252,8 @@ allreduce_fp8q_kernel(Peers P, int rank, int parity, const uint4* __restrict__ i
     for (int d = 1; d < W; ++d) {
         const int s = (rank + d) % W;
         const int64_t lo = seg_lo(s), hi = seg_hi(s);
-        const uint8_t* qsrc = P.buf[parity][s] + q_off;
-        const uint8_t* ssrc = P.buf[parity][s] + s_off;
+        const uint8_t* qsrc = P.buf[buffer][s] + q_off;
+        const uint8_t* ssrc = P.buf[buffer][s] + s_off;
         for (int64_t i = lo + tid; i < hi; i += stride) {
             const uint2 qv = ld_cg8(qsrc + (i - lo) * 8);
             const unsigned short sb = *reinterpret_cast<const volatile unsigned short*>(ssrc + ((i - lo) / gp) * 2);
@@ -287,7 +287,7 @@ allreduce_fp8q_kernel(Peers P, int rank, int parity, const uint4* __restrict__ i
 //             per-row fp8: scale = amax(|y|) / 448 (0 -> 1), q = fp8(y / scale))
 template <int W, bool QUANT>
 __global__ void __launch_bounds__(kThreads)
-allreduce_rmsnorm_kernel(Peers P, int rank, int parity, const uint4* __restrict__ in,
+allreduce_rmsnorm_kernel(Peers P, int rank, int buffer, const uint4* __restrict__ in,
                          const uint4* __restrict__ res_in, uint4* __restrict__ res_out, void* __restrict__ out,
                          float* __restrict__ scale_out, const uint4* __restrict__ weight, int64_t rows, int ppr,
                          float eps, int end_barrier, int two_shot) {
@@ -301,10 +301,10 @@ allreduce_rmsnorm_kernel(Peers P, int rank, int parity, const uint4* __restrict_
     }
     __syncthreads();
     const uint32_t epoch = s_epoch;
-    uint4* mine = reinterpret_cast<uint4*>(P.buf[parity][rank]);
+    uint4* mine = reinterpret_cast<uint4*>(P.buf[buffer][rank]);
     const uint4* bufs[W];
 #pragma unroll
-    for (int p = 0; p < W; ++p) bufs[p] = reinterpret_cast<const uint4*>(P.buf[parity][p]);
+    for (int p = 0; p < W; ++p) bufs[p] = reinterpret_cast<const uint4*>(P.buf[buffer][p]);
     if (in != mine)
         for (int64_t row = blockIdx.x; row < rows; row += gridDim.x)
             for (int p = threadIdx.x; p < ppr; p += blockDim.x) mine[row * ppr + p] = in[row * ppr + p];
@@ -413,7 +413,7 @@ struct Ctx {
     uint8_t* base = nullptr;               // own region
     std::vector<void*> opened;             // peer regions opened via IPC
     Peers peers{};
-    uint32_t epoch = 0;
+    uint32_t epoch = 0;                    // eager calls made (captured calls do not count)
     bool ready = false;
 };
 
@@ -424,6 +424,39 @@ Ctx* as_ctx(int64_t h) {
     AB_CHECK(c != nullptr, "null allreduce context");
     return c;
 }
+
+constexpr int kCapturedBuffer = 2;
+
+// Staging buffer and end barrier of a call about to be launched on `st`.  An eager
+// call takes the next eager call number and alternates buffers 0 and 1 with no end
+// barrier; a call captured into a CUDA graph takes buffer 2, ends with a barrier (a
+// replay may run between any two eager calls, or right after another replay) and
+// leaves the eager count alone.
+struct Slot {
+    int buffer;
+    int end_barrier;
+};
+
+Slot take_slot(Ctx* c, cudaStream_t st) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    AB_CUDA(cudaStreamIsCapturing(st, &cap));
+    if (cap != cudaStreamCaptureStatusNone) return {kCapturedBuffer, 1};
+    c->epoch += 1;
+    return {(int)(c->epoch & 1), 0};
+}
+
+bool is_capturing(cudaStream_t st) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    AB_CUDA(cudaStreamIsCapturing(st, &cap));
+    return cap != cudaStreamCaptureStatusNone;
+}
+
+// Buffer the next call will take, without taking it.
+int next_buffer_index(const Ctx* c, bool capturing) {
+    return capturing ? kCapturedBuffer : (int)((c->epoch + 1) & 1);
+}
+
+uint8_t* staging_ptr(const Ctx* c, int buffer) { return c->base + kSignalPad + (size_t)buffer * c->max_bytes; }
 
 }  // namespace
 
@@ -441,7 +474,7 @@ AB_ENTRY(custom_ar_init,
     c->world = (int)world;
     c->device = (int)device;
     c->max_bytes = (size_t)max_bytes;
-    const size_t total = kSignalPad + 2 * (size_t)max_bytes;
+    const size_t total = kSignalPad + 3 * (size_t)max_bytes;
     cudaError_t e = cudaMalloc(&c->base, total);
     if (e != cudaSuccess) {
         delete c;
@@ -481,8 +514,7 @@ AB_ENTRY(custom_ar_open_peers, (int64_t ctx, const void* handles), (ctx, handles
             b = static_cast<uint8_t*>(q);
         }
         c->peers.sig[p] = reinterpret_cast<Signal*>(b);
-        c->peers.buf[0][p] = b + kSignalPad;
-        c->peers.buf[1][p] = b + kSignalPad + c->max_bytes;
+        for (int k = 0; k < 3; ++k) c->peers.buf[k][p] = b + kSignalPad + (size_t)k * c->max_bytes;
     }
     c->ready = true;
 }
@@ -492,18 +524,25 @@ AB_ENTRY(custom_ar_open_loopback, (int64_t ctx), (ctx)) {
     AB_CHECK(!c->ready, "peers already opened");
     for (int p = 0; p < c->world; ++p) {
         c->peers.sig[p] = reinterpret_cast<Signal*>(c->base);
-        c->peers.buf[0][p] = c->base + kSignalPad;
-        c->peers.buf[1][p] = c->base + kSignalPad + c->max_bytes;
+        for (int k = 0; k < 3; ++k) c->peers.buf[k][p] = staging_ptr(c, k);
     }
     c->ready = true;
 }
 
-// Pointer of the staging buffer the next call will use (zero-copy producers write
-// their result there and pass it as `inp`).
+// Pointer of the staging buffer the next eager call will use (zero-copy producers
+// write their result there and pass it as `inp`).
 AB_ENTRY(custom_ar_next_buffer, (int64_t ctx, int64_t* ptr_out, int64_t* bytes_out), (ctx, ptr_out, bytes_out)) {
     Ctx* c = as_ctx(ctx);
-    const int parity = (int)((c->epoch + 1) & 1);
-    *ptr_out = reinterpret_cast<int64_t>(c->base + kSignalPad + parity * c->max_bytes);
+    *ptr_out = reinterpret_cast<int64_t>(staging_ptr(c, next_buffer_index(c, false)));
+    *bytes_out = (int64_t)c->max_bytes;
+}
+
+// The same for the next call made eagerly (capturing = 0) or inside a CUDA graph
+// capture (capturing != 0): captured calls have a staging buffer of their own.
+AB_ENTRY(custom_ar_next_buffer_ex, (int64_t ctx, int64_t capturing, int64_t* ptr_out, int64_t* bytes_out),
+         (ctx, capturing, ptr_out, bytes_out)) {
+    Ctx* c = as_ctx(ctx);
+    *ptr_out = reinterpret_cast<int64_t>(staging_ptr(c, next_buffer_index(c, capturing != 0)));
     *bytes_out = (int64_t)c->max_bytes;
 }
 
@@ -528,8 +567,10 @@ AB_ENTRY(custom_ar_all_reduce,
     AB_CHECK(inp->device_id == c->device, "tensor on a different device than the communicator");
     if (bytes == 0) return;
     DeviceGuard dg(c->device);
-    c->epoch += 1;
-    const int parity = (int)(c->epoch & 1);
+    cudaStream_t st = as_stream(stream);
+    const Slot slot = take_slot(c, st);
+    const int buffer = slot.buffer;
+    const int endb = slot.end_barrier;
     const int64_t n16 = (int64_t)(bytes / 16);
     // force_two_shot: 1 = two-shot, 0 = one-shot, negative = by size.  One-shot reads
     // (W-1) x the data over NVLink, two-shot 2 (W-1)/W x plus one more barrier: with
@@ -542,20 +583,16 @@ AB_ENTRY(custom_ar_all_reduce,
     grid = std::max(grid, 1);
     const uint4* src = (const uint4*)inp->ptr;
     uint4* dst = (uint4*)out->ptr;
-    cudaStream_t st = as_stream(stream);
     const int tw = two ? 1 : 0;
-    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-    AB_CUDA(cudaStreamIsCapturing(st, &cap));
-    const int endb = cap == cudaStreamCaptureStatusNone ? 0 : 1;  // captured: buffers are reused per replay
 #define AB_AR(TT)                                                                                               \
     switch (c->world) {                                                                                         \
-        case 2: allreduce_kernel<TT, 2><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, tw, endb); break; \
-        case 3: allreduce_kernel<TT, 3><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, tw, endb); break; \
-        case 4: allreduce_kernel<TT, 4><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, tw, endb); break; \
-        case 5: allreduce_kernel<TT, 5><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, tw, endb); break; \
-        case 6: allreduce_kernel<TT, 6><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, tw, endb); break; \
-        case 7: allreduce_kernel<TT, 7><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, tw, endb); break; \
-        default: allreduce_kernel<TT, 8><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n16, tw, endb); break; \
+        case 2: allreduce_kernel<TT, 2><<<grid, kThreads, 0, st>>>(c->peers, c->rank, buffer, src, dst, n16, tw, endb); break; \
+        case 3: allreduce_kernel<TT, 3><<<grid, kThreads, 0, st>>>(c->peers, c->rank, buffer, src, dst, n16, tw, endb); break; \
+        case 4: allreduce_kernel<TT, 4><<<grid, kThreads, 0, st>>>(c->peers, c->rank, buffer, src, dst, n16, tw, endb); break; \
+        case 5: allreduce_kernel<TT, 5><<<grid, kThreads, 0, st>>>(c->peers, c->rank, buffer, src, dst, n16, tw, endb); break; \
+        case 6: allreduce_kernel<TT, 6><<<grid, kThreads, 0, st>>>(c->peers, c->rank, buffer, src, dst, n16, tw, endb); break; \
+        case 7: allreduce_kernel<TT, 7><<<grid, kThreads, 0, st>>>(c->peers, c->rank, buffer, src, dst, n16, tw, endb); break; \
+        default: allreduce_kernel<TT, 8><<<grid, kThreads, 0, st>>>(c->peers, c->rank, buffer, src, dst, n16, tw, endb); break; \
     }
     if (inp->dtype_ == AITER_DTYPE_bf16) {
         AB_AR(__nv_bfloat16)
@@ -605,25 +642,23 @@ AB_ENTRY(custom_ar_all_reduce_fp8, (int64_t ctx, aiter_tensor_t* inp, aiter_tens
     AB_CHECK(((uintptr_t)inp->ptr & 15) == 0 && ((uintptr_t)out->ptr & 15) == 0, "buffers must be 16-byte aligned");
     AB_CHECK(inp->device_id == c->device, "tensor on a different device than the communicator");
     DeviceGuard dg(c->device);
-    c->epoch += 1;
-    const int parity = (int)(c->epoch & 1);
     const int64_t per_block = (int64_t)kThreads * 2;
     int grid = (int)std::min<int64_t>((n8 + per_block - 1) / per_block, std::min(kMaxBlocks, num_sms(c->device)));
     grid = std::max(grid, 1);
     cudaStream_t st = as_stream(stream);
-    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-    AB_CUDA(cudaStreamIsCapturing(st, &cap));
-    const int endb = cap == cudaStreamCaptureStatusNone ? 0 : 1;
+    const Slot slot = take_slot(c, st);
+    const int buffer = slot.buffer;
+    const int endb = slot.end_barrier;
     const uint4* src = (const uint4*)inp->ptr;
     uint4* dst = (uint4*)out->ptr;
     switch (c->world) {
-        case 2: allreduce_fp8q_kernel<2><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n8, gp, q_off, s_off, endb); break;
-        case 3: allreduce_fp8q_kernel<3><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n8, gp, q_off, s_off, endb); break;
-        case 4: allreduce_fp8q_kernel<4><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n8, gp, q_off, s_off, endb); break;
-        case 5: allreduce_fp8q_kernel<5><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n8, gp, q_off, s_off, endb); break;
-        case 6: allreduce_fp8q_kernel<6><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n8, gp, q_off, s_off, endb); break;
-        case 7: allreduce_fp8q_kernel<7><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n8, gp, q_off, s_off, endb); break;
-        default: allreduce_fp8q_kernel<8><<<grid, kThreads, 0, st>>>(c->peers, c->rank, parity, src, dst, n8, gp, q_off, s_off, endb); break;
+        case 2: allreduce_fp8q_kernel<2><<<grid, kThreads, 0, st>>>(c->peers, c->rank, buffer, src, dst, n8, gp, q_off, s_off, endb); break;
+        case 3: allreduce_fp8q_kernel<3><<<grid, kThreads, 0, st>>>(c->peers, c->rank, buffer, src, dst, n8, gp, q_off, s_off, endb); break;
+        case 4: allreduce_fp8q_kernel<4><<<grid, kThreads, 0, st>>>(c->peers, c->rank, buffer, src, dst, n8, gp, q_off, s_off, endb); break;
+        case 5: allreduce_fp8q_kernel<5><<<grid, kThreads, 0, st>>>(c->peers, c->rank, buffer, src, dst, n8, gp, q_off, s_off, endb); break;
+        case 6: allreduce_fp8q_kernel<6><<<grid, kThreads, 0, st>>>(c->peers, c->rank, buffer, src, dst, n8, gp, q_off, s_off, endb); break;
+        case 7: allreduce_fp8q_kernel<7><<<grid, kThreads, 0, st>>>(c->peers, c->rank, buffer, src, dst, n8, gp, q_off, s_off, endb); break;
+        default: allreduce_fp8q_kernel<8><<<grid, kThreads, 0, st>>>(c->peers, c->rank, buffer, src, dst, n8, gp, q_off, s_off, endb); break;
     }
     check_launch("custom_ar_all_reduce_fp8");
 }
@@ -674,9 +709,8 @@ AB_ENTRY(custom_ar_gemm_all_reduce,
     AB_CHECK(out->ndim == 2 && out->shape[0] == M && out->shape[1] == N, "out must be [M, N]");
     AB_CHECK((size_t)(M * N * 2) <= c->max_bytes, "GEMM output of ", M * N * 2, " bytes exceeds the registered ",
              c->max_bytes);
-    const int parity = (int)((c->epoch + 1) & 1);
     aiter_tensor_t stage{};
-    stage.ptr = c->base + kSignalPad + (size_t)parity * c->max_bytes;
+    stage.ptr = staging_ptr(c, next_buffer_index(c, is_capturing(as_stream(stream))));
     stage.numel_ = (size_t)(M * N);
     stage.ndim = 2;
     stage.shape[0] = M;
@@ -723,14 +757,12 @@ void run_allreduce_rmsnorm(int64_t ctx, aiter_tensor_t* inp, aiter_tensor_t* res
     AB_CHECK(inp->device_id == c->device, "tensor on a different device than the communicator");
     if (rows == 0) return;
     DeviceGuard dg(c->device);
-    c->epoch += 1;
-    const int parity = (int)(c->epoch & 1);
     const int ppr = (int)(hidden / 8);
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(rows, std::min(kMaxBlocks, num_sms(c->device))));
     cudaStream_t st = as_stream(stream);
-    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-    AB_CUDA(cudaStreamIsCapturing(st, &cap));
-    const int endb = cap == cudaStreamCaptureStatusNone ? 0 : 1;
+    const Slot slot = take_slot(c, st);
+    const int buffer = slot.buffer;
+    const int endb = slot.end_barrier;
     const uint4* src = (const uint4*)inp->ptr;
     // one-shot reads (W-1) x the rows over NVLink, two-shot 2 (W-1)/W x plus a barrier:
     // the size cut-over of the plain allreduce
@@ -740,11 +772,11 @@ void run_allreduce_rmsnorm(int64_t ctx, aiter_tensor_t* inp, aiter_tensor_t* res
     do {                                                                                                          \
         if (quant)                                                                                                \
             allreduce_rmsnorm_kernel<WW, true><<<grid, kThreads, 0, st>>>(                                        \
-                c->peers, c->rank, parity, src, (const uint4*)res_inp->ptr, (uint4*)res_out->ptr, out->ptr,       \
+                c->peers, c->rank, buffer, src, (const uint4*)res_inp->ptr, (uint4*)res_out->ptr, out->ptr,       \
                 (float*)scale_out->ptr, (const uint4*)weight->ptr, rows, ppr, eps, endb, tw);                     \
         else                                                                                                      \
             allreduce_rmsnorm_kernel<WW, false><<<grid, kThreads, 0, st>>>(                                       \
-                c->peers, c->rank, parity, src, (const uint4*)res_inp->ptr, (uint4*)res_out->ptr, out->ptr,       \
+                c->peers, c->rank, buffer, src, (const uint4*)res_inp->ptr, (uint4*)res_out->ptr, out->ptr,       \
                 nullptr, (const uint4*)weight->ptr, rows, ppr, eps, endb, tw);                                    \
     } while (0)
     switch (c->world) {
@@ -837,11 +869,8 @@ AB_ENTRY(custom_ar_gemm_all_reduce_fused,
     }
     DeviceGuard dg(c->device);
     cudaStream_t st = as_stream(stream);
-    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-    AB_CUDA(cudaStreamIsCapturing(st, &cap));
-    c->epoch += 1;
-    g16::FuseArgs F{c->peers, c->rank, c->world, (int)(c->epoch & 1),
-                    cap == cudaStreamCaptureStatusNone ? 0 : 1, slot};
+    const Slot sl = take_slot(c, st);
+    g16::FuseArgs F{c->peers, c->rank, c->world, sl.buffer, sl.end_barrier, slot};
     if (mode == g16::kOneShot)
         g16::run<g16::kOneShot>(a, w, (__nv_bfloat16*)out->ptr, out->strides[0], F, c->device, st);
     else

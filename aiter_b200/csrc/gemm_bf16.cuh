@@ -32,11 +32,11 @@ constexpr int kSwabMaxM = 512;  // up to this many rows: the swap-AB split-K ker
 
 enum Fuse : int { kPlain = 0, kOneShot = 1, kTwoShot = 2 };
 
-// Peer context of a fused call.  Staging buffer `parity` of rank p holds one slot
+// Peer context of a fused call.  Staging buffer `buffer` of rank p holds one slot
 // of `slot_bytes` per source rank: slot s = what rank s pushed to p.
 struct FuseArgs {
     ipc::Peers P;
-    int rank, world, parity, end_barrier;
+    int rank, world, buffer, end_barrier;
     int64_t slot_bytes;
 };
 
@@ -265,7 +265,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 // -> whole row segments of 2*CC bytes to the owner's slot
                 constexpr int CC = C::CC, LPR = CC * 2 / 16, RPI = 32 / LPR;
                 const int owner = tile % F.world;
-                uint8_t* dst_tile = F.P.buf[F.parity][owner] + (int64_t)F.rank * F.slot_bytes +
+                uint8_t* dst_tile = F.P.buf[F.buffer][owner] + (int64_t)F.rank * F.slot_bytes +
                                     (int64_t)(tile / F.world) * C::TILE_BYTES;
                 uint8_t* stg = push_smem + (warp - 4) * (32 * CC * 2);
 #pragma unroll
@@ -327,7 +327,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                     fused_ok = warp_wait_epoch(&F.P.sig[F.rank]->push[blockIdx.x][src], ipc::progress(epoch, j));
                 if (!fused_ok) break;
                 const int64_t toff = (int64_t)(tile / F.world) * C::TILE_BYTES;
-                const uint8_t* mine = F.P.buf[F.parity][F.rank];
+                const uint8_t* mine = F.P.buf[F.buffer][F.rank];
                 for (int i = et; i < PACKS; i += 256) {
                     if (m_blk * BM + i / PPR >= args.M) continue;
                     float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
@@ -352,7 +352,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 const int m_blk = tile / args.n_tiles, n_blk = tile % args.n_tiles;
                 fused_ok = warp_wait_epoch(&F.P.sig[owner]->ready[blockIdx.x], ipc::progress(epoch, j));
                 if (!fused_ok) break;
-                const uint8_t* src = F.P.buf[F.parity][owner] + (int64_t)owner * F.slot_bytes +
+                const uint8_t* src = F.P.buf[F.buffer][owner] + (int64_t)owner * F.slot_bytes +
                                      (int64_t)(tile / F.world) * C::TILE_BYTES;
                 constexpr int U = 8;
                 for (int i0 = et; i0 < PACKS; i0 += U * 256) {
@@ -603,9 +603,9 @@ gemm_bf16_swab_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_cons
                     *reinterpret_cast<uint2*>(args.out + (int64_t)gm * args.ldo + n_blk * 128 + 4 * (g % 32)) = pk;
                 } else if constexpr (FUSE == kOneShot) {
                     const int64_t off = (int64_t)F.rank * F.slot_bytes + img_off(g);
-                    for (int p = 0; p < F.world; ++p) *reinterpret_cast<uint2*>(F.P.buf[F.parity][p] + off) = pk;
+                    for (int p = 0; p < F.world; ++p) *reinterpret_cast<uint2*>(F.P.buf[F.buffer][p] + off) = pk;
                 } else {
-                    *reinterpret_cast<uint2*>(F.P.buf[F.parity][owner] + (int64_t)F.rank * F.slot_bytes +
+                    *reinterpret_cast<uint2*>(F.P.buf[F.buffer][owner] + (int64_t)F.rank * F.slot_bytes +
                                               img_off(g)) = pk;
                 }
             }
@@ -615,7 +615,7 @@ gemm_bf16_swab_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_cons
     if constexpr (FUSE != kPlain) {
         // phase 0: every rank's CTA b has pushed its rows
         bool ok = ipc::block_barrier(F.P, F.rank, F.world, 0, epoch);
-        const uint8_t* mine = F.P.buf[F.parity][F.rank];
+        const uint8_t* mine = F.P.buf[F.buffer][F.rank];
         if (ok && (FUSE == kOneShot || owner == F.rank)) {
             // sum the W images of this CTA's rows in rank order
             for (int g = threadIdx.x; g < groups; g += NUM_THREADS) {
@@ -635,7 +635,7 @@ gemm_bf16_swab_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_cons
             // phase 1: the owner's sum is published; every rank copies it
             ok = ok && ipc::block_barrier(F.P, F.rank, F.world, 1, epoch);
             if (ok) {
-                const uint8_t* src = F.P.buf[F.parity][owner] + (int64_t)owner * F.slot_bytes;
+                const uint8_t* src = F.P.buf[F.buffer][owner] + (int64_t)owner * F.slot_bytes;
                 for (int g = threadIdx.x; g < groups; g += NUM_THREADS) {
                     const int gm = m_blk * MT + rbase + g / 32;
                     *reinterpret_cast<uint2*>(args.out + (int64_t)gm * args.ldo + n_blk * 128 + 4 * (g % 32)) =

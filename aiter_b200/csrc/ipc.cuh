@@ -3,7 +3,12 @@
 //
 // Every rank owns one cudaMalloc'd region, exported with cudaIpcGetMemHandle and
 // opened by every peer:
-//   [ Signal (flags written by peers, own call counters) | staging 0 | staging 1 ]
+//   [ Signal (flags written by peers, own call counters) | staging 0 | 1 | 2 ]
+// Eager calls alternate between staging 0 and 1 (a rank cannot reach call k+2, which
+// rewrites call k's buffer, before every peer has entered call k+1, i.e. finished
+// reading call k).  Calls captured into a CUDA graph use staging 2 only and end with
+// a barrier, so a replay, whenever it runs, never shares a buffer with the eager
+// call before or after it, nor a replay with the next one.
 // Flags are epochs: CTA b of a call takes the next value of its own counter[b]
 // (only CTA b of this rank touches it and launches are stream-ordered), so every
 // rank, making the same calls with the same grids, counts the same epochs per CTA
@@ -28,7 +33,7 @@ static_assert(sizeof(Signal) <= kSignalPad, "signal block exceeds its pad");
 
 struct Peers {
     Signal* sig[kMaxRanks];      // every rank's signal block
-    uint8_t* buf[2][kMaxRanks];  // every rank's staging buffers
+    uint8_t* buf[3][kMaxRanks];  // every rank's staging buffers [eager 0 | eager 1 | captured]
 };
 
 // Error word of the peer waits (read with custom_ar_device_error()): 1 = a peer did

@@ -1,8 +1,9 @@
 """CustomAllreduce: the CUDA-IPC allreduce of libaiter_b200.so behind the
 reference's interface (aiter/dist/device_communicators/custom_all_reduce.py:243-739).
 
-Each rank allocates one IPC region in the library (signals + two staging buffers of
-`max_size` bytes); the 64-byte IPC handles are exchanged over the CPU (gloo) group,
+Each rank allocates one IPC region in the library (signals + three staging buffers of
+`max_size` bytes: two alternate between eager calls, one serves calls captured into
+CUDA graphs); the 64-byte IPC handles are exchanged over the CPU (gloo) group,
 as the reference exchanges them over its CPU group / TCP store
 (custom_all_reduce.py:140-153,219-240), and every rank opens all peers' regions.
 """
@@ -199,10 +200,14 @@ class CustomAllreduce:
     def next_buffer_tensor(self, shape, dtype=torch.bfloat16) -> torch.Tensor:
         """A tensor viewing the staging buffer the next all_reduce will read.  A
         producer that writes its result there and passes the tensor to all_reduce
-        skips the input copy.  Valid until the call after next."""
+        skips the input copy.  Eagerly it is valid until the call after next; during
+        a CUDA graph capture it is the buffer every captured call shares, valid until
+        the next captured call."""
         ptr, nbytes = ctypes.c_int64(0), ctypes.c_int64(0)
-        _lib.check_status("custom_ar_next_buffer",
-                          _lib.lib().custom_ar_next_buffer(self._ctx, ctypes.byref(ptr), ctypes.byref(nbytes)))
+        capturing = 1 if torch.cuda.is_current_stream_capturing() else 0
+        _lib.check_status("custom_ar_next_buffer_ex",
+                          _lib.lib().custom_ar_next_buffer_ex(self._ctx, capturing, ctypes.byref(ptr),
+                                                              ctypes.byref(nbytes)))
         n = 1
         for d in shape:
             n *= int(d)

@@ -252,8 +252,9 @@ int gemm_a16w16(aiter_tensor_t* a, aiter_tensor_t* w, aiter_tensor_t* out, void*
 /* Replaces the reference's HIP-IPC custom allreduce (aiter/ops/custom_all_reduce.py:
  * init_custom_ar / all_reduce / dispose -> csrc/kernels/custom_all_reduce.cu:74-117,
  * csrc/include/custom_all_reduce.cuh:2243-2420).  One process per GPU.
- * custom_ar_init allocates this rank's IPC region (signals + 2 staging buffers of
- * max_bytes) and writes its 64-byte cudaIpcMemHandle to handle_out; the caller
+ * custom_ar_init allocates this rank's IPC region (signals + 3 staging buffers of
+ * max_bytes: eager calls alternate the first two, calls captured into a CUDA graph
+ * use the third and end with a barrier) and writes its 64-byte cudaIpcMemHandle to handle_out; the caller
  * exchanges the handles (the reference uses its CPU group / TCP store,
  * custom_all_reduce.py:140-153,219-240) and passes all `world` of them, in rank
  * order, to custom_ar_open_peers. */
@@ -264,9 +265,12 @@ int custom_ar_open_peers(int64_t ctx, const void* handles);
  * region, so barriers wait on flags no peer will ever write (exercises the bounded
  * waits on one GPU). */
 int custom_ar_open_loopback(int64_t ctx);
-/* Staging buffer the next all_reduce will use: a producer that writes its bf16
- * result there and passes it as `inp` skips the input copy. */
+/* Staging buffer the next eager all_reduce will use: a producer that writes its
+ * bf16 result there and passes it as `inp` skips the input copy. */
 int custom_ar_next_buffer(int64_t ctx, int64_t* ptr_out, int64_t* bytes_out);
+/* The same for the next call made eagerly (capturing = 0) or during a CUDA graph
+ * capture (capturing != 0). */
+int custom_ar_next_buffer_ex(int64_t ctx, int64_t capturing, int64_t* ptr_out, int64_t* bytes_out);
 /* out = sum over ranks of inp (bf16, fp16 or fp32, accumulated in fp32 in rank order, identical
  * bits on every rank).  force_two_shot: 1 = two-shot (reduce-scatter + all-gather
  * over peer memory), 0 = one-shot, negative = by size (one-shot always at 2 ranks, up to
