@@ -19,6 +19,8 @@ from .moe_op import (biased_grouped_topk, biased_grouped_topk_hip, dynamic_per_g
                      per_group_quant_hip, topk_softmax)
 from .fused_moe import fused_moe, fused_topk, moe_sorting, get_inter_dim
 from ._lib import device_error
+from .quick_all_reduce import (init_custom_qr, qr_all_reduce, qr_destroy, qr_device_error, qr_get_handle,
+                               qr_max_size, qr_open_handles)
 from . import torch_ops  # registers torch.ops.aiter_b200.* (fake impls for torch.compile)
 
 __all__ = [
@@ -28,4 +30,6 @@ __all__ = [
     "moe_stage2_fp8_blockscale", "fused_moe", "fused_topk", "moe_sorting", "get_inter_dim",
     "device_error", "dynamic_per_group_scaled_quant_fp4", "per_1x32_f4_quant_hip", "mxfp4_moe_sort_hip",
     "mxfp4_moe_sort_fwd", "fused_dynamic_mxfp4_quant_moe_sort_hip", "fused_dynamic_mxfp4_quant_moe_sort",
+    "init_custom_qr", "qr_get_handle", "qr_open_handles", "qr_all_reduce", "qr_destroy", "qr_max_size",
+    "qr_device_error",
 ]

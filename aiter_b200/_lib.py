@@ -131,6 +131,8 @@ def lib():
         L.moe_sorting_get_workspace_size.argtypes = [ctypes.c_int64] * 4
         L.aiter_device_error.restype = ctypes.c_int
         L.aiter_device_error.argtypes = [ctypes.c_int]
+        L.qr_max_size.restype = ctypes.c_int64
+        L.qr_max_size.argtypes = []
         c64, vp, p64 = ctypes.c_int64, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64)
         for name, args in (("custom_ar_init", [c64, c64, c64, c64, p64, vp]),
                            ("custom_ar_open_peers", [c64, vp]), ("custom_ar_open_loopback", [c64]),
@@ -150,7 +152,13 @@ def lib():
                             [ctypes.c_float, ctypes.POINTER(aiter_tensor_t), vp]),
                            ("custom_ar_allreduce_rmsnorm_ex", [c64] + [ctypes.POINTER(aiter_tensor_t)] * 5 +
                             [ctypes.c_float, ctypes.POINTER(aiter_tensor_t), c64, vp]),
-                           ("custom_ar_dispose", [c64]), ("custom_ar_device_error", [ctypes.c_int])):
+                           ("custom_ar_dispose", [c64]), ("custom_ar_device_error", [ctypes.c_int]),
+                           ("init_custom_qr", [c64, c64, c64, c64, p64, vp]), ("qr_open_handles", [c64, vp]),
+                           ("qr_all_reduce", [c64, ctypes.POINTER(aiter_tensor_t), ctypes.POINTER(aiter_tensor_t),
+                                              c64, c64, vp]),
+                           ("qr_all_reduce_emulated", [c64, ctypes.POINTER(aiter_tensor_t),
+                                                       ctypes.POINTER(aiter_tensor_t), c64, c64, vp]),
+                           ("qr_destroy", [c64]), ("qr_device_error", [ctypes.c_int])):
             fn = getattr(L, name)
             fn.restype = ctypes.c_int
             fn.argtypes = args

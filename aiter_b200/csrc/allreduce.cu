@@ -5,13 +5,14 @@
 //
 // Every rank owns one cudaMalloc'd region, exported with cudaIpcGetMemHandle and
 // opened by every peer:
-//   [ Signal (flags written by peers, own call counters) | staging 0 | staging 1 ]
-// Call n stages its input in buffer n % 2 (host-side count).  Eagerly, a rank starts
-// call n+2 (same buffer) only after the start barrier of call n+1, which every peer
-// reaches only after finishing call n, so nothing a slow peer still reads is
-// overwritten.  Under CUDA-graph capture the buffer of each captured call is fixed
-// for every replay, so captured calls end with a third barrier: no rank leaves the
-// call before every peer has finished reading its buffer.
+//   [ Signal (flags written by peers, own call counters) | staging 0 | 1 | 2 ]
+// Eager call n stages its input in buffer n % 2 (host-side count of eager calls).
+// A rank starts call n+2 (same buffer) only after the start barrier of call n+1,
+// which every peer reaches only after finishing call n, so nothing a slow peer
+// still reads is overwritten.  Calls captured into a CUDA graph use buffer 2, do
+// not count as eager calls, and end with a third barrier: no rank leaves the call
+// before every peer has finished reading its buffer, so a replay may run between
+// any two eager calls or right after another replay.
 //
 // Epochs live in device memory: CTA b of a call increments its own counter[b]
 // (only CTA b of this rank touches it, launches are stream-ordered), so replayed

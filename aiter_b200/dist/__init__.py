@@ -5,6 +5,7 @@ from .communication_op import (shard_moe_weights_for_tp, tensor_model_parallel_a
                                tensor_model_parallel_fused_allreduce_rmsnorm_quant, tensor_model_parallel_fused_moe,
                                tensor_model_parallel_gemm_all_reduce)
 from .custom_all_reduce import CustomAllreduce
+from .quick_all_reduce import QuickAllReduce, QuickReduceRegime
 from .parallel_state import (GraphCaptureContext, GroupCoordinator, destroy_distributed_environment,
                              destroy_model_parallel, get_tp_group, graph_capture, init_distributed_environment,
                              initialize_model_parallel)

@@ -16,6 +16,7 @@ import torch
 import torch.distributed as dist
 
 from .custom_all_reduce import CustomAllreduce
+from .quick_all_reduce import QuickAllReduce
 
 _TP: Optional["GroupCoordinator"] = None
 
@@ -53,15 +54,24 @@ class GroupCoordinator:
         self.device = torch.device(f"cuda:{local_rank}") if torch.cuda.is_available() and backend == "nccl" \
             else torch.device("cpu")
         self.ca_comm = None
+        self.qr_comm = None
         if use_custom_allreduce and self.world_size > 1 and self.device.type == "cuda":
             self.ca_comm = CustomAllreduce(self.cpu_group, self.device, ca_max_size)
+        if self.world_size > 1 and self.device.type == "cuda":
+            # disabled unless AITER_QUICK_REDUCE_QUANTIZATION names a regime
+            # (communicator_cuda.py:92-102 in the reference)
+            self.qr_comm = QuickAllReduce(self.cpu_group, self.device)
 
     def all_reduce(self, input_: torch.Tensor, use_new: bool = True, open_fp8_quant: bool = False,
                    prefill_support: bool = False) -> torch.Tensor:
-        """Out-of-place allreduce (parallel_state.py:376-407): the IPC allreduce for
-        eligible tensors, the NCCL group otherwise."""
+        """Out-of-place allreduce (parallel_state.py:376-407, communicator_cuda.py:
+        157-204): the quick allreduce when enabled and the tensor is eligible, else
+        the IPC allreduce for eligible tensors, the NCCL group otherwise."""
         if self.world_size == 1:
             return input_
+        qr = self.qr_comm
+        if qr is not None and not qr.disabled and qr.should_quick_allreduce(input_):
+            return qr.quick_all_reduce(input_)
         if self.ca_comm is not None and not self.ca_comm.disabled:
             out = self.ca_comm.custom_all_reduce(input_, use_new, open_fp8_quant)
             if out is not None:
@@ -119,6 +129,9 @@ class GroupCoordinator:
         if self.ca_comm is not None:
             self.ca_comm.close()
             self.ca_comm = None
+        if self.qr_comm is not None:
+            self.qr_comm.close()
+            self.qr_comm = None
 
 
 def init_distributed_environment(world_size=-1, rank=-1, distributed_init_method="env://", local_rank=-1,

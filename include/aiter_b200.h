@@ -321,6 +321,38 @@ int custom_ar_dispose(int64_t ctx);
 /* Error word of the allreduce barriers (1 = a peer did not arrive within 2 s). */
 int custom_ar_device_error(int clear);
 
+/* ---- quick allreduce: two-shot allreduce with quantised NVLink traffic ----- */
+/* Replaces the reference's QuickReduce (aiter/ops/quick_all_reduce.py:13-38 ->
+ * csrc/kernels/quick_all_reduce.cu:11-98, csrc/include/quick_all_reduce.cuh:581-991;
+ * aiter/dist/device_communicators/quick_all_reduce.py:59-268).  One process per GPU,
+ * world sizes 2, 4 and 8.  init_custom_qr (reference :11-26) allocates this rank's
+ * IPC region (signals + 2 regions of qr_max_size bytes, rounded up to 32 KB; <= 0
+ * takes qr_max_size()) on `device` and writes its 64-byte cudaIpcMemHandle to
+ * handle_out (the reference's qr_get_handle, :35-43); qr_open_handles (:44-58)
+ * takes every rank's handle in rank order. */
+int init_custom_qr(int64_t rank, int64_t world, int64_t qr_max_size, int64_t device, int64_t* ctx_out,
+                   void* handle_out);
+int qr_open_handles(int64_t ctx, const void* handles);
+/* out = sum over ranks of inp (fp16 or bf16, same dtype and size, contiguous, a
+ * multiple of 16 bytes, not overlapping).  quant_level 0 = FP, 1 = FP8 (e4m3fn),
+ * 2 = INT6, 3 = INT4 (any other value = FP, as the reference's dispatch): every
+ * rank's contribution and the owner's sum are quantised in groups of 32 with a
+ * scale per group; sums run in the arithmetic type (fp16, or bf16 unless
+ * cast_bf2half) in rank order.  Every rank gets identical bits.  (:62-93) */
+int qr_all_reduce(int64_t ctx, aiter_tensor_t* inp, aiter_tensor_t* out, int64_t quant_level,
+                  int64_t cast_bf2half, void* stream);
+int qr_destroy(int64_t ctx);
+/* Test hook with no reference counterpart: the quick allreduce of `world` ranks
+ * emulated on one GPU in one cooperative launch (the ranks' CTAs wait on one another
+ * inside a single launch), with private regions.  inp and out are [world, N]; row r
+ * of out receives rank r's result.  Synchronous. */
+int qr_all_reduce_emulated(int64_t world, aiter_tensor_t* inp, aiter_tensor_t* out, int64_t quant_level,
+                           int64_t cast_bf2half, void* stream);
+/* Default registered size, 2 GiB (:95-98). */
+int64_t qr_max_size(void);
+/* Error word of the quick allreduce's peer waits (1 = a peer did not arrive within 2 s). */
+int qr_device_error(int clear);
+
 #ifdef __cplusplus
 }
 #endif
