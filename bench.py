@@ -56,7 +56,8 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--fused-gemm-ar", action="store_true",
                    help="gemm_ar mode: also time the one-kernel GEMM + allreduce (custom_ar_gemm_all_reduce_fused)")
-    p.add_argument("--mode", default="moe", choices=["moe", "moe_sweep", "a8w4", "tp_moe", "gemm_ar", "routing"],
+    p.add_argument("--mode", default="moe", choices=["moe", "moe_sweep", "a8w4", "tp_moe", "gemm_ar", "routing",
+                                                     "allreduce"],
                    help="moe: config 1 at --M (N>1: data-parallel replicas); moe_sweep: config 1 token sweep "
                         "on one GPU; a8w4: config 2 on one GPU; tp_moe: config 3; gemm_ar: config 4; "
                         "routing: topk_softmax and moe_sorting alone (achieved HBM GB/s)")
@@ -846,13 +847,59 @@ def run_gemm_ar(args, rank, world, local):
                                                    "parallelism": f"tp{world}"}, "sweep": rows}
 
 
+def run_allreduce(args, rank, world, local):
+    """Allreduce sweep: the IPC custom allreduce, the quick allreduce at each level
+    (FP, FP8, INT6, INT4; cast_bf2half for bf16, the reference's default) and NCCL,
+    for bf16 and fp16 messages of 256 KB .. 256 MB per rank.  Latency per call, max
+    over ranks, and bus bandwidth 2 (W-1)/W * bytes / t (NCCL's convention)."""
+    import aiter_b200 as aiter
+    from aiter_b200.dist import parallel_state as ps
+    if world < 2:
+        return {"mode": "allreduce", "unavailable": "an allreduce needs at least 2 GPUs"}
+    top = 256 * 1024 * 1024
+    tp = ps.initialize_model_parallel(world, local_rank=local, ca_max_size=top)
+    dev = torch.device("cuda", local)
+    qr = None
+    if world in (2, 4, 8):
+        qr = aiter.init_custom_qr(rank, world, top)
+        handles = [None] * world
+        torch.distributed.all_gather_object(handles, aiter.qr_get_handle(qr), group=tp.cpu_group)
+        aiter.qr_open_handles(qr, handles)
+    rows = []
+    for dtype in (torch.bfloat16, torch.float16):
+        for nbytes in (256 << 10, 1 << 20, 4 << 20, 16 << 20, 64 << 20, top):
+            x = torch.randn(nbytes // 2, device=dev, generator=torch.Generator(device=dev).manual_seed(rank)
+                            ).to(dtype)
+            y = torch.empty_like(x)
+            arms = {"custom_us": lambda: tp.ca_comm.all_reduce(x, out=y),
+                    "nccl_us": lambda: torch.distributed.all_reduce(y, group=tp.device_group)}
+            if qr is not None:
+                for lvl, name in enumerate(("fp", "fp8", "int6", "int4")):
+                    arms[f"qr_{name}_us"] = (lambda lv: (lambda: aiter.qr_all_reduce(qr, x, y, lv, True)))(lvl)
+            row = {"dtype": str(dtype).split(".")[-1], "bytes": nbytes}
+            for k, f in arms.items():
+                us = 1e3 * _time_loop(f, args.steps, args.warmup, world)
+                row[k] = round(us, 2)
+                row[k.replace("_us", "_busbw_GBs")] = round(2.0 * (world - 1) / world * nbytes / (us * 1e-6) / 1e9, 1)
+            rows.append(row)
+            del x, y
+    err = aiter.qr_device_error() if qr is not None else 0
+    if qr is not None:
+        aiter.qr_destroy(qr)
+    ps.destroy_model_parallel()
+    return {"metric": "allreduce latency sweep", "mode": "allreduce", "unit": "us", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": False, "data": "synthetic N(0,1)",
+            "config": {"workload": "allreduce of 256 KB .. 256 MB per rank", "parallelism": f"tp{world}"},
+            "qr_device_error": err, "sweep": rows}
+
+
 def main():
     args = parse()
     rank, world, local = dist_setup(args.gpus)
     try:
-        if args.mode in ("tp_moe", "gemm_ar", "moe_sweep", "a8w4", "routing"):
+        if args.mode in ("tp_moe", "gemm_ar", "moe_sweep", "a8w4", "routing", "allreduce"):
             res = {"tp_moe": run_tp_moe, "gemm_ar": run_gemm_ar, "moe_sweep": run_moe_sweep,
-                   "a8w4": run_a8w4, "routing": run_routing}[args.mode](
+                   "a8w4": run_a8w4, "routing": run_routing, "allreduce": run_allreduce}[args.mode](
                 args, rank, world, local)
             if rank == 0:
                 print(json.dumps(res), flush=True)
