@@ -158,7 +158,15 @@ def lib():
                                               c64, c64, vp]),
                            ("qr_all_reduce_emulated", [c64, ctypes.POINTER(aiter_tensor_t),
                                                        ctypes.POINTER(aiter_tensor_t), c64, c64, vp]),
-                           ("qr_destroy", [c64]), ("qr_device_error", [ctypes.c_int])):
+                           ("qr_destroy", [c64]), ("qr_device_error", [ctypes.c_int]),
+                           ("ep_init", [c64] * 10 + [p64, vp]), ("ep_open_handles", [c64, vp]),
+                           ("ep_buffers", [c64, p64, p64]),
+                           ("ep_dispatch", [c64] + [ctypes.POINTER(aiter_tensor_t)] * 4 + [vp]),
+                           ("ep_combine", [c64] + [ctypes.POINTER(aiter_tensor_t)] * 2 + [vp]),
+                           ("ep_emu_init", [c64] * 9 + [p64]), ("ep_emu_buffers", [c64, c64, p64, p64]),
+                           ("ep_emu_dispatch", [c64] + [ctypes.POINTER(aiter_tensor_t)] * 4 + [vp]),
+                           ("ep_emu_combine", [c64] + [ctypes.POINTER(aiter_tensor_t)] * 2 + [vp]),
+                           ("ep_destroy", [c64]), ("ep_device_error", [ctypes.c_int])):
             fn = getattr(L, name)
             fn.restype = ctypes.c_int
             fn.argtypes = args
@@ -225,6 +233,21 @@ def check_status(name, ret):
         msg = raw.decode(errors="replace") if raw else f"status={ret}"
         L.aiter_clear_last_error()
         raise RuntimeError(f"{name} failed: {msg}")
+
+
+def device_view(ptr, shape, dtype, device):
+    """A tensor over library-owned device memory at `ptr` (no copy; the memory
+    stays owned by the library object that returned the pointer)."""
+    esz = torch.empty((), dtype=dtype).element_size()
+    typestr = {1: "|u1", 2: "<i2", 4: "<i4", 8: "<i8"}[esz]
+
+    class _View:
+        pass
+
+    v = _View()
+    v.__cuda_array_interface__ = {"shape": tuple(int(d) for d in shape), "typestr": typestr,
+                                  "data": (int(ptr), False), "version": 3, "strides": None}
+    return torch.as_tensor(v, device=device).view(dtype)
 
 
 def device_error(clear=True):

@@ -214,15 +214,7 @@ class CustomAllreduce:
         esz = torch.empty((), dtype=dtype).element_size()
         if n * esz > nbytes.value:
             raise ValueError(f"{n * esz} bytes exceed the staging buffer ({nbytes.value})")
-        typestr = {1: "|u1", 2: "<i2", 4: "<i4", 8: "<i8"}[esz]
-
-        class _View:
-            pass
-
-        v = _View()
-        v.__cuda_array_interface__ = {"shape": tuple(int(d) for d in shape), "typestr": typestr,
-                                      "data": (ptr.value, False), "version": 3, "strides": None}
-        return torch.as_tensor(v, device=self.device).view(dtype)
+        return _lib.device_view(ptr.value, shape, dtype, self.device)
 
     def close(self):
         if self._ctx:

@@ -353,6 +353,51 @@ int64_t qr_max_size(void);
 /* Error word of the quick allreduce's peer waits (1 = a peer did not arrive within 2 s). */
 int qr_device_error(int clear);
 
+/* ---- expert-parallel dispatch / combine over NVLink ----------------------- */
+/* The token all-to-all around an EP fused MoE, replacing the MoRI
+ * EpDispatchCombineOp the reference drives (aiter/dist/device_communicators/
+ * all2all.py:21-98, op_tests/multigpu_tests/test_dispatch_combine.py:76-171), intra-node.
+ * Rank r owns experts [r * experts_per_rank, (r + 1) * experts_per_rank).
+ * ep_init allocates this rank's IPC region for tokens of `hidden` elements of
+ * token_dtype (fp8, bf16 or fp16) with scale_dim f32 scales each, up to max_tokens
+ * per rank, and outputs of comb_dtype (bf16 or fp16); it writes the 64-byte
+ * cudaIpcMemHandle; ep_open_handles takes every rank's handle in rank order. */
+int ep_init(int64_t rank, int64_t world, int64_t hidden, int64_t token_dtype, int64_t scale_dim,
+            int64_t max_tokens, int64_t experts_per_rank, int64_t topk, int64_t comb_dtype, int64_t device,
+            int64_t* ctx_out, void* handle_out);
+int ep_open_handles(int64_t ctx, const void* handles);
+/* ptrs_out[6] = device pointers of this rank's receive arrays: tokens [rows, hidden],
+ * scales [rows, scale_dim] f32, ids [rows, topk] i32, weights [rows, topk] f32, the
+ * received count (i32 scalar: num_local_tokens of the EP MoE) and the source tags
+ * [rows] i32 (source << 24 | token); rows_out = world * max_tokens. */
+int ep_buffers(int64_t ctx, int64_t* ptrs_out, int64_t* rows_out);
+/* dispatch: tokens [T, hidden], weights [T, topk] f32, scales [T, scale_dim] f32
+ * (NULL when scale_dim is 0), ids [T, topk] i32 (global expert ids; others go
+ * nowhere), T <= max_tokens.  Every token goes once to every rank owning one of its
+ * experts; rank d receives source 0's tokens, then source 1's, ..., in token order.
+ * Calls must alternate with ep_combine. */
+int ep_dispatch(int64_t ctx, aiter_tensor_t* tokens, aiter_tensor_t* weights, aiter_tensor_t* scales,
+                aiter_tensor_t* ids, void* stream);
+/* combine: out [>= world * max_tokens, hidden] (row i = output of received row i)
+ * -> y [T, hidden], T = the last dispatch's tokens: y[t] = sum over the ranks t went
+ * to, in rank order, accumulated in fp32 and rounded once; 0 for a token that went
+ * nowhere. */
+int ep_combine(int64_t ctx, aiter_tensor_t* out, aiter_tensor_t* y, void* stream);
+/* Test hooks with no reference counterpart: `world` ranks emulated on one GPU (the
+ * ranks' CTAs run as rows of one cooperative launch), private regions, synchronous.
+ * ep_emu_dispatch takes tokens [world, T, hidden], weights / ids [world, T, topk],
+ * scales [world, T, scale_dim]; ep_emu_combine takes out [world, world * max_tokens,
+ * hidden] and writes y [world, T, hidden]. */
+int ep_emu_init(int64_t world, int64_t hidden, int64_t token_dtype, int64_t scale_dim, int64_t max_tokens,
+                int64_t experts_per_rank, int64_t topk, int64_t comb_dtype, int64_t device, int64_t* ctx_out);
+int ep_emu_buffers(int64_t ctx, int64_t rank, int64_t* ptrs_out, int64_t* rows_out);
+int ep_emu_dispatch(int64_t ctx, aiter_tensor_t* tokens, aiter_tensor_t* weights, aiter_tensor_t* scales,
+                    aiter_tensor_t* ids, void* stream);
+int ep_emu_combine(int64_t ctx, aiter_tensor_t* out, aiter_tensor_t* y, void* stream);
+int ep_destroy(int64_t ctx);
+/* Error word of the EP kernels' peer waits (1 = a peer did not arrive within 2 s). */
+int ep_device_error(int clear);
+
 #ifdef __cplusplus
 }
 #endif

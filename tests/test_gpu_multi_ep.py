@@ -1,0 +1,153 @@
+"""Multi-GPU EP dispatch / combine (EpDispatchCombineOp), one process per GPU, the
+flow of the reference's test (op_tests/multigpu_tests/test_dispatch_combine.py:
+76-171, 202-260).  Skipped with fewer than 2 GPUs, and until the kernels have been
+run on a multi-GPU box, unless AITER_B200_TEST_UNRUN=1.
+
+* fp8 tokens with 1x128 scales: every rank's received arrays bit-exact against
+  oracle/ep.py; combine of a deterministic expert stand-in bit-exact;
+* end to end: dispatch -> fused_moe with the rank's expert mask and the received
+  count as num_local_tokens -> combine, against fused_moe over all experts on the
+  same rank (tolerance of the reference's check; the stage-2 scatter-add is bf16
+  atomics in no fixed order), three repeats (buffer reuse across calls);
+* a rank with no tokens and bf16 tokens without scales.
+"""
+import os
+import sys
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+
+from dist_util import run_ranks
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+pytestmark = [
+    pytest.mark.gpu,
+    pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs"),
+    pytest.mark.skipif(os.environ.get("AITER_B200_TEST_UNRUN") != "1",
+                       reason="EP dispatch / combine not yet run on a multi-GPU box"),
+]
+
+T, D, I, E, K = 96, 1024, 512, 32, 4
+
+
+def _rank_case(r, world, empty_rank=None):
+    """Rank r's tokens and routing (seeded; every rank can rebuild every rank's)."""
+    from oracle import inputs, routing
+    rng = np.random.default_rng(100 + r)
+    n = 0 if (empty_rank is not None and r == empty_rank) else T
+    hidden = inputs.make_hidden(rng, max(n, 1), D)[:n]
+    tw, tid, _ = routing.topk_softmax(inputs.make_logits(rng, max(n, 1), E), K, True)
+    return {"hidden": hidden, "topk_weights": tw[:n], "topk_ids": tid[:n]}
+
+
+def _close(y, ref):
+    """At most 1 % of the elements beyond 1e-2 + 1e-2 |ref| (bf16 partial sums and
+    atomics in no fixed order)."""
+    bad = (y - ref).abs() > 1e-2 + 1e-2 * ref.abs()
+    return bad.float().mean().item() <= 0.01
+
+
+def _worker(rank, world, port):
+    sys.path.insert(0, ROOT)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    import aiter_b200 as aiter
+    from aiter_b200.dist import parallel_state as ps
+    from aiter_b200.dist.ep import EpDispatchCombineConfig, EpDispatchCombineOp
+    from oracle import ep, inputs
+    from aiter_b200 import _lib
+    from oracle.codecs import fp8_e4m3_decode, round_bf16
+    from oracle.quant import per_1x128_quant
+    ps.init_distributed_environment(world, rank, f"tcp://127.0.0.1:{port}", rank, "nccl", timeout_s=60)
+    tp = ps.initialize_model_parallel(world, local_rank=rank)
+    dev = torch.device("cuda", rank)
+    El = E // world
+    wts = inputs.make_moe_case(7, 8, D, I, E, K)               # the same experts on every rank
+    w1 = torch.from_numpy(wts["w1_q"]).view(torch.float8_e4m3fn).to(dev)
+    w2 = torch.from_numpy(wts["w2_q"]).view(torch.float8_e4m3fn).to(dev)
+    w1s, w2s = torch.from_numpy(wts["w1_s"]).to(dev), torch.from_numpy(wts["w2_s"]).to(dev)
+    lo, hi = rank * El, (rank + 1) * El
+    mask = torch.zeros(E, dtype=torch.int32, device=dev)
+    mask[lo:hi] = 1
+    kw = dict(quant_type=aiter.QuantType.per_1x128)
+
+    cfg = EpDispatchCombineConfig(data_type=torch.float8_e4m3fn, rank=rank, world_size=world, hidden_dim=D,
+                                  scale_dim=D // 128, scale_type_size=4, max_token_type_size=2,
+                                  max_num_inp_token_per_rank=T, num_experts_per_rank=El, num_experts_per_token=K)
+    op = EpDispatchCombineOp(cfg, group=tp.cpu_group)
+    for rep, empty in enumerate([None, None, world - 1]):
+        cases = [_rank_case(r, world, empty) for r in range(world)]
+        qs = [per_1x128_quant(c["hidden"]) for c in cases]
+        mine, (q, s) = cases[rank], qs[rank]
+        tok = torch.from_numpy(q).view(torch.float8_e4m3fn).to(dev)
+        sc = torch.from_numpy(s).to(dev)
+        tw = torch.from_numpy(mine["topk_weights"]).to(dev)
+        tid = torch.from_numpy(mine["topk_ids"]).to(torch.int32).to(dev)
+        x, w, xs, ids, n = op.dispatch(tok, tw, sc, tid)
+        torch.cuda.synchronize()
+        assert _lib.lib().ep_device_error(1) == 0
+        per_rank = [{"tokens": qs[r][0], "weights": cases[r]["topk_weights"],
+                     "ids": cases[r]["topk_ids"].astype(np.int32), "scales": qs[r][1]} for r in range(world)]
+        want = ep.dispatch(per_rank, El, world)[rank]
+        nr = int(n.item())
+        assert nr == len(want["src"])
+        if nr:
+            assert np.array_equal(x[:nr].view(torch.uint8).cpu().numpy(), np.stack(want["tokens"]))
+            assert np.array_equal(xs[:nr].cpu().numpy(), np.stack(want["scales"]))
+            assert np.array_equal(ids[:nr].cpu().numpy(), np.stack(want["ids"]))
+            assert np.array_equal(w[:nr].cpu().numpy(), np.stack(want["weights"]))
+        if rep == 0:
+            # combine of a deterministic stand-in: rank d returns its rows' dequantised codes x (d + 1)
+            stand = torch.zeros(op.capacity, D, dtype=torch.bfloat16, device=dev)
+            stand[:nr] = (x[:nr].float() * (rank + 1)).to(torch.bfloat16)
+            y = op.combine(stand, tw, tid)
+            torch.cuda.synchronize()
+            recv_all = ep.dispatch(per_rank, El, world)
+            outs = [round_bf16(fp8_e4m3_decode(np.stack(recv_all[d]["tokens"])) * (d + 1)) if recv_all[d]["src"]
+                    else np.zeros((0, D), np.float32) for d in range(world)]
+            want_y = ep.combine(outs, recv_all, [c["topk_ids"].shape[0] for c in cases], round_bf16)[rank]
+            assert np.array_equal(y.float().cpu().numpy(), want_y)
+            continue
+        # end to end through the EP MoE
+        out = aiter.fused_moe(x, w1[lo:hi].contiguous(), w2[lo:hi].contiguous(), w, ids, expert_mask=mask,
+                              num_local_tokens=n, w1_scale=w1s[lo:hi].contiguous(), w2_scale=w2s[lo:hi].contiguous(),
+                              a1_scale=xs, **kw)
+        y = op.combine(out, tw, tid)
+        torch.cuda.synchronize()
+        assert _lib.lib().ep_device_error(1) == 0
+        if tok.shape[0]:
+            full = aiter.fused_moe(tok, w1, w2, tw, tid, w1_scale=w1s, w2_scale=w2s, a1_scale=sc, **kw)
+            torch.cuda.synchronize()
+            assert _close(y.float(), full.float()), rep
+        else:
+            assert y.shape == (0, D)
+    op.close()
+    dist.barrier(group=tp.cpu_group)
+    # bf16 tokens without scales
+    cfg16 = EpDispatchCombineConfig(data_type=torch.bfloat16, rank=rank, world_size=world, hidden_dim=D, scale_dim=0,
+                                    scale_type_size=0, max_token_type_size=2, max_num_inp_token_per_rank=T,
+                                    num_experts_per_rank=El, num_experts_per_token=K)
+    op16 = EpDispatchCombineOp(cfg16, group=tp.cpu_group)
+    cases = [_rank_case(r, world) for r in range(world)]
+    tok = torch.from_numpy(cases[rank]["hidden"]).to(torch.bfloat16).to(dev)
+    tw = torch.from_numpy(cases[rank]["topk_weights"]).to(dev)
+    tid = torch.from_numpy(cases[rank]["topk_ids"]).to(torch.int32).to(dev)
+    x, w, xs, ids, n = op16.dispatch(tok, tw, None, tid)
+    assert xs is None
+    out = aiter.fused_moe(x, w1[lo:hi].contiguous(), w2[lo:hi].contiguous(), w, ids, expert_mask=mask,
+                          num_local_tokens=n, w1_scale=w1s[lo:hi].contiguous(), w2_scale=w2s[lo:hi].contiguous(), **kw)
+    y = op16.combine(out, tw, tid)
+    full = aiter.fused_moe(tok, w1, w2, tw, tid, w1_scale=w1s, w2_scale=w2s, **kw)
+    torch.cuda.synchronize()
+    assert _close(y.float(), full.float())
+    op16.close()
+    ps.destroy_model_parallel()
+    dist.destroy_process_group()
+
+
+def test_ep_dispatch_combine_multi_gpu():
+    world = min(torch.cuda.device_count(), 8)
+    world = 2 if world < 4 else (4 if world < 8 else 8)
+    run_ranks(_worker, world)
