@@ -107,6 +107,8 @@ SIGNATURES = {
     "moe_stage1_fp8_blockscale": [T, T, T, T, T, T, T, T, T, I64, I64, I64],
     "moe_stage1_fp8_blockscale_ex": [T, T, T, T, T, T, T, T, T, I64, I64, I64, OT, I64],
     "moe_stage2_fp8_blockscale": [T, T, T, T, T, T, T, OT, T, I64],
+    "moe_stage1_fp8_blockscale_bias": [T, T, T, T, T, T, T, T, T, I64, I64, I64, OT, I64, T],
+    "moe_stage2_fp8_blockscale_bias": [T, T, T, T, T, T, T, OT, T, I64, T],
 }
 
 _CT = {T: ctypes.POINTER(aiter_tensor_t), OT: ctypes.POINTER(aiter_tensor_t), I64: ctypes.c_int64,

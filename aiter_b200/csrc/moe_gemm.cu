@@ -74,6 +74,8 @@ struct GemmArgs {
     int doweight;    // stage 1: multiply gate/up by the row's top-k weight (doweight_stage1)
     int inter_f16;   // stage 1: round the intermediate to fp16 (else bf16) before the requant
     int out_f16;     // stage 2: fp16 output (else bf16); sorted_w == nullptr: weight 1
+    const float* bias;  // BIAS kernels: f32 [E, bias_ld] (stage 1: 2I gate|up, stage 2: D)
+    int bias_ld;
 };
 
 // Half tile: sorted row 64 of the block is padding.  Within an expert's segment the
@@ -156,12 +158,16 @@ __device__ __forceinline__ void scatter_add8(void* out, int64_t off, const float
 // STAGE 1: B tile = 128 gate rows + 128 up rows of w1 (BN must be 256), epilogue
 //          act(gate)*up -> 1x128 fp8 requant of the 128 outputs, TMA-stored.
 // STAGE 2: B tile = BN consecutive rows of w2, epilogue weighted scatter-add.
+// BIAS: the expert's f32 bias is added to the GEMM output before the activation
+//       (stage 1, after the doweight multiply) or before the top-k weight (stage 2),
+//       as torch_moe_stage1/2 add w1_bias / w2_bias (aiter/fused_moe.py:1572-1573,
+//       1662-1663); the kernels without it are unchanged.
 //
 // Warp roles: 0 TMA producer, 1 TMEM owner + MMA issuer, 2 block-scale prefetcher
 // (cp.async of a_scale[kb][tile rows] and the two w-scales of the tile's column
 // blocks into an SRING-deep smem ring, so the epilogue never waits on a global
 // load), 4..11 epilogue.
-template <int STAGE, int BN_>
+template <int STAGE, int BN_, bool BIAS = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmO, const GemmArgs args) {
@@ -417,13 +423,22 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             if (!ok) break;
             const int tok = sid & 0xFFFFFF;
             const bool valid = tok < args.M;
+            // BIAS: this thread's bias columns (the expert's row of the bias matrix)
+            const float* brow = nullptr;
+            if constexpr (BIAS)
+                brow = args.bias + (int64_t)min(max(args.sorted_eids[m_blk], 0), args.E - 1) * args.bias_ld;
             if (STAGE == 1 && half) {
                 // 32 gate / up pairs -> 32 outputs: columns 64h + 32hh .. of the tile
                 float amax = 0.f;
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
-                    const float g = args.doweight ? acc[j] * wrow : acc[j];
-                    const float u = args.doweight ? acc[32 + j] * wrow : acc[32 + j];
+                    float g = args.doweight ? acc[j] * wrow : acc[j];
+                    float u = args.doweight ? acc[32 + j] * wrow : acc[32 + j];
+                    if constexpr (BIAS) {
+                        const int cg = n_blk * 128 + 64 * h + 32 * hh + j;
+                        g += brow[cg];
+                        u += brow[args.out_cols + cg];
+                    }
                     const float yb = round_inter(act_pair(g, u, args.act), args.inter_f16);
                     acc[j] = yb;
                     amax = fmaxf(amax, fabsf(yb));
@@ -464,6 +479,12 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             } else if (STAGE == 2 && half) {
                 if (valid) {
                     const int64_t base = (int64_t)tok * args.out_cols + n_blk * BN_ + 128 * h + 32 * hh;
+                    if constexpr (BIAS) {
+#pragma unroll
+                        for (int r = 0; r < 2; ++r)
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) acc[32 * r + j] += brow[n_blk * BN_ + 128 * h + 64 * r + 32 * hh + j];
+                    }
 #pragma unroll
                     for (int r = 0; r < 2; ++r) {
 #pragma unroll
@@ -475,8 +496,13 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 float amax = 0.f;
 #pragma unroll
                 for (int j = 0; j < 64; ++j) {
-                    const float g = args.doweight ? acc[j] * wrow : acc[j];
-                    const float u = args.doweight ? acc[64 + j] * wrow : acc[64 + j];
+                    float g = args.doweight ? acc[j] * wrow : acc[j];
+                    float u = args.doweight ? acc[64 + j] * wrow : acc[64 + j];
+                    if constexpr (BIAS) {
+                        const int cg = n_blk * 128 + 64 * h + j;
+                        g += brow[cg];
+                        u += brow[args.out_cols + cg];
+                    }
                     const float yb = round_inter(act_pair(g, u, args.act), args.inter_f16);
                     acc[j] = yb;
                     amax = fmaxf(amax, fabsf(yb));
@@ -522,6 +548,10 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             } else {
                 if (valid) {
                     const int64_t base = (int64_t)tok * args.out_cols + n_blk * BN_ + CPT * h;
+                    if constexpr (BIAS) {
+#pragma unroll
+                        for (int j = 0; j < CPT; ++j) acc[j] += brow[n_blk * BN_ + CPT * h + j];
+                    }
 #pragma unroll
                     for (int c = 0; c < CPT / 8; ++c) scatter_add8(args.out, base + 8 * c, &acc[8 * c], wrow, args.out_f16);
                 }
@@ -641,6 +671,14 @@ int half_tiles_enabled() {
     return on;
 }
 
+template <int STAGE, int BN_, bool BIAS>
+void launch_k(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO, const GemmArgs& a, int grid,
+              int dev, cudaStream_t st) {
+    constexpr int smem = Cfg<BN_>::SMEM_BYTES;
+    ab::set_max_smem_once((const void*)moe_gemm_fp8_kernel<STAGE, BN_, BIAS>, smem, dev);
+    moe_gemm_fp8_kernel<STAGE, BN_, BIAS><<<grid, NUM_THREADS, smem, st>>>(tmA, tmB, tmO, a);
+}
+
 template <int STAGE, int BN_>
 void launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO, GemmArgs a, int dev,
             cudaStream_t st) {
@@ -649,9 +687,10 @@ void launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& t
     const int tiles = a.max_m_blocks * a.n_tiles;
     if (tiles == 0) return;
     const int grid = std::min(tiles, ab::num_sms(dev));
-    constexpr int smem = Cfg<BN_>::SMEM_BYTES;
-    ab::set_max_smem_once((const void*)moe_gemm_fp8_kernel<STAGE, BN_>, smem, dev);
-    moe_gemm_fp8_kernel<STAGE, BN_><<<grid, NUM_THREADS, smem, st>>>(tmA, tmB, tmO, a);
+    if (a.bias)
+        launch_k<STAGE, BN_, true>(tmA, tmB, tmO, a, grid, dev, st);
+    else
+        launch_k<STAGE, BN_, false>(tmA, tmB, tmO, a, grid, dev, st);
     ab::check_launch(STAGE == 1 ? "moe_stage1_fp8_blockscale" : "moe_stage2_fp8_blockscale");
 }
 
@@ -664,7 +703,8 @@ namespace {
 void run_stage1(aiter_tensor_t* a1, aiter_tensor_t* a1_scale, aiter_tensor_t* w1, aiter_tensor_t* w1_scale,
                 aiter_tensor_t* sorted_token_ids, aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids,
                 aiter_tensor_t* out, aiter_tensor_t* out_scale, int64_t num_tokens, int64_t block_m,
-                int64_t activation, aiter_tensor_t* sorted_weights, int64_t inter_dtype, void* stream) {
+                int64_t activation, aiter_tensor_t* sorted_weights, int64_t inter_dtype, aiter_tensor_t* bias,
+                void* stream) {
     using namespace ab;
     Sorted c = check_sorting(sorted_token_ids, sorted_expert_ids, num_valid_ids, block_m);
     check_sorted_operand(a1, a1_scale, c.rows_pad, "a1", "a1_scale");
@@ -712,6 +752,13 @@ void run_stage1(aiter_tensor_t* a1, aiter_tensor_t* a1_scale, aiter_tensor_t* w1
         a.doweight = 1;
     }
     a.inter_f16 = inter_dtype == AITER_DTYPE_fp16 ? 1 : 0;
+    if (bias) {
+        need_dtype(bias, AITER_DTYPE_fp32, "bias");
+        need_contig(bias, "bias");
+        AB_CHECK((int64_t)bias->numel_ == (int64_t)E * N, "bias must be [E, 2 * inter_dim] f32");
+        a.bias = (const float*)bias->ptr;
+        a.bias_ld = N;
+    }
     DeviceGuard dg(a1->device_id);
     CUtensorMap tmA, tmB;
     make_tmap_2d_u8(&tmA, a1->ptr, (uint64_t)c.rows_pad, D, 128, 128, true);
@@ -730,7 +777,7 @@ AB_ENTRY(moe_stage1_fp8_blockscale,
          (a1, a1_scale, w1, w1_scale, sorted_token_ids, sorted_expert_ids, num_valid_ids, out, out_scale, num_tokens,
           block_m, activation, stream)) {
     run_stage1(a1, a1_scale, w1, w1_scale, sorted_token_ids, sorted_expert_ids, num_valid_ids, out, out_scale,
-               num_tokens, block_m, activation, nullptr, AITER_DTYPE_bf16, stream);
+               num_tokens, block_m, activation, nullptr, AITER_DTYPE_bf16, nullptr, stream);
 }
 
 AB_ENTRY(moe_stage1_fp8_blockscale_ex,
@@ -741,15 +788,27 @@ AB_ENTRY(moe_stage1_fp8_blockscale_ex,
          (a1, a1_scale, w1, w1_scale, sorted_token_ids, sorted_expert_ids, num_valid_ids, out, out_scale, num_tokens,
           block_m, activation, sorted_weights, inter_dtype, stream)) {
     run_stage1(a1, a1_scale, w1, w1_scale, sorted_token_ids, sorted_expert_ids, num_valid_ids, out, out_scale,
-               num_tokens, block_m, activation, sorted_weights, inter_dtype, stream);
+               num_tokens, block_m, activation, sorted_weights, inter_dtype, nullptr, stream);
 }
 
-AB_ENTRY(moe_stage2_fp8_blockscale,
-         (aiter_tensor_t * a2, aiter_tensor_t* a2_scale, aiter_tensor_t* w2, aiter_tensor_t* w2_scale,
+// The same with the expert bias of the gate/up GEMM (the exp_bias of
+// moe_cktile2stages_gemm1, aiter/ops/moe_op.py:344-403): f32 [E, 2 * inter_dim].
+AB_ENTRY(moe_stage1_fp8_blockscale_bias,
+         (aiter_tensor_t * a1, aiter_tensor_t* a1_scale, aiter_tensor_t* w1, aiter_tensor_t* w1_scale,
           aiter_tensor_t* sorted_token_ids, aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids,
-          aiter_tensor_t* sorted_weights, aiter_tensor_t* out, int64_t block_m, void* stream),
-         (a2, a2_scale, w2, w2_scale, sorted_token_ids, sorted_expert_ids, num_valid_ids, sorted_weights, out,
-          block_m, stream)) {
+          aiter_tensor_t* out, aiter_tensor_t* out_scale, int64_t num_tokens, int64_t block_m, int64_t activation,
+          aiter_tensor_t* sorted_weights, int64_t inter_dtype, aiter_tensor_t* bias, void* stream),
+         (a1, a1_scale, w1, w1_scale, sorted_token_ids, sorted_expert_ids, num_valid_ids, out, out_scale, num_tokens,
+          block_m, activation, sorted_weights, inter_dtype, bias, stream)) {
+    run_stage1(a1, a1_scale, w1, w1_scale, sorted_token_ids, sorted_expert_ids, num_valid_ids, out, out_scale,
+               num_tokens, block_m, activation, sorted_weights, inter_dtype, bias, stream);
+}
+
+namespace {
+void run_stage2(aiter_tensor_t* a2, aiter_tensor_t* a2_scale, aiter_tensor_t* w2, aiter_tensor_t* w2_scale,
+                aiter_tensor_t* sorted_token_ids, aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids,
+                aiter_tensor_t* sorted_weights, aiter_tensor_t* out, int64_t block_m, aiter_tensor_t* bias,
+                void* stream) {
     using namespace ab;
     Sorted c = check_sorting(sorted_token_ids, sorted_expert_ids, num_valid_ids, block_m);
     check_sorted_operand(a2, a2_scale, c.rows_pad, "a2", "a2_scale");
@@ -789,11 +848,42 @@ AB_ENTRY(moe_stage2_fp8_blockscale,
     a.out_cols = D;
     a.E = E;
     a.rows_pad = c.rows_pad;
+    if (bias) {
+        need_dtype(bias, AITER_DTYPE_fp32, "bias");
+        need_contig(bias, "bias");
+        AB_CHECK((int64_t)bias->numel_ == (int64_t)E * D, "bias must be [E, model_dim] f32");
+        a.bias = (const float*)bias->ptr;
+        a.bias_ld = D;
+    }
     DeviceGuard dg(a2->device_id);
     CUtensorMap tmA, tmB;
     make_tmap_2d_u8(&tmA, a2->ptr, (uint64_t)c.rows_pad, I, 128, 128, true);
     make_tmap_2d_u8(&tmB, w2->ptr, (uint64_t)E * D, I, 128, 128, true);
     launch<2, 256>(tmA, tmB, tmA, a, a2->device_id, as_stream(stream));
+}
+}  // namespace
+
+AB_ENTRY(moe_stage2_fp8_blockscale,
+         (aiter_tensor_t * a2, aiter_tensor_t* a2_scale, aiter_tensor_t* w2, aiter_tensor_t* w2_scale,
+          aiter_tensor_t* sorted_token_ids, aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids,
+          aiter_tensor_t* sorted_weights, aiter_tensor_t* out, int64_t block_m, void* stream),
+         (a2, a2_scale, w2, w2_scale, sorted_token_ids, sorted_expert_ids, num_valid_ids, sorted_weights, out,
+          block_m, stream)) {
+    run_stage2(a2, a2_scale, w2, w2_scale, sorted_token_ids, sorted_expert_ids, num_valid_ids, sorted_weights, out,
+               block_m, nullptr, stream);
+}
+
+// The same with the expert bias of the down GEMM (the exp_bias of
+// moe_cktile2stages_gemm2, aiter/ops/moe_op.py:406-465): f32 [E, model_dim], added
+// before the top-k weight.
+AB_ENTRY(moe_stage2_fp8_blockscale_bias,
+         (aiter_tensor_t * a2, aiter_tensor_t* a2_scale, aiter_tensor_t* w2, aiter_tensor_t* w2_scale,
+          aiter_tensor_t* sorted_token_ids, aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids,
+          aiter_tensor_t* sorted_weights, aiter_tensor_t* out, int64_t block_m, aiter_tensor_t* bias, void* stream),
+         (a2, a2_scale, w2, w2_scale, sorted_token_ids, sorted_expert_ids, num_valid_ids, sorted_weights, out,
+          block_m, bias, stream)) {
+    run_stage2(a2, a2_scale, w2, w2_scale, sorted_token_ids, sorted_expert_ids, num_valid_ids, sorted_weights, out,
+               block_m, bias, stream);
 }
 
 // Error word of every mbarrier wait outside the allreduce context: this unit's

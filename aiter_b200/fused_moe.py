@@ -157,8 +157,24 @@ def _fused_moe_impl(hidden_states, w1, w2, topk_weight, topk_ids, expert_mask=No
         raise NotImplementedError("only gate+up (g1u1) MoE weights are supported")
     if activation not in (ActivationType.Silu, ActivationType.Gelu, ActivationType.Swiglu):
         raise NotImplementedError(f"activation {activation} not supported")
-    if bias1 is not None or bias2 is not None or hidden_pad or intermediate_pad:
-        raise NotImplementedError("bias / padding variants are not supported")
+    # hidden_pad / intermediate_pad only tell the reference's cktile kernels which
+    # trailing weight rows / columns are zero so that they can skip them
+    # (aiter/fused_moe.py:985-1028); the weights are zero there, so the result is the
+    # same without skipping.  The experts' biases are used, as in the reference, only by
+    # the per_1x32 Swiglu path with bf16 / fp16 activations (aiter/fused_moe.py:985-1008,
+    # 1228-1238); other configurations ignore them there and here.
+    use_bias = (quant_type == QuantType.per_1x32 and activation == ActivationType.Swiglu
+                and dtype in (dtypes.bf16, dtypes.fp16) and (bias1 is not None or bias2 is not None))
+    b1 = b2 = None
+    if use_bias:
+        if bias1 is not None:
+            b1 = bias1.to(device=hidden_states.device, dtype=dtypes.fp32).contiguous().view(E, -1)
+            if b1.shape[1] != 2 * inter_dim:
+                raise ValueError(f"bias1 must be [E, 2 * inter_dim], got {tuple(bias1.shape)}")
+        if bias2 is not None:
+            b2 = bias2.to(device=hidden_states.device, dtype=dtypes.fp32).contiguous().view(E, -1)
+            if b2.shape[1] != model_dim:
+                raise ValueError(f"bias2 must be [E, model_dim], got {tuple(bias2.shape)}")
     global_E = expert_mask.numel() if expert_mask is not None else E
     if quant_type == QuantType.per_1x32:
         # A8W4 as BASELINE defines it: fp8 1x128 activations, MXFP4 weights.  The
@@ -196,8 +212,8 @@ def _fused_moe_impl(hidden_states, w1, w2, topk_weight, topk_ids, expert_mask=No
         moe_op.moe_stage1_fp8_blockscale(a1, a1s, w1, w1_scale, sorted_ids, sorted_expert_ids, num_valid_ids,
                                          a2, a2s, M, block_m, activation,
                                          sorted_weights=sorted_weights if doweight_stage1 else None,
-                                         inter_dtype=dtype)
+                                         inter_dtype=dtype, bias=b1)
         moe_op.moe_stage2_fp8_blockscale(a2, a2s, w2, w2_scale, sorted_ids, sorted_expert_ids, num_valid_ids,
-                                         None if doweight_stage1 else sorted_weights, moe_buf, block_m)
+                                         None if doweight_stage1 else sorted_weights, moe_buf, block_m, bias=b2)
         return moe_buf
     raise NotImplementedError(f"quant_type {quant_type} is not supported by the B200 path")

@@ -187,11 +187,16 @@ def moe_stage1_fp8_blockscale(a1: Tensor, a1_scale: Tensor, w1: Tensor, w1_scale
                               sorted_token_ids: Tensor, sorted_expert_ids: Tensor, num_valid_ids: Tensor,
                               out: Tensor, out_scale: Tensor, num_tokens: int, block_m: int = 128,
                               activation=ActivationType.Silu, sorted_weights: Optional[Tensor] = None,
-                              inter_dtype=dtypes.bf16) -> Tuple[Tensor, Tensor]:
+                              inter_dtype=dtypes.bf16, bias: Optional[Tensor] = None) -> Tuple[Tensor, Tensor]:
     """Gate/up grouped GEMM with fused act and 1x128 fp8 requant; sorted-row in and out.
     `sorted_weights` given: doweight_stage1 (gate/up scaled by the top-k weight before
-    the activation); `inter_dtype`: bf16 or fp16 rounding of the intermediate."""
-    if sorted_weights is None and inter_dtype == dtypes.bf16:
+    the activation); `inter_dtype`: bf16 or fp16 rounding of the intermediate; `bias`:
+    the experts' f32 [E, 2 * inter_dim] bias, added before the activation."""
+    if bias is not None:
+        _lib.call("moe_stage1_fp8_blockscale_bias", a1, a1_scale, w1, w1_scale, sorted_token_ids,
+                  sorted_expert_ids, num_valid_ids, out, out_scale, num_tokens, block_m, int(activation),
+                  sorted_weights, _lib.dtype_code(inter_dtype), bias)
+    elif sorted_weights is None and inter_dtype == dtypes.bf16:
         _lib.call("moe_stage1_fp8_blockscale", a1, a1_scale, w1, w1_scale, sorted_token_ids, sorted_expert_ids,
                   num_valid_ids, out, out_scale, num_tokens, block_m, int(activation))
     else:
@@ -203,9 +208,15 @@ def moe_stage1_fp8_blockscale(a1: Tensor, a1_scale: Tensor, w1: Tensor, w1_scale
 
 def moe_stage2_fp8_blockscale(a2: Tensor, a2_scale: Tensor, w2: Tensor, w2_scale: Tensor,
                               sorted_token_ids: Tensor, sorted_expert_ids: Tensor, num_valid_ids: Tensor,
-                              sorted_weights: Optional[Tensor], out: Tensor, block_m: int = 128) -> Tensor:
+                              sorted_weights: Optional[Tensor], out: Tensor, block_m: int = 128,
+                              bias: Optional[Tensor] = None) -> Tensor:
     """Down grouped GEMM; adds the top-k weighted rows into out [M, D] (bf16 or fp16);
-    `sorted_weights` None: unweighted (the weights were applied in stage 1)."""
-    _lib.call("moe_stage2_fp8_blockscale", a2, a2_scale, w2, w2_scale, sorted_token_ids, sorted_expert_ids,
-              num_valid_ids, sorted_weights, out, block_m)
+    `sorted_weights` None: unweighted (the weights were applied in stage 1); `bias`: the
+    experts' f32 [E, D] bias, added before the top-k weight."""
+    if bias is not None:
+        _lib.call("moe_stage2_fp8_blockscale_bias", a2, a2_scale, w2, w2_scale, sorted_token_ids,
+                  sorted_expert_ids, num_valid_ids, sorted_weights, out, block_m, bias)
+    else:
+        _lib.call("moe_stage2_fp8_blockscale", a2, a2_scale, w2, w2_scale, sorted_token_ids, sorted_expert_ids,
+                  num_valid_ids, sorted_weights, out, block_m)
     return out

@@ -241,6 +241,24 @@ int moe_stage2_fp8_blockscale(aiter_tensor_t* a2, aiter_tensor_t* a2_scale, aite
                               aiter_tensor_t* sorted_weights, aiter_tensor_t* out, int64_t block_m,
                               void* stream);
 
+/* The two stages with the experts' biases (the exp_bias of moe_cktile2stages_gemm1 /
+ * gemm2, aiter/ops/moe_op.py:344-465, which fused_moe passes for per_1x32 Swiglu,
+ * aiter/fused_moe.py:1228-1238): stage 1 adds bias [E, 2 * inter_dim] f32 to the
+ * gate/up GEMM output after the doweight multiply and before the activation; stage 2
+ * adds bias [E, model_dim] f32 to the down GEMM output before the top-k weight
+ * (torch_moe_stage1/2, aiter/fused_moe.py:1572-1573, 1662-1663). */
+int moe_stage1_fp8_blockscale_bias(aiter_tensor_t* a1, aiter_tensor_t* a1_scale, aiter_tensor_t* w1,
+                                   aiter_tensor_t* w1_scale, aiter_tensor_t* sorted_token_ids,
+                                   aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids,
+                                   aiter_tensor_t* out, aiter_tensor_t* out_scale, int64_t num_tokens,
+                                   int64_t block_m, int64_t activation, aiter_tensor_t* sorted_weights,
+                                   int64_t inter_dtype, aiter_tensor_t* bias, void* stream);
+int moe_stage2_fp8_blockscale_bias(aiter_tensor_t* a2, aiter_tensor_t* a2_scale, aiter_tensor_t* w2,
+                                   aiter_tensor_t* w2_scale, aiter_tensor_t* sorted_token_ids,
+                                   aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids,
+                                   aiter_tensor_t* sorted_weights, aiter_tensor_t* out, int64_t block_m,
+                                   aiter_tensor_t* bias, void* stream);
+
 /* ---- bf16 GEMM (the GEMM half of GEMM + allreduce) ------------------------ */
 /* out[M, N] = A[M, K] @ W[N, K]^T, bf16 in / fp32 accumulate / bf16 out, on
  * tcgen05 kind::f16.  Replaces tgemm.mm / gemm_a16w16 (aiter/tuned_gemm.py:224-308,

@@ -50,11 +50,13 @@ def round_to(x, dtype):
     return codecs.round_bf16(x)
 
 
-def stage1(a_deq, w1_deq, topk_ids, activation="silu", expert_list=None, topk_weights=None, dtype="bf16"):
+def stage1(a_deq, w1_deq, topk_ids, activation="silu", expert_list=None, topk_weights=None, dtype="bf16",
+           bias=None):
     """a_deq: [M, D] f32, w1_deq: callable e -> [2I, D] f32 (or array [E,2I,D]).
     With `topk_weights` the GEMM output is multiplied by the token's top-k weight
-    before the activation (doweight, aiter/fused_moe.py:1569-1570).  Returns f32 [M, k, I]
-    rounded to `dtype` (bf16 or fp16)."""
+    before the activation (doweight, aiter/fused_moe.py:1569-1570); `bias` [E, 2I] is
+    then added (w1_bias, :1572-1573).  Returns f32 [M, k, I] rounded to `dtype` (bf16
+    or fp16)."""
     M, k = topk_ids.shape
     get_w = w1_deq if callable(w1_deq) else (lambda e: w1_deq[e])
     E = int(topk_ids.max()) + 1 if expert_list is None else None
@@ -68,6 +70,8 @@ def stage1(a_deq, w1_deq, topk_ids, activation="silu", expert_list=None, topk_we
         h = a_deq[tok] @ w.T
         if topk_weights is not None:
             h = (h * np.asarray(topk_weights, dtype=F32)[tok, slot][:, None]).astype(F32)
+        if bias is not None:
+            h = (h + np.asarray(bias, dtype=F32)[int(e)][None, :]).astype(F32)
         if out is None:
             out = np.zeros((M, k, w.shape[0]), dtype=F32)
         out[tok, slot] = h
@@ -82,10 +86,11 @@ def stage1(a_deq, w1_deq, topk_ids, activation="silu", expert_list=None, topk_we
     return round_to(np.asarray(y, dtype=F32), dtype)
 
 
-def stage2(a2_deq, w2_deq, topk_weights, topk_ids, expert_list=None, doweight=True, dtype="bf16"):
+def stage2(a2_deq, w2_deq, topk_weights, topk_ids, expert_list=None, doweight=True, dtype="bf16", bias=None):
     """a2_deq: [M, k, I] f32; w2_deq: callable e -> [D, I] or array [E, D, I].
-    Returns f32 [M, D] rounded to `dtype`; `doweight=False` when stage 1 applied the
-    top-k weights."""
+    `bias` [E, D] is added to each expert's output before the top-k weight (w2_bias,
+    aiter/fused_moe.py:1662-1665).  Returns f32 [M, D] rounded to `dtype`;
+    `doweight=False` when stage 1 applied the top-k weights."""
     M, k = topk_ids.shape
     get_w = w2_deq if callable(w2_deq) else (lambda e: w2_deq[e])
     experts = np.unique(topk_ids) if expert_list is None else expert_list
@@ -96,6 +101,8 @@ def stage2(a2_deq, w2_deq, topk_weights, topk_ids, expert_list=None, doweight=Tr
             continue
         w = get_w(int(e))
         y = a2_deq[tok, slot] @ w.T
+        if bias is not None:
+            y = (y + np.asarray(bias, dtype=F32)[int(e)][None, :]).astype(F32)
         if out is None:
             out = np.zeros((M, k, w.shape[0]), dtype=F32)
         out[tok, slot] = y
@@ -105,34 +112,37 @@ def stage2(a2_deq, w2_deq, topk_weights, topk_ids, expert_list=None, doweight=Tr
 
 
 def fused_moe_fp8_blockscale(hidden, w1_q, w1_s, w2_q, w2_s, topk_weights, topk_ids,
-                             activation="silu", return_intermediate=False, doweight_stage1=False, dtype="bf16"):
+                             activation="silu", return_intermediate=False, doweight_stage1=False, dtype="bf16",
+                             bias1=None, bias2=None):
     """QuantType.per_1x128 end to end. hidden: [M, D] bf16 (or fp16) values (f32 array);
-    `dtype` is the activation / intermediate / output type."""
+    `dtype` is the activation / intermediate / output type; bias1 [E, 2I] / bias2
+    [E, D] the experts' biases of the two GEMMs."""
     a1_q, a1_s = quant.per_1x128_quant(hidden)
     a1 = quant.dequant_1x128(a1_q, a1_s)
     w1 = lambda e: quant.dequant_128x128(w1_q[e:e + 1], w1_s[e:e + 1])[0]
     w2 = lambda e: quant.dequant_128x128(w2_q[e:e + 1], w2_s[e:e + 1])[0]
     out1 = stage1(a1, w1, topk_ids, activation, topk_weights=topk_weights if doweight_stage1 else None,
-                  dtype=dtype)
+                  dtype=dtype, bias=bias1)
     a2_q, a2_s = quant.per_1x128_quant(out1)
     a2 = quant.dequant_1x128(a2_q, a2_s)
-    out = stage2(a2, w2, topk_weights, topk_ids, doweight=not doweight_stage1, dtype=dtype)
+    out = stage2(a2, w2, topk_weights, topk_ids, doweight=not doweight_stage1, dtype=dtype, bias=bias2)
     if return_intermediate:
         return out, dict(a1_q=a1_q, a1_s=a1_s, out1=out1, a2_q=a2_q, a2_s=a2_s)
     return out
 
 
 def fused_moe_a8w4(hidden, w1_p, w1_e, w2_p, w2_e, topk_weights, topk_ids,
-                   activation="silu", return_intermediate=False):
-    """A8W4 as BASELINE defines it: fp8 1x128 activations, MXFP4 weights."""
+                   activation="silu", return_intermediate=False, bias1=None, bias2=None):
+    """A8W4 as BASELINE defines it: fp8 1x128 activations, MXFP4 weights; with
+    Swiglu the reference's per_1x32 path also takes the experts' biases."""
     a1_q, a1_s = quant.per_1x128_quant(hidden)
     a1 = quant.dequant_1x128(a1_q, a1_s)
     w1 = lambda e: quant.dequant_mxfp4(w1_p[e], w1_e[e])
     w2 = lambda e: quant.dequant_mxfp4(w2_p[e], w2_e[e])
-    out1 = stage1(a1, w1, topk_ids, activation)
+    out1 = stage1(a1, w1, topk_ids, activation, bias=bias1)
     a2_q, a2_s = quant.per_1x128_quant(out1)
     a2 = quant.dequant_1x128(a2_q, a2_s)
-    out = stage2(a2, w2, topk_weights, topk_ids)
+    out = stage2(a2, w2, topk_weights, topk_ids, bias=bias2)
     if return_intermediate:
         return out, dict(a1_q=a1_q, a1_s=a1_s, out1=out1, a2_q=a2_q, a2_s=a2_s)
     return out

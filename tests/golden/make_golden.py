@@ -224,7 +224,8 @@ def main(root):
             out[f"moe_fp8/{tag}/{kk}"] = v
     for tag, (seed, opts) in {"swiglu": (21, dict(activation=ActivationType.Swiglu)),
                               "doweight": (22, dict(doweight_stage1=True)),
-                              "fp16": (23, dict(dtype=torch.float16))}.items():
+                              "fp16": (23, dict(dtype=torch.float16)),
+                              "bias_swiglu": (24, dict(activation=ActivationType.Swiglu, bias=True))}.items():
         case = moe_reference_fp8(ref, seed, 32, 1024, 512, 8, 2, **opts)
         for kk, v in case.items():
             out[f"moe_fp8_opts/{tag}/{kk}"] = v
@@ -249,11 +250,18 @@ def _float_case(seed, M, D, I, E, k, zipf=None):
 
 
 def moe_reference_fp8(ref, seed, M, D, I, E, k, activation=ActivationType.Silu, doweight_stage1=False,
-                      dtype=torch.bfloat16):
+                      dtype=torch.bfloat16, bias=False):
     """The reference's 2-stage pipeline (op_tests/test_moe_2stage.py:187-231) with its
     options: activation, doweight_stage1 (top-k weight applied to the stage-1 GEMM output,
-    not in stage 2) and the activation / output dtype (bf16 or fp16)."""
+    not in stage 2), the activation / output dtype (bf16 or fp16) and the experts'
+    biases (drawn as op_tests/test_moe_2stage.py:62,70 draws them: clamp(randn, -1, 1)
+    in the activation dtype; the kernels take them as f32, :146-147)."""
     hidden, tw, tid, w1, w2 = _float_case(seed, M, D, I, E, k)
+    b1 = b2 = None
+    if bias:
+        brng = np.random.default_rng(seed + 1000)
+        b1 = torch.from_numpy(brng.standard_normal((E, 2 * I)).astype(np.float32)).to(dtype).clamp(-1.0, 1.0)
+        b2 = torch.from_numpy(brng.standard_normal((E, D)).astype(np.float32)).to(dtype).clamp(-1.0, 1.0)
     fp8 = torch.float8_e4m3fn
     w1q, w1s = ref.weight_per_128x128_quant(torch.from_numpy(w1), fp8)
     w2q, w2s = ref.weight_per_128x128_quant(torch.from_numpy(w2), fp8)
@@ -264,16 +272,19 @@ def moe_reference_fp8(ref, seed, M, D, I, E, k, activation=ActivationType.Silu, 
     tw_t, tid_t = torch.from_numpy(tw), torch.from_numpy(tid)
     out1 = ref.torch_moe_stage1(a1q, w1q, w2q, tw_t, tid_t, dtype=dtype,
                                 activation=activation, quant_type=QuantType.per_128x128,
-                                a1_scale=a1s, w1_scale=w1s, doweight=doweight_stage1)
+                                a1_scale=a1s, w1_scale=w1s, doweight=doweight_stage1, w1_bias=b1)
     a2q, a2s = ref.pertoken_quant(out1.view(M, -1, 128), quant_dtype=fp8)
     a2s = a2s.view(M, k, -1)
     out2 = ref.torch_moe_stage2(a2q.view(M, k, -1), w1q, w2q, tw_t, tid_t, dtype=dtype,
                                 quant_type=QuantType.per_128x128, w2_scale=w2s, a2_scale=a2s,
-                                doweight=not doweight_stage1)
-    return dict(w1q_sha=np.frombuffer(sha(t2n(w1q)).encode(), dtype=np.uint8),
-                w2q_sha=np.frombuffer(sha(t2n(w2q)).encode(), dtype=np.uint8),
-                w1s=t2n(w1s), w2s=t2n(w2s), a1q=t2n(a1q), a1s=t2n(a1s),
-                out1=t2n(out1), a2s=t2n(a2s), out=t2n(out2), topk_ids=tid, topk_weights=tw)
+                                doweight=not doweight_stage1, w2_bias=b2)
+    res = dict(w1q_sha=np.frombuffer(sha(t2n(w1q)).encode(), dtype=np.uint8),
+               w2q_sha=np.frombuffer(sha(t2n(w2q)).encode(), dtype=np.uint8),
+               w1s=t2n(w1s), w2s=t2n(w2s), a1q=t2n(a1q), a1s=t2n(a1s),
+               out1=t2n(out1), a2s=t2n(a2s), out=t2n(out2), topk_ids=tid, topk_weights=tw)
+    if bias:
+        res.update(bias1=b1.float().numpy(), bias2=b2.float().numpy())
+    return res
 
 
 def moe_reference_a8w4(ref, seed, M, D, I, E, k):

@@ -212,15 +212,19 @@ def test_unshuffle_weight_inverts_the_reference_shuffle(golden):
 
 @pytest.mark.parametrize("tag,opts", [("swiglu", dict(activation="swiglu")),
                                       ("doweight", dict(doweight_stage1=True)),
-                                      ("fp16", dict(dtype="fp16"))])
+                                      ("fp16", dict(dtype="fp16")),
+                                      ("bias_swiglu", dict(activation="swiglu"))])
 def test_moe_fp8_options_match_reference(golden, tag, opts):
     """fused_moe options of the reference pipeline: Swiglu (aiter/fused_moe.py:1473-1480),
-    doweight_stage1 (top-k weight on the stage-1 GEMM output, none in stage 2), and fp16
-    activations / intermediate / output."""
+    doweight_stage1 (top-k weight on the stage-1 GEMM output, none in stage 2), fp16
+    activations / intermediate / output, and the experts' biases of both GEMMs
+    (w1_bias / w2_bias of torch_moe_stage1/2, :1572-1573, 1662-1663)."""
     g = golden_group(golden, "moe_fp8_opts")[tag]
-    seed = {"swiglu": 21, "doweight": 22, "fp16": 23}[tag]
+    seed = {"swiglu": 21, "doweight": 22, "fp16": 23, "bias_swiglu": 24}[tag]
     c = inputs.make_moe_case(seed, 32, 1024, 512, 8, 2)
     assert np.array_equal(c["topk_ids"], g["topk_ids"])
+    if "bias1" in g:
+        opts = dict(opts, bias1=g["bias1"], bias2=g["bias2"])
     hidden = c["hidden"]
     if opts.get("dtype") == "fp16":
         hidden = hidden.astype(np.float16).astype(np.float32)

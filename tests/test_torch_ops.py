@@ -69,8 +69,16 @@ def test_fused_moe_rejects_what_the_b200_path_does_not_run():
     sh.is_shuffled = True
     with pytest.raises(ValueError, match="pre-shuffled"):
         fused_moe(x, sh, w2, tw, ti, quant_type=QuantType.per_1x128)
-    with pytest.raises(NotImplementedError, match="bias"):
-        fused_moe(x, w1, w2, tw, ti, quant_type=QuantType.per_1x128, bias1=torch.zeros(E, 2 * I))
+    # the experts' biases are used only on the per_1x32 Swiglu path (the reference
+    # ignores them elsewhere); there a wrong shape raises before any launch
+    w1p = torch.zeros(E, 2 * I, D // 2, dtype=torch.uint8)
+    w2p = torch.zeros(E, D, I // 2, dtype=torch.uint8)
+    with pytest.raises(ValueError, match="bias1 must be"):
+        fused_moe(x, w1p, w2p, tw, ti, quant_type=QuantType.per_1x32, activation=ActivationType.Swiglu,
+                  bias1=torch.zeros(E, I))
+    with pytest.raises(ValueError, match="bias2 must be"):
+        fused_moe(x, w1p, w2p, tw, ti, quant_type=QuantType.per_1x32, activation=ActivationType.Swiglu,
+                  bias2=torch.zeros(E, D + 1))
     with pytest.raises(NotImplementedError, match="g1u1"):
         fused_moe(x, w1[:, :I], w2, tw, ti, quant_type=QuantType.per_1x128)
     with pytest.raises(NotImplementedError, match="quant_type"):
