@@ -107,6 +107,12 @@ SIGNATURES = {
     "moe_stage1_fp8_blockscale": [T, T, T, T, T, T, T, T, T, I64, I64, I64],
     "moe_stage1_fp8_blockscale_ex": [T, T, T, T, T, T, T, T, T, I64, I64, I64, OT, I64],
     "moe_stage2_fp8_blockscale": [T, T, T, T, T, T, T, OT, T, I64],
+    "topk_sigmoid": [T, T, T],
+    "moe_sum": [T, T],
+    "silu_and_mul": [T, T],
+    "gelu_and_mul": [T, T],
+    "gelu_tanh_and_mul": [T, T],
+    "scaled_silu_and_mul": [T, T, T],
     "moe_stage1_fp8_blockscale_bias": [T, T, T, T, T, T, T, T, T, I64, I64, I64, OT, I64, T],
     "moe_stage2_fp8_blockscale_bias": [T, T, T, T, T, T, T, OT, T, I64, T],
 }

@@ -183,6 +183,18 @@ def moe_gather_quant_1x128(hidden_states: Tensor, token_sorted_pos: Tensor, topk
     return out, out_scale
 
 
+def topk_sigmoid(topk_weights: Tensor, topk_indices: Tensor, gating_output: Tensor) -> None:
+    """aiter.topk_sigmoid (aiter/ops/moe_op.py:40-42): the topk largest logits per token
+    (descending) into topk_indices, sigmoid of each (fp32 math) into topk_weights."""
+    _lib.call("topk_sigmoid", topk_weights, topk_indices, gating_output)
+
+
+def moe_sum(input: Tensor, output: Tensor) -> None:
+    """aiter.moe_sum (aiter/ops/moe_op.py:45-46): output [M, D] = input [M, topk, D]
+    summed over the slots."""
+    _lib.call("moe_sum", input, output)
+
+
 def moe_stage1_fp8_blockscale(a1: Tensor, a1_scale: Tensor, w1: Tensor, w1_scale: Tensor,
                               sorted_token_ids: Tensor, sorted_expert_ids: Tensor, num_valid_ids: Tensor,
                               out: Tensor, out_scale: Tensor, num_tokens: int, block_m: int = 128,

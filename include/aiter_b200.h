@@ -95,6 +95,21 @@ int biased_grouped_topk(aiter_tensor_t* gating_output, aiter_tensor_t* correctio
                         int64_t num_expert_group, int64_t topk_grp, int need_renorm,
                         float routed_scaling_factor, void* stream);
 
+/* Replaces aiter.topk_sigmoid (aiter/ops/moe_op.py:40-42 ->
+ * csrc/py_itfs_ck/topk_sigmoid_kernels.cu:15-66): per token the topk largest logits of
+ * gating_output [tokens, experts <= 1024] (fp32/bf16/fp16, contiguous), in descending
+ * order (equal values: lower expert first), topk_indices [tokens, topk] i32 and
+ * topk_weights [tokens, topk] (fp32/bf16/fp16) = sigmoid(logit) computed in fp32. */
+int topk_sigmoid(aiter_tensor_t* topk_weights, aiter_tensor_t* topk_indices, aiter_tensor_t* gating_output,
+                 void* stream);
+
+/* Replaces aiter.moe_sum (aiter/ops/moe_op.py:45-46 -> csrc/kernels/topk_softmax_kernels.cu:
+ * 737-854): output [tokens, hidden] = sum over the topk slots of input [tokens, topk,
+ * hidden] (fp32/bf16/fp16); for topk 2, 4 and 5 the sum is rounded to the element type
+ * after every slot, as the reference's kernel adds in the element type; otherwise it
+ * accumulates in fp32 and rounds once, as its at::sum_out fallback. */
+int moe_sum(aiter_tensor_t* input, aiter_tensor_t* output, void* stream);
+
 /* ---- sorting ------------------------------------------------------------- */
 
 /* Workspace bytes moe_sorting_fwd needs for these sizes (0 = none).
@@ -258,6 +273,18 @@ int moe_stage2_fp8_blockscale_bias(aiter_tensor_t* a2, aiter_tensor_t* a2_scale,
                                    aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids,
                                    aiter_tensor_t* sorted_weights, aiter_tensor_t* out, int64_t block_m,
                                    aiter_tensor_t* bias, void* stream);
+
+/* ---- gated activations (the split-K tail of the reference's fused_moe) ----- */
+/* Replace aiter.silu_and_mul / gelu_and_mul / gelu_tanh_and_mul / scaled_silu_and_mul
+ * (aiter/ops/activation.py:10-23 -> csrc/kernels/activation_kernels.cu:24-160, 337-360;
+ * used by aiter/fused_moe.py:1719-1724): input [..., 2d] = [x | y] -> out [..., d] =
+ * act(x) * y computed in fp32.  fp32 input: out fp32, bf16 or fp16; bf16 / fp16 input:
+ * out of the same type.  The scaled form multiplies by 1 / scale[0] (f32 tensor, read on
+ * the device) and writes fp8 e4m3 (round to nearest, saturating). */
+int silu_and_mul(aiter_tensor_t* out, aiter_tensor_t* input, void* stream);
+int gelu_and_mul(aiter_tensor_t* out, aiter_tensor_t* input, void* stream);
+int gelu_tanh_and_mul(aiter_tensor_t* out, aiter_tensor_t* input, void* stream);
+int scaled_silu_and_mul(aiter_tensor_t* out, aiter_tensor_t* input, aiter_tensor_t* scale, void* stream);
 
 /* ---- bf16 GEMM (the GEMM half of GEMM + allreduce) ------------------------ */
 /* out[M, N] = A[M, K] @ W[N, K]^T, bf16 in / fp32 accumulate / bf16 out, on

@@ -189,3 +189,19 @@ def fused_moe_fp8_blockscale_threaded(hidden, w1_q, w1_s, w2_q, w2_s, topk_weigh
     if doweight:
         out = out * np.asarray(topk_weights, dtype=F32)[:, :, None]
     return round_to(out.sum(axis=1, dtype=F32), dtype)
+
+
+def moe_sum(x, dtype="bf16"):
+    """`moe_sum` (aiter/ops/moe_op.py:45-46, csrc/kernels/topk_softmax_kernels.cu:737-854):
+    [M, k, D] -> [M, D].  For k = 2, 4, 5 the reference's kernel adds slot by slot in the
+    element type (one rounding per add); other k go through at::sum_out (fp32
+    accumulation, one rounding).  `dtype`: "fp32", "bf16" or "fp16"."""
+    x = np.asarray(x, dtype=F32)
+    k = x.shape[1]
+    rnd = (lambda a: a.astype(F32)) if dtype == "fp32" else (lambda a: round_to(a, dtype))
+    acc = np.zeros((x.shape[0], x.shape[2]), dtype=F32)
+    for s in range(k):
+        acc = (acc + x[:, s]).astype(F32)
+        if k in (2, 4, 5):
+            acc = rnd(acc)
+    return rnd(acc)

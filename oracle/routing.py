@@ -85,3 +85,15 @@ def biased_grouped_topk(gating, correction_bias, topk, num_expert_group, topk_gr
         w = w / w.sum(axis=-1, keepdims=True, dtype=np.float32)
     w = (w * np.float32(routed_scaling_factor)).astype(np.float32)
     return w, ids.astype(np.int32)
+
+
+def topk_sigmoid(logits, topk):
+    """`topk_sigmoid` (aiter/ops/moe_op.py:40-42; torch reference
+    op_tests/test_moe_topk_sigmoid.py:30-35): the topk largest logits per row in
+    descending order (equal values: lower index first) and sigmoid of each in fp32.
+    Returns (weights f32 [M, k], ids i32 [M, k])."""
+    x = np.asarray(logits, dtype=np.float32)
+    ids = np.argsort(-x, axis=-1, kind="stable")[:, :topk].astype(np.int32)
+    v = np.take_along_axis(x, ids.astype(np.int64), axis=-1)
+    w = (np.float32(1.0) / (np.float32(1.0) + np.exp(-v))).astype(np.float32)
+    return w, ids

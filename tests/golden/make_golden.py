@@ -233,6 +233,24 @@ def main(root):
         case = moe_reference_a8w4(ref, seed, M, D, I, E, k)
         for kk, v in case.items():
             out[f"moe_a8w4/{tag}/{kk}"] = v
+    # ---------------------------------------------------------------- topk_sigmoid, silu_and_mul
+    # rows of unique values, as op_tests/test_moe_topk_sigmoid.py:114-125 draws them
+    for tag, (E, k, M, dt) in {"e64_k4_bf16": (64, 4, 16, torch.bfloat16),
+                                "e128_k8_fp16": (128, 8, 16, torch.float16),
+                                "e128_k1_fp32": (128, 1, 8, torch.float32)}.items():
+        g = torch.Generator().manual_seed(E * 10 + k)
+        base = torch.arange(-1, 1, 2.0 / E).repeat((M, 1)).to(dt)
+        perm = torch.argsort(torch.rand(base.shape, generator=g), dim=-1)
+        logits = torch.gather(base, -1, perm)
+        w, ids = ref.topk_sigmoid_torch(logits.clone(), k)
+        out[f"topk_sigmoid/{tag}/logits"] = logits.float().numpy()
+        out[f"topk_sigmoid/{tag}/weights"] = t2n(w)
+        out[f"topk_sigmoid/{tag}/ids"] = t2n(ids)
+    for tag, (M, N, dt) in {"bf16": (8, 512, torch.bfloat16), "fp32": (8, 384, torch.float32)}.items():
+        g = torch.Generator().manual_seed(N)
+        inp = torch.randn(M, N, generator=g).to(dt)
+        out[f"silu_and_mul/{tag}/input"] = inp.float().numpy()
+        out[f"silu_and_mul/{tag}/out"] = ref.torch_silu_and_mul(inp).float().numpy()
     np.savez_compressed(os.path.join(HERE, "golden.npz"), **out)
     print("wrote", len(out), "arrays", os.path.getsize(os.path.join(HERE, "golden.npz")), "bytes")
 

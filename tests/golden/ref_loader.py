@@ -112,6 +112,11 @@ class Reference:
         self._load(run_torch, "op_tests/test_moe_sorting_mxfp4.py", ["run_torch"])
         ns["moe_mxfp4_sort_torch"] = run_torch["run_torch"]
         self._load(ns, "op_tests/test_moeTopkSoftmax.py", ["test_nofuse"])
+        # torch references of topk_sigmoid and silu_and_mul, kept under their own names
+        ts = dict(torch=torch)
+        self._load(ts, "op_tests/test_moe_topk_sigmoid.py", ["run_torch"])
+        ns["topk_sigmoid_torch"] = ts["run_torch"]
+        self._load(ns, "op_tests/test_activation.py", ["torch_silu_and_mul"])
         self._load(ns, "op_tests/test_moe_2stage.py", ["weight_per_128x128_quant"],
                    nested_in="test_fmoe")
         self._load(ns, "op_tests/test_moe_blockscale.py", ["torch_moe_blockscale"])

@@ -234,3 +234,41 @@ def test_moe_fp8_options_match_reference(golden, tag, opts):
     np.testing.assert_allclose(st["out1"], g["out1"], rtol=1e-2, atol=1e-3)
     np.testing.assert_allclose(out, g["out"], rtol=2e-2, atol=2e-2)
     assert np.mean(np.abs(out - g["out"]) > 1e-3) < 0.02
+
+
+@pytest.mark.parametrize("tag", ["e64_k4_bf16", "e128_k8_fp16", "e128_k1_fp32"])
+def test_topk_sigmoid_oracle_matches_reference(golden, tag):
+    """topk_sigmoid against the reference's torch routing (torch.topk, then sigmoid in
+    fp32; op_tests/test_moe_topk_sigmoid.py:30-35)."""
+    from oracle.routing import topk_sigmoid
+    g = golden_group(golden, "topk_sigmoid")[tag]
+    k = g["ids"].shape[1]
+    w, ids = topk_sigmoid(g["logits"], k)
+    assert np.array_equal(ids, g["ids"])
+    np.testing.assert_allclose(w, g["weights"], rtol=1e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("tag", ["bf16", "fp32"])
+def test_silu_and_mul_oracle_matches_reference(golden, tag):
+    """silu_and_mul against the reference test's torch_silu_and_mul
+    (op_tests/test_activation.py:13-17, checked there with atol = rtol = 1e-2); the
+    torch path rounds silu(x) to bf16 before the product, the kernel rounds once."""
+    from oracle.activation import act_and_mul
+    g = golden_group(golden, "silu_and_mul")[tag]
+    got = act_and_mul(g["input"], "silu", tag)
+    np.testing.assert_allclose(got, g["out"], rtol=1e-2, atol=1e-2)
+    if tag == "fp32":
+        np.testing.assert_allclose(got, g["out"], rtol=1e-6, atol=1e-6)
+
+
+def test_moe_sum_oracle_rounding_rule():
+    """moe_sum rounds after every slot for topk 2, 4, 5 (the reference kernel adds in the
+    element type) and once otherwise (its at::sum_out fallback)."""
+    from oracle.codecs import round_bf16
+    from oracle.moe import moe_sum
+    x = np.zeros((1, 4, 8), np.float32)
+    x[0, :, 0] = [1.0, 2.0 ** -9, 2.0 ** -9, 2.0 ** -9]       # bf16 ulp at 1 is 2^-7
+    assert moe_sum(x, "bf16")[0, 0] == 1.0                     # each add rounds back to 1
+    x3 = np.concatenate([x, np.zeros((1, 2, 8), np.float32)], axis=1)[:, [0, 1, 2, 3, 4, 5]]
+    x3[0, :, 0] = [1.0, 2.0 ** -9, 2.0 ** -9, 2.0 ** -9, 2.0 ** -9, 0.0]
+    assert moe_sum(x3, "bf16")[0, 0] == round_bf16(np.float32(1.0 + 4 * 2.0 ** -9))
