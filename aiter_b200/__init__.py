@@ -16,7 +16,7 @@ from .moe_op import (biased_grouped_topk, biased_grouped_topk_hip, dynamic_per_g
                      fused_dynamic_mxfp4_quant_moe_sort_hip, grouped_topk, moe_gather_quant_1x128,
                      moe_sorting_fwd, moe_sorting_get_workspace_size, moe_stage1_fp8_blockscale,
                      moe_stage2_fp8_blockscale, mxfp4_moe_sort_fwd, mxfp4_moe_sort_hip, per_1x32_f4_quant_hip,
-                     per_group_quant_hip, topk_softmax, topk_sigmoid, moe_sum)
+                     per_group_quant_hip, topk_softmax, topk_sigmoid, moe_sum, moe_sorting_opus_fwd)
 from .activation import gelu_and_mul, gelu_tanh_and_mul, scaled_silu_and_mul, silu_and_mul
 from .fused_moe import fused_moe, fused_topk, moe_sorting, get_inter_dim
 from ._lib import device_error
@@ -33,5 +33,5 @@ __all__ = [
     "mxfp4_moe_sort_fwd", "fused_dynamic_mxfp4_quant_moe_sort_hip", "fused_dynamic_mxfp4_quant_moe_sort",
     "init_custom_qr", "qr_get_handle", "qr_open_handles", "qr_all_reduce", "qr_destroy", "qr_max_size",
     "qr_device_error", "topk_sigmoid", "moe_sum", "silu_and_mul", "gelu_and_mul", "gelu_tanh_and_mul",
-    "scaled_silu_and_mul",
+    "scaled_silu_and_mul", "moe_sorting_opus_fwd",
 ]

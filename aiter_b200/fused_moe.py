@@ -16,6 +16,7 @@ Swiglu, doweight_stage1, bf16 or fp16 activations and output.  Weights are taken
 (`is_shuffled=True`, aiter/ops/shuffle.py:7-27) are rejected.
 """
 import functools
+import os
 from dataclasses import dataclass
 from typing import Optional
 
@@ -48,6 +49,31 @@ def nextPow2(n):
 
 def get_padded_M(M):
     return nextPow2(M) if M < 32768 else 32768
+
+
+@functools.lru_cache(maxsize=2048)
+def get_block_size_M(token, topk, expert, inter_dim):
+    """Sort unit for a problem (aiter/fused_moe.py:514-529 balances 32/64/128-row tiles over
+    the CUs).  The tcgen05 grouped GEMM tiles 128 sorted rows (64-row half tiles are
+    chosen inside the kernel), so the unit is always 128."""
+    return BLOCK_SIZE_M
+
+
+@functools.lru_cache(maxsize=2048)
+def use_nt(token, topk, e):
+    """The reference's non-temporal-load switch (aiter/fused_moe.py:531-537), same rule and
+    AITER_USE_NT override; the B200 kernels stream weights through TMA either way."""
+    v = int(os.environ.get("AITER_USE_NT", "-1"))
+    if v != -1:
+        return bool(v)
+    return (token * topk // e) < 64
+
+
+@functools.lru_cache(maxsize=2048)
+def get_ksplit(token, topk, expert, inter_dim, model_dim):
+    """Split-K factor (aiter/fused_moe.py:539-567 splits decode-size stage 1 over idle
+    CUs).  The B200 stage 1 does not split K: always 0."""
+    return 0
 
 
 @dataclass

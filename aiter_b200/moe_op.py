@@ -68,6 +68,18 @@ def moe_sorting_fwd(topk_ids: Tensor, topk_weights: Tensor, sorted_token_ids: Te
               local_expert_mask, num_local_tokens, dispatch_policy, workspace, token_sorted_pos)
 
 
+def moe_sorting_opus_fwd(topk_ids: Tensor, topk_weights: Tensor, sorted_token_ids: Tensor,
+                         sorted_weights: Tensor, sorted_expert_ids: Tensor, num_valid_ids: Tensor,
+                         moe_buf: Tensor, num_experts: int, unit_size: int,
+                         local_expert_mask: Optional[Tensor] = None, num_local_tokens: Optional[Tensor] = None,
+                         dispatch_policy: int = 0) -> None:
+    """aiter.moe_sorting_opus_fwd (aiter/ops/moe_sorting_opus.py:12-25): the opus sorting
+    kernel has the same contract as moe_sorting_fwd (csrc/include/moe_sorting_opus.h:274-322),
+    so both names run the same kernels here."""
+    moe_sorting_fwd(topk_ids, topk_weights, sorted_token_ids, sorted_weights, sorted_expert_ids, num_valid_ids,
+                    moe_buf, num_experts, unit_size, local_expert_mask, num_local_tokens, dispatch_policy)
+
+
 def dynamic_per_token_scaled_quant(out: Tensor, input: Tensor, scales: Tensor,
                                    scale_ub: Optional[Tensor] = None, shuffle_scale: bool = False,
                                    num_rows: Optional[Tensor] = None, num_rows_factor: int = 1) -> None:
