@@ -160,6 +160,10 @@ def lib():
                             [ctypes.c_float, ctypes.POINTER(aiter_tensor_t), vp]),
                            ("custom_ar_allreduce_rmsnorm_ex", [c64] + [ctypes.POINTER(aiter_tensor_t)] * 5 +
                             [ctypes.c_float, ctypes.POINTER(aiter_tensor_t), c64, vp]),
+                           ("custom_ar_all_gather", [c64, ctypes.POINTER(aiter_tensor_t),
+                                                     ctypes.POINTER(aiter_tensor_t), c64, vp]),
+                           ("custom_ar_reduce_scatter", [c64, ctypes.POINTER(aiter_tensor_t),
+                                                         ctypes.POINTER(aiter_tensor_t), vp]),
                            ("custom_ar_dispose", [c64]), ("custom_ar_device_error", [ctypes.c_int]),
                            ("init_custom_qr", [c64, c64, c64, c64, p64, vp]), ("qr_open_handles", [c64, vp]),
                            ("qr_all_reduce", [c64, ctypes.POINTER(aiter_tensor_t), ctypes.POINTER(aiter_tensor_t),

@@ -175,6 +175,88 @@ allreduce_kernel(Peers P, int rank, int buffer, const uint4* __restrict__ in, ui
 }
 
 // ---------------------------------------------------------------------------
+// All-gather and reduce-scatter over the same staging buffers and per-CTA barriers
+// (the reference's custom all-gather / reduce-scatter kernels,
+// csrc/include/custom_all_reduce.cuh:678-800).  As in the allreduce, pack i of the
+// staged input is copied, and later read on every rank, by thread (i - lo) mod stride,
+// so a CTA reads only what the same CTA index of each peer staged before the barrier.
+
+// out = every rank's input in rank order: dim 0 (c16 == 0: out [W, n16 packs]) or the
+// last dim (c16 packs per input row: out row r = [rank 0's row r | rank 1's | ...]).
+template <int W>
+__global__ void __launch_bounds__(kThreads)
+allgather_kernel(Peers P, int rank, int buffer, const uint4* __restrict__ in, uint4* __restrict__ out, int64_t n16,
+                 int64_t c16, int end_barrier) {
+    __shared__ uint32_t s_epoch;
+    if (threadIdx.x == 0) s_epoch = next_epoch(P, rank);
+    __syncthreads();
+    const uint32_t epoch = s_epoch;
+    uint4* mine = reinterpret_cast<uint4*>(P.buf[buffer][rank]);
+    const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    if (in != mine)
+        for (int64_t i = tid; i < n16; i += stride) mine[i] = in[i];
+    if (!block_barrier(P, rank, W, 0, epoch)) return;
+#pragma unroll 1
+    for (int s = 0; s < W; ++s) {
+        const int p = (rank + s) % W;  // own rows first, then spread the peer traffic
+        const uint4* src = reinterpret_cast<const uint4*>(P.buf[buffer][p]);
+        for (int64_t i = tid; i < n16; i += 4 * stride) {
+            uint4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (i + u * stride < n16) v[u] = ld_cg(src + i + u * stride);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int64_t j = i + u * stride;
+                if (j < n16) {
+                    const int64_t o = c16 == 0 ? (int64_t)p * n16 + j : (j / c16) * (W * c16) + p * c16 + j % c16;
+                    out[o] = v[u];
+                }
+            }
+        }
+    }
+    if (end_barrier) block_barrier(P, rank, W, 2, epoch);
+}
+
+// out = segment `rank` (n16 / W packs) of the sum over ranks of the inputs, summed
+// in rank order in fp32 and rounded once (the first phase of the two-shot allreduce).
+template <typename T, int W>
+__global__ void __launch_bounds__(kThreads)
+reduce_scatter_kernel(Peers P, int rank, int buffer, const uint4* __restrict__ in, uint4* __restrict__ out,
+                      int64_t n16, int end_barrier) {
+    __shared__ uint32_t s_epoch;
+    if (threadIdx.x == 0) s_epoch = next_epoch(P, rank);
+    __syncthreads();
+    const uint32_t epoch = s_epoch;
+    uint4* mine = reinterpret_cast<uint4*>(P.buf[buffer][rank]);
+    const uint4* bufs[W];
+#pragma unroll
+    for (int p = 0; p < W; ++p) bufs[p] = reinterpret_cast<const uint4*>(P.buf[buffer][p]);
+    const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t seg = n16 / W;
+    if (in != mine) {
+        for (int s = 0; s < W; ++s) {
+            const int64_t lo = (int64_t)s * seg;
+            for (int64_t i = lo + tid; i < lo + seg; i += stride) mine[i] = in[i];
+        }
+    }
+    if (!block_barrier(P, rank, W, 0, epoch)) return;
+    const int64_t lo = (int64_t)rank * seg;
+    for (int64_t i = lo + tid; i < lo + seg; i += stride) {
+        uint4 v[W];
+#pragma unroll
+        for (int p = 0; p < W; ++p) v[p] = ld_cg(bufs[p] + i);
+        float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+        for (int p = 0; p < W; ++p) Elem<T>::acc(a, v[p]);
+        out[i - lo] = Elem<T>::pack(a);
+    }
+    if (end_barrier) block_barrier(P, rank, W, 2, epoch);
+}
+
+// ---------------------------------------------------------------------------
 // fp8-quantised two-shot allreduce of fp16 data: the reference's allReduceQuantFp8
 // (csrc/include/custom_all_reduce.cuh:1018-1088), used with open_fp8_quant for fp16
 // messages of at least 128 * 2048 elements (csrc/kernels/custom_all_reduce.cu:90-96).
@@ -662,6 +744,116 @@ AB_ENTRY(custom_ar_all_reduce_fp8, (int64_t ctx, aiter_tensor_t* inp, aiter_tens
         default: allreduce_fp8q_kernel<8><<<grid, kThreads, 0, st>>>(c->peers, c->rank, buffer, src, dst, n8, gp, q_off, s_off, endb); break;
     }
     check_launch("custom_ar_all_reduce_fp8");
+}
+
+// All-gather over peer memory (the reference's custom all-gather,
+// aiter/dist/parallel_state.py:492-501, csrc/include/custom_all_reduce.cuh:678-740):
+// inp [..] of any dtype (a multiple of 16 bytes), out = the W inputs in rank order
+// along dim 0 (last_dim == 0: out [W * inp.shape[0], ...]) or along the last dim
+// (last_dim != 0: out [..., W * inp.shape[-1]], rows a multiple of 16 bytes).
+AB_ENTRY(custom_ar_all_gather, (int64_t ctx, aiter_tensor_t* inp, aiter_tensor_t* out, int64_t last_dim, void* stream),
+         (ctx, inp, out, last_dim, stream)) {
+    using namespace ab;
+    Ctx* c = as_ctx(ctx);
+    AB_CHECK(c->ready, "custom_ar_open_peers has not been called");
+    need(inp, "inp");
+    need(out, "out");
+    AB_CHECK(inp->dtype_ == out->dtype_, "inp and out dtypes differ");
+    need_contig(inp, "inp");
+    need_contig(out, "out");
+    const size_t esz = elem_size(inp->dtype_);
+    const size_t bytes = inp->numel_ * esz;
+    AB_CHECK(out->numel_ == inp->numel_ * (size_t)c->world, "out must hold world x inp elements");
+    AB_CHECK(bytes % 16 == 0, "all-gather size must be a multiple of 16 bytes");
+    AB_CHECK(bytes <= c->max_bytes, "all-gather of ", bytes, " bytes exceeds the registered ", c->max_bytes);
+    AB_CHECK(((uintptr_t)inp->ptr & 15) == 0 && ((uintptr_t)out->ptr & 15) == 0, "buffers must be 16-byte aligned");
+    AB_CHECK(inp->device_id == c->device && out->device_id == c->device,
+             "tensor on a different device than the communicator");
+    int64_t c16 = 0;
+    if (last_dim) {
+        AB_CHECK(inp->ndim >= 1, "inp needs a last dim");
+        const int64_t rowb = inp->shape[inp->ndim - 1] * (int64_t)esz;
+        AB_CHECK(rowb % 16 == 0, "rows must be a multiple of 16 bytes for a last-dim all-gather");
+        c16 = rowb / 16;
+    }
+    if (bytes == 0) return;
+    DeviceGuard dg(c->device);
+    cudaStream_t st = as_stream(stream);
+    const Slot slot = take_slot(c, st);
+    const int64_t n16 = (int64_t)(bytes / 16);
+    const int64_t per_block = (int64_t)kThreads * 2;
+    const int grid = (int)std::max<int64_t>(
+        1, std::min<int64_t>((n16 + per_block - 1) / per_block, std::min(kMaxBlocks, num_sms(c->device))));
+    const uint4* src = (const uint4*)inp->ptr;
+    uint4* dst = (uint4*)out->ptr;
+    switch (c->world) {
+        case 2: allgather_kernel<2><<<grid, kThreads, 0, st>>>(c->peers, c->rank, slot.buffer, src, dst, n16, c16, slot.end_barrier); break;
+        case 3: allgather_kernel<3><<<grid, kThreads, 0, st>>>(c->peers, c->rank, slot.buffer, src, dst, n16, c16, slot.end_barrier); break;
+        case 4: allgather_kernel<4><<<grid, kThreads, 0, st>>>(c->peers, c->rank, slot.buffer, src, dst, n16, c16, slot.end_barrier); break;
+        case 5: allgather_kernel<5><<<grid, kThreads, 0, st>>>(c->peers, c->rank, slot.buffer, src, dst, n16, c16, slot.end_barrier); break;
+        case 6: allgather_kernel<6><<<grid, kThreads, 0, st>>>(c->peers, c->rank, slot.buffer, src, dst, n16, c16, slot.end_barrier); break;
+        case 7: allgather_kernel<7><<<grid, kThreads, 0, st>>>(c->peers, c->rank, slot.buffer, src, dst, n16, c16, slot.end_barrier); break;
+        default: allgather_kernel<8><<<grid, kThreads, 0, st>>>(c->peers, c->rank, slot.buffer, src, dst, n16, c16, slot.end_barrier); break;
+    }
+    check_launch("custom_ar_all_gather");
+}
+
+// Reduce-scatter over peer memory (the reference's custom reduce-scatter,
+// aiter/dist/parallel_state.py:511-538, csrc/include/custom_all_reduce.cuh:740-800):
+// inp [n] (bf16, fp16 or fp32; n a multiple of world, every rank's share a multiple
+// of 16 bytes), out [n / world] = elements [rank * n / world, (rank + 1) * n / world)
+// of the sum over ranks, accumulated in fp32 in rank order (identical to the same
+// elements of custom_ar_all_reduce's result).
+AB_ENTRY(custom_ar_reduce_scatter, (int64_t ctx, aiter_tensor_t* inp, aiter_tensor_t* out, void* stream),
+         (ctx, inp, out, stream)) {
+    using namespace ab;
+    Ctx* c = as_ctx(ctx);
+    AB_CHECK(c->ready, "custom_ar_open_peers has not been called");
+    need(inp, "inp");
+    need(out, "out");
+    AB_CHECK(inp->dtype_ == AITER_DTYPE_bf16 || inp->dtype_ == AITER_DTYPE_fp16 || inp->dtype_ == AITER_DTYPE_fp32,
+             "reduce-scatter supports bf16, fp16 and fp32, got ", dtype_name(inp->dtype_));
+    need_dtype(out, inp->dtype_, "out");
+    need_contig(inp, "inp");
+    need_contig(out, "out");
+    const size_t esz = elem_size(inp->dtype_);
+    const size_t bytes = inp->numel_ * esz;
+    AB_CHECK(inp->numel_ % (size_t)c->world == 0 && out->numel_ == inp->numel_ / (size_t)c->world,
+             "out must hold inp.numel / world elements");
+    AB_CHECK((bytes / (size_t)c->world) % 16 == 0, "every rank's share must be a multiple of 16 bytes");
+    AB_CHECK(bytes <= c->max_bytes, "reduce-scatter of ", bytes, " bytes exceeds the registered ", c->max_bytes);
+    AB_CHECK(((uintptr_t)inp->ptr & 15) == 0 && ((uintptr_t)out->ptr & 15) == 0, "buffers must be 16-byte aligned");
+    AB_CHECK(inp->device_id == c->device && out->device_id == c->device,
+             "tensor on a different device than the communicator");
+    if (bytes == 0) return;
+    DeviceGuard dg(c->device);
+    cudaStream_t st = as_stream(stream);
+    const Slot slot = take_slot(c, st);
+    const int64_t n16 = (int64_t)(bytes / 16);
+    const int64_t per_block = (int64_t)kThreads * 2;
+    const int grid = (int)std::max<int64_t>(
+        1, std::min<int64_t>((n16 / c->world + per_block - 1) / per_block, std::min(kMaxBlocks, num_sms(c->device))));
+    const uint4* src = (const uint4*)inp->ptr;
+    uint4* dst = (uint4*)out->ptr;
+#define AB_RS(TT)                                                                                                  \
+    switch (c->world) {                                                                                            \
+        case 2: reduce_scatter_kernel<TT, 2><<<grid, kThreads, 0, st>>>(c->peers, c->rank, slot.buffer, src, dst, n16, slot.end_barrier); break; \
+        case 3: reduce_scatter_kernel<TT, 3><<<grid, kThreads, 0, st>>>(c->peers, c->rank, slot.buffer, src, dst, n16, slot.end_barrier); break; \
+        case 4: reduce_scatter_kernel<TT, 4><<<grid, kThreads, 0, st>>>(c->peers, c->rank, slot.buffer, src, dst, n16, slot.end_barrier); break; \
+        case 5: reduce_scatter_kernel<TT, 5><<<grid, kThreads, 0, st>>>(c->peers, c->rank, slot.buffer, src, dst, n16, slot.end_barrier); break; \
+        case 6: reduce_scatter_kernel<TT, 6><<<grid, kThreads, 0, st>>>(c->peers, c->rank, slot.buffer, src, dst, n16, slot.end_barrier); break; \
+        case 7: reduce_scatter_kernel<TT, 7><<<grid, kThreads, 0, st>>>(c->peers, c->rank, slot.buffer, src, dst, n16, slot.end_barrier); break; \
+        default: reduce_scatter_kernel<TT, 8><<<grid, kThreads, 0, st>>>(c->peers, c->rank, slot.buffer, src, dst, n16, slot.end_barrier); break; \
+    }
+    if (inp->dtype_ == AITER_DTYPE_bf16) {
+        AB_RS(__nv_bfloat16)
+    } else if (inp->dtype_ == AITER_DTYPE_fp16) {
+        AB_RS(__half)
+    } else {
+        AB_RS(float)
+    }
+#undef AB_RS
+    check_launch("custom_ar_reduce_scatter");
 }
 
 AB_ENTRY(custom_ar_dispose, (int64_t ctx), (ctx)) {

@@ -1,10 +1,12 @@
 """Multi-GPU plumbing of the path (the role of aiter/dist): process groups, the
 CUDA-IPC custom and quick allreduces, EP dispatch / combine and the collective
 front-ends."""
-from .communication_op import (shard_moe_weights_for_tp, tensor_model_parallel_all_reduce,
+from .communication_op import (broadcast_tensor_dict, shard_moe_weights_for_tp, tensor_model_parallel_all_gather,
+                               tensor_model_parallel_all_reduce, tensor_model_parallel_custom_all_gather,
                                tensor_model_parallel_fused_allreduce_rmsnorm,
                                tensor_model_parallel_fused_allreduce_rmsnorm_quant, tensor_model_parallel_fused_moe,
-                               tensor_model_parallel_gemm_all_reduce)
+                               tensor_model_parallel_gather, tensor_model_parallel_gemm_all_reduce,
+                               tensor_model_parallel_reduce_scatter)
 from .custom_all_reduce import CustomAllreduce
 from .ep import EpAll2AllManager, EpDispatchCombineConfig, EpDispatchCombineOp
 from .quick_all_reduce import QuickAllReduce, QuickReduceRegime

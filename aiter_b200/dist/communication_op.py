@@ -10,6 +10,34 @@ def tensor_model_parallel_all_reduce(input_: torch.Tensor, use_new: bool = True,
     return get_tp_group().all_reduce(input_, use_new, open_fp8_quant, prefill_support)
 
 
+def tensor_model_parallel_custom_all_gather(input_: torch.Tensor) -> torch.Tensor:
+    """(communication_op.py:68-69 in the reference)"""
+    return get_tp_group().custom_all_gather(input_)
+
+
+def tensor_model_parallel_reduce_scatter(input_: torch.Tensor, use_custom: bool = True,
+                                         dim: int = 0) -> torch.Tensor:
+    """(communication_op.py:72-77)"""
+    return get_tp_group().reduce_scatter_tensor(input_, use_custom, dim)
+
+
+def tensor_model_parallel_all_gather(input_: torch.Tensor, use_custom: bool = False, dim: int = -1) -> torch.Tensor:
+    """(communication_op.py:80-86)"""
+    return get_tp_group().all_gather(input_, use_custom, dim)
+
+
+def tensor_model_parallel_gather(input_: torch.Tensor, dst: int = 0, dim: int = -1):
+    """(communication_op.py:89-93)"""
+    return get_tp_group().gather(input_, dst, dim)
+
+
+def broadcast_tensor_dict(tensor_dict=None, src: int = 0):
+    """(communication_op.py:96-101)"""
+    if not torch.distributed.is_initialized():
+        return tensor_dict
+    return get_tp_group().broadcast_tensor_dict(tensor_dict, src)
+
+
 def tensor_model_parallel_gemm_all_reduce(a: torch.Tensor, w: torch.Tensor, fused: bool = False) -> torch.Tensor:
     """allreduce(a @ w^T) over the TP group, GEMM and allreduce sharing the IPC
     staging buffer (`fused=True`: one kernel, the GEMM pushing its tiles to the

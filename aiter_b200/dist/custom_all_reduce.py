@@ -10,6 +10,7 @@ as the reference exchanges them over its CPU group / TCP store
 import contextlib
 import ctypes
 import logging
+from typing import Optional
 
 import torch
 import torch.distributed as dist
@@ -123,6 +124,44 @@ class CustomAllreduce:
         if ret:
             _lib.check_status(name, ret)
         return out
+
+    def custom_all_gather(self, inp: torch.Tensor, dim: int = 0) -> Optional[torch.Tensor]:
+        """All-gather over peer memory along dim 0 or the last dim (the reference's
+        custom all-gather); None when the tensor is not eligible (size, alignment)."""
+        if self.disabled:
+            return None
+        nd = inp.dim()
+        dim = dim + nd if dim < 0 else dim
+        esz = inp.element_size()
+        nbytes = inp.numel() * esz
+        last = nd > 0 and dim == nd - 1 and dim != 0
+        if not inp.is_contiguous() or nbytes % 16 or nbytes > self.max_size or (dim != 0 and not last) \
+                or (last and (inp.shape[-1] * esz) % 16):
+            return None
+        shape = list(inp.shape) if nd else [1]
+        shape[dim if nd else 0] *= self.world_size
+        out = torch.empty(shape, dtype=inp.dtype, device=inp.device)
+        a, b = _lib.to_aiter(inp), _lib.to_aiter(out)
+        ret = self._L.custom_ar_all_gather(self._ctx, ctypes.byref(a), ctypes.byref(b), 1 if last else 0,
+                                           _lib.current_stream_ptr(self.device.index))
+        if ret:
+            _lib.check_status("custom_ar_all_gather", ret)
+        return out
+
+    def custom_reduce_scatter(self, inp: torch.Tensor, out: torch.Tensor) -> bool:
+        """Reduce-scatter over peer memory into `out` (numel / world elements, this rank's
+        share of the sum); False when the tensor is not eligible."""
+        if self.disabled or inp.dtype not in self._DTYPES or not inp.is_contiguous():
+            return False
+        nbytes = inp.numel() * inp.element_size()
+        if inp.numel() % self.world_size or (nbytes // self.world_size) % 16 or nbytes > self.max_size:
+            return False
+        a, b = _lib.to_aiter(inp), _lib.to_aiter(out)
+        ret = self._L.custom_ar_reduce_scatter(self._ctx, ctypes.byref(a), ctypes.byref(b),
+                                               _lib.current_stream_ptr(self.device.index))
+        if ret:
+            _lib.check_status("custom_ar_reduce_scatter", ret)
+        return True
 
     def custom_all_reduce(self, input: torch.Tensor, use_new: bool = True, open_fp8_quant: bool = False):
         if self.disabled or not self.should_custom_ar(input):

@@ -10,7 +10,8 @@ import contextlib
 import dataclasses
 import datetime
 import os
-from typing import Optional
+from collections import namedtuple
+from typing import Any, Dict, List, Optional, Tuple, Union
 
 import torch
 import torch.distributed as dist
@@ -33,6 +34,23 @@ def _rmsnorm_after(ar: torch.Tensor, res: torch.Tensor, w: torch.Tensor, eps: fl
     amax = y.abs().amax(dim=-1, keepdim=True)
     scale = torch.where(amax == 0, torch.ones_like(amax), amax / 448.0)
     return (y / scale).to(torch.float8_e4m3fn), res_out, scale
+
+
+TensorMetadata = namedtuple("TensorMetadata", ["device", "dtype", "size"])
+
+
+def _split_tensor_dict(tensor_dict: Dict[str, Any]) -> Tuple[List[Tuple[str, Any]], List[torch.Tensor]]:
+    """(metadata list, tensors): tensors become TensorMetadata entries, other values
+    travel as they are (parallel_state.py:55-78 in the reference)."""
+    metadata_list, tensor_list = [], []
+    for key, value in tensor_dict.items():
+        if isinstance(value, torch.Tensor):
+            device = value.device.type
+            metadata_list.append((key, TensorMetadata(device, value.dtype, value.size())))
+            tensor_list.append(value)
+        else:
+            metadata_list.append((key, value))
+    return metadata_list, tensor_list
 
 
 @dataclasses.dataclass
@@ -78,6 +96,114 @@ class GroupCoordinator:
                 return out
         out = input_.clone()
         dist.all_reduce(out, group=self.device_group)
+        return out
+
+    def custom_all_gather(self, input_: torch.Tensor) -> torch.Tensor:
+        """All-gather along dim 0 over peer memory (parallel_state.py:500-501 in the
+        reference), NCCL when the IPC path does not take the tensor."""
+        return self.all_gather(input_, use_custom=True, dim=0)
+
+    def all_gather(self, input_: torch.Tensor, use_custom: bool = False, dim: int = -1) -> torch.Tensor:
+        """Concatenate every rank's tensor along `dim` (parallel_state.py:540-577).
+        use_custom: the IPC all-gather for dim 0 or the last dim when eligible."""
+        world = self.world_size
+        if world == 1:
+            return input_
+        assert -input_.dim() <= dim < input_.dim(), f"Invalid dim ({dim}) for input tensor with shape {input_.size()}"
+        if dim < 0:
+            dim += input_.dim()
+        if use_custom and self.ca_comm is not None and not self.ca_comm.disabled:
+            out = self.ca_comm.custom_all_gather(input_, dim)
+            if out is not None:
+                return out
+        size = input_.size()
+        # [world * n0, ...] is the output layout every backend accepts; viewed as [world, ...]
+        flat = torch.empty((world * size[0],) + tuple(size[1:]), dtype=input_.dtype, device=input_.device)
+        dist.all_gather_into_tensor(flat, input_.contiguous(), group=self.device_group)
+        out = flat.view((world,) + tuple(size)).movedim(0, dim)
+        return out.reshape(size[:dim] + (world * size[dim],) + size[dim + 1:])
+
+    def reduce_scatter_tensor(self, input_: torch.Tensor, use_custom: bool = True, dim: int = 0) -> torch.Tensor:
+        """This rank's 1/world share of the sum along dim 0 (parallel_state.py:511-538):
+        [n0 / world, ...] when dim 0 divides, else the flat share.  use_custom: the IPC
+        reduce-scatter (rank-ordered fp32 sums, the allreduce's bits) when eligible."""
+        world = self.world_size
+        assert world > 1, "error! world_size = 1"
+        assert input_.numel() % world == 0, "input shape error, input.numel() % world_size should equals to 0"
+        if input_.shape[0] % world == 0:
+            out_shape = (input_.shape[0] // world,) + tuple(input_.shape[1:])
+        else:
+            out_shape = (input_.numel() // world,)
+        out = torch.empty(out_shape, dtype=input_.dtype, device=input_.device)
+        if use_custom and self.ca_comm is not None and not self.ca_comm.disabled:
+            if self.ca_comm.custom_reduce_scatter(input_, out):
+                return out
+        src = input_.contiguous()
+        if out.dim() == 1 and input_.dim() != 1:
+            src = src.reshape(-1)  # flat shares: [n] in, [n / world] out
+        dist.reduce_scatter_tensor(out, src, group=self.device_group)
+        return out
+
+    def gather(self, input_: torch.Tensor, dst: int = 0, dim: int = -1) -> Optional[torch.Tensor]:
+        """Concatenation along `dim` on rank `dst` of the group, None elsewhere
+        (parallel_state.py:579-610)."""
+        world = self.world_size
+        if world == 1:
+            return input_
+        assert -input_.dim() <= dim < input_.dim(), f"Invalid dim ({dim}) for input tensor with shape {input_.size()}"
+        if dim < 0:
+            dim += input_.dim()
+        gather_list = [torch.empty_like(input_) for _ in range(world)] if self.rank_in_group == dst else None
+        dist.gather(input_, gather_list, dst=self.ranks[dst], group=self.device_group)
+        return torch.cat(gather_list, dim=dim) if self.rank_in_group == dst else None
+
+    def broadcast(self, input_: torch.Tensor, src: int = 0) -> torch.Tensor:
+        assert src < self.world_size, f"Invalid src rank ({src})"
+        if self.world_size == 1:
+            return input_
+        dist.broadcast(input_, src=self.ranks[src], group=self.device_group)
+        return input_
+
+    def broadcast_object(self, obj: Optional[Any] = None, src: int = 0):
+        assert src < self.world_size, f"Invalid src rank ({src})"
+        if self.world_size == 1:
+            return obj
+        holder = [obj if self.rank_in_group == src else None]
+        dist.broadcast_object_list(holder, src=self.ranks[src], group=self.cpu_group)
+        return holder[0]
+
+    def broadcast_tensor_dict(self, tensor_dict: Optional[Dict[str, Union[torch.Tensor, Any]]] = None,
+                              src: int = 0) -> Optional[Dict[str, Union[torch.Tensor, Any]]]:
+        """Broadcast a dict of tensors and plain values from rank `src` (parallel_state.py:
+        731-800): the metadata goes over the CPU group, CPU tensors over the CPU group
+        and device tensors over the device group."""
+        if not dist.is_initialized() or self.world_size == 1:
+            return tensor_dict
+        assert src < self.world_size, f"Invalid src rank ({src})"
+        if self.rank_in_group == src:
+            assert isinstance(tensor_dict, dict), f"Expecting a dictionary, got {type(tensor_dict)}"
+            metadata_list, tensors = _split_tensor_dict(tensor_dict)
+            self.broadcast_object(metadata_list, src=src)
+            handles = [dist.broadcast(t, src=self.ranks[src], async_op=True,
+                                      group=self.cpu_group if t.is_cpu else self.device_group)
+                       for t in tensors if t.numel() > 0]
+            for h in handles:
+                h.wait()
+            return tensor_dict
+        metadata_list = self.broadcast_object(None, src=src)
+        out, handles = {}, []
+        for key, value in metadata_list:
+            if isinstance(value, TensorMetadata):
+                dev = torch.device("cpu") if value.device == "cpu" else self.device
+                t = torch.empty(value.size, dtype=value.dtype, device=dev)
+                if t.numel() > 0:
+                    handles.append(dist.broadcast(t, src=self.ranks[src], async_op=True,
+                                                  group=self.cpu_group if t.is_cpu else self.device_group))
+                out[key] = t
+            else:
+                out[key] = value
+        for h in handles:
+            h.wait()
         return out
 
     def fused_allreduce_rmsnorm(self, input_: torch.Tensor, residual_inp_: torch.Tensor, weight_: torch.Tensor,

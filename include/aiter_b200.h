@@ -362,6 +362,17 @@ int custom_ar_allreduce_rmsnorm(int64_t ctx, aiter_tensor_t* inp, aiter_tensor_t
 int custom_ar_allreduce_rmsnorm_ex(int64_t ctx, aiter_tensor_t* inp, aiter_tensor_t* res_inp,
                                    aiter_tensor_t* res_out, aiter_tensor_t* out, aiter_tensor_t* weight,
                                    float eps, aiter_tensor_t* scale_out, int64_t force_two_shot, void* stream);
+/* All-gather over peer memory (the reference's custom all-gather,
+ * aiter/dist/parallel_state.py:492-501, csrc/include/custom_all_reduce.cuh:678-740):
+ * inp of any dtype (a multiple of 16 bytes, <= max_bytes), out = the world inputs in
+ * rank order along dim 0 (last_dim == 0) or along the last dim (last_dim != 0; input
+ * rows a multiple of 16 bytes). */
+int custom_ar_all_gather(int64_t ctx, aiter_tensor_t* inp, aiter_tensor_t* out, int64_t last_dim, void* stream);
+/* Reduce-scatter over peer memory (the reference's custom reduce-scatter,
+ * aiter/dist/parallel_state.py:511-538): inp [n] bf16 / fp16 / fp32 (n a multiple of
+ * world, each share a multiple of 16 bytes), out [n / world] = this rank's share of
+ * the rank-ordered fp32 sum (the same bits as those elements of custom_ar_all_reduce). */
+int custom_ar_reduce_scatter(int64_t ctx, aiter_tensor_t* inp, aiter_tensor_t* out, void* stream);
 int custom_ar_dispose(int64_t ctx);
 /* Error word of the allreduce barriers (1 = a peer did not arrive within 2 s). */
 int custom_ar_device_error(int clear);

@@ -117,3 +117,37 @@ def test_nccl_group_rejected_for_handle_exchange():
             CustomAllreduce(G(), 0)
     finally:
         dist.get_backend = orig
+
+
+def _group_collectives(rank, world, port):
+    """all_gather (dim 0, last, middle), reduce_scatter_tensor (divisible and flat),
+    gather, broadcast_tensor_dict and the front-ends, on the non-custom path."""
+    _init(rank, world, port)
+    from aiter_b200.dist import communication_op as co
+    from aiter_b200.dist import parallel_state as ps
+    ps.initialize_model_parallel(world, local_rank=rank, backend="gloo", use_custom_allreduce=False)
+    x = torch.arange(24, dtype=torch.float32).reshape(2, 3, 4) + 100 * rank
+    parts = [torch.arange(24, dtype=torch.float32).reshape(2, 3, 4) + 100 * r for r in range(world)]
+    for dim in (0, 1, -1):
+        got = co.tensor_model_parallel_all_gather(x, dim=dim)
+        assert torch.equal(got, torch.cat(parts, dim=dim)), dim
+    assert torch.equal(co.tensor_model_parallel_custom_all_gather(x), torch.cat(parts, dim=0))
+    y = torch.arange(12, dtype=torch.float32).reshape(4, 3) * (rank + 1)
+    total = sum(torch.arange(12, dtype=torch.float32).reshape(4, 3) * (r + 1) for r in range(world))
+    rs = co.tensor_model_parallel_reduce_scatter(y)
+    assert rs.shape == (4 // world, 3) and torch.equal(rs, total.chunk(world, dim=0)[rank])
+    z = torch.arange(6, dtype=torch.float32).reshape(3, 2) * (rank + 1)   # 3 rows: flat shares
+    ztot = sum(torch.arange(6, dtype=torch.float32).reshape(3, 2) * (r + 1) for r in range(world)).reshape(-1)
+    rz = co.tensor_model_parallel_reduce_scatter(z)
+    assert rz.shape == (6 // world,) and torch.equal(rz, ztot.chunk(world)[rank])
+    g = co.tensor_model_parallel_gather(x, dst=0, dim=0)
+    assert (torch.equal(g, torch.cat(parts, dim=0)) if rank == 0 else g is None)
+    d = co.broadcast_tensor_dict({"a": torch.ones(2, 2) * 7, "n": 3, "e": torch.empty(0)} if rank == 0 else None,
+                                 src=0)
+    assert torch.equal(d["a"], torch.ones(2, 2) * 7) and d["n"] == 3 and d["e"].numel() == 0
+    ps.destroy_model_parallel()
+    dist.destroy_process_group()
+
+
+def test_group_coordinator_collectives_fallback_path():
+    run_ranks(_group_collectives, 2)

@@ -8,7 +8,9 @@ AITER_B200_TEST_UNRUN=1.
 * open_fp8_quant with fp16: every rank's output bit-exact against the restatement of
   the reference's allReduceQuantFp8 (oracle/allreduce.py), including group sizes
   below 128 and a message whose pack count leaves a remainder for the last rank;
-  bf16 and small fp16 messages ignore the flag (plain allreduce bits).
+  bf16 and small fp16 messages ignore the flag (plain allreduce bits);
+* IPC all-gather along dim 0 and the last dim (exact concatenation) and reduce-scatter
+  (this rank's share of the rank-ordered fp32 sum, the allreduce's bits).
 """
 import os
 import sys
@@ -90,6 +92,34 @@ def _worker(rank, world, port):
         z = ca.all_reduce(xs[rank].to(dev))
         torch.cuda.synchronize()
         assert torch.equal(y, z), (dtype, n)
+    # IPC all-gather (dim 0 and last dim) and reduce-scatter
+    for i, (dtype, shape) in enumerate([(torch.bfloat16, (64, 512)), (torch.float32, (3, 1024)),
+                                        (torch.float16, (1, 8))]):
+        xs = [t.reshape(shape) for t in _inputs(int(np.prod(shape)), world, 80 + i, dtype)]
+        x = xs[rank].to(dev)
+        g0 = ca.custom_all_gather(x, 0)
+        gl = ca.custom_all_gather(x, -1)
+        torch.cuda.synchronize()
+        assert _lib.lib().custom_ar_device_error(1) == 0
+        assert torch.equal(g0.cpu(), torch.cat(xs, dim=0)), (dtype, shape)
+        if (shape[-1] * x.element_size()) % 16 == 0:
+            assert torch.equal(gl.cpu(), torch.cat(xs, dim=-1)), (dtype, shape)
+        assert torch.equal(tp.all_gather(x, use_custom=True, dim=0).cpu(), torch.cat(xs, dim=0))
+    for i, (dtype, n) in enumerate([(torch.bfloat16, world * 4096), (torch.float32, world * 1000),
+                                    (torch.float16, world * 8)]):
+        xs = _inputs(n, world, 90 + i, dtype)
+        x = xs[rank].to(dev)
+        out = torch.empty(n // world, dtype=dtype, device=dev)
+        assert ca.custom_reduce_scatter(x, out)
+        full = ca.all_reduce(x)
+        torch.cuda.synchronize()
+        assert _lib.lib().custom_ar_device_error(1) == 0
+        want = allreduce_rank_order([t.numpy() for t in xs], xs[0].numpy().dtype).reshape(-1)
+        seg = n // world
+        assert np.array_equal(out.cpu().numpy(), want[rank * seg:(rank + 1) * seg]), (dtype, n)
+        assert torch.equal(out, full.reshape(-1)[rank * seg:(rank + 1) * seg])
+        rs = tp.reduce_scatter_tensor(x.reshape(world, -1))
+        assert torch.equal(rs.reshape(-1), out)
     ps.destroy_model_parallel()
     dist.destroy_process_group()
 
