@@ -10,6 +10,16 @@ from .communication_op import (broadcast_tensor_dict, shard_moe_weights_for_tp, 
 from .custom_all_reduce import CustomAllreduce
 from .ep import EpAll2AllManager, EpDispatchCombineConfig, EpDispatchCombineOp
 from .quick_all_reduce import QuickAllReduce, QuickReduceRegime
+from .communication_op import (data_parallel_all_gather, data_parallel_all_reduce, data_parallel_broadcast,
+                               data_parallel_broadcast_tensor_dict, data_parallel_gather, data_parallel_reduce_scatter,
+                               expert_parallel_all_gather, expert_parallel_all_reduce, expert_parallel_broadcast,
+                               expert_parallel_broadcast_tensor_dict, expert_parallel_gather,
+                               expert_parallel_reduce_scatter, pipeline_model_parallel_all_gather,
+                               pipeline_model_parallel_all_reduce, pipeline_model_parallel_broadcast,
+                               pipeline_model_parallel_broadcast_tensor_dict, pipeline_model_parallel_recv,
+                               pipeline_model_parallel_send)
 from .parallel_state import (GraphCaptureContext, GroupCoordinator, destroy_distributed_environment,
-                             destroy_model_parallel, get_tp_group, graph_capture, init_distributed_environment,
-                             initialize_model_parallel)
+                             destroy_model_parallel, ensure_model_parallel_initialized, get_dp_group, get_ep_group,
+                             get_pp_group, get_tensor_model_parallel_rank, get_tensor_model_parallel_world_size,
+                             get_tp_group, graph_capture, init_distributed_environment, initialize_model_parallel,
+                             model_parallel_is_initialized)

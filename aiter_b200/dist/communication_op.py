@@ -1,7 +1,8 @@
-"""Collective front-ends (aiter/dist/communication_op.py:30-37)."""
+"""Collective front-ends (aiter/dist/communication_op.py:30-244): the TP group's, and
+the EP / DP / PP groups' thin wrappers."""
 import torch
 
-from .parallel_state import get_tp_group
+from .parallel_state import get_dp_group, get_ep_group, get_pp_group, get_tp_group
 
 
 def tensor_model_parallel_all_reduce(input_: torch.Tensor, use_new: bool = True, open_fp8_quant: bool = False,
@@ -119,3 +120,84 @@ def tensor_model_parallel_fused_moe(hidden_states, w1, w2, topk_weight, topk_ids
     stage = ca.next_buffer_tensor((M, D), torch.bfloat16)
     fused_moe(hidden_states, w1, w2, topk_weight, topk_ids, moe_buf=stage, **kwargs)
     return ca.all_reduce(stage)
+
+
+# ---------------------------------------------------------------- EP / DP / PP groups
+# (communication_op.py:105-244 in the reference)
+
+def expert_parallel_all_reduce(input_, use_new=True, open_fp8_quant=False):
+    return get_ep_group().all_reduce(input_, use_new, open_fp8_quant)
+
+
+def expert_parallel_all_gather(input_, use_custom=False, dim=-1):
+    return get_ep_group().all_gather(input_, use_custom, dim)
+
+
+def expert_parallel_reduce_scatter(input_, use_custom=True, dim=0):
+    return get_ep_group().reduce_scatter_tensor(input_, use_custom, dim)
+
+
+def expert_parallel_gather(input_, dst=0, dim=-1):
+    return get_ep_group().gather(input_, dst, dim)
+
+
+def expert_parallel_broadcast(input_, src=0):
+    return get_ep_group().broadcast(input_, src)
+
+
+def expert_parallel_broadcast_tensor_dict(tensor_dict=None, src=0):
+    if not torch.distributed.is_initialized():
+        return tensor_dict
+    return get_ep_group().broadcast_tensor_dict(tensor_dict, src)
+
+
+def data_parallel_all_reduce(input_, use_new=True, open_fp8_quant=False):
+    return get_dp_group().all_reduce(input_, use_new, open_fp8_quant)
+
+
+def data_parallel_all_gather(input_, use_custom=False, dim=-1):
+    return get_dp_group().all_gather(input_, use_custom, dim)
+
+
+def data_parallel_reduce_scatter(input_, use_custom=True, dim=0):
+    return get_dp_group().reduce_scatter_tensor(input_, use_custom, dim)
+
+
+def data_parallel_gather(input_, dst=0, dim=-1):
+    return get_dp_group().gather(input_, dst, dim)
+
+
+def data_parallel_broadcast(input_, src=0):
+    return get_dp_group().broadcast(input_, src)
+
+
+def data_parallel_broadcast_tensor_dict(tensor_dict=None, src=0):
+    if not torch.distributed.is_initialized():
+        return tensor_dict
+    return get_dp_group().broadcast_tensor_dict(tensor_dict, src)
+
+
+def pipeline_model_parallel_all_reduce(input_, use_new=True, open_fp8_quant=False):
+    return get_pp_group().all_reduce(input_, use_new, open_fp8_quant)
+
+
+def pipeline_model_parallel_all_gather(input_, use_custom=False, dim=-1):
+    return get_pp_group().all_gather(input_, use_custom, dim)
+
+
+def pipeline_model_parallel_broadcast(input_, src=0):
+    return get_pp_group().broadcast(input_, src)
+
+
+def pipeline_model_parallel_send(input_, dst=None):
+    get_pp_group().send(input_, dst)
+
+
+def pipeline_model_parallel_recv(size, dtype, src=None):
+    return get_pp_group().recv(size, dtype, src)
+
+
+def pipeline_model_parallel_broadcast_tensor_dict(tensor_dict=None, src=0):
+    if not torch.distributed.is_initialized():
+        return tensor_dict
+    return get_pp_group().broadcast_tensor_dict(tensor_dict, src)

@@ -20,6 +20,9 @@ from .custom_all_reduce import CustomAllreduce
 from .quick_all_reduce import QuickAllReduce
 
 _TP: Optional["GroupCoordinator"] = None
+_PP: Optional["GroupCoordinator"] = None
+_DP: Optional["GroupCoordinator"] = None
+_EP: Optional["GroupCoordinator"] = None
 
 
 def _rmsnorm_after(ar: torch.Tensor, res: torch.Tensor, w: torch.Tensor, eps: float, quant: bool):
@@ -60,7 +63,7 @@ class GraphCaptureContext:
 
 class GroupCoordinator:
     def __init__(self, ranks, local_rank, backend="nccl", use_custom_allreduce=True,
-                 ca_max_size=128 * 1024 * 1024, timeout_s=120):
+                 ca_max_size=128 * 1024 * 1024, timeout_s=120, use_quick_allreduce=True, group_name=""):
         self.ranks = list(ranks)
         self.world_size = len(self.ranks)
         self.rank = dist.get_rank()
@@ -75,10 +78,21 @@ class GroupCoordinator:
         self.qr_comm = None
         if use_custom_allreduce and self.world_size > 1 and self.device.type == "cuda":
             self.ca_comm = CustomAllreduce(self.cpu_group, self.device, ca_max_size)
-        if self.world_size > 1 and self.device.type == "cuda":
+        if use_quick_allreduce and self.world_size > 1 and self.device.type == "cuda":
             # disabled unless AITER_QUICK_REDUCE_QUANTIZATION names a regime
             # (communicator_cuda.py:92-102 in the reference)
             self.qr_comm = QuickAllReduce(self.cpu_group, self.device)
+        self.unique_name = group_name
+        self._all2all_manager = None
+
+    @property
+    def all2all_manager(self):
+        """The EP group's dispatch / combine manager, created on first use
+        (communicator_cuda.py:104-146 in the reference, whose EP groups build MoRI's)."""
+        if self._all2all_manager is None and self.world_size > 1:
+            from .ep import EpAll2AllManager
+            self._all2all_manager = EpAll2AllManager(self.cpu_group)
+        return self._all2all_manager
 
     def all_reduce(self, input_: torch.Tensor, use_new: bool = True, open_fp8_quant: bool = False,
                    prefill_support: bool = False) -> torch.Tensor:
@@ -206,6 +220,20 @@ class GroupCoordinator:
             h.wait()
         return out
 
+    def send(self, tensor: torch.Tensor, dst: Optional[int] = None) -> None:
+        """Send to group rank `dst` (default: the next one; parallel_state.py:937-947)."""
+        if dst is None:
+            dst = (self.rank_in_group + 1) % self.world_size
+        dist.send(tensor, self.ranks[dst], self.device_group)
+
+    def recv(self, size, dtype, src: Optional[int] = None) -> torch.Tensor:
+        """Receive from group rank `src` (default: the previous one; :949-970)."""
+        if src is None:
+            src = (self.rank_in_group - 1) % self.world_size
+        tensor = torch.empty(size, dtype=dtype, device=self.device)
+        dist.recv(tensor, self.ranks[src], self.device_group)
+        return tensor
+
     def fused_allreduce_rmsnorm(self, input_: torch.Tensor, residual_inp_: torch.Tensor, weight_: torch.Tensor,
                                 eps: float, prefill_support: bool = False):
         """(out, residual_out) = (RMSNorm(allreduce(input_) + residual_inp_) * weight_,
@@ -258,6 +286,9 @@ class GroupCoordinator:
         if self.qr_comm is not None:
             self.qr_comm.close()
             self.qr_comm = None
+        if self._all2all_manager is not None:
+            self._all2all_manager.destroy()
+            self._all2all_manager = None
 
 
 def init_distributed_environment(world_size=-1, rank=-1, distributed_init_method="env://", local_rank=-1,
@@ -276,28 +307,88 @@ def init_distributed_environment(world_size=-1, rank=-1, distributed_init_method
     return local_rank
 
 
-def initialize_model_parallel(tensor_model_parallel_size=1, local_rank=None, backend="nccl",
-                              use_custom_allreduce=True, ca_max_size=128 * 1024 * 1024):
-    global _TP
-    world = dist.get_world_size()
-    assert world % tensor_model_parallel_size == 0
-    if local_rank is None:
-        local_rank = int(os.environ.get("LOCAL_RANK", str(dist.get_rank())))
+def _init_groups(group_ranks, local_rank, backend, name, use_custom_allreduce=False, ca_max_size=0,
+                 use_quick_allreduce=False):
+    """Every rank creates every group (a torch.distributed requirement); the rank keeps
+    a GroupCoordinator for the group that contains it."""
     me = dist.get_rank()
-    for g in range(world // tensor_model_parallel_size):
-        ranks = list(range(g * tensor_model_parallel_size, (g + 1) * tensor_model_parallel_size))
+    mine = None
+    for ranks in group_ranks:
         if me in ranks:
-            # every rank creates every group (torch.distributed requirement): only ours is kept
-            _TP = GroupCoordinator(ranks, local_rank, backend, use_custom_allreduce, ca_max_size)
+            mine = GroupCoordinator(ranks, local_rank, backend, use_custom_allreduce, ca_max_size,
+                                    use_quick_allreduce=use_quick_allreduce, group_name=name)
         else:
             dist.new_group(ranks, backend=backend)
             dist.new_group(ranks, backend="gloo")
+    return mine
+
+
+def initialize_model_parallel(tensor_model_parallel_size=1, pipeline_model_parallel_size=1, backend=None,
+                              data_parallel_size=1, local_rank=None, use_custom_allreduce=True,
+                              ca_max_size=128 * 1024 * 1024):
+    """TP, PP, DP and EP groups with the reference's rank layout
+    (parallel_state.py:1147-1275): ranks = [.., dp, pp, tp] with TP fastest; the EP group
+    merges DP x TP of one pipeline stage.  The TP group carries the custom (and, when
+    enabled, the quick) allreduce.  Returns the TP group."""
+    global _TP, _PP, _DP, _EP
+    assert _TP is None, "tensor model parallel group is already initialized"
+    world = dist.get_world_size()
+    tp, pp, dp = tensor_model_parallel_size, pipeline_model_parallel_size, data_parallel_size
+    assert world % (tp * pp * dp) == 0, f"world size {world} is not a multiple of tp * pp * dp = {tp * pp * dp}"
+    backend = backend or dist.get_backend()
+    if local_rank is None:
+        local_rank = int(os.environ.get("LOCAL_RANK", str(dist.get_rank())))
+    all_ranks = torch.arange(world).reshape(-1, dp, pp, tp)
+    lists = lambda t, n: [x.tolist() for x in t.reshape(-1, n).unbind(0)]
+    _TP = _init_groups(lists(all_ranks, tp), local_rank, backend, "tp", use_custom_allreduce, ca_max_size,
+                       use_quick_allreduce=True)
+    _PP = _init_groups(lists(all_ranks.transpose(2, 3), pp), local_rank, backend, "pp")
+    _DP = _init_groups(lists(all_ranks.transpose(1, 3), dp), local_rank, backend, "dp")
+    _EP = _init_groups(lists(all_ranks.transpose(1, 2), dp * tp), local_rank, backend, "ep")
     return _TP
+
+
+def ensure_model_parallel_initialized(tensor_model_parallel_size, pipeline_model_parallel_size=1, backend=None,
+                                      data_parallel_size=1):
+    """(parallel_state.py:1278-1308)"""
+    if not model_parallel_is_initialized():
+        initialize_model_parallel(tensor_model_parallel_size, pipeline_model_parallel_size, backend,
+                                  data_parallel_size)
+        return
+    assert get_tp_group().world_size == tensor_model_parallel_size, "tensor parallel group already initialized"
+    assert get_pp_group().world_size == pipeline_model_parallel_size, "pipeline parallel group already initialized"
+
+
+def model_parallel_is_initialized() -> bool:
+    return _TP is not None and _PP is not None
 
 
 def get_tp_group() -> GroupCoordinator:
     assert _TP is not None, "tensor model parallel group is not initialized"
     return _TP
+
+
+def get_pp_group() -> GroupCoordinator:
+    assert _PP is not None, "pipeline model parallel group is not initialized"
+    return _PP
+
+
+def get_dp_group() -> GroupCoordinator:
+    assert _DP is not None, "data parallel group is not initialized"
+    return _DP
+
+
+def get_ep_group() -> GroupCoordinator:
+    assert _EP is not None, "expert parallel group is not initialized"
+    return _EP
+
+
+def get_tensor_model_parallel_world_size() -> int:
+    return get_tp_group().world_size
+
+
+def get_tensor_model_parallel_rank() -> int:
+    return get_tp_group().rank_in_group
 
 
 @contextlib.contextmanager
@@ -310,10 +401,11 @@ def graph_capture():
 
 
 def destroy_model_parallel():
-    global _TP
-    if _TP is not None:
-        _TP.destroy()
-    _TP = None
+    global _TP, _PP, _DP, _EP
+    for g in (_TP, _PP, _DP, _EP):
+        if g is not None:
+            g.destroy()
+    _TP = _PP = _DP = _EP = None
 
 
 def destroy_distributed_environment():

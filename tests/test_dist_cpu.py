@@ -151,3 +151,44 @@ def _group_collectives(rank, world, port):
 
 def test_group_coordinator_collectives_fallback_path():
     run_ranks(_group_collectives, 2)
+
+
+def _group_layout(rank, world, port, tp, pp, dp):
+    """The reference's rank layout (parallel_state.py:1181-1264): ranks [.., dp, pp, tp]
+    with TP fastest, EP = DP x TP of a pipeline stage; the EP / DP / PP front-ends and
+    PP send / recv on gloo ranks."""
+    _init(rank, world, port)
+    from aiter_b200.dist import communication_op as co
+    from aiter_b200.dist import parallel_state as ps
+    ps.initialize_model_parallel(tp, pp, "gloo", dp, local_rank=rank, use_custom_allreduce=False)
+    grid = torch.arange(world).reshape(-1, dp, pp, tp)
+    where = (grid == rank).nonzero()[0].tolist()          # [outer, d, p, t]
+    o, d, p, t = where
+    assert ps.get_tp_group().ranks == grid[o, d, p, :].tolist()
+    assert ps.get_pp_group().ranks == grid[o, d, :, t].tolist()
+    assert ps.get_dp_group().ranks == grid[o, :, p, t].tolist()
+    assert ps.get_ep_group().ranks == grid[o, :, p, :].reshape(-1).tolist()
+    assert ps.get_tensor_model_parallel_world_size() == tp and ps.get_tensor_model_parallel_rank() == t
+    x = torch.full((2, 4), float(rank + 1))
+    ep_sum = float(sum(r + 1 for r in ps.get_ep_group().ranks))
+    assert torch.equal(co.expert_parallel_all_reduce(x), torch.full((2, 4), ep_sum))
+    dp_sum = float(sum(r + 1 for r in ps.get_dp_group().ranks))
+    assert torch.equal(co.data_parallel_all_reduce(x), torch.full((2, 4), dp_sum))
+    g = co.expert_parallel_all_gather(x, dim=0)
+    assert torch.equal(g[:, 0], torch.tensor([float(r + 1) for r in ps.get_ep_group().ranks]).repeat_interleave(2))
+    if pp > 1:
+        pg = ps.get_pp_group()
+        if pg.rank_in_group == 0:
+            co.pipeline_model_parallel_send(torch.arange(6, dtype=torch.float32) + rank)
+        elif pg.rank_in_group == 1:
+            got = co.pipeline_model_parallel_recv((6,), torch.float32)
+            assert torch.equal(got, torch.arange(6, dtype=torch.float32) + pg.ranks[0])
+    b = co.expert_parallel_broadcast(torch.full((3,), float(rank)), src=1)
+    assert torch.equal(b, torch.full((3,), float(ps.get_ep_group().ranks[1])))
+    ps.destroy_model_parallel()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("tp,pp,dp", [(2, 2, 1), (2, 1, 2)])
+def test_model_parallel_group_layout(tp, pp, dp):
+    run_ranks(_group_layout, 4, tp, pp, dp)
