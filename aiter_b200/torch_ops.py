@@ -112,3 +112,53 @@ def gemm_a16w16(a: Tensor, w: Tensor) -> Tensor:
 @gemm_a16w16.register_fake
 def _gemm_a16w16_fake(a, w):
     return a.new_empty((a.shape[0], w.shape[0]), dtype=torch.bfloat16)
+
+
+@torch.library.custom_op(f"{NS}::topk_sigmoid", mutates_args=("topk_weights", "topk_indices"))
+def topk_sigmoid(topk_weights: Tensor, topk_indices: Tensor, gating_output: Tensor) -> None:
+    moe_op.topk_sigmoid(topk_weights, topk_indices, gating_output)
+
+
+@topk_sigmoid.register_fake
+def _topk_sigmoid_fake(topk_weights, topk_indices, gating_output):
+    return None
+
+
+@torch.library.custom_op(f"{NS}::moe_sum", mutates_args=("output",))
+def moe_sum(input: Tensor, output: Tensor) -> None:
+    moe_op.moe_sum(input, output)
+
+
+@moe_sum.register_fake
+def _moe_sum_fake(input, output):
+    return None
+
+
+def _register_act(name):
+    from . import activation
+
+    @torch.library.custom_op(f"{NS}::{name}", mutates_args=("out",))
+    def op(out: Tensor, input: Tensor) -> None:
+        getattr(activation, name)(out, input)
+
+    @op.register_fake
+    def _fake(out, input):
+        return None
+
+    return op
+
+
+silu_and_mul = _register_act("silu_and_mul")
+gelu_and_mul = _register_act("gelu_and_mul")
+gelu_tanh_and_mul = _register_act("gelu_tanh_and_mul")
+
+
+@torch.library.custom_op(f"{NS}::scaled_silu_and_mul", mutates_args=("out",))
+def scaled_silu_and_mul(out: Tensor, input: Tensor, scale: Tensor) -> None:
+    from . import activation
+    activation.scaled_silu_and_mul(out, input, scale)
+
+
+@scaled_silu_and_mul.register_fake
+def _scaled_silu_and_mul_fake(out, input, scale):
+    return None

@@ -10,7 +10,8 @@ from aiter_b200 import dtypes
 
 def test_ops_are_registered():
     for name in ("fused_moe_", "topk_softmax", "grouped_topk", "biased_grouped_topk", "moe_sorting_fwd",
-                 "gemm_a16w16"):
+                 "gemm_a16w16", "topk_sigmoid", "moe_sum", "silu_and_mul", "gelu_and_mul", "gelu_tanh_and_mul",
+                 "scaled_silu_and_mul"):
         assert hasattr(torch.ops.aiter_b200, name), name
 
 
@@ -85,3 +86,18 @@ def test_fused_moe_rejects_what_the_b200_path_does_not_run():
         fused_moe(x, w1, w2, tw, ti, quant_type=QuantType.per_Token)
     with pytest.raises(NotImplementedError, match="activation"):
         fused_moe(x, w1, w2, tw, ti, quant_type=QuantType.per_1x128, activation=ActivationType.No)
+
+
+
+def test_new_mutating_ops_trace_with_fake_tensors():
+    """topk_sigmoid, moe_sum and the gated activations trace under FakeTensorMode
+    (torch.compile's first step) without running a kernel."""
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    with FakeTensorMode():
+        w = torch.empty(4, 2)
+        ids = torch.empty(4, 2, dtype=torch.int32)
+        torch.ops.aiter_b200.topk_sigmoid(w, ids, torch.empty(4, 16))
+        torch.ops.aiter_b200.moe_sum(torch.empty(4, 2, 64, dtype=torch.bfloat16), torch.empty(4, 64, dtype=torch.bfloat16))
+        torch.ops.aiter_b200.silu_and_mul(torch.empty(4, 32, dtype=torch.bfloat16), torch.empty(4, 64, dtype=torch.bfloat16))
+        torch.ops.aiter_b200.scaled_silu_and_mul(torch.empty(4, 32, dtype=torch.float8_e4m3fn),
+                                                 torch.empty(4, 64), torch.empty(1))
