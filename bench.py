@@ -57,7 +57,7 @@ def parse():
     p.add_argument("--fused-gemm-ar", action="store_true",
                    help="gemm_ar mode: also time the one-kernel GEMM + allreduce (custom_ar_gemm_all_reduce_fused)")
     p.add_argument("--mode", default="moe", choices=["moe", "moe_sweep", "a8w4", "tp_moe", "gemm_ar", "routing",
-                                                     "allreduce"],
+                                                     "allreduce", "ep"],
                    help="moe: config 1 at --M (N>1: data-parallel replicas); moe_sweep: config 1 token sweep "
                         "on one GPU; a8w4: config 2 on one GPU; tp_moe: config 3; gemm_ar: config 4; "
                         "routing: topk_softmax and moe_sorting alone (achieved HBM GB/s)")
@@ -893,13 +893,88 @@ def run_allreduce(args, rank, world, local):
             "qr_device_error": err, "sweep": rows}
 
 
+def run_ep(args, rank, world, local):
+    """Expert parallelism on config-1 shapes: every rank holds E / world experts and
+    --M // world tokens (fp8 1x128, top-8 of all E); one step = EP dispatch over NVLink
+    -> fused MoE on the received rows with the rank's expert mask -> combine.  The
+    comparison arm moves the same rows with NCCL all_to_all_single (tokens, scales,
+    ids and weights out, expert outputs back) around the same MoE.  Latency per step,
+    max over ranks."""
+    import aiter_b200 as aiter
+    from aiter_b200.dist import parallel_state as ps
+    from aiter_b200.dist.ep import EpDispatchCombineConfig, EpDispatchCombineOp
+    if world < 2:
+        return {"mode": "ep", "unavailable": "expert parallelism needs at least 2 GPUs"}
+    tp = ps.initialize_model_parallel(world, local_rank=local)
+    dev = torch.device("cuda", local)
+    El = E // world
+    T = max(1, args.M // world)
+    g = torch.Generator(device=dev).manual_seed(7)              # the same experts on every rank
+    from aiter_b200 import weights as W
+    w1q, w1s = W.quant_weight_128x128(torch.randn(El, 2 * I, D, device=dev, generator=g) / D ** 0.5)
+    w2q, w2s = W.quant_weight_128x128(torch.randn(El, D, I, device=dev, generator=g) / I ** 0.5)
+    torch.cuda.empty_cache()
+    gt = torch.Generator(device=dev).manual_seed(100 + rank)
+    hidden = torch.randn(T, D, device=dev, generator=gt).to(torch.bfloat16)
+    tw, tid = aiter.fused_topk(hidden, torch.randn(T, E, device=dev, generator=gt), TOPK, True)
+    tok, sc = aiter.per_group_quant_hip(hidden, quant_dtype=torch.float8_e4m3fn, group_size=128)
+    sc = sc.view(T, D // 128)
+    mask = torch.zeros(E, dtype=torch.int32, device=dev)
+    mask[rank * El:(rank + 1) * El] = 1
+    cfg = EpDispatchCombineConfig(data_type=torch.float8_e4m3fn, rank=rank, world_size=world, hidden_dim=D,
+                                  scale_dim=D // 128, scale_type_size=4, max_token_type_size=2,
+                                  max_num_inp_token_per_rank=T, num_experts_per_rank=El, num_experts_per_token=TOPK)
+    op = EpDispatchCombineOp(cfg, group=tp.cpu_group)
+    kw = dict(quant_type=aiter.QuantType.per_1x128, w1_scale=w1s, w2_scale=w2s)
+
+    def ours():
+        x, w, xs, ids, n = op.dispatch(tok, tw, sc, tid)
+        out = aiter.fused_moe(x, w1q, w2q, w, ids, expert_mask=mask, num_local_tokens=n, a1_scale=xs, **kw)
+        return op.combine(out, tw, tid)
+
+    # NCCL arm: every token to every rank (the all-to-all of a dense layout: rows whose
+    # experts live elsewhere are masked out by the MoE), outputs summed back
+    def nccl():
+        gtok = torch.empty(world * T, D, dtype=torch.uint8, device=dev)
+        torch.distributed.all_to_all_single(gtok, tok.view(torch.uint8).repeat(world, 1), group=tp.device_group)
+        gsc = torch.empty(world * T, D // 128, device=dev)
+        torch.distributed.all_to_all_single(gsc, sc.repeat(world, 1).contiguous(), group=tp.device_group)
+        gid = torch.empty(world * T, TOPK, dtype=torch.int32, device=dev)
+        torch.distributed.all_to_all_single(gid, tid.repeat(world, 1).contiguous(), group=tp.device_group)
+        gw = torch.empty(world * T, TOPK, device=dev)
+        torch.distributed.all_to_all_single(gw, tw.repeat(world, 1).contiguous(), group=tp.device_group)
+        out = aiter.fused_moe(gtok.view(torch.float8_e4m3fn), w1q, w2q, gw, gid, expert_mask=mask, a1_scale=gsc, **kw)
+        back = torch.empty_like(out)
+        torch.distributed.all_to_all_single(back, out, group=tp.device_group)
+        return back.view(world, T, D).float().sum(0).to(torch.bfloat16)
+
+    y = ours()
+    ref = nccl()
+    torch.cuda.synchronize()
+    ok = bool(((y.float() - ref.float()).abs() > 2e-2 + 2e-2 * ref.float().abs()).float().mean().item() <= 0.01)
+    with ClockSampler(local) as clk:
+        ms = _time_loop(ours, args.steps, args.warmup, world)
+    ms_nccl = _time_loop(nccl, args.steps, args.warmup, world)
+    op.close()
+    ps.destroy_model_parallel()
+    return {"metric": METRIC, "mode": "ep", "value": round(T * world / (ms * 1e-3), 1), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp8-e4m3",
+            "data": "synthetic", "matches_nccl_arm": ok,
+            "config": {"workload": "expert-parallel FP8 blockscale MoE on config-1 shapes", "tokens_per_rank": T,
+                       "hidden": D, "inter": I, "experts": E, "experts_per_rank": El, "topk": TOPK,
+                       "parallelism": f"ep{world}"},
+            "nccl_all_to_all_arm": {"ms_per_step": round(ms_nccl, 4), "value": round(T * world / (ms_nccl * 1e-3), 1)},
+            "clocks": clk.summary()}
+
+
 def main():
     args = parse()
     rank, world, local = dist_setup(args.gpus)
     try:
-        if args.mode in ("tp_moe", "gemm_ar", "moe_sweep", "a8w4", "routing", "allreduce"):
+        if args.mode in ("tp_moe", "gemm_ar", "moe_sweep", "a8w4", "routing", "allreduce", "ep"):
             res = {"tp_moe": run_tp_moe, "gemm_ar": run_gemm_ar, "moe_sweep": run_moe_sweep,
-                   "a8w4": run_a8w4, "routing": run_routing, "allreduce": run_allreduce}[args.mode](
+                   "a8w4": run_a8w4, "routing": run_routing, "allreduce": run_allreduce, "ep": run_ep}[args.mode](
                 args, rank, world, local)
             if rank == 0:
                 print(json.dumps(res), flush=True)
