@@ -62,6 +62,10 @@ def dtype_code(dt):
 
 _PACK = struct.Struct("<QQi4x8q8qii")  # the 160-byte aiter_tensor_t layout
 _ZEROS = (0,) * 8
+# one format per rank: the unused shape / stride slots are pad bytes (zeros), so the
+# tensor's own shape and stride tuples go in without concatenation
+_PACKS = [struct.Struct(f"<QQi4x{nd}q{(8 - nd) * 8}x{nd}q{(8 - nd) * 8}xii") for nd in range(9)]
+assert all(p.size == 160 for p in _PACKS)
 
 
 def to_aiter(t: torch.Tensor) -> aiter_tensor_t:
@@ -69,9 +73,12 @@ def to_aiter(t: torch.Tensor) -> aiter_tensor_t:
     if nd > 8:
         raise ValueError("at most 8 dims")
     n = t.numel()
-    return aiter_tensor_t.from_buffer_copy(_PACK.pack(
-        t.data_ptr() if n > 0 else 0, n, nd, *(tuple(t.shape) + _ZEROS[nd:]), *(t.stride() + _ZEROS[nd:]),
-        dtype_code(t.dtype), t.get_device()))
+    try:
+        code = _DTYPE_CODES[t.dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {t.dtype}") from None
+    return aiter_tensor_t.from_buffer_copy(_PACKS[nd].pack(t.data_ptr() if n > 0 else 0, n, nd, *t.shape,
+                                                           *t.stride(), code, t.get_device()))
 
 
 def current_stream_ptr(device_index: int) -> int:
