@@ -1008,7 +1008,8 @@ def _append_tmem_row(rows, v, warps, shape, x, lanes, iters, sms, ms, cycles):
     cyc = cycles.double().mean().item()
     bytes_sm = iters * lanes * 4 * 512 * 4
     rows.append({"variant": v, "warps": warps,
-                 "load": ["32x32b", "32x32b x2 per wait", "16x32bx2", "16x256b x2", "32x32b + 32 FMA"][shape],
+                 "load": ["32x32b", "32x32b x2 per wait", "16x32bx2", "16x256b x2", "32x32b + 32 FMA",
+                          "32x32b wide"][shape],
                  "cols_per_load": x, "lanes": lanes, "ms": round(ms, 4),
                  "B_per_clk_per_sm": round(bytes_sm / cyc, 2),
                  "TBs": round(bytes_sm * sms / (ms * 1e-3) / 1e12, 2),

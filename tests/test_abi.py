@@ -109,7 +109,7 @@ def test_tmem_probe_table_and_argument_checks():
     for v in range(n):
         assert L.tmem_ld_probe_info(v, info) == 0
         warps, shape, x, lanes = list(info)
-        assert warps in (4, 8, 16) and 0 <= shape <= 4 and x in (16, 32, 64) and lanes in (16, 32)
+        assert warps in (4, 8, 16) and 0 <= shape <= 5 and x in (16, 32, 64) and lanes in (16, 32)
     assert L.tmem_ld_probe_info(n, info) == -1
     cyc = torch.zeros(148, dtype=torch.int64)
     sink = torch.zeros(148 * 512)
