@@ -25,7 +25,11 @@ import torch
 from . import dtypes, moe_op
 from .enums import ActivationType, QuantType
 
-BLOCK_SIZE_M = 128
+# The reference's module default sort unit (aiter/fused_moe.py:22): the default block_size
+# of the public moe_sorting.  The tcgen05 grouped GEMMs tile GEMM_BLOCK_M sorted rows, so
+# fused_moe sorts with that unit.
+BLOCK_SIZE_M = 32
+GEMM_BLOCK_M = 128
 
 quant_remap = {QuantType.per_128x128: QuantType.per_1x128}
 
@@ -56,7 +60,7 @@ def get_block_size_M(token, topk, expert, inter_dim):
     """Sort unit for a problem (aiter/fused_moe.py:514-529 balances 32/64/128-row tiles over
     the CUs).  The tcgen05 grouped GEMM tiles 128 sorted rows (64-row half tiles are
     chosen inside the kernel), so the unit is always 128."""
-    return BLOCK_SIZE_M
+    return GEMM_BLOCK_M
 
 
 @functools.lru_cache(maxsize=2048)
@@ -91,7 +95,7 @@ def get_2stage_cfgs(padded_M, model_dim, inter_dim, expert, topk, dtype, q_dtype
                     q_type, use_g1u1, activation, doweight_stage1):
     """Frozen heuristic table (replaces the tuned-CSV lookup of
     aiter/fused_moe.py:719-911): the grouped GEMM tiles 128 sorted rows."""
-    return MOEMetadata(block_m=BLOCK_SIZE_M)
+    return MOEMetadata(block_m=GEMM_BLOCK_M)
 
 
 def _moe_sorting_ext(topk_ids, topk_weights, num_experts, model_dim, moebuf_dtype, block_size,
@@ -218,8 +222,8 @@ def _fused_moe_impl(hidden_states, w1, w2, topk_weight, topk_ids, expert_mask=No
         meta = get_2stage_cfgs(get_padded_M(M), model_dim, inter_dim, E, topk, dtype, dtypes.fp8,
                                w1.dtype, quant_type, True, activation, doweight_stage1)
         block_m = meta.block_m if not block_size_M else int(block_size_M)
-        if block_m != BLOCK_SIZE_M:
-            raise NotImplementedError(f"block_size_M={block_m}: the grouped GEMM tiles {BLOCK_SIZE_M} rows")
+        if block_m != GEMM_BLOCK_M:
+            raise NotImplementedError(f"block_size_M={block_m}: the grouped GEMM tiles {GEMM_BLOCK_M} rows")
         sorted_ids, sorted_weights, sorted_expert_ids, num_valid_ids, moe_buf, pos = _moe_sorting_ext(
             topk_ids, topk_weight, global_E, model_dim, dtype, block_m, expert_mask, num_local_tokens,
             moe_sorting_dispatch_policy, with_pos=True, moe_buf=moe_buf)
