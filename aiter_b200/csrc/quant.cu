@@ -1,10 +1,13 @@
-// Dynamic per-group fp8 quantisation (1 x group, group in {32, 64, 128}).
+// Dynamic per-group fp8 / int8 quantisation (1 x group, group in {32, 64, 128}).
 //
 // Restates dynamic_per_group_scaled_quant_kernel (csrc/kernels/quant_kernels.cu:20-133)
 // with the arithmetic of the reference's torch oracle `pertoken_quant`
-// (aiter/ops/quant.py:42-72): scale = amax / 448 (scale 0 -> 1), q = fp8(x / scale)
-// with round-to-nearest-even.  Each group is handled by group/8 lanes, 8 elements
-// (16 bytes of bf16) per lane; amax by shuffles inside the lane segment.
+// (aiter/ops/quant.py:42-72): scale = amax / dtype_max (scale 0 -> 1); fp8:
+// q = fp8(x / scale) with round-to-nearest-even (dtype_max 448); int8: q = x / scale
+// truncated toward zero, as torch's float -> int8 conversion and the reference kernel's
+// static_cast (csrc/include/aiter_opus_plus.h:87-102) do (dtype_max 127).  Each group
+// is handled by group/8 lanes, 8 elements (16 bytes of bf16) per lane; amax by shuffles
+// inside the lane segment.
 #include "common.cuh"
 
 namespace {
@@ -47,7 +50,7 @@ struct Vec8<float> {
     }
 };
 
-template <typename T, int GROUP>
+template <typename T, int GROUP, bool I8 = false>
 __global__ void __launch_bounds__(256)
 group_quant_kernel(const T* __restrict__ x, uint8_t* __restrict__ q, float* __restrict__ scales,
                    int64_t ngroups, const int* __restrict__ num_rows, int64_t rows_factor_groups,
@@ -75,15 +78,23 @@ group_quant_kernel(const T* __restrict__ x, uint8_t* __restrict__ q, float* __re
         for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
 #pragma unroll
         for (int o = LPG / 2; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        float scale = amax / 448.0f;
+        float scale = amax / (I8 ? 127.0f : 448.0f);
         if (scale == 0.f) scale = 1.0f;
         if (on) {
             uint32_t w[2];
 #pragma unroll
             for (int i = 0; i < 2; ++i) {
-                __nv_fp8x4_e4m3 p4(make_float4(v[4 * i] / scale, v[4 * i + 1] / scale,
-                                               v[4 * i + 2] / scale, v[4 * i + 3] / scale));
-                w[i] = *reinterpret_cast<uint32_t*>(&p4);
+                if constexpr (I8) {
+                    uint32_t b = 0;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        b |= (uint32_t)(uint8_t)(int8_t)__float2int_rz(v[4 * i + j] / scale) << (8 * j);
+                    w[i] = b;
+                } else {
+                    __nv_fp8x4_e4m3 p4(make_float4(v[4 * i] / scale, v[4 * i + 1] / scale,
+                                                   v[4 * i + 2] / scale, v[4 * i + 3] / scale));
+                    w[i] = *reinterpret_cast<uint32_t*>(&p4);
+                }
             }
             *reinterpret_cast<uint2*>(q + g * GROUP + sub * 8) = make_uint2(w[0], w[1]);
             if (sub == 0) {
@@ -110,7 +121,9 @@ AB_ENTRY(dynamic_per_token_scaled_quant,
     need(input, "input");
     need(scales, "scales");
     AB_CHECK(scale_ub == nullptr, "scale_ub is not supported");
-    need_dtype(out, AITER_DTYPE_fp8, "out");
+    AB_CHECK(out->dtype_ == AITER_DTYPE_fp8 || out->dtype_ == AITER_DTYPE_i8, "out must be fp8 or i8, got ",
+             dtype_name(out->dtype_));
+    const bool i8 = out->dtype_ == AITER_DTYPE_i8;
     need_dtype(scales, AITER_DTYPE_fp32, "scales");
     need_contig(out, "out");
     need_contig(input, "input");
@@ -137,9 +150,14 @@ AB_ENTRY(dynamic_per_token_scaled_quant,
     auto go = [&](auto tz, auto gz) {
         using T = decltype(tz);
         constexpr int G = decltype(gz)::value;
-        group_quant_kernel<T, G><<<blocks, 256, 0, st>>>((const T*)input->ptr, (uint8_t*)out->ptr,
-                                                         (float*)scales->ptr, ngroups, nr, factor_groups,
-                                                         shuffle_scale, gpr, nrows);
+        if (i8)
+            group_quant_kernel<T, G, true><<<blocks, 256, 0, st>>>((const T*)input->ptr, (uint8_t*)out->ptr,
+                                                                   (float*)scales->ptr, ngroups, nr, factor_groups,
+                                                                   shuffle_scale, gpr, nrows);
+        else
+            group_quant_kernel<T, G><<<blocks, 256, 0, st>>>((const T*)input->ptr, (uint8_t*)out->ptr,
+                                                             (float*)scales->ptr, ngroups, nr, factor_groups,
+                                                             shuffle_scale, gpr, nrows);
     };
     auto by_group = [&](auto tz) {
         if (group == 128) go(tz, std::integral_constant<int, 128>{});

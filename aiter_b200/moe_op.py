@@ -87,13 +87,15 @@ def dynamic_per_token_scaled_quant(out: Tensor, input: Tensor, scales: Tensor,
               num_rows, num_rows_factor)
 
 
-def per_group_quant_hip(x: Tensor, scale: Optional[Tensor] = None, quant_dtype=dtypes.fp8,
+def per_group_quant_hip(x: Tensor, scale: Optional[Tensor] = None, quant_dtype=dtypes.i8,
                         group_size: int = 128, transpose_scale: bool = False,
                         num_rows: Optional[Tensor] = None, num_rows_factor: int = 1) -> Tuple[Tensor, Tensor]:
-    """1 x group_size dynamic quantisation -> (fp8 [.., K], f32 scales [.., K/group])."""
+    """1 x group_size dynamic quantisation -> (fp8 or int8 [.., K], f32 scales [.., K/group]).
+    The default output dtype is the reference's, int8 (aiter/ops/quant.py:261-264); the
+    MoE path passes fp8."""
     if scale is not None:
         raise ValueError("unsupported: static per group quant")
-    if quant_dtype != dtypes.fp8:
+    if quant_dtype not in (dtypes.fp8, dtypes.i8):
         raise ValueError(f"unsupported quant dtype {quant_dtype}")
     if group_size not in (32, 64, 128):
         raise ValueError(f"unsupported group size {group_size=}, only support [32, 64, 128]")

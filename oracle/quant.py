@@ -3,6 +3,8 @@
 * `per_1x128_quant`   -- `pertoken_quant` over 128-wide groups
                          (aiter/ops/quant.py:42-72 via per_block_quant_wrapper :152-170):
                          scale = amax / 448 (0 -> 1), q = fp8(x / scale).
+* `per_group_quant_i8` -- the same with int8 output: scale = amax / 127 (0 -> 1),
+                         q = x / scale truncated toward zero (torch's float -> int8).
 * `weight_128x128_quant` -- the 128x128 block quantiser of
                          op_tests/test_moe_2stage.py:84-110.
 * `per_1x32_f4_quant` -- MXFP4 with e8m0 scales (aiter/ops/quant.py:75-106):
@@ -25,6 +27,20 @@ def per_1x128_quant(x, group=128):
     scale[scale == 0] = F32(1.0)
     y = (g / scale).astype(F32)
     q = codecs.fp8_e4m3_encode(y).reshape(shp)
+    return q, scale.reshape(shp[:-1] + (shp[-1] // group,))
+
+
+def per_group_quant_i8(x, group=128):
+    """pertoken_quant(quant_dtype=int8) over `group`-wide groups (aiter/ops/quant.py:42-72):
+    x: [..., K] float -> (int8 [..., K], scale f32 [..., K/group])."""
+    x = np.asarray(x, dtype=F32)
+    shp = x.shape
+    g = x.reshape(-1, group)
+    amax = np.abs(g).max(axis=-1, keepdims=True)
+    scale = (amax / F32(127.0)).astype(F32)
+    scale[scale == 0] = F32(1.0)
+    y = (g / scale).astype(F32)
+    q = np.trunc(y).astype(np.int8).reshape(shp)
     return q, scale.reshape(shp[:-1] + (shp[-1] // group,))
 
 

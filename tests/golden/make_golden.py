@@ -153,6 +153,9 @@ def main(root):
     out["quant1x128/x"] = x
     out["quant1x128/q"] = t2n(q).reshape(16, 512)
     out["quant1x128/scale"] = t2n(s).reshape(16, 4)
+    q8, s8 = ref.pertoken_quant(torch.from_numpy(x).view(16, -1, 128), quant_dtype=torch.int8)
+    out["quant1x128_i8/q"] = t2n(q8).reshape(16, 512)
+    out["quant1x128_i8/scale"] = t2n(s8).reshape(16, 4)
     w = (rng.standard_normal((2, 256, 384), dtype=np.float32) / np.float32(np.sqrt(384))).astype(np.float32)
     wq, ws = ref.weight_per_128x128_quant(torch.from_numpy(w), torch.float8_e4m3fn)
     out["quant128x128/w"] = w

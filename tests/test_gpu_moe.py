@@ -157,7 +157,7 @@ def test_fused_moe_preq_input_and_repeat_calls():
 
 def torch_reference_tokens(hidden, w1q, w1s, w2q, w2s, tw, tid, tokens):
     """fp32 torch reference of the 2-stage blockscale path for a subset of tokens."""
-    a1q, a1s = aiter.per_group_quant_hip(hidden[tokens])
+    a1q, a1s = aiter.per_group_quant_hip(hidden[tokens], quant_dtype=torch.float8_e4m3fn)
     a1 = (a1q.float().view(len(tokens), -1, 128) * a1s[..., None]).view(len(tokens), -1)
     outs = []
     I = w2q.shape[2]

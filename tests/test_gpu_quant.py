@@ -1,5 +1,9 @@
 """1 x group fp8 quantisation vs the oracle (`pertoken_quant` over 128 groups,
-aiter/ops/quant.py:42-72): codes and scales bit-exact."""
+aiter/ops/quant.py:42-72): codes and scales bit-exact.  The int8 output (the default
+dtype of the reference's per_group_quant_hip) runs only with AITER_B200_TEST_UNRUN=1
+until it has been run on a B200."""
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -32,7 +36,7 @@ def test_group_quant_small_groups(group):
     rng = np.random.default_rng(group)
     x = rng.standard_normal((64, 512), dtype=np.float32)
     xt = to_dev(x, torch.bfloat16)
-    q, s = aiter.per_group_quant_hip(xt, group_size=group)
+    q, s = aiter.per_group_quant_hip(xt, quant_dtype=torch.float8_e4m3fn, group_size=group)
     q0, s0 = quant.per_1x128_quant(xt.float().cpu().numpy(), group=group)
     assert np.array_equal(s.cpu().numpy().view(np.uint32), s0.view(np.uint32))
     assert np.array_equal(codes(q), q0)
@@ -54,3 +58,20 @@ def test_group_quant_transposed_scale_and_num_rows():
             assert st[c * M + r] == s0[r, c]
     assert np.array_equal(codes(q)[:30], q0[:30])
     assert np.all(codes(q)[30:] == codecs.fp8_e4m3_encode(np.float32(0.5)))
+
+
+@pytest.mark.skipif(os.environ.get("AITER_B200_TEST_UNRUN") != "1", reason="int8 group quant not yet run on a B200")
+@pytest.mark.parametrize("group", [32, 128])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_group_quant_int8_bit_exact(group, dtype):
+    rng = np.random.default_rng(group + 11)
+    x = rng.standard_normal((40, 1024), dtype=np.float32) * 3
+    x[0, :group] = 0.0          # zero group -> scale 1
+    x[2, 5] = -900.0            # outlier
+    xt = to_dev(x, dtype)
+    q, s = aiter.per_group_quant_hip(xt, group_size=group)   # default dtype: int8
+    torch.cuda.synchronize()
+    assert q.dtype == torch.int8
+    q0, s0 = quant.per_group_quant_i8(xt.float().cpu().numpy(), group=group)
+    assert np.array_equal(s.cpu().numpy().view(np.uint32), s0.view(np.uint32))
+    assert np.array_equal(q.cpu().numpy(), q0)

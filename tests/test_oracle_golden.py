@@ -57,6 +57,13 @@ def test_per_1x128_quant(golden):
     assert np.array_equal(q, golden["quant1x128/q"])
 
 
+def test_per_group_quant_i8(golden):
+    """int8 output, the reference per_group_quant_hip's default dtype."""
+    q, s = quant.per_group_quant_i8(golden["quant1x128/x"])
+    assert np.array_equal(s.view(np.uint32), golden["quant1x128_i8/scale"].view(np.uint32))
+    assert np.array_equal(q, golden["quant1x128_i8/q"])
+
+
 def test_weight_128x128_quant(golden):
     q, s = quant.weight_128x128_quant(golden["quant128x128/w"])
     assert np.array_equal(s.view(np.uint32), golden["quant128x128/scale"].view(np.uint32))
