@@ -36,7 +36,12 @@ def exchange_handles(group, handle: bytes):
 class CustomAllreduce:
     _SUPPORTED_WORLD_SIZES = [2, 4, 6, 8]
 
-    def __init__(self, group, device, max_size=128 * 1024 * 1024):
+    def __init__(self, group, device, max_size=128 * 1024 * 1024, enable_register_for_capturing: bool = True):
+        """`enable_register_for_capturing` is the reference's switch for reading captured
+        inputs in place from registered buffers (custom_all_reduce.py:248-253); here every
+        call reads its input through this rank's IPC-shared staging buffers, captured or
+        not, so the flag is recorded and changes nothing."""
+        self.enable_register_for_capturing = enable_register_for_capturing
         self.disabled = True
         self._IS_CAPTURING = False
         self._ctx = 0
@@ -125,22 +130,55 @@ class CustomAllreduce:
             _lib.check_status(name, ret)
         return out
 
-    def custom_all_gather(self, inp: torch.Tensor, dim: int = 0) -> Optional[torch.Tensor]:
-        """All-gather over peer memory along dim 0 or the last dim (the reference's
-        custom all-gather); None when the tensor is not eligible (size, alignment)."""
-        if self.disabled:
-            return None
+    # ---- buffer registration (custom_all_reduce.py:405-421).  Inputs and outputs are
+    # never read or written in place by peers here: each call stages through this rank's
+    # IPC-shared buffers, which were exchanged at construction, so there is nothing to
+    # register, eagerly or after a graph capture.
+    def register_input_buffer(self, inp: torch.Tensor):
+        return None
+
+    def register_output_buffer(self, out: torch.Tensor):
+        return None
+
+    def register_graph_buffers(self):
+        return None
+
+    def _gather_last(self, inp: torch.Tensor, dim: int):
+        """(eligible, along the last dim) for an all-gather of `inp` along `dim`."""
         nd = inp.dim()
         dim = dim + nd if dim < 0 else dim
         esz = inp.element_size()
         nbytes = inp.numel() * esz
         last = nd > 0 and dim == nd - 1 and dim != 0
-        if not inp.is_contiguous() or nbytes % 16 or nbytes > self.max_size or (dim != 0 and not last) \
-                or (last and (inp.shape[-1] * esz) % 16):
-            return None
-        shape = list(inp.shape) if nd else [1]
-        shape[dim if nd else 0] *= self.world_size
-        out = torch.empty(shape, dtype=inp.dtype, device=inp.device)
+        ok = (not self.disabled and inp.is_contiguous() and nbytes % 16 == 0
+              and nbytes <= self.max_size and (dim == 0 or last)
+              and not (last and (inp.shape[-1] * esz) % 16) and inp.device == self.device)
+        return ok, last
+
+    def should_custom_ag(self, inp: torch.Tensor, dim: int = 0) -> bool:
+        """All-gather eligibility (custom_all_reduce.py:439-451): contiguous, a 16-byte
+        multiple, this rank's input within the staging size (peers read it from there),
+        along dim 0 or the last dim (the last dim also needs 16-byte rows)."""
+        return self._gather_last(inp, dim)[0]
+
+    def _allgather_out_shape(self, inp: torch.Tensor, dim: int):
+        """Output shape of an all-gather along dim 0 or the last dim; 1-D otherwise
+        (custom_all_reduce.py:544-553)."""
+        nd = inp.dim()
+        if nd == 0:
+            return (self.world_size,)
+        if dim == 0:
+            return (inp.shape[0] * self.world_size,) + tuple(inp.shape[1:])
+        if dim == -1 or dim == nd - 1:
+            return tuple(inp.shape[:-1]) + (inp.shape[-1] * self.world_size,)
+        return (inp.numel() * self.world_size,)
+
+    def _all_gather(self, inp: torch.Tensor, out: Optional[torch.Tensor], dim: int) -> torch.Tensor:
+        ok, last = self._gather_last(inp, dim)
+        if not ok:
+            raise ValueError(f"custom all-gather does not take this tensor (shape {tuple(inp.shape)}, dim {dim})")
+        if out is None:
+            out = torch.empty(self._allgather_out_shape(inp, dim), dtype=inp.dtype, device=inp.device)
         a, b = _lib.to_aiter(inp), _lib.to_aiter(out)
         ret = self._L.custom_ar_all_gather(self._ctx, ctypes.byref(a), ctypes.byref(b), 1 if last else 0,
                                            _lib.current_stream_ptr(self.device.index))
@@ -148,19 +186,46 @@ class CustomAllreduce:
             _lib.check_status("custom_ar_all_gather", ret)
         return out
 
-    def custom_reduce_scatter(self, inp: torch.Tensor, out: torch.Tensor) -> bool:
-        """Reduce-scatter over peer memory into `out` (numel / world elements, this rank's
-        share of the sum); False when the tensor is not eligible."""
+    def all_gather_reg(self, inp: torch.Tensor, out: torch.Tensor = None, dim: int = 0) -> torch.Tensor:
+        """All-gather of a (captured) input (custom_all_reduce.py:555-569); the same
+        staged kernel as all_gather_unreg here."""
+        return self._all_gather(inp, out, dim)
+
+    def all_gather_unreg(self, inp: torch.Tensor, out: torch.Tensor = None, dim: int = 0) -> torch.Tensor:
+        """All-gather through the staging buffers (custom_all_reduce.py:571-589)."""
+        return self._all_gather(inp, out, dim)
+
+    def custom_all_gather(self, inp: torch.Tensor, dim: int = 0) -> Optional[torch.Tensor]:
+        """All-gather over peer memory along dim 0 or the last dim (the reference's
+        custom all-gather); None when the tensor is not eligible (size, alignment)."""
+        if not self.should_custom_ag(inp, dim):
+            return None
+        return self._all_gather(inp, None, dim)
+
+    def _rs_eligible(self, inp: torch.Tensor) -> bool:
         if self.disabled or inp.dtype not in self._DTYPES or not inp.is_contiguous():
             return False
         nbytes = inp.numel() * inp.element_size()
-        if inp.numel() % self.world_size or (nbytes // self.world_size) % 16 or nbytes > self.max_size:
-            return False
+        return not (inp.numel() % self.world_size or (nbytes // self.world_size) % 16 or nbytes > self.max_size)
+
+    def reduce_scatter(self, inp: torch.Tensor, out: torch.Tensor, *, registered: bool = False):
+        """Reduce-scatter over peer memory into `out` (numel / world elements, this rank's
+        share of the rank-ordered fp32 sum; custom_all_reduce.py:514-530).  `registered`
+        is accepted for the reference's signature: inputs are always staged here."""
+        if not self._rs_eligible(inp):
+            raise ValueError(f"custom reduce-scatter does not take this tensor (shape {tuple(inp.shape)})")
         a, b = _lib.to_aiter(inp), _lib.to_aiter(out)
         ret = self._L.custom_ar_reduce_scatter(self._ctx, ctypes.byref(a), ctypes.byref(b),
                                                _lib.current_stream_ptr(self.device.index))
         if ret:
             _lib.check_status("custom_ar_reduce_scatter", ret)
+
+    def custom_reduce_scatter(self, input: torch.Tensor, output: torch.Tensor) -> bool:
+        """Reduce-scatter into `output` when the tensor is eligible (custom_all_reduce.py:
+        532-542); returns whether it ran (the reference returns None either way)."""
+        if not self._rs_eligible(input):
+            return False
+        self.reduce_scatter(input, output)
         return True
 
     def custom_all_reduce(self, input: torch.Tensor, use_new: bool = True, open_fp8_quant: bool = False):

@@ -10,6 +10,7 @@ import contextlib
 import dataclasses
 import datetime
 import os
+import pickle
 from collections import namedtuple
 from typing import Any, Dict, List, Optional, Tuple, Union
 
@@ -94,18 +95,44 @@ class GroupCoordinator:
             self._all2all_manager = EpAll2AllManager(self.cpu_group)
         return self._all2all_manager
 
-    def all_reduce(self, input_: torch.Tensor, use_new: bool = True, open_fp8_quant: bool = False,
+    # ---- the group's ranks (parallel_state.py:310-343): global ranks, ring order
+    @property
+    def first_rank(self):
+        return self.ranks[0]
+
+    @property
+    def last_rank(self):
+        return self.ranks[-1]
+
+    @property
+    def is_first_rank(self):
+        return self.rank == self.ranks[0]
+
+    @property
+    def is_last_rank(self):
+        return self.rank == self.ranks[-1]
+
+    @property
+    def next_rank(self):
+        return self.ranks[(self.rank_in_group + 1) % self.world_size]
+
+    @property
+    def prev_rank(self):
+        return self.ranks[(self.rank_in_group - 1) % self.world_size]
+
+    def all_reduce(self, input_: torch.Tensor, ca_use_new: bool = True, ca_fp8_quant: bool = False,
                    prefill_support: bool = False) -> torch.Tensor:
         """Out-of-place allreduce (parallel_state.py:376-407, communicator_cuda.py:
         157-204): the quick allreduce when enabled and the tensor is eligible, else
-        the IPC allreduce for eligible tensors, the NCCL group otherwise."""
+        the IPC allreduce for eligible tensors (ca_fp8_quant: its fp8-quantised form),
+        the NCCL group otherwise."""
         if self.world_size == 1:
             return input_
         qr = self.qr_comm
         if qr is not None and not qr.disabled and qr.should_quick_allreduce(input_):
             return qr.quick_all_reduce(input_)
         if self.ca_comm is not None and not self.ca_comm.disabled:
-            out = self.ca_comm.custom_all_reduce(input_, use_new, open_fp8_quant)
+            out = self.ca_comm.custom_all_reduce(input_, ca_use_new, ca_fp8_quant)
             if out is not None:
                 return out
         out = input_.clone()
@@ -186,11 +213,104 @@ class GroupCoordinator:
         dist.broadcast_object_list(holder, src=self.ranks[src], group=self.cpu_group)
         return holder[0]
 
+    def broadcast_object_list(self, obj_list: List[Any], src: int = 0, group=None):
+        """Broadcast a list of picklable objects in place from group rank `src`
+        (parallel_state.py:651-666)."""
+        assert src < self.world_size, f"Invalid src rank ({src})"
+        if self.world_size == 1:
+            return obj_list
+        dist.broadcast_object_list(obj_list, src=self.ranks[src], group=self.cpu_group)
+        return obj_list
+
+    def send_object(self, obj: Any, dst: int) -> None:
+        """Pickle `obj` and send it to group rank `dst` over the CPU group: its length,
+        then its bytes (parallel_state.py:668-693)."""
+        assert dst < self.world_size, f"Invalid dst rank ({dst})"
+        assert dst != self.rank_in_group, "Invalid destination rank. Destination rank is the same as the current rank."
+        payload = torch.frombuffer(bytearray(pickle.dumps(obj)), dtype=torch.uint8)
+        dist.send(torch.tensor([payload.numel()], dtype=torch.long), dst=self.ranks[dst], group=self.cpu_group)
+        dist.send(payload, dst=self.ranks[dst], group=self.cpu_group)
+
+    def recv_object(self, src: int) -> Any:
+        """Receive an object sent by send_object from group rank `src` (:695-729)."""
+        assert src < self.world_size, f"Invalid src rank ({src})"
+        assert src != self.rank_in_group, "Invalid source rank. Source rank is the same as the current rank."
+        n = torch.empty(1, dtype=torch.long)
+        dist.recv(n, src=self.ranks[src], group=self.cpu_group)
+        payload = torch.empty(int(n.item()), dtype=torch.uint8)
+        dist.recv(payload, src=self.ranks[src], group=self.cpu_group)
+        return pickle.loads(payload.numpy().tobytes())
+
+    def send_tensor_dict(self, tensor_dict: Dict[str, Union[torch.Tensor, Any]], dst: Optional[int] = None,
+                         all_gather_group: Optional["GroupCoordinator"] = None):
+        """Send a dict of tensors and plain values to group rank `dst` (default: the next
+        one; parallel_state.py:813-864): metadata by send_object, then each non-empty
+        tensor (CPU tensors over the CPU group, device tensors over the device group).
+        With `all_gather_group`, each rank of that group sends only its 1/W slice of
+        every divisible tensor and the receiver all-gathers the slices."""
+        if not dist.is_initialized() or self.world_size == 1:
+            return tensor_dict
+        w = 1 if all_gather_group is None else all_gather_group.world_size
+        r = 0 if all_gather_group is None else all_gather_group.rank_in_group
+        if dst is None:
+            dst = (self.rank_in_group + 1) % self.world_size
+        assert dst < self.world_size, f"Invalid dst rank ({dst})"
+        assert isinstance(tensor_dict, dict), f"Expecting a dictionary, got {type(tensor_dict)}"
+        metadata_list, tensors = _split_tensor_dict(tensor_dict)
+        self.send_object(metadata_list, dst=dst)
+        for t in tensors:
+            if t.numel() == 0:
+                continue
+            if all_gather_group is not None and t.numel() % w == 0:
+                t = t.reshape(w, -1)[r]
+            dist.send(t.contiguous(), dst=self.ranks[dst], group=self.cpu_group if t.is_cpu else self.device_group)
+        return None
+
+    def recv_tensor_dict(self, src: Optional[int] = None, all_gather_group: Optional["GroupCoordinator"] = None):
+        """Receive a dict sent by send_tensor_dict from group rank `src` (default: the
+        previous one; parallel_state.py:866-926)."""
+        if not dist.is_initialized() or self.world_size == 1:
+            return None
+        w = 1 if all_gather_group is None else all_gather_group.world_size
+        r = 0 if all_gather_group is None else all_gather_group.rank_in_group
+        if src is None:
+            src = (self.rank_in_group - 1) % self.world_size
+        assert src < self.world_size, f"Invalid src rank ({src})"
+        out = {}
+        for key, value in self.recv_object(src=src):
+            if not isinstance(value, TensorMetadata):
+                out[key] = value
+                continue
+            dev = torch.device("cpu") if value.device == "cpu" else self.device
+            t = torch.empty(value.size, dtype=value.dtype, device=dev)
+            if t.numel() == 0:
+                out[key] = t
+                continue
+            sliced = all_gather_group is not None and t.numel() % w == 0
+            part = t.reshape(w, -1)[r] if sliced else t
+            buf = torch.empty_like(part) if sliced else part
+            dist.recv(buf, src=self.ranks[src], group=self.cpu_group if t.is_cpu else self.device_group)
+            if sliced:
+                buf = all_gather_group.all_gather(buf, dim=0).reshape(value.size)
+            out[key] = buf
+        return out
+
+    def barrier(self):
+        """Barrier over the CPU group (parallel_state.py:928-935: an NCCL barrier would
+        allocate device tensors behind the caller's back)."""
+        dist.barrier(group=self.cpu_group)
+
+    def prepare_communication_buffer_for_model(self, model: torch.nn.Module):
+        """Hook for communicators that register model buffers (parallel_state.py:965-967).
+        The IPC allreduce stages through its own buffers, so there is nothing to do."""
+        return None
+
     def broadcast_tensor_dict(self, tensor_dict: Optional[Dict[str, Union[torch.Tensor, Any]]] = None,
-                              src: int = 0) -> Optional[Dict[str, Union[torch.Tensor, Any]]]:
+                              src: int = 0, group=None, metadata_group=None) -> Optional[Dict[str, Union[torch.Tensor, Any]]]:
         """Broadcast a dict of tensors and plain values from rank `src` (parallel_state.py:
         731-800): the metadata goes over the CPU group, CPU tensors over the CPU group
-        and device tensors over the device group."""
+        and device tensors over the device group (`group` / `metadata_group` are accepted
+        for the reference's signature; this group's own are used)."""
         if not dist.is_initialized() or self.world_size == 1:
             return tensor_dict
         assert src < self.world_size, f"Invalid src rank ({src})"

@@ -192,3 +192,61 @@ def _group_layout(rank, world, port, tp, pp, dp):
 @pytest.mark.parametrize("tp,pp,dp", [(2, 2, 1), (2, 1, 2)])
 def test_model_parallel_group_layout(tp, pp, dp):
     run_ranks(_group_layout, 4, tp, pp, dp)
+
+
+def _group_p2p_objects(rank, world, port):
+    """Ring ranks, object and tensor-dict point-to-point, object-list broadcast, barrier
+    and the keyword names of all_reduce (parallel_state.py:310-343, 376-383, 651-935)."""
+    _init(rank, world, port)
+    from aiter_b200.dist import parallel_state as ps
+    tp = ps.initialize_model_parallel(world, local_rank=rank, backend="gloo", use_custom_allreduce=False)
+    assert tp.first_rank == 0 and tp.last_rank == world - 1
+    assert tp.is_first_rank == (rank == 0) and tp.is_last_rank == (rank == world - 1)
+    assert tp.next_rank == (rank + 1) % world and tp.prev_rank == (rank - 1) % world
+    y = tp.all_reduce(torch.full((3,), float(rank)), ca_use_new=True, ca_fp8_quant=False)
+    assert torch.equal(y, torch.full((3,), float(sum(range(world)))))
+    lst = [{"k": rank}, "s"] if rank == 1 else [None, None]
+    assert tp.broadcast_object_list(lst, src=1) == [{"k": 1}, "s"]
+    if rank == 0:
+        tp.send_object({"step": 7, "names": ["a", "b"]}, dst=1)
+        tp.send_tensor_dict({"x": torch.arange(6, dtype=torch.float32).reshape(2, 3), "n": 5, "e": torch.empty(0)})
+    elif rank == 1:
+        assert tp.recv_object(src=0) == {"step": 7, "names": ["a", "b"]}
+        d = tp.recv_tensor_dict()
+        assert torch.equal(d["x"], torch.arange(6, dtype=torch.float32).reshape(2, 3))
+        assert d["n"] == 5 and d["e"].numel() == 0
+    tp.barrier()
+    assert tp.prepare_communication_buffer_for_model(torch.nn.Linear(2, 2)) is None
+    ps.destroy_model_parallel()
+    dist.destroy_process_group()
+
+
+def test_group_coordinator_ring_and_object_p2p():
+    run_ranks(_group_p2p_objects, 2)
+
+
+def test_custom_allreduce_gather_scatter_eligibility_and_shapes():
+    """The reference CustomAllreduce's host-side helpers (custom_all_reduce.py:405-553)
+    on an object with no IPC context: registration is a no-op, all-gather eligibility
+    and output shapes, reduce-scatter eligibility."""
+    from aiter_b200.dist.custom_all_reduce import CustomAllreduce
+    ca = CustomAllreduce.__new__(CustomAllreduce)
+    ca.disabled, ca.world_size, ca.max_size, ca.device = False, 4, 1 << 20, torch.device("cpu")
+    x = torch.empty(8, 64, dtype=torch.bfloat16)
+    assert ca.register_input_buffer(x) is None and ca.register_output_buffer(x) is None
+    assert ca.register_graph_buffers() is None
+    assert ca.should_custom_ag(x) and ca.should_custom_ag(x, -1)
+    assert ca.should_custom_ag(x, 1)                        # dim 1 is the last dim of a 2-D tensor
+    assert ca.should_custom_ag(torch.empty(8, 64, 2, dtype=torch.bfloat16), 0)
+    assert not ca.should_custom_ag(torch.empty(8, 64, 2, dtype=torch.bfloat16), 1)   # middle dim
+    assert not ca.should_custom_ag(torch.empty(8, 3, dtype=torch.bfloat16), -1)       # 6-byte rows
+    assert not ca.should_custom_ag(torch.empty(8, 64, dtype=torch.bfloat16)[:, :32])  # not contiguous
+    assert not ca.should_custom_ag(torch.empty(1 << 20, dtype=torch.bfloat16))         # above max_size
+    assert ca._allgather_out_shape(x, 0) == (32, 64) and ca._allgather_out_shape(x, -1) == (8, 256)
+    assert ca._allgather_out_shape(torch.empty(2, 3, 4), 1) == (96,)
+    assert ca._rs_eligible(torch.empty(8, 64, dtype=torch.bfloat16))
+    assert not ca._rs_eligible(torch.empty(3, 8, dtype=torch.bfloat16))               # 12-byte shares
+    assert not ca._rs_eligible(torch.empty(8, 64, dtype=torch.int32))                 # dtype
+    ca.disabled = True
+    assert not ca.should_custom_ag(x) and ca.custom_all_gather(x) is None
+    assert ca.custom_reduce_scatter(x, torch.empty(2, 64, dtype=torch.bfloat16)) is False

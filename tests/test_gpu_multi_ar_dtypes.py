@@ -63,7 +63,7 @@ def _worker(rank, world, port):
     npd = np.float16
     for j, n in enumerate([128 * 2048, 128 * 2048 * 3, world * 64 * 4097, 128 * 2048 + 8 * 3]):
         xs = _inputs(n, world, 50 + j, torch.float16)
-        y = tp.all_reduce(xs[rank].to(dev), open_fp8_quant=True)
+        y = tp.all_reduce(xs[rank].to(dev), ca_fp8_quant=True)
         torch.cuda.synchronize()
         assert _lib.lib().custom_ar_device_error(1) == 0
         want = allreduce_fp8_quant([x.numpy() for x in xs])[rank]
@@ -88,7 +88,7 @@ def _worker(rank, world, port):
     # the flag is ignored for bf16 and for fp16 below 128 * 2048 elements
     for dtype, n in ((torch.bfloat16, 128 * 2048), (torch.float16, 4096)):
         xs = _inputs(n, world, 70, dtype)
-        y = tp.all_reduce(xs[rank].to(dev), open_fp8_quant=True)
+        y = tp.all_reduce(xs[rank].to(dev), ca_fp8_quant=True)
         z = ca.all_reduce(xs[rank].to(dev))
         torch.cuda.synchronize()
         assert torch.equal(y, z), (dtype, n)
