@@ -21,5 +21,8 @@ from .communication_op import (data_parallel_all_gather, data_parallel_all_reduc
 from .parallel_state import (GraphCaptureContext, GroupCoordinator, destroy_distributed_environment,
                              destroy_model_parallel, ensure_model_parallel_initialized, get_dp_group, get_ep_group,
                              get_pp_group, get_tensor_model_parallel_rank, get_tensor_model_parallel_world_size,
-                             get_tp_group, graph_capture, init_distributed_environment, initialize_model_parallel,
-                             model_parallel_is_initialized)
+                             get_tp_group, get_world_group, graph_capture, in_the_same_node_as,
+                             init_distributed_environment, init_model_parallel_group, init_world_group,
+                             initialize_model_parallel, is_global_first_rank, model_parallel_is_initialized,
+                             patch_tensor_parallel_group, prepare_communication_buffer_for_model,
+                             set_custom_all_reduce)

@@ -24,6 +24,9 @@ _TP: Optional["GroupCoordinator"] = None
 _PP: Optional["GroupCoordinator"] = None
 _DP: Optional["GroupCoordinator"] = None
 _EP: Optional["GroupCoordinator"] = None
+_WORLD: Optional["GroupCoordinator"] = None
+_ENABLE_CUSTOM_ALL_REDUCE = True
+_TP_STATE_PATCHED = False
 
 
 def _rmsnorm_after(ar: torch.Tensor, res: torch.Tensor, w: torch.Tensor, eps: float, quant: bool):
@@ -411,19 +414,58 @@ class GroupCoordinator:
             self._all2all_manager = None
 
 
+def set_custom_all_reduce(enable: bool):
+    """Whether groups built afterwards attach the IPC allreduce (parallel_state.py:1082-1084)."""
+    global _ENABLE_CUSTOM_ALL_REDUCE
+    _ENABLE_CUSTOM_ALL_REDUCE = enable
+
+
+def init_world_group(ranks: List[int], local_rank: int, backend: str) -> GroupCoordinator:
+    """The group of every rank, without device communicators (parallel_state.py:990-999)."""
+    return GroupCoordinator(ranks, local_rank, backend, use_custom_allreduce=False, use_quick_allreduce=False,
+                            group_name="world")
+
+
+def get_world_group() -> GroupCoordinator:
+    assert _WORLD is not None, "world group is not initialized"
+    return _WORLD
+
+
+def init_model_parallel_group(group_ranks: List[List[int]], local_rank: int, backend: str,
+                              use_message_queue_broadcaster: bool = False,
+                              group_name: Optional[str] = None) -> GroupCoordinator:
+    """A group per rank list of `group_ranks`; returns the one holding this rank
+    (parallel_state.py:1002-1017).  The IPC allreduce is attached unless disabled by
+    set_custom_all_reduce; no message-queue broadcaster exists here (objects go over
+    the group's CPU group)."""
+    return _init_groups(group_ranks, local_rank, backend, group_name or "", _ENABLE_CUSTOM_ALL_REDUCE,
+                        128 * 1024 * 1024)
+
+
 def init_distributed_environment(world_size=-1, rank=-1, distributed_init_method="env://", local_rank=-1,
-                                 backend="nccl", timeout_s=120):
+                                 backend="nccl", data_parallel_size=1, data_parallel_rank=0, timeout_s=120):
+    """Start torch.distributed and the world group (parallel_state.py:1087-1145).  With
+    data_parallel_size > 1 the given rank / world size are those inside one data-parallel
+    replica and are widened to the global ones, as the reference does."""
+    global _WORLD
+    if world_size == -1:
+        world_size = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank == -1:
+        rank = int(os.environ.get("RANK", "0"))
+    if data_parallel_size > 1:
+        rank = data_parallel_rank * world_size + rank
+        world_size = data_parallel_size * world_size
     if not dist.is_initialized():
-        if world_size == -1:
-            world_size = int(os.environ.get("WORLD_SIZE", "1"))
-        if rank == -1:
-            rank = int(os.environ.get("RANK", "0"))
         dist.init_process_group(backend=backend, init_method=distributed_init_method, world_size=world_size,
                                 rank=rank, timeout=datetime.timedelta(seconds=timeout_s))
     if local_rank == -1:
         local_rank = int(os.environ.get("LOCAL_RANK", str(dist.get_rank())))
     if backend == "nccl" and torch.cuda.is_available():
         torch.cuda.set_device(local_rank)
+    if _WORLD is None:
+        _WORLD = init_world_group(list(range(dist.get_world_size())), local_rank, backend)
+    else:
+        assert _WORLD.world_size == dist.get_world_size(), "world group already initialized with a different world size"
     return local_rank
 
 
@@ -460,8 +502,8 @@ def initialize_model_parallel(tensor_model_parallel_size=1, pipeline_model_paral
         local_rank = int(os.environ.get("LOCAL_RANK", str(dist.get_rank())))
     all_ranks = torch.arange(world).reshape(-1, dp, pp, tp)
     lists = lambda t, n: [x.tolist() for x in t.reshape(-1, n).unbind(0)]
-    _TP = _init_groups(lists(all_ranks, tp), local_rank, backend, "tp", use_custom_allreduce, ca_max_size,
-                       use_quick_allreduce=True)
+    _TP = _init_groups(lists(all_ranks, tp), local_rank, backend, "tp",
+                       use_custom_allreduce and _ENABLE_CUSTOM_ALL_REDUCE, ca_max_size, use_quick_allreduce=True)
     _PP = _init_groups(lists(all_ranks.transpose(2, 3), pp), local_rank, backend, "pp")
     _DP = _init_groups(lists(all_ranks.transpose(1, 3), dp), local_rank, backend, "dp")
     _EP = _init_groups(lists(all_ranks.transpose(1, 2), dp * tp), local_rank, backend, "ep")
@@ -528,7 +570,51 @@ def destroy_model_parallel():
     _TP = _PP = _DP = _EP = None
 
 
+@contextlib.contextmanager
+def patch_tensor_parallel_group(tp_group: GroupCoordinator):
+    """Use `tp_group` as the TP group inside the context (a draft model with another TP
+    degree; parallel_state.py:1320-1341)."""
+    global _TP, _TP_STATE_PATCHED
+    assert not _TP_STATE_PATCHED, "Should not call when it's already patched"
+    _TP_STATE_PATCHED = True
+    old = get_tp_group()
+    _TP = tp_group
+    try:
+        yield
+    finally:
+        _TP_STATE_PATCHED = False
+        _TP = old
+
+
+def in_the_same_node_as(pg, source_rank: int = 0) -> List[bool]:
+    """For each rank of `pg` (a CPU / gloo group), whether it runs on the same host as
+    group rank `source_rank` (parallel_state.py:1386-1452); compared by host name."""
+    import socket
+    names = [None] * dist.get_world_size(group=pg)
+    dist.all_gather_object(names, socket.gethostname(), group=pg)
+    return [n == names[source_rank] for n in names]
+
+
+def is_global_first_rank() -> bool:
+    """Global rank 0 across every parallel dimension, True without torch.distributed
+    (parallel_state.py:1455-1483)."""
+    if _WORLD is not None:
+        return _WORLD.is_first_rank
+    return not dist.is_initialized() or dist.get_rank() == 0
+
+
+def prepare_communication_buffer_for_model(model: torch.nn.Module):
+    """Let every group's communicators size buffers for `model` (parallel_state.py:1526-1544)."""
+    for g in (_TP, _PP, _DP, _EP):
+        if g is not None:
+            g.prepare_communication_buffer_for_model(model)
+
+
 def destroy_distributed_environment():
+    global _WORLD
     destroy_model_parallel()
+    if _WORLD is not None:
+        _WORLD.destroy()
+    _WORLD = None
     if dist.is_initialized():
         dist.destroy_process_group()

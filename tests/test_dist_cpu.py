@@ -250,3 +250,31 @@ def test_custom_allreduce_gather_scatter_eligibility_and_shapes():
     ca.disabled = True
     assert not ca.should_custom_ag(x) and ca.custom_all_gather(x) is None
     assert ca.custom_reduce_scatter(x, torch.empty(2, 64, dtype=torch.bfloat16)) is False
+
+
+def _world_and_helpers(rank, world, port):
+    """init_distributed_environment's world group and the module helpers of
+    parallel_state (parallel_state.py:985-1017, 1082-1145, 1320-1544) on gloo ranks."""
+    sys.path.insert(0, ROOT)
+    from aiter_b200.dist import parallel_state as ps
+    ps.init_distributed_environment(world, rank, f"tcp://127.0.0.1:{port}", rank, "gloo", timeout_s=60)
+    wg = ps.get_world_group()
+    assert wg.ranks == list(range(world)) and wg.rank_in_group == rank and wg.ca_comm is None
+    assert ps.is_global_first_rank() == (rank == 0)
+    assert ps.in_the_same_node_as(wg.cpu_group, source_rank=0) == [True] * world
+    ps.set_custom_all_reduce(False)
+    g = ps.init_model_parallel_group([[0], [1]], rank, "gloo", group_name="solo")
+    assert g.ranks == [rank] and g.unique_name == "solo" and g.ca_comm is None
+    tp = ps.initialize_model_parallel(world, local_rank=rank, backend="gloo")
+    assert tp.ca_comm is None
+    with ps.patch_tensor_parallel_group(g):
+        assert ps.get_tp_group() is g and ps.get_tensor_model_parallel_world_size() == 1
+    assert ps.get_tp_group() is tp
+    ps.prepare_communication_buffer_for_model(torch.nn.Linear(2, 2))
+    ps.set_custom_all_reduce(True)
+    ps.destroy_distributed_environment()
+    assert not dist.is_initialized()
+
+
+def test_world_group_and_parallel_state_helpers():
+    run_ranks(_world_and_helpers, 2)
