@@ -149,7 +149,7 @@ def fused_moe_a8w4(hidden, w1_p, w1_e, w2_p, w2_e, topk_weights, topk_ids,
 
 
 def fused_moe_fp8_blockscale_threaded(hidden, w1_q, w1_s, w2_q, w2_s, topk_weights, topk_ids,
-                                      threads=None, activation="silu"):
+                                      threads=None, activation="silu", doweight=True, dtype="bf16"):
     """Same arithmetic as `fused_moe_fp8_blockscale`, experts processed by a thread
     pool (numpy releases the GIL in the decode and the matmuls).  Used as the timed
     CPU baseline; every call dequantises the weights of every routed expert, as the

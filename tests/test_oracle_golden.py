@@ -279,3 +279,20 @@ def test_moe_sum_oracle_rounding_rule():
     x3 = np.concatenate([x, np.zeros((1, 2, 8), np.float32)], axis=1)[:, [0, 1, 2, 3, 4, 5]]
     x3[0, :, 0] = [1.0, 2.0 ** -9, 2.0 ** -9, 2.0 ** -9, 2.0 ** -9, 0.0]
     assert moe_sum(x3, "bf16")[0, 0] == round_bf16(np.float32(1.0 + 4 * 2.0 ** -9))
+
+
+@pytest.mark.parametrize("tag,shape", [("cfg0", (0, 32, 1024, 512, 8, 2)), ("cfg0_m7", (7, 7, 1024, 256, 8, 2))])
+def test_torch_port_of_reference_cpu_path_matches_reference(golden, tag, shape):
+    """The timed CPU baseline (oracle/moe_torch.py, torch CPU ops in the reference's
+    order) reproduces the reference pipeline's bf16 output bit for bit."""
+    import torch
+    from oracle import moe_torch
+    g = golden_group(golden, "moe_fp8")[tag]
+    seed, M, D, I, E, k = shape
+    c = inputs.make_moe_case(seed, M, D, I, E, k)
+    fp8 = lambda a: torch.from_numpy(a).view(torch.float8_e4m3fn)
+    out = moe_torch.fused_moe_fp8_blockscale(
+        torch.from_numpy(c["hidden"]).to(torch.bfloat16), fp8(c["w1_q"]), torch.from_numpy(c["w1_s"]),
+        fp8(c["w2_q"]), torch.from_numpy(c["w2_s"]), torch.from_numpy(c["topk_weights"]),
+        torch.from_numpy(c["topk_ids"]))
+    assert np.array_equal(out.float().numpy(), g["out"])
