@@ -15,6 +15,7 @@
 //                  fused_moe uses the first two (aiter/fused_moe.py:1719-1724).
 // All are memory-bound: 16-byte vector loads and stores, grids sized to the data.
 #include "common.cuh"
+#include "rexp.cuh"
 
 namespace {
 
@@ -264,7 +265,7 @@ topk_sigmoid_kernel(TW* __restrict__ weights, int32_t* __restrict__ ids, const T
                 }
             }
             if (lane == 0) {
-                weights[t * k + j] = from_f<TW>(1.0f / (1.0f + expf(-bv)));
+                weights[t * k + j] = from_f<TW>(abd::rsigmoid(bv));
                 ids[t * k + j] = bi;
             }
             if ((bi & 31) == lane) v[bi >> 5] = -INFINITY;  // taken

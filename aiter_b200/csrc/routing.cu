@@ -2,14 +2,27 @@
 //
 // One warp per token row.  Lane l holds experts l, l+32, l+64, ... (coalesced
 // loads); selection runs k rounds of a warp arg-max in which the larger value
-// wins and, on equal values, the lower expert index wins -- the tie rule of the
-// reference kernel (csrc/kernels/topk_softmax_kernels.cu:356-362).  Weights
-// follow the reference's torch arithmetic order: softmax over all experts
-// (exp(x - max) * (1 / sum)), then p / sum(p over the k picks)
-// (op_tests/test_moeTopkSoftmax.py:21-41).
+// wins and, on equal values, the lower expert index wins.
+//
+// Arithmetic contract (restated bit for bit by oracle/routing.py, and following the
+// reference's torch path, op_tests/test_moeTopkSoftmax.py:21-41 and
+// aiter/ops/topk.py:116-197, in torch's CPU order):
+//  * exp = abd::rexp(): Cody & Waite range reduction x = n ln2 + r with ln 2 split into
+//    a 21-bit head and a tail, the degree-13 Taylor polynomial of e^r in IEEE double
+//    with separately rounded multiplies and adds (__dmul_rn / __dadd_rn: never
+//    contracted into FMAs), times 2^n, rounded once to fp32 -- the correctly
+//    rounded e^x except within ~2^-50 of an fp32 rounding boundary;
+//  * softmax: max; e_i = exp(x_i - max); sum of 16-lane vectors in order (lane j
+//    takes elements j, j+16, ...; a partial last vector only its first E mod 16
+//    lanes), then the butterfly lane j + lane j^8, ^4, ^2, ^1 (torch's AVX-512
+//    softmax); E < 16 sums element by element; p_i = e_i * (1 / sum);
+//  * top-k of p (ties: lower index); renormalisation divides by the kept weights'
+//    sum in the order torch's CPU sum kernel uses for a row of k floats (ksum);
+//  * sigmoid(x) = 1 / (1 + exp(-x)), each step rounded to fp32.
 #include <math.h>
 
 #include "common.cuh"
+#include "rexp.cuh"
 
 namespace {
 
@@ -48,6 +61,63 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
+// Softmax denominator of the routing contract over e[j] = element lane + 32 j
+// (0 beyond E); every lane returns the sum.
+template <int VPT>
+__device__ __forceinline__ float softmax_sum(const float (&e)[VPT], int lane, int E) {
+    float acc = 0.f;
+    if (E < 16) {
+        // element by element from e_0 (VPT == 1: lane i holds e_i)
+        acc = __shfl_sync(0xffffffffu, e[0], 0);
+        for (int i = 1; i < E; ++i) acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, e[0], i));
+        return acc;
+    }
+    // vector lane c = lane & 15 (lanes 0..15 accumulate); vector t = 2 j + (upper half)
+    const int c = lane & 15;
+    const int full = E >> 4, rem = E & 15;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+        const float upper = __shfl_down_sync(0xffffffffu, e[j], 16);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int t = 2 * j + h;
+            const float v = h ? upper : e[j];
+            if (t == 0) acc = v;
+            else if (t < full || (t == full && c < rem)) acc = __fadd_rn(acc, v);
+        }
+    }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+    return __shfl_sync(0xffffffffu, acc, 0);
+}
+
+// Sum of the k kept weights (lane r holds pick r) in the order of torch's CPU sum
+// over a contiguous row of k floats; every lane returns the sum.
+__device__ __forceinline__ float ksum(float my_w, int k) {
+    auto w = [&](int i) { return __shfl_sync(0xffffffffu, my_w, i); };
+    if (k < 8) {
+        float a[4] = {0.f, 0.f, 0.f, 0.f};
+        const int nil = k >> 2;
+        for (int i = 0; i < nil; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) a[j] = __fadd_rn(a[j], w(4 * i + j));
+        for (int i = 4 * nil; i < k; ++i) a[0] = __fadd_rn(a[0], w(i));
+        return __fadd_rn(__fadd_rn(__fadd_rn(a[0], a[1]), a[2]), a[3]);
+    }
+    const int nv = k >> 3;
+    float l[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) l[j] = w(j);
+    for (int v = 1; v < nv; ++v)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) l[j] = __fadd_rn(l[j], w(8 * v + j));
+    float r = 0.f;
+    for (int i = 8 * nv; i < k; ++i) r = __fadd_rn(r, w(i));
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r = __fadd_rn(r, l[j]);
+    return r;
+}
+
 // Arg-max over the lane's VPT values (index lane + 32*j), then across the warp.
 template <int VPT>
 __device__ __forceinline__ ArgMax row_argmax(const float (&v)[VPT], int lane) {
@@ -82,42 +152,35 @@ topk_softmax_kernel(const T* __restrict__ gating, int64_t g_stride, int M, int E
         int e = lane + 32 * j;
         v[j] = e < E ? abd::to_f32(g[e]) : -INFINITY;
     }
-    // softmax statistics over all routed experts
+    // softmax over all routed experts
     float mx = v[0];
 #pragma unroll
     for (int j = 1; j < VPT; ++j) mx = fmaxf(mx, v[j]);
     mx = warp_max(mx);
-    float s = 0.f;
+    float e[VPT];
 #pragma unroll
-    for (int j = 0; j < VPT; ++j)
-        if (lane + 32 * j < E) s += expf(v[j] - mx);
-    s = warp_sum(s);
-    const float rz = 1.0f / s;
+    for (int j = 0; j < VPT; ++j) e[j] = (lane + 32 * j < E) ? abd::rexp(__fsub_rn(v[j], mx)) : 0.f;
+    const float rz = __frcp_rn(softmax_sum<VPT>(e, lane, E));
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) v[j] = (lane + 32 * j < E) ? __fmul_rn(e[j], rz) : -INFINITY;
 
     float my_p = 0.f;
     int my_id = 0;
     for (int r = 0; r < k; ++r) {
         ArgMax a = row_argmax<VPT>(v, lane);
-        float p = expf(a.v - mx) * rz;
-        if (lane == r) { my_p = p; my_id = a.i; }
+        if (lane == r) { my_p = a.v; my_id = a.i; }
         knock_out<VPT>(v, lane, a.i);
     }
-    float denom = 1.f;
-    if (renorm) {
-        // sum of the kept weights in selection order (lane 0 first)
-        float acc = 0.f;
-        for (int r = 0; r < k; ++r) acc += __shfl_sync(0xffffffffu, my_p, r);
-        denom = acc;
-    }
+    const float denom = renorm ? ksum(my_p, k) : 1.f;
     if (lane < k) {
-        w[(int64_t)row * w_stride + lane] = renorm ? my_p / denom : my_p;
+        w[(int64_t)row * w_stride + lane] = renorm ? __fdiv_rn(my_p, denom) : my_p;
         ids[(int64_t)row * id_stride + lane] = my_id;
         if (tei) tei[(int64_t)row * tei_stride + lane] = lane * M + row;
     }
     // shared experts: sigmoid of the trailing logits, written after the k picks
     for (int s2 = lane; s2 < num_shared; s2 += 32) {
         float x = abd::to_f32(g[E + s2]);
-        w[(int64_t)row * w_stride + k + s2] = 1.0f / (1.0f + expf(-x));
+        w[(int64_t)row * w_stride + k + s2] = abd::rsigmoid(x);
     }
 }
 
@@ -148,25 +211,22 @@ grouped_topk_kernel(const T* __restrict__ gating, int64_t g_stride, const T* __r
 #pragma unroll
         for (int j = 1; j < VPT; ++j) mx = fmaxf(mx, score[j]);
         mx = warp_max(mx);
-        float s = 0.f;
 #pragma unroll
-        for (int j = 0; j < VPT; ++j) {
-            score[j] = (lane + 32 * j < E) ? expf(score[j] - mx) : 0.f;
-            s += score[j];
-        }
-        s = warp_sum(s);
+        for (int j = 0; j < VPT; ++j)
+            score[j] = (lane + 32 * j < E) ? abd::rexp(__fsub_rn(score[j], mx)) : 0.f;
+        const float rz = __frcp_rn(softmax_sum<VPT>(score, lane, E));
 #pragma unroll
-        for (int j = 0; j < VPT; ++j) score[j] = score[j] / s;
+        for (int j = 0; j < VPT; ++j) score[j] = __fmul_rn(score[j], rz);
     } else {
 #pragma unroll
-        for (int j = 0; j < VPT; ++j) score[j] = 1.0f / (1.0f + expf(-score[j]));
+        for (int j = 0; j < VPT; ++j) score[j] = abd::rsigmoid(score[j]);
     }
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
         int e = lane + 32 * j;
         float b = 0.f;
         if (BIASED && e < E) b = abd::to_f32(bias[e]);
-        choice[j] = e < E ? score[j] + b : -INFINITY;
+        choice[j] = e < E ? __fadd_rn(score[j], b) : -INFINITY;
         if (e >= E) score[j] = -INFINITY;
     }
     // group scores: lane gi holds group gi's score
@@ -191,7 +251,7 @@ grouped_topk_kernel(const T* __restrict__ gating, int64_t g_stride, const T* __r
                 if (e < E && e / gs == gi && e != a.i) m2 = fmaxf(m2, choice[j]);
             }
             m2 = warp_max(m2);
-            gsc = a.v + m2;
+            gsc = __fadd_rn(a.v, m2);
         }
         if (lane == gi) gscore = gsc;
     }
@@ -225,15 +285,10 @@ grouped_topk_kernel(const T* __restrict__ gating, int64_t g_stride, const T* __r
         if (lane == r) { my_w = sc; my_id = a.i; }
         knock_out<VPT>(tmp, lane, a.i);
     }
-    float denom = 1.f;
-    if (renorm) {
-        float acc = 0.f;
-        for (int r = 0; r < k; ++r) acc += __shfl_sync(0xffffffffu, my_w, r);
-        denom = acc;
-    }
+    const float denom = renorm ? ksum(my_w, k) : 1.f;
     if (lane < k) {
-        float out = renorm ? my_w / denom : my_w;
-        w[(int64_t)row * w_stride + lane] = out * scaling;
+        float out = renorm ? __fdiv_rn(my_w, denom) : my_w;
+        w[(int64_t)row * w_stride + lane] = __fmul_rn(out, scaling);
         ids[(int64_t)row * id_stride + lane] = my_id;
     }
 }

@@ -16,6 +16,8 @@
 //   * multi-CTA: kernel 1 writes per-chunk expert histograms to the workspace,
 //     kernel 2 has every chunk-CTA rebuild the expert bases from the histograms and
 //     scatter its chunk.  Extra CTAs of the first kernel zero moe_buf meanwhile.
+#include <cuda.h>  // CUcontext / CUresult types only: no driver library is linked
+
 #include <mutex>
 
 #include "common.cuh"
@@ -384,13 +386,18 @@ AB_ENTRY(moe_sorting_fwd,
 // pool at start-up and treats any later allocation as a fault, or a plain C host
 // program that links this library without a device allocator of its own.  For
 // them the sorting histograms (the only scratch the multi-CTA sort needs) live in
-// this fixed device array.  It is part of the library image, so every GPU that
-// loads the library holds these 1 MiB until the process exits.
+// this fixed device array of 1 MiB.  CUDA loads a library's device code lazily (by
+// default since CUDA 12.2), so the array is placed on a GPU when this file's code
+// is first used there -- by the first call of the entry point below on that
+// device, whatever its size -- and stays until the process exits.  That first call
+// therefore needs the memory to be free: make it at start-up, before the caller
+// takes the free HBM, and before any stream capture.
 //
 // In host code `g_sort_scratch` is only a stand-in symbol, not a device address:
-// its address on the current device comes from cudaGetSymbolAddress, fetched once
-// per device on that device's first call and cached.  That first call therefore
-// makes a CUDA runtime query; issue it before any stream capture.
+// its address on the current device comes from cudaGetSymbolAddress, looked up on
+// the device's first call and cached per device (runtime device ids 0..63)
+// together with the CUDA context it belongs to; a call under another context (the
+// device was reset) looks it up again.
 //
 // Every call uses the same array, which keeps whatever the last call wrote.  The
 // count kernel overwrites every histogram entry a call reads, so nothing has to
@@ -400,22 +407,46 @@ static __device__ __align__(256) int g_sort_scratch[kSortScratchInts];
 
 namespace {
 
+struct ScratchSlot {
+    CUcontext ctx;
+    int* ptr;
+};
 std::mutex g_scratch_mu;
-int* g_scratch_dev[64] = {nullptr};
+ScratchSlot g_scratch_dev[64] = {};
+
+// The current driver context, through the runtime's driver entry-point lookup (the
+// library links only the CUDA runtime); null if the lookup is unavailable.
+CUcontext current_context() {
+    using GetCtx = CUresult (*)(CUcontext*);
+    static const GetCtx fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return (GetCtx) nullptr;
+        return reinterpret_cast<GetCtx>(f);
+    }();
+    CUcontext c = nullptr;
+    if (fn && fn(&c) != CUDA_SUCCESS) c = nullptr;
+    return c;
+}
 
 int* sort_scratch_on_current_device() {
     int dev = -1;
     AB_CUDA(cudaGetDevice(&dev));
     AB_CHECK(dev >= 0 && dev < 64, "unsupported device id ", dev);
+    const CUcontext ctx = current_context();
     std::lock_guard<std::mutex> lk(g_scratch_mu);
-    if (!g_scratch_dev[dev]) {
+    ScratchSlot& slot = g_scratch_dev[dev];
+    if (!slot.ptr || slot.ctx != ctx) {
         void* p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&p, g_sort_scratch);
         if (e != cudaSuccess || p == nullptr)
             ab::fail("cudaGetSymbolAddress(g_sort_scratch) failed: ", cudaGetErrorString(e));
-        g_scratch_dev[dev] = static_cast<int*>(p);
+        slot.ptr = static_cast<int*>(p);
+        slot.ctx = ctx;
     }
-    return g_scratch_dev[dev];
+    return slot.ptr;
 }
 
 }  // namespace
@@ -436,13 +467,20 @@ AB_ENTRY(moe_sorting_fwd_static_scratch,
                                                               topk_ids->shape[1], dispatch_policy);
     const int64_t have = (int64_t)sizeof(int) * kSortScratchInts;
     AB_CHECK(need_bytes <= have, "this sort needs ", need_bytes, " bytes of scratch but the built-in array holds ",
-             have, " (", kSortScratchInts, " ints = ceil(tokens/tokens_per_chunk) * experts); use moe_sorting_fwd "
-             "with a workspace for larger inputs");
+             have, " (", kSortScratchInts, " ints >= ceil(tokens / floor(1024 / topk)) * experts); use "
+             "moe_sorting_fwd with a workspace for larger inputs");
     aiter_tensor_t ws{};
     aiter_tensor_t* wsp = nullptr;
-    if (need_bytes > 0) {
+    int* scratch = nullptr;
+    {
+        // every call, even one small enough for the one-CTA sort, places the array on
+        // the device and caches its address, so a small call at start-up prepares
+        // the device for the larger calls that follow
         DeviceGuard dg(topk_ids->device_id);
-        ws.ptr = sort_scratch_on_current_device();
+        scratch = sort_scratch_on_current_device();
+    }
+    if (need_bytes > 0) {
+        ws.ptr = scratch;
         ws.numel_ = (size_t)have;
         ws.ndim = 1;
         ws.shape[0] = have;

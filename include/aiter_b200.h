@@ -137,12 +137,15 @@ int moe_sorting_fwd(aiter_tensor_t* topk_ids, aiter_tensor_t* topk_weights,
  * device memory while they run (a serving engine that gave all free HBM to its
  * KV-cache pool at start-up, a C host without its own device allocator).  It has
  * no counterpart in the reference, whose binding allocates the workspace with
- * torch.  The histograms use a 1 MiB array inside the library (held on every GPU
- * that loads it); inputs needing more (moe_sorting_get_workspace_size > 1 MiB,
- * e.g. more than 262144 = ceil(M*topk/1024) * E) are rejected with an error.  The
- * first call on a device looks the array up (issue it before any stream capture);
- * all calls share the array, so calls that overlap on the GPU race.  No
- * cudaMalloc/cudaFree or other allocation is made. */
+ * torch.  The histograms use a 1 MiB array inside the library; inputs needing more
+ * (moe_sorting_get_workspace_size > 1 MiB, i.e. ceil(M / floor(1024 / topk)) * E >
+ * 262144 when the multi-CTA sort runs) are rejected with an error.  CUDA loads the
+ * library's code lazily, so the array is placed on a GPU by the first call of this
+ * function on that device (any input size, e.g. one token): make that call at
+ * start-up, before the free HBM is taken and before any stream capture.  The
+ * array's address is cached per device (ids 0..63) and looked up again under a
+ * new CUDA context.  All calls share the array, so calls that overlap on the GPU
+ * race.  No cudaMalloc/cudaFree or other allocation is made. */
 int moe_sorting_fwd_static_scratch(aiter_tensor_t* topk_ids, aiter_tensor_t* topk_weights,
                                    aiter_tensor_t* sorted_token_ids, aiter_tensor_t* sorted_weights,
                                    aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids,

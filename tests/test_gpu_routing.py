@@ -1,6 +1,10 @@
-"""Routing kernels vs the reference's torch outputs (golden) and the oracle.
-ids are compared exactly; weights to 2e-6 relative (the reference's own test
-allows 1e-2, op_tests/test_moeTopkSoftmax.py:124-125)."""
+"""Routing kernels vs the oracle and the reference's torch outputs (golden).
+
+ids are compared exactly everywhere.  Weights are compared bit for bit (as uint32)
+with the oracle, which restates the kernels' arithmetic contract, and against the
+reference's torch outputs within the per-case ulp table of routing_ulps.py (torch's
+softmax exp approximation and its unsorted grouped top-k order; the reference's own
+test allows 1e-2, op_tests/test_moeTopkSoftmax.py:124-125)."""
 import numpy as np
 import pytest
 import torch
@@ -9,6 +13,11 @@ import aiter_b200 as aiter
 from conftest import golden_group
 from gpu_util import dev, requires_cuda, to_dev
 from oracle import routing
+from routing_ulps import MAX_ULPS, ulps
+
+
+def bits(a):
+    return np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
 
 pytestmark = [pytest.mark.gpu, requires_cuda]
 
@@ -31,7 +40,9 @@ def test_topk_softmax_matches_reference_golden(golden):
         k = g["ids"].shape[1]
         w, ids, tei = _run_topk(g["gating"], k, renorm, stride_pad=10)
         assert np.array_equal(ids, g["ids"]), case
-        np.testing.assert_allclose(w, g["weights"], rtol=2e-6, atol=1e-8, err_msg=case)
+        assert ulps(w, g["weights"]).max() <= MAX_ULPS["topk/" + case], case
+        w0, _, _ = routing.topk_softmax(g["gating"], k, renorm)
+        assert np.array_equal(bits(w), bits(w0)), case
         M = g["gating"].shape[0]
         assert np.array_equal(tei, np.arange(k)[None, :] * M + np.arange(M)[:, None])
 
@@ -48,7 +59,7 @@ def test_topk_softmax_vs_oracle(E, k, dtype):
         w0, ids0, _ = routing.topk_softmax(g_cast, k, renorm)
         # bf16/fp16 logits tie often: the lower expert index wins in both
         assert np.array_equal(ids, ids0)
-        np.testing.assert_allclose(w, w0, rtol=3e-6, atol=1e-8)
+        assert np.array_equal(bits(w), bits(w0))
 
 
 def test_topk_softmax_strided_gating_rows():
@@ -60,7 +71,7 @@ def test_topk_softmax_strided_gating_rows():
     aiter.topk_softmax(w, ids, torch.empty_like(ids), g, True)
     w0, ids0, _ = routing.topk_softmax(g.cpu().numpy(), 8, True)
     assert np.array_equal(ids.cpu().numpy(), ids0)
-    np.testing.assert_allclose(w.cpu().numpy(), w0, rtol=3e-6)
+    assert np.array_equal(bits(w.cpu().numpy()), bits(w0))
 
 
 def test_topk_softmax_shared_expert_sigmoid():
@@ -71,8 +82,8 @@ def test_topk_softmax_shared_expert_sigmoid():
     aiter.topk_softmax(w, ids, torch.empty_like(ids), to_dev(g), True, 2, "sigmoid")
     w0, ids0, _ = routing.topk_softmax(g[:, :64], 8, True)
     assert np.array_equal(ids.cpu().numpy(), ids0)
-    np.testing.assert_allclose(w.cpu().numpy()[:, :8], w0, rtol=3e-6)
-    np.testing.assert_allclose(w.cpu().numpy()[:, 8:], 1 / (1 + np.exp(-g[:, 64:])), rtol=1e-6)
+    assert np.array_equal(bits(w.cpu().numpy()[:, :8]), bits(w0))
+    assert np.array_equal(bits(w.cpu().numpy()[:, 8:]), bits(routing._sigmoid(g[:, 64:])))
 
 
 def test_topk_softmax_empty_input():
@@ -95,7 +106,9 @@ def test_grouped_topk_matches_reference_golden(golden):
         i0, w0 = _sorted(ids.cpu().numpy(), w.cpu().numpy())
         i1, w1 = _sorted(g["ids"], g["weights"])
         assert np.array_equal(i0, i1), case
-        np.testing.assert_allclose(w0, w1, rtol=3e-6, err_msg=case)
+        assert ulps(w0, w1).max() <= MAX_ULPS["gtopk/" + case], case
+        wo, io = routing.grouped_topk(g["gating"], k, G, TG, True, case.endswith("softmax"))
+        assert np.array_equal(ids.cpu().numpy(), io) and np.array_equal(bits(w.cpu().numpy()), bits(wo)), case
 
 
 def test_biased_grouped_topk_matches_reference_golden(golden):
@@ -107,7 +120,9 @@ def test_biased_grouped_topk_matches_reference_golden(golden):
         i0, w0 = _sorted(ids.cpu().numpy(), w.cpu().numpy())
         i1, w1 = _sorted(g["ids"], g["weights"])
         assert np.array_equal(i0, i1), case
-        np.testing.assert_allclose(w0, w1, rtol=3e-6, err_msg=case)
+        assert ulps(w0, w1).max() <= MAX_ULPS["btopk/" + case], case
+        wo, io = routing.biased_grouped_topk(g["gating"], g["bias"], k, G, TG, True)
+        assert np.array_equal(ids.cpu().numpy(), io) and np.array_equal(bits(w.cpu().numpy()), bits(wo)), case
 
 
 @pytest.mark.parametrize("scale", [1.0, 2.5])
@@ -120,14 +135,10 @@ def test_grouped_topk_deepseek_shape_vs_oracle(scale):
     ids = torch.empty(M, k, dtype=torch.int32, device=dev())
     aiter.biased_grouped_topk(to_dev(g), to_dev(bias), w, ids, G, TG, True, scale)
     w0, ids0 = routing.biased_grouped_topk(g, bias, k, G, TG, True, scale)
-    i0, ww0 = _sorted(ids.cpu().numpy(), w.cpu().numpy())
-    i1, ww1 = _sorted(ids0, w0)
-    assert np.array_equal(i0, i1)
-    np.testing.assert_allclose(ww0, ww1, rtol=3e-6)
+    assert np.array_equal(ids.cpu().numpy(), ids0)
+    assert np.array_equal(bits(w.cpu().numpy()), bits(w0))
     for soft in (True, False):
         aiter.grouped_topk(to_dev(g), w, ids, G, TG, True, soft, scale)
         w0, ids0 = routing.grouped_topk(g, k, G, TG, True, soft, scale)
-        i0, ww0 = _sorted(ids.cpu().numpy(), w.cpu().numpy())
-        i1, ww1 = _sorted(ids0, w0)
-        assert np.array_equal(i0, i1)
-        np.testing.assert_allclose(ww0, ww1, rtol=3e-6)
+        assert np.array_equal(ids.cpu().numpy(), ids0)
+        assert np.array_equal(bits(w.cpu().numpy()), bits(w0))

@@ -7,6 +7,7 @@ import pytest
 
 from conftest import golden_group
 from oracle import codecs, inputs, moe, quant, routing, sorting
+from routing_ulps import MAX_ULPS, ulps
 
 
 def _sha(a):
@@ -118,7 +119,7 @@ def test_topk_softmax_matches_reference(golden):
         k = g["ids"].shape[1]
         w, ids, tei = routing.topk_softmax(g["gating"], k, renorm)
         assert np.array_equal(ids, g["ids"]), case
-        np.testing.assert_allclose(w, g["weights"], rtol=2e-6, atol=1e-7, err_msg=case)
+        assert ulps(w, g["weights"]).max() <= MAX_ULPS["topk/" + case], case
         M = g["gating"].shape[0]
         assert tei[1, 0] == 1 and tei[0, 1] == M
 
@@ -135,7 +136,7 @@ def test_grouped_topk_matches_reference(golden):
         i0, w0 = _sorted_by_id(ids, w)
         i1, w1 = _sorted_by_id(g["ids"], g["weights"])
         assert np.array_equal(i0, i1), case
-        np.testing.assert_allclose(w0, w1, rtol=2e-6, atol=1e-7, err_msg=case)
+        assert ulps(w0, w1).max() <= MAX_ULPS["gtopk/" + case], case
 
 
 def test_biased_grouped_topk_matches_reference(golden):
@@ -145,7 +146,30 @@ def test_biased_grouped_topk_matches_reference(golden):
         i0, w0 = _sorted_by_id(ids, w)
         i1, w1 = _sorted_by_id(g["ids"], g["weights"])
         assert np.array_equal(i0, i1), case
-        np.testing.assert_allclose(w0, w1, rtol=2e-6, atol=1e-7, err_msg=case)
+        assert ulps(w0, w1).max() <= MAX_ULPS["btopk/" + case], case
+
+
+def test_routing_exp_is_correctly_rounded_on_a_dense_sample():
+    """rexp against e^x computed in double and rounded once to fp32, over the whole
+    range the softmax uses (x - max in [-104, 0]) and the sigmoid's [-30, 30], plus
+    the special values."""
+    rng = np.random.default_rng(0)
+    x = np.concatenate([rng.uniform(-104, 0, 400_000), rng.uniform(-30, 30, 400_000),
+                        np.arange(-1000, 1000) / 64.0]).astype(np.float32)
+    assert np.array_equal(routing.rexp(x), np.exp(x.astype(np.float64)).astype(np.float32))
+    sp = routing.rexp(np.array([0.0, -np.inf, np.inf, -200.0, 200.0, np.nan], np.float32))
+    assert sp[0] == 1.0 and sp[1] == 0.0 and np.isinf(sp[2]) and sp[3] == 0.0 and np.isinf(sp[4])
+    assert np.isnan(sp[5])
+
+
+def test_routing_ksum_is_torch_cpu_sum_order():
+    """The renormalising sum's order is torch's CPU sum over a contiguous row of k
+    floats, for every k the kernels accept."""
+    import torch
+    rng = np.random.default_rng(1)
+    for k in range(1, 33):
+        w = rng.random((4000, k), dtype=np.float32)
+        assert np.array_equal(routing.ksum(w), torch.from_numpy(w).sum(dim=-1).numpy()), k
 
 
 # ------------------------------------------------------------------ MoE pipeline
@@ -252,7 +276,7 @@ def test_topk_sigmoid_oracle_matches_reference(golden, tag):
     k = g["ids"].shape[1]
     w, ids = topk_sigmoid(g["logits"], k)
     assert np.array_equal(ids, g["ids"])
-    np.testing.assert_allclose(w, g["weights"], rtol=1e-6, atol=1e-7)
+    assert ulps(w, g["weights"]).max() <= MAX_ULPS["topk_sigmoid/" + tag]
 
 
 @pytest.mark.parametrize("tag", ["bf16", "fp32"])
@@ -293,6 +317,6 @@ def test_torch_port_of_reference_cpu_path_matches_reference(golden, tag, shape):
     fp8 = lambda a: torch.from_numpy(a).view(torch.float8_e4m3fn)
     out = moe_torch.fused_moe_fp8_blockscale(
         torch.from_numpy(c["hidden"]).to(torch.bfloat16), fp8(c["w1_q"]), torch.from_numpy(c["w1_s"]),
-        fp8(c["w2_q"]), torch.from_numpy(c["w2_s"]), torch.from_numpy(c["topk_weights"]),
-        torch.from_numpy(c["topk_ids"]))
+        fp8(c["w2_q"]), torch.from_numpy(c["w2_s"]), torch.from_numpy(g["topk_weights"]),
+        torch.from_numpy(g["topk_ids"]))
     assert np.array_equal(out.float().numpy(), g["out"])
