@@ -1,8 +1,7 @@
-"""Collective front-ends (aiter/dist/communication_op.py:30-244): the TP group's, and
-the EP / DP / PP groups' thin wrappers."""
+"""Collective front-ends of the TP and EP groups (aiter/dist/communication_op.py:30-244)."""
 import torch
 
-from .parallel_state import get_dp_group, get_ep_group, get_pp_group, get_tp_group
+from .parallel_state import get_ep_group, get_tp_group
 
 
 def tensor_model_parallel_all_reduce(input_: torch.Tensor, use_new: bool = True, open_fp8_quant: bool = False,
@@ -30,13 +29,6 @@ def tensor_model_parallel_all_gather(input_: torch.Tensor, use_custom: bool = Fa
 def tensor_model_parallel_gather(input_: torch.Tensor, dst: int = 0, dim: int = -1):
     """(communication_op.py:89-93)"""
     return get_tp_group().gather(input_, dst, dim)
-
-
-def broadcast_tensor_dict(tensor_dict=None, src: int = 0):
-    """(communication_op.py:96-101)"""
-    if not torch.distributed.is_initialized():
-        return tensor_dict
-    return get_tp_group().broadcast_tensor_dict(tensor_dict, src)
 
 
 def tensor_model_parallel_gemm_all_reduce(a: torch.Tensor, w: torch.Tensor, fused: bool = False) -> torch.Tensor:
@@ -122,8 +114,8 @@ def tensor_model_parallel_fused_moe(hidden_states, w1, w2, topk_weight, topk_ids
     return ca.all_reduce(stage)
 
 
-# ---------------------------------------------------------------- EP / DP / PP groups
-# (communication_op.py:105-244 in the reference)
+# ---------------------------------------------------------------- EP group
+# (communication_op.py:105-136 in the reference)
 
 def expert_parallel_all_reduce(input_, use_new=True, open_fp8_quant=False):
     return get_ep_group().all_reduce(input_, use_new, open_fp8_quant)
@@ -143,61 +135,3 @@ def expert_parallel_gather(input_, dst=0, dim=-1):
 
 def expert_parallel_broadcast(input_, src=0):
     return get_ep_group().broadcast(input_, src)
-
-
-def expert_parallel_broadcast_tensor_dict(tensor_dict=None, src=0):
-    if not torch.distributed.is_initialized():
-        return tensor_dict
-    return get_ep_group().broadcast_tensor_dict(tensor_dict, src)
-
-
-def data_parallel_all_reduce(input_, use_new=True, open_fp8_quant=False):
-    return get_dp_group().all_reduce(input_, use_new, open_fp8_quant)
-
-
-def data_parallel_all_gather(input_, use_custom=False, dim=-1):
-    return get_dp_group().all_gather(input_, use_custom, dim)
-
-
-def data_parallel_reduce_scatter(input_, use_custom=True, dim=0):
-    return get_dp_group().reduce_scatter_tensor(input_, use_custom, dim)
-
-
-def data_parallel_gather(input_, dst=0, dim=-1):
-    return get_dp_group().gather(input_, dst, dim)
-
-
-def data_parallel_broadcast(input_, src=0):
-    return get_dp_group().broadcast(input_, src)
-
-
-def data_parallel_broadcast_tensor_dict(tensor_dict=None, src=0):
-    if not torch.distributed.is_initialized():
-        return tensor_dict
-    return get_dp_group().broadcast_tensor_dict(tensor_dict, src)
-
-
-def pipeline_model_parallel_all_reduce(input_, use_new=True, open_fp8_quant=False):
-    return get_pp_group().all_reduce(input_, use_new, open_fp8_quant)
-
-
-def pipeline_model_parallel_all_gather(input_, use_custom=False, dim=-1):
-    return get_pp_group().all_gather(input_, use_custom, dim)
-
-
-def pipeline_model_parallel_broadcast(input_, src=0):
-    return get_pp_group().broadcast(input_, src)
-
-
-def pipeline_model_parallel_send(input_, dst=None):
-    get_pp_group().send(input_, dst)
-
-
-def pipeline_model_parallel_recv(size, dtype, src=None):
-    return get_pp_group().recv(size, dtype, src)
-
-
-def pipeline_model_parallel_broadcast_tensor_dict(tensor_dict=None, src=0):
-    if not torch.distributed.is_initialized():
-        return tensor_dict
-    return get_pp_group().broadcast_tensor_dict(tensor_dict, src)

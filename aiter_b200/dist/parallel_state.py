@@ -1,18 +1,23 @@
-"""Process groups for tensor parallelism (the role of aiter/dist/parallel_state.py).
+"""Process groups of the tensor- and expert-parallel MoE path (the role of
+aiter/dist/parallel_state.py for this path).
 
 One process per GPU.  `init_distributed_environment` starts torch.distributed
-(nccl) (parallel_state.py:1087-1145); `initialize_model_parallel` builds the TP
-GroupCoordinator (parallel_state.py:1147, get_tp_group :1022).  Like the reference,
-a GroupCoordinator holds an NCCL device group plus a gloo CPU group
-(parallel_state.py:262-270), and attaches the custom allreduce to the CPU group.
+(nccl) and the world group (parallel_state.py:1087-1145); `initialize_model_parallel`
+builds the TP group, which carries the IPC allreduces, and the EP group of the
+expert-parallel dispatch / combine (parallel_state.py:1147-1275, get_tp_group :1022).
+A GroupCoordinator holds an NCCL device group and a gloo CPU group for the IPC
+handle exchange (parallel_state.py:262-270).
+
+Pipeline and data parallelism are not part of this library's path: the MoE layer
+and its TP / EP collectives.  `initialize_model_parallel` keeps the reference's
+pipeline / data-parallel size arguments so that callers bind unchanged, and rejects
+sizes above 1.
 """
 import contextlib
 import dataclasses
 import datetime
 import os
-import pickle
-from collections import namedtuple
-from typing import Any, Dict, List, Optional, Tuple, Union
+from typing import Any, List, Optional
 
 import torch
 import torch.distributed as dist
@@ -21,8 +26,6 @@ from .custom_all_reduce import CustomAllreduce
 from .quick_all_reduce import QuickAllReduce
 
 _TP: Optional["GroupCoordinator"] = None
-_PP: Optional["GroupCoordinator"] = None
-_DP: Optional["GroupCoordinator"] = None
 _EP: Optional["GroupCoordinator"] = None
 _WORLD: Optional["GroupCoordinator"] = None
 _ENABLE_CUSTOM_ALL_REDUCE = True
@@ -41,23 +44,6 @@ def _rmsnorm_after(ar: torch.Tensor, res: torch.Tensor, w: torch.Tensor, eps: fl
     amax = y.abs().amax(dim=-1, keepdim=True)
     scale = torch.where(amax == 0, torch.ones_like(amax), amax / 448.0)
     return (y / scale).to(torch.float8_e4m3fn), res_out, scale
-
-
-TensorMetadata = namedtuple("TensorMetadata", ["device", "dtype", "size"])
-
-
-def _split_tensor_dict(tensor_dict: Dict[str, Any]) -> Tuple[List[Tuple[str, Any]], List[torch.Tensor]]:
-    """(metadata list, tensors): tensors become TensorMetadata entries, other values
-    travel as they are (parallel_state.py:55-78 in the reference)."""
-    metadata_list, tensor_list = [], []
-    for key, value in tensor_dict.items():
-        if isinstance(value, torch.Tensor):
-            device = value.device.type
-            metadata_list.append((key, TensorMetadata(device, value.dtype, value.size())))
-            tensor_list.append(value)
-        else:
-            metadata_list.append((key, value))
-    return metadata_list, tensor_list
 
 
 @dataclasses.dataclass
@@ -98,7 +84,7 @@ class GroupCoordinator:
             self._all2all_manager = EpAll2AllManager(self.cpu_group)
         return self._all2all_manager
 
-    # ---- the group's ranks (parallel_state.py:310-343): global ranks, ring order
+    # ---- the group's end ranks (parallel_state.py:310-327), global rank numbers
     @property
     def first_rank(self):
         return self.ranks[0]
@@ -114,14 +100,6 @@ class GroupCoordinator:
     @property
     def is_last_rank(self):
         return self.rank == self.ranks[-1]
-
-    @property
-    def next_rank(self):
-        return self.ranks[(self.rank_in_group + 1) % self.world_size]
-
-    @property
-    def prev_rank(self):
-        return self.ranks[(self.rank_in_group - 1) % self.world_size]
 
     def all_reduce(self, input_: torch.Tensor, ca_use_new: bool = True, ca_fp8_quant: bool = False,
                    prefill_support: bool = False) -> torch.Tensor:
@@ -216,88 +194,6 @@ class GroupCoordinator:
         dist.broadcast_object_list(holder, src=self.ranks[src], group=self.cpu_group)
         return holder[0]
 
-    def broadcast_object_list(self, obj_list: List[Any], src: int = 0, group=None):
-        """Broadcast a list of picklable objects in place from group rank `src`
-        (parallel_state.py:651-666)."""
-        assert src < self.world_size, f"Invalid src rank ({src})"
-        if self.world_size == 1:
-            return obj_list
-        dist.broadcast_object_list(obj_list, src=self.ranks[src], group=self.cpu_group)
-        return obj_list
-
-    def send_object(self, obj: Any, dst: int) -> None:
-        """Pickle `obj` and send it to group rank `dst` over the CPU group: its length,
-        then its bytes (parallel_state.py:668-693)."""
-        assert dst < self.world_size, f"Invalid dst rank ({dst})"
-        assert dst != self.rank_in_group, "Invalid destination rank. Destination rank is the same as the current rank."
-        payload = torch.frombuffer(bytearray(pickle.dumps(obj)), dtype=torch.uint8)
-        dist.send(torch.tensor([payload.numel()], dtype=torch.long), dst=self.ranks[dst], group=self.cpu_group)
-        dist.send(payload, dst=self.ranks[dst], group=self.cpu_group)
-
-    def recv_object(self, src: int) -> Any:
-        """Receive an object sent by send_object from group rank `src` (:695-729)."""
-        assert src < self.world_size, f"Invalid src rank ({src})"
-        assert src != self.rank_in_group, "Invalid source rank. Source rank is the same as the current rank."
-        n = torch.empty(1, dtype=torch.long)
-        dist.recv(n, src=self.ranks[src], group=self.cpu_group)
-        payload = torch.empty(int(n.item()), dtype=torch.uint8)
-        dist.recv(payload, src=self.ranks[src], group=self.cpu_group)
-        return pickle.loads(payload.numpy().tobytes())
-
-    def send_tensor_dict(self, tensor_dict: Dict[str, Union[torch.Tensor, Any]], dst: Optional[int] = None,
-                         all_gather_group: Optional["GroupCoordinator"] = None):
-        """Send a dict of tensors and plain values to group rank `dst` (default: the next
-        one; parallel_state.py:813-864): metadata by send_object, then each non-empty
-        tensor (CPU tensors over the CPU group, device tensors over the device group).
-        With `all_gather_group`, each rank of that group sends only its 1/W slice of
-        every divisible tensor and the receiver all-gathers the slices."""
-        if not dist.is_initialized() or self.world_size == 1:
-            return tensor_dict
-        w = 1 if all_gather_group is None else all_gather_group.world_size
-        r = 0 if all_gather_group is None else all_gather_group.rank_in_group
-        if dst is None:
-            dst = (self.rank_in_group + 1) % self.world_size
-        assert dst < self.world_size, f"Invalid dst rank ({dst})"
-        assert isinstance(tensor_dict, dict), f"Expecting a dictionary, got {type(tensor_dict)}"
-        metadata_list, tensors = _split_tensor_dict(tensor_dict)
-        self.send_object(metadata_list, dst=dst)
-        for t in tensors:
-            if t.numel() == 0:
-                continue
-            if all_gather_group is not None and t.numel() % w == 0:
-                t = t.reshape(w, -1)[r]
-            dist.send(t.contiguous(), dst=self.ranks[dst], group=self.cpu_group if t.is_cpu else self.device_group)
-        return None
-
-    def recv_tensor_dict(self, src: Optional[int] = None, all_gather_group: Optional["GroupCoordinator"] = None):
-        """Receive a dict sent by send_tensor_dict from group rank `src` (default: the
-        previous one; parallel_state.py:866-926)."""
-        if not dist.is_initialized() or self.world_size == 1:
-            return None
-        w = 1 if all_gather_group is None else all_gather_group.world_size
-        r = 0 if all_gather_group is None else all_gather_group.rank_in_group
-        if src is None:
-            src = (self.rank_in_group - 1) % self.world_size
-        assert src < self.world_size, f"Invalid src rank ({src})"
-        out = {}
-        for key, value in self.recv_object(src=src):
-            if not isinstance(value, TensorMetadata):
-                out[key] = value
-                continue
-            dev = torch.device("cpu") if value.device == "cpu" else self.device
-            t = torch.empty(value.size, dtype=value.dtype, device=dev)
-            if t.numel() == 0:
-                out[key] = t
-                continue
-            sliced = all_gather_group is not None and t.numel() % w == 0
-            part = t.reshape(w, -1)[r] if sliced else t
-            buf = torch.empty_like(part) if sliced else part
-            dist.recv(buf, src=self.ranks[src], group=self.cpu_group if t.is_cpu else self.device_group)
-            if sliced:
-                buf = all_gather_group.all_gather(buf, dim=0).reshape(value.size)
-            out[key] = buf
-        return out
-
     def barrier(self):
         """Barrier over the CPU group (parallel_state.py:928-935: an NCCL barrier would
         allocate device tensors behind the caller's back)."""
@@ -307,55 +203,6 @@ class GroupCoordinator:
         """Hook for communicators that register model buffers (parallel_state.py:965-967).
         The IPC allreduce stages through its own buffers, so there is nothing to do."""
         return None
-
-    def broadcast_tensor_dict(self, tensor_dict: Optional[Dict[str, Union[torch.Tensor, Any]]] = None,
-                              src: int = 0, group=None, metadata_group=None) -> Optional[Dict[str, Union[torch.Tensor, Any]]]:
-        """Broadcast a dict of tensors and plain values from rank `src` (parallel_state.py:
-        731-800): the metadata goes over the CPU group, CPU tensors over the CPU group
-        and device tensors over the device group (`group` / `metadata_group` are accepted
-        for the reference's signature; this group's own are used)."""
-        if not dist.is_initialized() or self.world_size == 1:
-            return tensor_dict
-        assert src < self.world_size, f"Invalid src rank ({src})"
-        if self.rank_in_group == src:
-            assert isinstance(tensor_dict, dict), f"Expecting a dictionary, got {type(tensor_dict)}"
-            metadata_list, tensors = _split_tensor_dict(tensor_dict)
-            self.broadcast_object(metadata_list, src=src)
-            handles = [dist.broadcast(t, src=self.ranks[src], async_op=True,
-                                      group=self.cpu_group if t.is_cpu else self.device_group)
-                       for t in tensors if t.numel() > 0]
-            for h in handles:
-                h.wait()
-            return tensor_dict
-        metadata_list = self.broadcast_object(None, src=src)
-        out, handles = {}, []
-        for key, value in metadata_list:
-            if isinstance(value, TensorMetadata):
-                dev = torch.device("cpu") if value.device == "cpu" else self.device
-                t = torch.empty(value.size, dtype=value.dtype, device=dev)
-                if t.numel() > 0:
-                    handles.append(dist.broadcast(t, src=self.ranks[src], async_op=True,
-                                                  group=self.cpu_group if t.is_cpu else self.device_group))
-                out[key] = t
-            else:
-                out[key] = value
-        for h in handles:
-            h.wait()
-        return out
-
-    def send(self, tensor: torch.Tensor, dst: Optional[int] = None) -> None:
-        """Send to group rank `dst` (default: the next one; parallel_state.py:937-947)."""
-        if dst is None:
-            dst = (self.rank_in_group + 1) % self.world_size
-        dist.send(tensor, self.ranks[dst], self.device_group)
-
-    def recv(self, size, dtype, src: Optional[int] = None) -> torch.Tensor:
-        """Receive from group rank `src` (default: the previous one; :949-970)."""
-        if src is None:
-            src = (self.rank_in_group - 1) % self.world_size
-        tensor = torch.empty(size, dtype=dtype, device=self.device)
-        dist.recv(tensor, self.ranks[src], self.device_group)
-        return tensor
 
     def fused_allreduce_rmsnorm(self, input_: torch.Tensor, residual_inp_: torch.Tensor, weight_: torch.Tensor,
                                 eps: float, prefill_support: bool = False):
@@ -444,17 +291,15 @@ def init_model_parallel_group(group_ranks: List[List[int]], local_rank: int, bac
 
 def init_distributed_environment(world_size=-1, rank=-1, distributed_init_method="env://", local_rank=-1,
                                  backend="nccl", data_parallel_size=1, data_parallel_rank=0, timeout_s=120):
-    """Start torch.distributed and the world group (parallel_state.py:1087-1145).  With
-    data_parallel_size > 1 the given rank / world size are those inside one data-parallel
-    replica and are widened to the global ones, as the reference does."""
+    """Start torch.distributed and the world group (parallel_state.py:1087-1145).
+    `data_parallel_size` / `data_parallel_rank` keep the reference's signature; sizes
+    above 1 are rejected (data parallelism is outside this library's path)."""
     global _WORLD
+    _check_single("data_parallel", data_parallel_size)
     if world_size == -1:
         world_size = int(os.environ.get("WORLD_SIZE", "1"))
     if rank == -1:
         rank = int(os.environ.get("RANK", "0"))
-    if data_parallel_size > 1:
-        rank = data_parallel_rank * world_size + rank
-        world_size = data_parallel_size * world_size
     if not dist.is_initialized():
         dist.init_process_group(backend=backend, init_method=distributed_init_method, world_size=world_size,
                                 rank=rank, timeout=datetime.timedelta(seconds=timeout_s))
@@ -485,28 +330,34 @@ def _init_groups(group_ranks, local_rank, backend, name, use_custom_allreduce=Fa
     return mine
 
 
+def _check_single(what: str, size: int):
+    if size != 1:
+        raise NotImplementedError(f"{what} size {size}: pipeline and data parallelism are outside this library's "
+                                  f"path (the MoE layer and its tensor- / expert-parallel collectives)")
+
+
 def initialize_model_parallel(tensor_model_parallel_size=1, pipeline_model_parallel_size=1, backend=None,
                               data_parallel_size=1, local_rank=None, use_custom_allreduce=True,
                               ca_max_size=128 * 1024 * 1024):
-    """TP, PP, DP and EP groups with the reference's rank layout
-    (parallel_state.py:1147-1275): ranks = [.., dp, pp, tp] with TP fastest; the EP group
-    merges DP x TP of one pipeline stage.  The TP group carries the custom (and, when
-    enabled, the quick) allreduce.  Returns the TP group."""
-    global _TP, _PP, _DP, _EP
+    """TP and EP groups (parallel_state.py:1147-1275).  Consecutive ranks form a TP group
+    (TP is the fastest-varying dimension of the reference's layout); with no data
+    parallelism the EP group of a rank is its TP group.  The TP group carries the IPC
+    allreduce and, when AITER_QUICK_REDUCE_QUANTIZATION names a regime, the quick
+    allreduce.  Returns the TP group."""
+    global _TP, _EP
     assert _TP is None, "tensor model parallel group is already initialized"
+    _check_single("pipeline_model_parallel", pipeline_model_parallel_size)
+    _check_single("data_parallel", data_parallel_size)
     world = dist.get_world_size()
-    tp, pp, dp = tensor_model_parallel_size, pipeline_model_parallel_size, data_parallel_size
-    assert world % (tp * pp * dp) == 0, f"world size {world} is not a multiple of tp * pp * dp = {tp * pp * dp}"
+    tp = tensor_model_parallel_size
+    assert world % tp == 0, f"world size {world} is not a multiple of tensor_model_parallel_size {tp}"
     backend = backend or dist.get_backend()
     if local_rank is None:
         local_rank = int(os.environ.get("LOCAL_RANK", str(dist.get_rank())))
-    all_ranks = torch.arange(world).reshape(-1, dp, pp, tp)
-    lists = lambda t, n: [x.tolist() for x in t.reshape(-1, n).unbind(0)]
-    _TP = _init_groups(lists(all_ranks, tp), local_rank, backend, "tp",
-                       use_custom_allreduce and _ENABLE_CUSTOM_ALL_REDUCE, ca_max_size, use_quick_allreduce=True)
-    _PP = _init_groups(lists(all_ranks.transpose(2, 3), pp), local_rank, backend, "pp")
-    _DP = _init_groups(lists(all_ranks.transpose(1, 3), dp), local_rank, backend, "dp")
-    _EP = _init_groups(lists(all_ranks.transpose(1, 2), dp * tp), local_rank, backend, "ep")
+    groups = [list(range(g * tp, (g + 1) * tp)) for g in range(world // tp)]
+    _TP = _init_groups(groups, local_rank, backend, "tp", use_custom_allreduce and _ENABLE_CUSTOM_ALL_REDUCE,
+                       ca_max_size, use_quick_allreduce=True)
+    _EP = _init_groups(groups, local_rank, backend, "ep")
     return _TP
 
 
@@ -518,26 +369,15 @@ def ensure_model_parallel_initialized(tensor_model_parallel_size, pipeline_model
                                   data_parallel_size)
         return
     assert get_tp_group().world_size == tensor_model_parallel_size, "tensor parallel group already initialized"
-    assert get_pp_group().world_size == pipeline_model_parallel_size, "pipeline parallel group already initialized"
 
 
 def model_parallel_is_initialized() -> bool:
-    return _TP is not None and _PP is not None
+    return _TP is not None and _EP is not None
 
 
 def get_tp_group() -> GroupCoordinator:
     assert _TP is not None, "tensor model parallel group is not initialized"
     return _TP
-
-
-def get_pp_group() -> GroupCoordinator:
-    assert _PP is not None, "pipeline model parallel group is not initialized"
-    return _PP
-
-
-def get_dp_group() -> GroupCoordinator:
-    assert _DP is not None, "data parallel group is not initialized"
-    return _DP
 
 
 def get_ep_group() -> GroupCoordinator:
@@ -563,11 +403,11 @@ def graph_capture():
 
 
 def destroy_model_parallel():
-    global _TP, _PP, _DP, _EP
-    for g in (_TP, _PP, _DP, _EP):
+    global _TP, _EP
+    for g in (_TP, _EP):
         if g is not None:
             g.destroy()
-    _TP = _PP = _DP = _EP = None
+    _TP = _EP = None
 
 
 @contextlib.contextmanager
@@ -605,7 +445,7 @@ def is_global_first_rank() -> bool:
 
 def prepare_communication_buffer_for_model(model: torch.nn.Module):
     """Let every group's communicators size buffers for `model` (parallel_state.py:1526-1544)."""
-    for g in (_TP, _PP, _DP, _EP):
+    for g in (_TP, _EP):
         if g is not None:
             g.prepare_communication_buffer_for_model(model)
 

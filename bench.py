@@ -923,10 +923,10 @@ def run_a8w4(args, rank, world, local):
 
 def run_routing(args, rank, world, local):
     """topk_softmax and moe_sorting_fwd alone at the config-1 (E=128) and config-2 (E=256,
-    Zipf-skewed) routing shapes over the token sweep: CUDA-event time per call (inputs
-    and outputs far smaller than L2 except the zeroed output, so the figures are
-    launch- and latency-bound at small M) and achieved bytes / s against the measured HBM
-    peak.  Algorithmic bytes: topk_softmax M*E*4 (fp32 logits) + M*k*12 (weights, ids,
+    Zipf-skewed) routing shapes over the token sweep: time per call replayed from a CUDA
+    graph (below M of about 16384 the inputs fit in L2 and a call is latency-bound; the
+    sweep runs to M = 262144, where the bytes dominate) and achieved bytes / s against
+    the measured HBM peak.  Algorithmic bytes: topk_softmax M*E*4 (fp32 logits) + M*k*12 (weights, ids,
     token-expert indices); sorting M*k*8 read + rows*8 written (ids, weights) + block ids
     + M*D*2 of output zeroing."""
     from aiter_b200 import moe_op
@@ -939,7 +939,7 @@ def run_routing(args, rank, world, local):
         if zipf:
             perm = torch.randperm(E_, generator=torch.Generator().manual_seed(7)) + 1
             bias = torch.log((1.0 / perm.double() ** 1.1) / (1.0 / perm.double() ** 1.1).sum()).float().to(dev)
-        for M in (1, 16, 128, 1024, 4096, 16384):
+        for M in (1, 16, 128, 1024, 4096, 16384, 65536, 262144):
             logits = torch.randn(M, E_, device=dev, generator=g)
             if bias is not None:
                 logits = logits + bias
@@ -958,8 +958,10 @@ def run_routing(args, rank, world, local):
             topk = lambda: moe_op.topk_softmax(tw, tid, tei, logits, True)
             sort = lambda: moe_op.moe_sorting_fwd(tid, tw, sid, sw, seid, nv, out, E_, B, None, None, 0,
                                                   ws if ws_n else None, None)
-            us_t = 1e3 * _time_loop(topk, args.steps, args.warmup, world)
-            us_s = 1e3 * _time_loop(sort, args.steps, args.warmup, world)
+            # replayed from a CUDA graph: the kernels' own time, without the eager
+            # per-call host overhead of the Python / ctypes front-end
+            us_t = 1e3 * _graph_time(topk, args.steps)
+            us_s = 1e3 * _graph_time(sort, args.steps)
             bytes_t = M * E_ * 4 + M * TOPK * 12
             bytes_s = M * TOPK * 8 + max_pad * 8 + seid.numel() * 4 + M * D * 2
             gbs_t, gbs_s = bytes_t / (us_t * 1e-6) / 1e9, bytes_s / (us_s * 1e-6) / 1e9

@@ -121,7 +121,7 @@ def test_nccl_group_rejected_for_handle_exchange():
 
 def _group_collectives(rank, world, port):
     """all_gather (dim 0, last, middle), reduce_scatter_tensor (divisible and flat),
-    gather, broadcast_tensor_dict and the front-ends, on the non-custom path."""
+    gather and the front-ends, on the non-custom path."""
     _init(rank, world, port)
     from aiter_b200.dist import communication_op as co
     from aiter_b200.dist import parallel_state as ps
@@ -142,9 +142,6 @@ def _group_collectives(rank, world, port):
     assert rz.shape == (6 // world,) and torch.equal(rz, ztot.chunk(world)[rank])
     g = co.tensor_model_parallel_gather(x, dst=0, dim=0)
     assert (torch.equal(g, torch.cat(parts, dim=0)) if rank == 0 else g is None)
-    d = co.broadcast_tensor_dict({"a": torch.ones(2, 2) * 7, "n": 3, "e": torch.empty(0)} if rank == 0 else None,
-                                 src=0)
-    assert torch.equal(d["a"], torch.ones(2, 2) * 7) and d["n"] == 3 and d["e"].numel() == 0
     ps.destroy_model_parallel()
     dist.destroy_process_group()
 
@@ -153,76 +150,56 @@ def test_group_coordinator_collectives_fallback_path():
     run_ranks(_group_collectives, 2)
 
 
-def _group_layout(rank, world, port, tp, pp, dp):
-    """The reference's rank layout (parallel_state.py:1181-1264): ranks [.., dp, pp, tp]
-    with TP fastest, EP = DP x TP of a pipeline stage; the EP / DP / PP front-ends and
-    PP send / recv on gloo ranks."""
+def _group_layout(rank, world, port, tp):
+    """TP groups of consecutive ranks (TP fastest, as the reference's layout,
+    parallel_state.py:1181-1264), the EP group equal to the TP group without data
+    parallelism, the EP front-ends; pipeline / data-parallel sizes above 1 rejected."""
     _init(rank, world, port)
     from aiter_b200.dist import communication_op as co
     from aiter_b200.dist import parallel_state as ps
-    ps.initialize_model_parallel(tp, pp, "gloo", dp, local_rank=rank, use_custom_allreduce=False)
-    grid = torch.arange(world).reshape(-1, dp, pp, tp)
-    where = (grid == rank).nonzero()[0].tolist()          # [outer, d, p, t]
-    o, d, p, t = where
-    assert ps.get_tp_group().ranks == grid[o, d, p, :].tolist()
-    assert ps.get_pp_group().ranks == grid[o, d, :, t].tolist()
-    assert ps.get_dp_group().ranks == grid[o, :, p, t].tolist()
-    assert ps.get_ep_group().ranks == grid[o, :, p, :].reshape(-1).tolist()
-    assert ps.get_tensor_model_parallel_world_size() == tp and ps.get_tensor_model_parallel_rank() == t
+    for bad in (dict(pipeline_model_parallel_size=2), dict(data_parallel_size=2)):
+        with pytest.raises(NotImplementedError, match="outside this library"):
+            ps.initialize_model_parallel(tp, backend="gloo", local_rank=rank, use_custom_allreduce=False, **bad)
+    ps.initialize_model_parallel(tp, 1, "gloo", 1, local_rank=rank, use_custom_allreduce=False)
+    first = rank // tp * tp
+    assert ps.get_tp_group().ranks == list(range(first, first + tp))
+    assert ps.get_ep_group().ranks == ps.get_tp_group().ranks
+    assert ps.get_tensor_model_parallel_world_size() == tp and ps.get_tensor_model_parallel_rank() == rank - first
     x = torch.full((2, 4), float(rank + 1))
     ep_sum = float(sum(r + 1 for r in ps.get_ep_group().ranks))
     assert torch.equal(co.expert_parallel_all_reduce(x), torch.full((2, 4), ep_sum))
-    dp_sum = float(sum(r + 1 for r in ps.get_dp_group().ranks))
-    assert torch.equal(co.data_parallel_all_reduce(x), torch.full((2, 4), dp_sum))
     g = co.expert_parallel_all_gather(x, dim=0)
     assert torch.equal(g[:, 0], torch.tensor([float(r + 1) for r in ps.get_ep_group().ranks]).repeat_interleave(2))
-    if pp > 1:
-        pg = ps.get_pp_group()
-        if pg.rank_in_group == 0:
-            co.pipeline_model_parallel_send(torch.arange(6, dtype=torch.float32) + rank)
-        elif pg.rank_in_group == 1:
-            got = co.pipeline_model_parallel_recv((6,), torch.float32)
-            assert torch.equal(got, torch.arange(6, dtype=torch.float32) + pg.ranks[0])
     b = co.expert_parallel_broadcast(torch.full((3,), float(rank)), src=1)
     assert torch.equal(b, torch.full((3,), float(ps.get_ep_group().ranks[1])))
     ps.destroy_model_parallel()
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("tp,pp,dp", [(2, 2, 1), (2, 1, 2)])
-def test_model_parallel_group_layout(tp, pp, dp):
-    run_ranks(_group_layout, 4, tp, pp, dp)
+@pytest.mark.parametrize("tp", [2, 4])
+def test_model_parallel_group_layout(tp):
+    run_ranks(_group_layout, 4, tp)
 
 
-def _group_p2p_objects(rank, world, port):
-    """Ring ranks, object and tensor-dict point-to-point, object-list broadcast, barrier
-    and the keyword names of all_reduce (parallel_state.py:310-343, 376-383, 651-935)."""
+def _group_ranks_and_barrier(rank, world, port):
+    """End ranks, the keyword names of all_reduce, object broadcast and the barrier
+    (parallel_state.py:310-327, 376-383, 928-935)."""
     _init(rank, world, port)
     from aiter_b200.dist import parallel_state as ps
     tp = ps.initialize_model_parallel(world, local_rank=rank, backend="gloo", use_custom_allreduce=False)
     assert tp.first_rank == 0 and tp.last_rank == world - 1
     assert tp.is_first_rank == (rank == 0) and tp.is_last_rank == (rank == world - 1)
-    assert tp.next_rank == (rank + 1) % world and tp.prev_rank == (rank - 1) % world
     y = tp.all_reduce(torch.full((3,), float(rank)), ca_use_new=True, ca_fp8_quant=False)
     assert torch.equal(y, torch.full((3,), float(sum(range(world)))))
-    lst = [{"k": rank}, "s"] if rank == 1 else [None, None]
-    assert tp.broadcast_object_list(lst, src=1) == [{"k": 1}, "s"]
-    if rank == 0:
-        tp.send_object({"step": 7, "names": ["a", "b"]}, dst=1)
-        tp.send_tensor_dict({"x": torch.arange(6, dtype=torch.float32).reshape(2, 3), "n": 5, "e": torch.empty(0)})
-    elif rank == 1:
-        assert tp.recv_object(src=0) == {"step": 7, "names": ["a", "b"]}
-        d = tp.recv_tensor_dict()
-        assert torch.equal(d["x"], torch.arange(6, dtype=torch.float32).reshape(2, 3))
-        assert d["n"] == 5 and d["e"].numel() == 0
+    assert tp.broadcast_object({"k": rank} if rank == 1 else None, src=1) == {"k": 1}
     tp.barrier()
     assert tp.prepare_communication_buffer_for_model(torch.nn.Linear(2, 2)) is None
     ps.destroy_model_parallel()
     dist.destroy_process_group()
 
 
-def test_group_coordinator_ring_and_object_p2p():
-    run_ranks(_group_p2p_objects, 2)
+def test_group_coordinator_ranks_objects_barrier():
+    run_ranks(_group_ranks_and_barrier, 2)
 
 
 def test_custom_allreduce_gather_scatter_eligibility_and_shapes():

@@ -1,9 +1,6 @@
 """Single-GPU parity of the EP dispatch / combine kernels: all W ranks emulated as
 CTA rows of cooperative launches (ep_emu_*), every rank's received arrays and
-combined outputs bit-exact against oracle/ep.py.  Skipped until the kernels have
-been run on a GPU, unless AITER_B200_TEST_UNRUN=1."""
-import os
-
+combined outputs bit-exact against oracle/ep.py."""
 import numpy as np
 import pytest
 import torch
@@ -11,8 +8,6 @@ import torch
 pytestmark = [
     pytest.mark.gpu,
     pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU"),
-    pytest.mark.skipif(os.environ.get("AITER_B200_TEST_UNRUN") != "1",
-                       reason="EP dispatch / combine not yet run on a GPU"),
 ]
 
 

@@ -6,7 +6,6 @@
   region, so nobody writes the awaited flags) must give up after ~2 s, set the error
   word the host reads, and leave the GPU usable."""
 import ctypes
-import os
 import time
 
 import pytest
@@ -51,8 +50,6 @@ def test_gemm_every_tile_width_vs_torch(M, N, K):
 
 # Cluster splits that do not divide the activation tile: N=3072 gives 24 tiles and a
 # split of 6 (32- to 256-row tiles), N=1536 at M=512 gives 24 tiles of 256 rows.
-@pytest.mark.skipif(os.environ.get("AITER_B200_TEST_UNRUN") != "1",
-                    reason="uneven cluster split rows not yet run on a B200")
 @pytest.mark.parametrize("M,N,K", [(1, 3072, 1024), (60, 3072, 2048), (300, 3072, 1024), (512, 1536, 4096),
                                    (511, 1536, 1024), (33, 1536, 512)])
 def test_gemm_uneven_cluster_split_vs_torch(M, N, K):

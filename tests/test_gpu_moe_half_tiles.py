@@ -3,8 +3,7 @@ re-run with AITER_B200_MOE_HALF_TILES=1: expert blocks whose rows 64.. are all
 padding then run as M=64 tcgen05 tiles whose epilogue reads half the TMEM bytes.
 Its shapes hit such blocks everywhere (few tokens per expert) and at config-1 size
 (about half the experts' last blocks at M=4096).  The variable is read once per
-process, so the suite runs in a child process.  Runs only with AITER_B200_TEST_UNRUN=1
-until the M=64 tiles have been run on a B200."""
+process, so the suite runs in a child process."""
 import os
 import subprocess
 import sys
@@ -14,9 +13,7 @@ import torch
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA device"),
-              pytest.mark.skipif(os.environ.get("AITER_B200_TEST_UNRUN") != "1",
-                                 reason="M=64 half tiles not yet run on a B200")]
+              pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA device")]
 
 
 def test_moe_parity_suite_with_half_tiles():

@@ -1,6 +1,5 @@
 """GPU parity of topk_sigmoid, moe_sum and the gated activations (moe_misc.cu)
-against the reference's torch functions (golden vectors) and the oracle.  Runs only
-with AITER_B200_TEST_UNRUN=1 until these kernels have been run on a B200.
+against the reference's torch functions (golden vectors) and the oracle.
 
 * topk_sigmoid: ids bit-exact, weights within 1e-6 (fp32 sigmoid), every experts /
   topk / dtype of the reference's test grid (op_tests/test_moe_topk_sigmoid.py:113-116);
@@ -12,8 +11,6 @@ with AITER_B200_TEST_UNRUN=1 until these kernels have been run on a B200.
   output dtype pair the reference accepts; scaled_silu_and_mul: fp8 codes within one
   step; unsupported dtype pairs raise.
 """
-import os
-
 import numpy as np
 import pytest
 import torch
@@ -25,9 +22,7 @@ from oracle import activation as oact
 from oracle.moe import moe_sum as moe_sum_ref
 from oracle.routing import topk_sigmoid as topk_sigmoid_ref
 
-pytestmark = [pytest.mark.gpu, requires_cuda,
-              pytest.mark.skipif(os.environ.get("AITER_B200_TEST_UNRUN") != "1",
-                                 reason="topk_sigmoid / moe_sum / act_and_mul not yet run on a B200")]
+pytestmark = [pytest.mark.gpu, requires_cuda]
 
 DT = {"fp32": torch.float32, "bf16": torch.bfloat16, "fp16": torch.float16}
 

@@ -7,11 +7,8 @@
 DeepSeek-like: 56 K blocks in stage 1, 2 in stage 2, two 128-wide inter tiles.  Weights are
 drawn and quantised on the GPU (N(0,1)/sqrt(K), 128x128 blocks) and the oracle dequantises
 only the experts the tokens are routed to.  Tolerance as the other MoE parity tests
-(rtol = atol = 2e-2, at most 1 % of elements beyond 1e-2).  Runs only with
-AITER_B200_TEST_UNRUN=1 until these shapes have been run on a B200.
+(rtol = atol = 2e-2, at most 1 % of elements beyond 1e-2).
 """
-import os
-
 import numpy as np
 import pytest
 import torch
@@ -20,9 +17,7 @@ import aiter_b200 as aiter
 from gpu_util import check_no_device_error, requires_cuda
 from oracle import moe
 
-pytestmark = [pytest.mark.gpu, requires_cuda,
-              pytest.mark.skipif(os.environ.get("AITER_B200_TEST_UNRUN") != "1",
-                                 reason="the reference's default test shapes not yet run on a B200")]
+pytestmark = [pytest.mark.gpu, requires_cuda]
 
 _CACHE = {}
 

@@ -3,10 +3,7 @@
 fused_dynamic_mxfp4_quant_moe_sort_hip): bit-exact against the reference's torch
 functions (golden vectors: per_1x32_f4_quant, e8m0_shuffle and the sorted-layout
 reference of op_tests/test_moe_sorting_mxfp4.py) and against the oracle at config-2
-size.  Runs only with AITER_B200_TEST_UNRUN=1 until these kernels have been run on a
-B200."""
-import os
-
+size."""
 import numpy as np
 import pytest
 import torch
@@ -14,9 +11,7 @@ import torch
 from conftest import golden_group
 from gpu_util import check_no_device_error, dev, requires_cuda, to_dev
 
-pytestmark = [pytest.mark.gpu, requires_cuda,
-              pytest.mark.skipif(os.environ.get("AITER_B200_TEST_UNRUN") != "1",
-                                 reason="MXFP4 quant + sort kernels not yet run on a B200")]
+pytestmark = [pytest.mark.gpu, requires_cuda]
 
 CASES = ["s1_t37_d512_e8_k2_b32", "s2_t37_d512_e8_k2_b32", "s1_t300_d1024_e16_k4_b128", "s2_t64_d256_e32_k8_b64"]
 

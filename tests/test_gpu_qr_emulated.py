@@ -1,11 +1,8 @@
 """Single-GPU parity of the quick allreduce kernel: all W ranks emulated in one
 cooperative launch (qr_all_reduce_emulated; CTA row y plays rank y), every rank's
 output bit-exact against the restatement of the reference's QuickReduce
-(oracle/quick_reduce.py) and identical across ranks.  Skipped until the kernel has
-been run on a GPU, unless AITER_B200_TEST_UNRUN=1.
+(oracle/quick_reduce.py) and identical across ranks.
 """
-import os
-
 import numpy as np
 import pytest
 import torch
@@ -13,8 +10,6 @@ import torch
 pytestmark = [
     pytest.mark.gpu,
     pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU"),
-    pytest.mark.skipif(os.environ.get("AITER_B200_TEST_UNRUN") != "1",
-                       reason="quick allreduce not yet run on a GPU"),
 ]
 
 MODES = [(torch.float16, False), (torch.bfloat16, False), (torch.bfloat16, True)]

@@ -1,9 +1,6 @@
 """1 x group fp8 quantisation vs the oracle (`pertoken_quant` over 128 groups,
 aiter/ops/quant.py:42-72): codes and scales bit-exact.  The int8 output (the default
-dtype of the reference's per_group_quant_hip) runs only with AITER_B200_TEST_UNRUN=1
-until it has been run on a B200."""
-import os
-
+dtype of the reference's per_group_quant_hip) is bit-exact as well."""
 import numpy as np
 import pytest
 import torch
@@ -60,7 +57,6 @@ def test_group_quant_transposed_scale_and_num_rows():
     assert np.all(codes(q)[30:] == codecs.fp8_e4m3_encode(np.float32(0.5)))
 
 
-@pytest.mark.skipif(os.environ.get("AITER_B200_TEST_UNRUN") != "1", reason="int8 group quant not yet run on a B200")
 @pytest.mark.parametrize("group", [32, 128])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 def test_group_quant_int8_bit_exact(group, dtype):
