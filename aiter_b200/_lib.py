@@ -122,7 +122,6 @@ SIGNATURES = {
     "scaled_silu_and_mul": [T, T, T],
     "moe_stage1_fp8_blockscale_bias": [T, T, T, T, T, T, T, T, T, I64, I64, I64, OT, I64, T],
     "moe_stage2_fp8_blockscale_bias": [T, T, T, T, T, T, T, OT, T, I64, T],
-    "tmem_ld_probe": [I64, I64, T, T],
 }
 
 _CT = {T: ctypes.POINTER(aiter_tensor_t), OT: ctypes.POINTER(aiter_tensor_t), I64: ctypes.c_int64,
@@ -149,10 +148,6 @@ def lib():
         L.aiter_device_error.argtypes = [ctypes.c_int]
         L.qr_max_size.restype = ctypes.c_int64
         L.qr_max_size.argtypes = []
-        L.tmem_ld_probe_variants.restype = ctypes.c_int
-        L.tmem_ld_probe_variants.argtypes = []
-        L.tmem_ld_probe_info.restype = ctypes.c_int
-        L.tmem_ld_probe_info.argtypes = [ctypes.c_int64, ctypes.POINTER(ctypes.c_int64)]
         c64, vp, p64 = ctypes.c_int64, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64)
         for name, args in (("custom_ar_init", [c64, c64, c64, c64, p64, vp]),
                            ("custom_ar_open_peers", [c64, vp]), ("custom_ar_open_loopback", [c64]),

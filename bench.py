@@ -63,11 +63,10 @@ def parse():
     p.add_argument("--fused-gemm-ar", action="store_true",
                    help="gemm_ar mode: also time the one-kernel GEMM + allreduce (custom_ar_gemm_all_reduce_fused)")
     p.add_argument("--mode", default="moe", choices=["moe", "moe_sweep", "a8w4", "tp_moe", "gemm_ar", "routing",
-                                                     "allreduce", "ep", "tmem_ld"],
-                   help="moe: config 1 at --M (N>1: data-parallel replicas); moe_sweep: config 1 token sweep "
-                        "on one GPU; a8w4: config 2 on one GPU; tp_moe: config 3; gemm_ar: config 4; "
-                        "routing: topk_softmax and moe_sorting alone (achieved HBM GB/s); tmem_ld: TMEM -> register "
-                        "read throughput per SM (the promotion roof; one GPU)")
+                                                     "allreduce", "ep"],
+                   help="moe: config 1 at --M (N>1 under torch.distributed.run: config 3, tensor-parallel); "
+                        "moe_sweep: config 1 token sweep on one GPU; a8w4: config 2 on one GPU; tp_moe: config 3; "
+                        "gemm_ar: config 4; routing: topk_softmax and moe_sorting alone (achieved HBM GB/s)")
     return p.parse_args()
 
 
@@ -1150,52 +1149,6 @@ def run_ep(args, rank, world, local):
             "clocks": clk.summary()}
 
 
-def run_tmem_ld(args, rank, world, local):
-    """TMEM -> register read throughput (tcgen05.ld) of every SM at once, for each load
-    shape / warp count of the probe kernel.  Bytes per SM per launch = iters x lanes read
-    x 4 subpartitions x 512 columns x 4 B; B/clk/SM from the CTAs' own clock64 spans, TB/s
-    from CUDA events.  `tmem_read_TBs` = the best 32-lane shape, the roof of the grouped
-    GEMM's per-K-block promotion (its epilogue reads every accumulator once per 128-K block)."""
-    from aiter_b200 import _lib
-    L = _lib.lib()
-    dev = torch.device("cuda", local)
-    sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    iters = 2000
-    cycles = torch.zeros(sms, dtype=torch.int64, device=dev)
-    sink = torch.zeros(sms * 16 * 32, dtype=torch.float32, device=dev)
-    stream = torch.cuda.current_stream(dev)
-    info = (ctypes.c_int64 * 4)()
-    rows = []
-    with ClockSampler(local) as clk:
-        for v in range(L.tmem_ld_probe_variants()):
-            _lib.check_status("tmem_ld_probe_info", L.tmem_ld_probe_info(v, info))
-            warps, shape, x, lanes = list(info)
-            for it in (10, 10, iters):  # two warm-up launches, then the timed one
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                torch.cuda.synchronize(dev)
-                e0.record(stream)
-                _lib.call("tmem_ld_probe", v, it, cycles, sink, stream=stream.cuda_stream)
-                e1.record(stream)
-                torch.cuda.synchronize(dev)
-            _append_tmem_row(rows, v, warps, shape, x, lanes, iters, sms, e0.elapsed_time(e1), cycles)
-    best = max((r for r in rows if r["lanes"] == 32), key=lambda r: r["TBs"])
-    return {"mode": "tmem_ld", "sms": sms, "iters": iters, "variants": rows, "tmem_read_TBs": best["TBs"],
-            "tmem_read_B_per_clk_per_sm": best["B_per_clk_per_sm"], "best_variant": best["variant"],
-            "clocks": clk.summary(), "gpu_launches": 3 * len(rows)}
-
-
-def _append_tmem_row(rows, v, warps, shape, x, lanes, iters, sms, ms, cycles):
-    cyc = cycles.double().mean().item()
-    bytes_sm = iters * lanes * 4 * 512 * 4
-    rows.append({"variant": v, "warps": warps,
-                 "load": ["32x32b", "32x32b x2 per wait", "16x32bx2", "16x256b x2", "32x32b + 32 FMA",
-                          "32x32b wide"][shape],
-                 "cols_per_load": x, "lanes": lanes, "ms": round(ms, 4),
-                 "B_per_clk_per_sm": round(bytes_sm / cyc, 2),
-                 "TBs": round(bytes_sm * sms / (ms * 1e-3) / 1e12, 2),
-                 "clk_mhz": round(cyc / (ms * 1e3), 0)})
-
-
 def main():
     args = parse()
     if args.impl == "reference":
@@ -1210,10 +1163,10 @@ def main():
     try:
         if args.mode == "moe" and world > 1:
             args.mode = "tp_moe"          # N > 1: the sharded path (config 3)
-        if args.mode in ("tp_moe", "gemm_ar", "moe_sweep", "a8w4", "routing", "allreduce", "ep", "tmem_ld"):
+        if args.mode in ("tp_moe", "gemm_ar", "moe_sweep", "a8w4", "routing", "allreduce", "ep"):
             res = {"tp_moe": run_tp_moe, "gemm_ar": run_gemm_ar, "moe_sweep": run_moe_sweep,
                    "a8w4": run_a8w4, "routing": run_routing, "allreduce": run_allreduce, "ep": run_ep,
-                   "tmem_ld": run_tmem_ld}[args.mode](
+                   }[args.mode](
                 args, rank, world, local)
             if rank == 0:
                 print(json.dumps(res), flush=True)

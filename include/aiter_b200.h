@@ -289,17 +289,6 @@ int gelu_and_mul(aiter_tensor_t* out, aiter_tensor_t* input, void* stream);
 int gelu_tanh_and_mul(aiter_tensor_t* out, aiter_tensor_t* input, void* stream);
 int scaled_silu_and_mul(aiter_tensor_t* out, aiter_tensor_t* input, aiter_tensor_t* scale, void* stream);
 
-/* ---- diagnostic: TMEM read throughput -------------------------------------- */
-/* No reference counterpart.  Measures tcgen05.ld (TMEM -> registers) throughput on every
- * SM, the resource the grouped GEMMs' per-128-K block-scale promotion consumes.
- * tmem_ld_probe_info fills {warps, load shape, columns per load, lanes read} of a variant;
- * tmem_ld_probe launches one CTA per SM reading all 512 TMEM columns `iters` times and
- * writes each CTA's clock64 span to cycles (int64, >= SM count elements); sink (fp32,
- * >= SMs * warps * 32) keeps the values live. */
-int tmem_ld_probe_variants(void);
-int tmem_ld_probe_info(int64_t variant, int64_t* out4);
-int tmem_ld_probe(int64_t variant, int64_t iters, aiter_tensor_t* cycles, aiter_tensor_t* sink, void* stream);
-
 /* ---- bf16 GEMM (the GEMM half of GEMM + allreduce) ------------------------ */
 /* out[M, N] = A[M, K] @ W[N, K]^T, bf16 in / fp32 accumulate / bf16 out, on
  * tcgen05 kind::f16.  Replaces tgemm.mm / gemm_a16w16 (aiter/tuned_gemm.py:224-308,

@@ -97,23 +97,3 @@ def test_allreduce_entries_reject_bad_context_and_world():
     assert b"null allreduce context" in L.aiter_get_last_error()
     assert L.custom_ar_allreduce_rmsnorm(0, *([ctypes.byref(x)] * 5), 1e-6, None, None) != 0
     assert b"null allreduce context" in L.aiter_get_last_error()
-
-
-def test_tmem_probe_table_and_argument_checks():
-    """The TMEM read-throughput diagnostic describes its variants without a GPU and
-    rejects an unknown variant or iteration count before any launch."""
-    L = _lib.lib()
-    n = L.tmem_ld_probe_variants()
-    assert n >= 1
-    info = (ctypes.c_int64 * 4)()
-    for v in range(n):
-        assert L.tmem_ld_probe_info(v, info) == 0
-        warps, shape, x, lanes = list(info)
-        assert warps in (4, 8, 16) and 0 <= shape <= 5 and x in (16, 32, 64) and lanes in (16, 32)
-    assert L.tmem_ld_probe_info(n, info) == -1
-    cyc = torch.zeros(148, dtype=torch.int64)
-    sink = torch.zeros(148 * 512)
-    with pytest.raises(RuntimeError, match="unknown variant"):
-        _lib.call("tmem_ld_probe", n, 10, cyc, sink)
-    with pytest.raises(RuntimeError, match="iters out of range"):
-        _lib.call("tmem_ld_probe", 0, 0, cyc, sink)
