@@ -87,23 +87,47 @@ __device__ __forceinline__ bool half_block(const GemmArgs& a, int m_blk) {
     return a.half_tiles && (a.sorted_ids[m_blk * 128 + 64] & 0xFFFFFF) >= a.M;
 }
 
-// SiLU with the hardware exp2 and an approximate divide: the result is rounded to
-// bf16 right after, which hides their few-ulp fp32 error.
-__device__ __forceinline__ float act_fn(float g, int act) {
-    if (act == AITER_ACT_GELU) return 0.5f * g * (1.0f + erff(g * 0.70710678118654752f));
-    return __fdividef(g, 1.0f + __expf(-g));
+// Activations in the reference's fp32 order with CUDA's accurate expf / erff and
+// IEEE division (the result is rounded to bf16 right after; every last-bit
+// difference from the reference's torch path can move that rounding, and through
+// it the fp8 requant, so the cheaper approximations are not used here):
+// SiLU x / (1 + e^-x), GELU 0.5 x (1 + erf(x / sqrt 2)).  The activation is a template
+// parameter of the kernel, so each instance carries the code of one activation only.
+template <int ACT>
+__device__ __forceinline__ float act_fn(float g) {
+    if constexpr (ACT == AITER_ACT_GELU) return 0.5f * g * (1.0f + erff(g * 0.70710678118654752f));
+    return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
 }
 
 // Gated activation of a (gate, up) pair: act(gate) * up, or Swiglu
 // (aiter/fused_moe.py:1473-1480): min(gate, 7) * sigmoid(1.702 min(gate, 7)) *
-// (clamp(up, -7, 7) + 1).
-__device__ __forceinline__ float act_pair(float g, float u, int act) {
-    if (act == AITER_ACT_SWIGLU) {
+// (clamp(up, -7, 7) + 1), the sigmoid as 1 / (1 + e^-(1.702 g)).
+template <int ACT>
+__device__ __forceinline__ float act_pair(float g, float u) {
+    if constexpr (ACT == AITER_ACT_SWIGLU) {
         g = fminf(g, 7.0f);
         u = fminf(fmaxf(u, -7.0f), 7.0f);
-        return __fdividef(g, 1.0f + __expf(-1.702f * g)) * (u + 1.0f);
+        const float sig = __frcp_rn(__fadd_rn(1.0f, expf(__fmul_rn(-1.702f, g))));
+        return __fmul_rn(__fmul_rn(g, sig), __fadd_rn(u, 1.0f));
+    } else {
+        return __fmul_rn(act_fn<ACT>(g), u);
     }
-    return act_fn(g, act) * u;
+}
+
+// fp8 e4m3 codes (RNE, saturating) of the fp32 quotients RN(x_i / s), i.e. of the
+// reference's `(x / scale).to(fp8)`.  q = x * RN(1/s) is within 2^-23 relative of
+// x / s, so whenever q * (1 - 2^-20) and q * (1 + 2^-20) give the same fp8 codes the
+// exact quotient (and its fp32 rounding) lies between them and has those codes too;
+// only a quotient within 2^-20 of an fp8 rounding boundary takes the IEEE division.
+__device__ __forceinline__ uint32_t fp8x4_quotient(float x0, float x1, float x2, float x3, float s, float rs) {
+    const float lo = 1.0f - 0x1p-20f, hi = 1.0f + 0x1p-20f;
+    const float q0 = x0 * rs, q1 = x1 * rs, q2 = x2 * rs, q3 = x3 * rs;
+    __nv_fp8x4_e4m3 pl(make_float4(q0 * lo, q1 * lo, q2 * lo, q3 * lo));
+    __nv_fp8x4_e4m3 ph(make_float4(q0 * hi, q1 * hi, q2 * hi, q3 * hi));
+    const uint32_t cl = *reinterpret_cast<uint32_t*>(&pl), ch = *reinterpret_cast<uint32_t*>(&ph);
+    if (cl == ch) return cl;
+    __nv_fp8x4_e4m3 pe(make_float4(__fdiv_rn(x0, s), __fdiv_rn(x1, s), __fdiv_rn(x2, s), __fdiv_rn(x3, s)));
+    return *reinterpret_cast<uint32_t*>(&pe);
 }
 
 // The stage-1 intermediate is rounded to the activation dtype (bf16 or fp16) before
@@ -167,7 +191,7 @@ __device__ __forceinline__ void scatter_add8(void* out, int64_t off, const float
 // (cp.async of a_scale[kb][tile rows] and the two w-scales of the tile's column
 // blocks into an SRING-deep smem ring, so the epilogue never waits on a global
 // load), 4..11 epilogue.
-template <int STAGE, int BN_, bool BIAS = false>
+template <int STAGE, int BN_, bool BIAS, int ACT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmO, const GemmArgs args) {
@@ -439,7 +463,7 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                         g += brow[cg];
                         u += brow[args.out_cols + cg];
                     }
-                    const float yb = round_inter(act_pair(g, u, args.act), args.inter_f16);
+                    const float yb = round_inter(act_pair<ACT>(g, u), args.inter_f16);
                     acc[j] = yb;
                     amax = fmaxf(amax, fabsf(yb));
                 }
@@ -451,7 +475,7 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 amax = fmaxf(rb[erow], rb[128 + erow]);
                 float scale = amax / 448.0f;
                 if (scale == 0.f) scale = 1.0f;
-                const float rs = 1.0f / scale;
+                const float rs = __frcp_rn(scale);
                 uint8_t* orow = out_tile + erow * 128;
 #pragma unroll
                 for (int c = 0; c < 2; ++c) {
@@ -459,8 +483,7 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         const int j = 16 * c + 4 * i;
-                        __nv_fp8x4_e4m3 p4(make_float4(acc[j] * rs, acc[j + 1] * rs, acc[j + 2] * rs, acc[j + 3] * rs));
-                        w[i] = *reinterpret_cast<uint32_t*>(&p4);
+                        w[i] = fp8x4_quotient(acc[j], acc[j + 1], acc[j + 2], acc[j + 3], scale, rs);
                     }
                     const int chunk = (4 * h + 2 * hh + c) ^ (erow & 7);
                     *reinterpret_cast<uint4*>(orow + 16 * chunk) = make_uint4(w[0], w[1], w[2], w[3]);
@@ -503,7 +526,7 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                         g += brow[cg];
                         u += brow[args.out_cols + cg];
                     }
-                    const float yb = round_inter(act_pair(g, u, args.act), args.inter_f16);
+                    const float yb = round_inter(act_pair<ACT>(g, u), args.inter_f16);
                     acc[j] = yb;
                     amax = fmaxf(amax, fabsf(yb));
                 }
@@ -517,9 +540,10 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 amax = fmaxf(rb[row], rb[128 + row]);
                 float scale = amax / 448.0f;
                 if (scale == 0.f) scale = 1.0f;
-                const float rs = 1.0f / scale;
+                const float rs = __frcp_rn(scale);
                 // row `row` of the 128x128-byte tile, 128-byte swizzle: 16-byte chunk c
-                // of the row sits at chunk c ^ (row & 7)
+                // of the row sits at chunk c ^ (row & 7).  The codes are those of
+                // x / scale, as the reference's pertoken_quant divides.
                 uint8_t* orow = out_tile + row * 128;
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
@@ -527,8 +551,7 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         const int j = 16 * c + 4 * i;
-                        __nv_fp8x4_e4m3 p4(make_float4(acc[j] * rs, acc[j + 1] * rs, acc[j + 2] * rs, acc[j + 3] * rs));
-                        w[i] = *reinterpret_cast<uint32_t*>(&p4);
+                        w[i] = fp8x4_quotient(acc[j], acc[j + 1], acc[j + 2], acc[j + 3], scale, rs);
                     }
                     const int chunk = (4 * h + c) ^ (row & 7);
                     *reinterpret_cast<uint4*>(orow + 16 * chunk) = make_uint4(w[0], w[1], w[2], w[3]);
@@ -671,12 +694,27 @@ int half_tiles_enabled() {
     return on;
 }
 
-template <int STAGE, int BN_, bool BIAS>
+template <int STAGE, int BN_, bool BIAS, int ACT>
 void launch_k(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO, const GemmArgs& a, int grid,
               int dev, cudaStream_t st) {
     constexpr int smem = Cfg<BN_>::SMEM_BYTES;
-    ab::set_max_smem_once((const void*)moe_gemm_fp8_kernel<STAGE, BN_, BIAS>, smem, dev);
-    moe_gemm_fp8_kernel<STAGE, BN_, BIAS><<<grid, NUM_THREADS, smem, st>>>(tmA, tmB, tmO, a);
+    ab::set_max_smem_once((const void*)moe_gemm_fp8_kernel<STAGE, BN_, BIAS, ACT>, smem, dev);
+    moe_gemm_fp8_kernel<STAGE, BN_, BIAS, ACT><<<grid, NUM_THREADS, smem, st>>>(tmA, tmB, tmO, a);
+}
+
+// Stage 1 instantiates one kernel per activation (the stage-2 kernel has none).
+template <int STAGE, int BN_, bool BIAS>
+void launch_act(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO, const GemmArgs& a, int grid,
+                int dev, cudaStream_t st) {
+    if constexpr (STAGE == 2) {
+        launch_k<STAGE, BN_, BIAS, AITER_ACT_SILU>(tmA, tmB, tmO, a, grid, dev, st);
+    } else if (a.act == AITER_ACT_GELU) {
+        launch_k<STAGE, BN_, BIAS, AITER_ACT_GELU>(tmA, tmB, tmO, a, grid, dev, st);
+    } else if (a.act == AITER_ACT_SWIGLU) {
+        launch_k<STAGE, BN_, BIAS, AITER_ACT_SWIGLU>(tmA, tmB, tmO, a, grid, dev, st);
+    } else {
+        launch_k<STAGE, BN_, BIAS, AITER_ACT_SILU>(tmA, tmB, tmO, a, grid, dev, st);
+    }
 }
 
 template <int STAGE, int BN_>
@@ -688,9 +726,9 @@ void launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& t
     if (tiles == 0) return;
     const int grid = std::min(tiles, ab::num_sms(dev));
     if (a.bias)
-        launch_k<STAGE, BN_, true>(tmA, tmB, tmO, a, grid, dev, st);
+        launch_act<STAGE, BN_, true>(tmA, tmB, tmO, a, grid, dev, st);
     else
-        launch_k<STAGE, BN_, false>(tmA, tmB, tmO, a, grid, dev, st);
+        launch_act<STAGE, BN_, false>(tmA, tmB, tmO, a, grid, dev, st);
     ab::check_launch(STAGE == 1 ? "moe_stage1_fp8_blockscale" : "moe_stage2_fp8_blockscale");
 }
 
@@ -760,10 +798,10 @@ void run_stage1(aiter_tensor_t* a1, aiter_tensor_t* a1_scale, aiter_tensor_t* w1
         a.bias_ld = N;
     }
     DeviceGuard dg(a1->device_id);
-    CUtensorMap tmA, tmB;
+    CUtensorMap tmA, tmB, tmO;
     make_tmap_2d_u8(&tmA, a1->ptr, (uint64_t)c.rows_pad, D, 128, 128, true);
     make_tmap_2d_u8(&tmB, w1->ptr, (uint64_t)E * N, D, 128, 128, true);
-    CUtensorMap tmO;  // output tiles: 128 sorted rows x 128 fp8 columns
+    // output tiles: 128 sorted rows x 128 fp8 columns
     make_tmap_2d_u8(&tmO, out->ptr, (uint64_t)c.rows_pad, I, 128, 128, true);
     launch<1, 256>(tmA, tmB, tmO, a, a1->device_id, as_stream(stream));
 }

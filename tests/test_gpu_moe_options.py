@@ -3,8 +3,7 @@ Swiglu (aiter/fused_moe.py:1473-1480), doweight_stage1 (top-k weight on the stag
 GEMM output, none in stage 2), fp16 activations / output and the experts' biases
 (w1_bias / w2_bias), each against the reference's own torch pipeline (golden vectors,
 config-0 shape) and against the oracle at a larger shape; fused_moe passes the biases
-only on the per_1x32 Swiglu path, as the reference's dispatch does.  Runs only with
-AITER_B200_TEST_UNRUN=1 until these variants have been run on a B200."""
+only on the per_1x32 Swiglu path, as the reference's dispatch does."""
 import os
 
 import numpy as np
@@ -16,9 +15,7 @@ from conftest import golden_group
 from gpu_util import check_no_device_error, fp8_from_codes, requires_cuda, to_dev
 from oracle import inputs, moe
 
-pytestmark = [pytest.mark.gpu, requires_cuda,
-              pytest.mark.skipif(os.environ.get("AITER_B200_TEST_UNRUN") != "1",
-                                 reason="Swiglu / doweight_stage1 / fp16 variants not yet run on a B200")]
+pytestmark = [pytest.mark.gpu, requires_cuda]
 
 OPTS = {"swiglu": (21, dict(activation="swiglu")), "doweight": (22, dict(doweight_stage1=True)),
         "fp16": (23, dict(dtype="fp16"))}

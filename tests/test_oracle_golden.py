@@ -320,3 +320,28 @@ def test_torch_port_of_reference_cpu_path_matches_reference(golden, tag, shape):
         fp8(c["w2_q"]), torch.from_numpy(c["w2_s"]), torch.from_numpy(g["topk_weights"]),
         torch.from_numpy(g["topk_ids"]))
     assert np.array_equal(out.float().numpy(), g["out"])
+
+
+def test_fp8_requant_fast_path_equals_division():
+    """The stage-1 epilogue quantises x / scale through q = x * RN(1/scale) and takes the
+    IEEE division only when q * (1 -/+ 2^-20) straddle an fp8 rounding boundary.  Restated
+    here in fp32 numpy: wherever the two bracket codes agree they equal the codes of
+    RN(x / scale), on random groups and on quotients placed exactly on fp8 midpoints."""
+    rng = np.random.default_rng(3)
+    f = np.float32
+    enc = lambda v: codecs.fp8_e4m3_encode(np.clip(v, -448.0, 448.0).astype(f))
+    for trial in range(4):
+        x = (rng.standard_normal((4000, 128)) * rng.uniform(0.01, 50)).astype(f)
+        amax = np.abs(x).max(axis=1, keepdims=True)
+        s = (amax / f(448.0)).astype(f)
+        if trial == 3:   # quotients on exact fp8 midpoints (ties) and their neighbours
+            mids = ((codecs.FP8_E4M3_VALUES[1:126] + codecs.FP8_E4M3_VALUES[2:127]) / 2).astype(f)
+            x[:, :64] = (rng.choice(mids, (4000, 64)) * s).astype(f)
+        rs = (f(1.0) / s).astype(f)
+        q = (x * rs).astype(f)
+        cl = enc((q * f(1.0 - 2.0 ** -20)).astype(f))
+        ch = enc((q * f(1.0 + 2.0 ** -20)).astype(f))
+        exact = enc((x / s).astype(f))
+        fast = cl == ch
+        assert np.array_equal(cl[fast], exact[fast])
+        assert fast.mean() > (0.4 if trial == 3 else 0.999)
