@@ -87,16 +87,17 @@ __device__ __forceinline__ bool half_block(const GemmArgs& a, int m_blk) {
     return a.half_tiles && (a.sorted_ids[m_blk * 128 + 64] & 0xFFFFFF) >= a.M;
 }
 
-// Activations in the reference's fp32 order with CUDA's accurate expf / erff and
-// IEEE division (the result is rounded to bf16 right after; every last-bit
-// difference from the reference's torch path can move that rounding, and through
-// it the fp8 requant, so the cheaper approximations are not used here):
-// SiLU x / (1 + e^-x), GELU 0.5 x (1 + erf(x / sqrt 2)).  The activation is a template
-// parameter of the kernel, so each instance carries the code of one activation only.
+// Activations in the reference's fp32 order (SiLU x / (1 + e^-x), GELU 0.5 x (1 +
+// erf(x / sqrt 2)), Swiglu below) with CUDA's accurate expf / erff and a division
+// within 2 ulps (__fdividef): the result is rounded to bf16 right after, and a
+// last-bit difference from the reference moves that rounding only within a few fp32
+// ulps of a bf16 rounding boundary.  The activation is a template parameter of the
+// kernel, so each instance carries the code of one activation only (the unrolled
+// tile epilogue is otherwise large enough to thrash the instruction cache).
 template <int ACT>
 __device__ __forceinline__ float act_fn(float g) {
     if constexpr (ACT == AITER_ACT_GELU) return 0.5f * g * (1.0f + erff(g * 0.70710678118654752f));
-    return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+    return __fdividef(g, 1.0f + expf(-g));
 }
 
 // Gated activation of a (gate, up) pair: act(gate) * up, or Swiglu
@@ -107,25 +108,31 @@ __device__ __forceinline__ float act_pair(float g, float u) {
     if constexpr (ACT == AITER_ACT_SWIGLU) {
         g = fminf(g, 7.0f);
         u = fminf(fmaxf(u, -7.0f), 7.0f);
-        const float sig = __frcp_rn(__fadd_rn(1.0f, expf(__fmul_rn(-1.702f, g))));
-        return __fmul_rn(__fmul_rn(g, sig), __fadd_rn(u, 1.0f));
+        const float sig = __fdividef(1.0f, 1.0f + expf(-1.702f * g));
+        return g * sig * (u + 1.0f);
     } else {
-        return __fmul_rn(act_fn<ACT>(g), u);
+        return act_fn<ACT>(g) * u;
     }
 }
 
 // fp8 e4m3 codes (RNE, saturating) of the fp32 quotients RN(x_i / s), i.e. of the
-// reference's `(x / scale).to(fp8)`.  q = x * RN(1/s) is within 2^-23 relative of
-// x / s, so whenever q * (1 - 2^-20) and q * (1 + 2^-20) give the same fp8 codes the
-// exact quotient (and its fp32 rounding) lies between them and has those codes too;
-// only a quotient within 2^-20 of an fp8 rounding boundary takes the IEEE division.
-__device__ __forceinline__ uint32_t fp8x4_quotient(float x0, float x1, float x2, float x3, float s, float rs) {
+// reference's `(x / scale).to(fp8)`, in two steps.  fp8x4_bracket: q = x * RN(1/s) is
+// within 2^-23 relative of x / s, so when q * (1 - 2^-20) and q * (1 + 2^-20) give the
+// same fp8 codes, the exact quotient (and its fp32 rounding) lies between them and has
+// those codes too; otherwise `exact` is raised and the caller recomputes its codes
+// with fp8x4_ieee (IEEE division), which only a quotient within 2^-20 of an fp8
+// rounding boundary needs.
+__device__ __forceinline__ uint32_t fp8x4_bracket(float x0, float x1, float x2, float x3, float rs, bool& exact) {
     const float lo = 1.0f - 0x1p-20f, hi = 1.0f + 0x1p-20f;
     const float q0 = x0 * rs, q1 = x1 * rs, q2 = x2 * rs, q3 = x3 * rs;
     __nv_fp8x4_e4m3 pl(make_float4(q0 * lo, q1 * lo, q2 * lo, q3 * lo));
     __nv_fp8x4_e4m3 ph(make_float4(q0 * hi, q1 * hi, q2 * hi, q3 * hi));
     const uint32_t cl = *reinterpret_cast<uint32_t*>(&pl), ch = *reinterpret_cast<uint32_t*>(&ph);
-    if (cl == ch) return cl;
+    exact |= cl != ch;
+    return cl;
+}
+
+__device__ __forceinline__ uint32_t fp8x4_ieee(float x0, float x1, float x2, float x3, float s) {
     __nv_fp8x4_e4m3 pe(make_float4(__fdiv_rn(x0, s), __fdiv_rn(x1, s), __fdiv_rn(x2, s), __fdiv_rn(x3, s)));
     return *reinterpret_cast<uint32_t*>(&pe);
 }
@@ -477,16 +484,21 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 if (scale == 0.f) scale = 1.0f;
                 const float rs = __frcp_rn(scale);
                 uint8_t* orow = out_tile + erow * 128;
+                uint32_t w[8];
+                bool exact = false;
+#pragma unroll
+                for (int g = 0; g < 8; ++g)
+                    w[g] = fp8x4_bracket(acc[4 * g], acc[4 * g + 1], acc[4 * g + 2], acc[4 * g + 3], rs, exact);
+                if (exact) {
+#pragma unroll
+                    for (int g = 0; g < 8; ++g)
+                        w[g] = fp8x4_ieee(acc[4 * g], acc[4 * g + 1], acc[4 * g + 2], acc[4 * g + 3], scale);
+                }
 #pragma unroll
                 for (int c = 0; c < 2; ++c) {
-                    uint32_t w[4];
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int j = 16 * c + 4 * i;
-                        w[i] = fp8x4_quotient(acc[j], acc[j + 1], acc[j + 2], acc[j + 3], scale, rs);
-                    }
                     const int chunk = (4 * h + 2 * hh + c) ^ (erow & 7);
-                    *reinterpret_cast<uint4*>(orow + 16 * chunk) = make_uint4(w[0], w[1], w[2], w[3]);
+                    *reinterpret_cast<uint4*>(orow + 16 * chunk) =
+                        make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
                 }
                 if (h == 0 && hh == 0) args.out_scale[(int64_t)n_blk * args.rows_pad + srow] = scale;
                 fence_proxy_async_smem();
@@ -545,16 +557,21 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 // of the row sits at chunk c ^ (row & 7).  The codes are those of
                 // x / scale, as the reference's pertoken_quant divides.
                 uint8_t* orow = out_tile + row * 128;
+                uint32_t w[16];
+                bool exact = false;
+#pragma unroll
+                for (int g = 0; g < 16; ++g)
+                    w[g] = fp8x4_bracket(acc[4 * g], acc[4 * g + 1], acc[4 * g + 2], acc[4 * g + 3], rs, exact);
+                if (exact) {
+#pragma unroll
+                    for (int g = 0; g < 16; ++g)
+                        w[g] = fp8x4_ieee(acc[4 * g], acc[4 * g + 1], acc[4 * g + 2], acc[4 * g + 3], scale);
+                }
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
-                    uint32_t w[4];
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int j = 16 * c + 4 * i;
-                        w[i] = fp8x4_quotient(acc[j], acc[j + 1], acc[j + 2], acc[j + 3], scale, rs);
-                    }
                     const int chunk = (4 * h + c) ^ (row & 7);
-                    *reinterpret_cast<uint4*>(orow + 16 * chunk) = make_uint4(w[0], w[1], w[2], w[3]);
+                    *reinterpret_cast<uint4*>(orow + 16 * chunk) =
+                        make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
                 }
                 if (h == 0) args.out_scale[(int64_t)n_blk * args.rows_pad + srow] = scale;
                 fence_proxy_async_smem();

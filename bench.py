@@ -168,6 +168,17 @@ def peaks():
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
+def fp8_peak():
+    """Dense FP8 TFLOP/s denominator: cuBLAS FP8 GEMM measured on this pool's B200s
+    (profiles/fp8_gemm_peak_cublas.json), else 2 x the measured bf16 burst."""
+    pk, src = peaks()
+    try:
+        v = json.load(open(os.path.join(ROOT, "profiles", "fp8_gemm_peak_cublas.json")))["fp8_tflops"]
+        return float(v), "cuBLAS FP8 GEMM measured on a B200 of this pool (profiles/fp8_gemm_peak_cublas.json)"
+    except Exception:
+        return 2.0 * pk["bf16_tflops"], f"2 x bf16_tflops of MEASURED_PEAKS.json ({src}); fp8 dense = 2 x bf16 assumed"
+
+
 def tmem_peak_from_profile():
     """Measured TMEM -> register read throughput of a B200 (TB/s over all SMs) from the
     committed probe summary, or None when it has not been measured."""
@@ -339,8 +350,7 @@ def run_b200(args, rank, world, local):
     else:
         e2e_ms = max_over_ranks(pip_ms, world)
 
-    pk, src = peaks()
-    fp8_peak_tflops = 2.0 * pk["bf16_tflops"]
+    fp8_peak_tflops, fp8_src = fp8_peak()
     s1_flops = 4.0 * M * TOPK * D * I
     s1_ms = mean_ms["stage1_gemm"]
     achieved = s1_flops / (s1_ms * 1e-3) / 1e12
@@ -372,7 +382,7 @@ def run_b200(args, rank, world, local):
         "roofline": {"bound": "tensor", "kernel": "moe_stage1_fp8_blockscale (tcgen05 kind::f8f6f4)",
                      "achieved": round(achieved, 1), "peak": round(fp8_peak_tflops, 1), "unit": "TFLOP/s",
                      "frac": round(achieved / fp8_peak_tflops, 4),
-                     "peak_source": f"2 x bf16_tflops of MEASURED_PEAKS.json ({src}); fp8 dense runs at 2x bf16",
+                     "peak_source": fp8_src,
                      "traffic": traffic,
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch from "
                                        "profiles/moe_stage1_fp8_cfg1_traffic.json (a committed capture of this "
@@ -709,8 +719,7 @@ def run_tp_moe(args, rank, world, local):
         torch.distributed.all_reduce(o, group=tp.device_group)
 
     ms_nccl = _time_loop(nccl, K, args.warmup, world)
-    pk, src = peaks()
-    fp8_peak = 2.0 * pk["bf16_tflops"]
+    peak_fp8, fp8_src = fp8_peak()
     s1_flops = 4.0 * M * TOPK * D * ilp
     achieved = s1_flops / (kernel_ms_max["stage1_gemm"] * 1e-3) / 1e12
     n_bytes = M * D * 2
@@ -725,10 +734,9 @@ def run_tp_moe(args, rank, world, local):
            "kernel_ms": {k: round(v, 4) for k, v in kernel_ms_max.items()},
            "allreduce_share": round(kernel_ms_max["allreduce"] / (ms / K), 4),
            "roofline": {"bound": "tensor", "kernel": "moe_stage1_fp8_blockscale on the rank's shard",
-                        "achieved": round(achieved, 1), "peak": round(fp8_peak, 1), "unit": "TFLOP/s",
-                        "frac": round(achieved / fp8_peak, 4),
-                        "peak_source": f"2 x bf16_tflops of MEASURED_PEAKS.json ({src}); fp8 dense = 2 x bf16 "
-                                       f"(assumed, not measured)",
+                        "achieved": round(achieved, 1), "peak": round(peak_fp8, 1), "unit": "TFLOP/s",
+                        "frac": round(achieved / peak_fp8, 4),
+                        "peak_source": fp8_src,
                         "traffic": None,
                         "allreduce": {"bound": "nvlink", "bytes": n_bytes, "bus_GBs": round(bus, 1),
                                       "peak": 770.0, "unit": "GB/s", "frac": round(bus / 770.0, 4),
@@ -764,7 +772,7 @@ def run_moe_sweep(args, rank, world, local):
     output zeroing; FLOPs 6 M k D I."""
     from aiter_b200 import moe_op, dtypes
     pk, src = peaks()
-    fp8_peak = 2.0 * pk["bf16_tflops"]
+    peak_fp8, _ = fp8_peak()
     rows = []
     x = make_inputs(16384, seed=1234, E=E)
     B = 128
@@ -818,14 +826,14 @@ def run_moe_sweep(args, rank, world, local):
         gbs = bytes_ / (ms * 1e-3) / 1e9
         rows.append({"M": M, "ms_per_step": round(ms, 4), "ms_per_step_eager": round(ms_eager, 4),
                      "tokens_per_s": round(M / (ms * 1e-3), 1), "tflops": round(tfl, 2), "active_experts": active,
-                     "tensor_frac": round(tfl / fp8_peak, 4), "hbm_GBs": round(gbs, 1),
+                     "tensor_frac": round(tfl / peak_fp8, 4), "hbm_GBs": round(gbs, 1),
                      "hbm_frac": round(gbs / pk["hbm_gbs"], 4),
-                     "bound": "hbm" if gbs / pk["hbm_gbs"] > tfl / fp8_peak else "tensor",
+                     "bound": "hbm" if gbs / pk["hbm_gbs"] > tfl / peak_fp8 else "tensor",
                      "kernel_ms_eager": kernel_ms})
     return {"metric": METRIC, "mode": "moe_sweep", "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
             "warmup": args.warmup, "higher_is_better": True, "dtype": "fp8-e4m3", "data": "synthetic",
             "config": {"workload": "BASELINE config 1 token sweep", "hidden": D, "inter": I, "experts": E,
-                       "topk": TOPK}, "peaks": {"fp8_tflops": fp8_peak, "hbm_gbs": pk["hbm_gbs"], "source": src},
+                       "topk": TOPK}, "peaks": {"fp8_tflops": peak_fp8, "hbm_gbs": pk["hbm_gbs"], "source": src},
             "sweep": rows}
 
 
@@ -865,7 +873,7 @@ def run_a8w4(args, rank, world, local):
     prep_ms = t0.elapsed_time(t1)
     torch.cuda.empty_cache()
     pk, src = peaks()
-    fp8_peak = 2.0 * pk["bf16_tflops"]
+    peak_fp8, _ = fp8_peak()
     perm = torch.randperm(Ee, generator=torch.Generator().manual_seed(7)) + 1
     bias = torch.log((1.0 / perm.double() ** 1.1) / (1.0 / perm.double() ** 1.1).sum()).float().to(dev)
     rows = []
@@ -908,7 +916,7 @@ def run_a8w4(args, rank, world, local):
         tfl = fl / (ms * 1e-3) / 1e12
         gbs = bytes_ / (ms * 1e-3) / 1e9
         rows.append({"M": M, "ms_per_step": round(ms, 4), "tokens_per_s": round(M / (ms * 1e-3), 1),
-                     "tflops": round(tfl, 2), "active_experts": active, "tensor_frac": round(tfl / fp8_peak, 4),
+                     "tflops": round(tfl, 2), "active_experts": active, "tensor_frac": round(tfl / peak_fp8, 4),
                      "hbm_GBs_algorithmic": round(gbs, 1), "hbm_frac": round(gbs / pk["hbm_gbs"], 4)})
     return {"metric": METRIC.replace("E=128", "E=256").replace("inter 1536", "inter 2048").replace(
                 "FP8 blockscale", "A8W4: fp8 activations, MXFP4 weights"),
@@ -917,7 +925,7 @@ def run_a8w4(args, rank, world, local):
             "data": "synthetic", "config": {"workload": "BASELINE config 2: A8W4 fused MoE", "hidden": De,
                                             "inter": Ie, "experts": Ee, "topk": TOPK, "routing": "zipf s=1.1 bias"},
             "weight_prep_ms": round(prep_ms, 2),
-            "peaks": {"fp8_tflops": fp8_peak, "hbm_gbs": pk["hbm_gbs"], "source": src}, "sweep": rows}
+            "peaks": {"fp8_tflops": peak_fp8, "hbm_gbs": pk["hbm_gbs"], "source": src}, "sweep": rows}
 
 
 def run_routing(args, rank, world, local):
@@ -1031,7 +1039,7 @@ def run_gemm_ar(args, rank, world, local):
 def run_allreduce(args, rank, world, local):
     """Allreduce sweep: the IPC custom allreduce, the quick allreduce at each level
     (FP, FP8, INT6, INT4; cast_bf2half for bf16, the reference's default) and NCCL,
-    for bf16 and fp16 messages of 256 KB .. 256 MB per rank.  Latency per call, max
+    for bf16 and fp16 messages of 64 KB .. 256 MB per rank.  Latency per call, max
     over ranks, and bus bandwidth 2 (W-1)/W * bytes / t (NCCL's convention)."""
     import aiter_b200 as aiter
     from aiter_b200.dist import parallel_state as ps
@@ -1048,7 +1056,7 @@ def run_allreduce(args, rank, world, local):
         aiter.qr_open_handles(qr, handles)
     rows = []
     for dtype in (torch.bfloat16, torch.float16):
-        for nbytes in (256 << 10, 1 << 20, 4 << 20, 16 << 20, 64 << 20, top):
+        for nbytes in (64 << 10, 256 << 10, 1 << 20, 2 << 20, 4 << 20, 8 << 20, 16 << 20, 32 << 20, 64 << 20, top):
             x = torch.randn(nbytes // 2, device=dev, generator=torch.Generator(device=dev).manual_seed(rank)
                             ).to(dtype)
             y = torch.empty_like(x)
@@ -1070,7 +1078,7 @@ def run_allreduce(args, rank, world, local):
     ps.destroy_model_parallel()
     return {"metric": "allreduce latency sweep", "mode": "allreduce", "unit": "us", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": False, "data": "synthetic N(0,1)",
-            "config": {"workload": "allreduce of 256 KB .. 256 MB per rank", "parallelism": f"tp{world}"},
+            "config": {"workload": "allreduce of 64 KB .. 256 MB per rank", "parallelism": f"tp{world}"},
             "qr_device_error": err, "sweep": rows}
 
 
