@@ -221,9 +221,14 @@ def _fused_moe_impl(hidden_states, w1, w2, topk_weight, topk_ids, expert_mask=No
             raise TypeError("per_1x128 needs fp8 weights")
         meta = get_2stage_cfgs(get_padded_M(M), model_dim, inter_dim, E, topk, dtype, dtypes.fp8,
                                w1.dtype, quant_type, True, activation, doweight_stage1)
-        block_m = meta.block_m if not block_size_M else int(block_size_M)
-        if block_m != GEMM_BLOCK_M:
-            raise NotImplementedError(f"block_size_M={block_m}: the grouped GEMM tiles {GEMM_BLOCK_M} rows")
+        # block_size_M picks the tile height of the reference's kernels (16 / 32 / 64 / 128,
+        # aiter/fused_moe.py:514-529); the result does not depend on it.  The tcgen05
+        # grouped GEMM here always tiles 128 sorted rows (blocks whose rows 64.. are all
+        # padding can run as M=64 tiles), so any of those values is accepted and mapped
+        # to GEMM_BLOCK_M.
+        if block_size_M and int(block_size_M) not in (16, 32, 64, 128):
+            raise ValueError(f"block_size_M must be one of 16, 32, 64, 128, got {block_size_M}")
+        block_m = GEMM_BLOCK_M
         sorted_ids, sorted_weights, sorted_expert_ids, num_valid_ids, moe_buf, pos = _moe_sorting_ext(
             topk_ids, topk_weight, global_E, model_dim, dtype, block_m, expert_mask, num_local_tokens,
             moe_sorting_dispatch_policy, with_pos=True, moe_buf=moe_buf)

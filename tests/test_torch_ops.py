@@ -86,6 +86,10 @@ def test_fused_moe_rejects_what_the_b200_path_does_not_run():
         fused_moe(x, w1, w2, tw, ti, quant_type=QuantType.per_Token)
     with pytest.raises(NotImplementedError, match="activation"):
         fused_moe(x, w1, w2, tw, ti, quant_type=QuantType.per_1x128, activation=ActivationType.No)
+    # block_size_M takes the reference's tile heights (16 / 32 / 64 / 128, mapped to the
+    # 128-row tcgen05 tile); other values raise before any launch
+    with pytest.raises(ValueError, match="block_size_M must be"):
+        fused_moe(x, w1, w2, tw, ti, quant_type=QuantType.per_1x128, block_size_M=48)
 
 
 
