@@ -31,10 +31,10 @@ def tensor_model_parallel_gather(input_: torch.Tensor, dst: int = 0, dim: int = 
     return get_tp_group().gather(input_, dst, dim)
 
 
-def tensor_model_parallel_gemm_all_reduce(a: torch.Tensor, w: torch.Tensor, fused: bool = False) -> torch.Tensor:
+def tensor_model_parallel_gemm_all_reduce(a: torch.Tensor, w: torch.Tensor, fused: bool = None) -> torch.Tensor:
     """allreduce(a @ w^T) over the TP group, GEMM and allreduce sharing the IPC
     staging buffer (`fused=True`: one kernel, the GEMM pushing its tiles to the
-    peers).  Equals tensor_model_parallel_all_reduce(tgemm.mm(a, w)); the reference
+    peers; None: the one-kernel form for small M, the two-kernel form above).  Equals tensor_model_parallel_all_reduce(tgemm.mm(a, w)); the reference
     has no fused entry, this one is new."""
     return get_tp_group().gemm_all_reduce(a, w, fused=fused)
 

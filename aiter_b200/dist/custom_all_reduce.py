@@ -233,12 +233,20 @@ class CustomAllreduce:
             return None
         return self.all_reduce(input, open_fp8_quant=open_fp8_quant)
 
+    # Largest M at which the one-kernel form is the default: on two B200s it beat the
+    # two-kernel form at M <= 64, tied at 512 and lost at 2048 and above (bench.py
+    # --mode gemm_ar --fused-gemm-ar).
+    FUSED_MAX_M = 256
+
     def gemm_all_reduce(self, a: torch.Tensor, w: torch.Tensor, out: torch.Tensor = None, two_shot=None,
-                        fused: bool = False):
-        """allreduce(a @ w^T).  Default: the GEMM writes into the staging buffer and
-        the allreduce kernel reduces it (two launches, no copy).  `fused=True`: one
-        kernel whose GEMM epilogue pushes its tiles to the peers over NVLink while the
-        MMAs of the next tiles run, then sums them (same result bits)."""
+                        fused: bool = None):
+        """allreduce(a @ w^T).  Two forms with the same result bits: the two-kernel form
+        (the GEMM writes into the staging buffer and the allreduce kernel reduces it, no
+        copy) and the one-kernel form (`fused=True`: the GEMM epilogue pushes its tiles
+        to the peers over NVLink while the MMAs of the next tiles run, then sums them).
+        `fused=None` takes the one-kernel form up to FUSED_MAX_M rows."""
+        if fused is None:
+            fused = a.shape[0] <= self.FUSED_MAX_M
         if out is None:
             out = torch.empty((a.shape[0], w.shape[0]), dtype=torch.bfloat16, device=a.device)
         force = -1 if two_shot is None else (1 if two_shot else 0)

@@ -226,7 +226,7 @@ class GroupCoordinator:
                 return r
         return _rmsnorm_after(self.all_reduce(input_), residual_inp_, weight_, eps, quant=True)
 
-    def gemm_all_reduce(self, a: torch.Tensor, w: torch.Tensor, fused: bool = False) -> torch.Tensor:
+    def gemm_all_reduce(self, a: torch.Tensor, w: torch.Tensor, fused: bool = None) -> torch.Tensor:
         if self.world_size == 1:
             from ..gemm import gemm_a16w16
             return gemm_a16w16(a, w)

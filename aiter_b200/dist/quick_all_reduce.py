@@ -44,6 +44,10 @@ class QuickReduceRegime(Enum):
 
 # (world size, level) -> smallest message in bytes at which the quick allreduce beat the
 # custom IPC allreduce on B200; measured with bench.py --mode allreduce (fp16 kernels).
+# World size 2: no level won at any size from 64 KB to 256 MB (the custom allreduce ran
+# at 0.46-0.53 of the 770 GB/s peer bandwidth; quantising and decoding cost more than the
+# NVLink bytes they save), so no world-2 entry.  World sizes 4 and 8: not measured yet,
+# no entry.
 B200_MIN_BYTES = {}
 
 

@@ -61,7 +61,7 @@ def parse():
     p.add_argument("--E", type=int, default=128, help="experts (profiling cases use fewer)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--fused-gemm-ar", action="store_true",
-                   help="gemm_ar mode: also time the one-kernel GEMM + allreduce (custom_ar_gemm_all_reduce_fused)")
+                   help="gemm_ar mode: also time the one-kernel and the two-kernel GEMM + allreduce forms alone")
     p.add_argument("--mode", default="moe", choices=["moe", "moe_sweep", "a8w4", "tp_moe", "gemm_ar", "routing",
                                                      "allreduce", "ep"],
                    help="moe: config 1 at --M (N>1 under torch.distributed.run: config 3, tensor-parallel); "
@@ -341,7 +341,11 @@ def run_b200(args, rank, world, local):
     # result out inside the timed region.  Falls back to the serial loop's time if the
     # pipelined loop fails for any reason.
     e2e_mode = "pipelined: H2D of step i+1 and D2H of step i-1 on their own streams overlap step i"
-    pip_ms, pip_err = _e2e_pipelined(aiter, x, h_hidden, h_tw, h_tid, ref_out, K, args.warmup, world)
+    def call(hidden, tw, tid):
+        return aiter.fused_moe(hidden, x["w1q"], x["w2q"], tw, tid, quant_type=aiter.QuantType.per_1x128,
+                               activation=aiter.ActivationType.Silu, w1_scale=x["w1s"], w2_scale=x["w2s"])
+
+    pip_ms, pip_err = _e2e_pipelined(call, x, h_hidden, h_tw, h_tid, ref_out, K, args.warmup, world)
     # every rank takes the same collective steps whether or not its loop failed
     if max_over_ranks(0.0 if pip_err is None else 1.0, world) > 0:
         e2e_ms = e2e_serial_ms
@@ -401,11 +405,12 @@ def run_b200(args, rank, world, local):
     return res, x
 
 
-def _e2e_pipelined(aiter, x, h_hidden, h_tw, h_tid, ref_out, K, W, world):
-    """ms of K fused_moe calls from pinned host buffers with double-buffered device
-    inputs: step i's H2D (copy stream) overlaps step i-1's compute and step i-2's
-    D2H (second copy stream).  Events order each buffer's reuse; the last step's
-    output is checked against the device-resident result."""
+def _e2e_pipelined(call, x, h_hidden, h_tw, h_tid, ref_out, K, W, world):
+    """ms of K calls `call(hidden, topk_weights, topk_ids) -> output` from pinned host
+    buffers with double-buffered device inputs: step i's H2D (copy stream) overlaps
+    step i-1's compute and step i-2's D2H (second copy stream).  Events order each
+    buffer's reuse; the last step's output is checked against the device-resident
+    result."""
     dev = x["hidden"].device
     cmp = torch.cuda.current_stream()
     s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
@@ -430,9 +435,7 @@ def _e2e_pipelined(aiter, x, h_hidden, h_tw, h_tid, ref_out, K, W, world):
             cmp.wait_event(done_in[b])
             if used[b]:
                 cmp.wait_event(done_out[b])           # h_out[b] of step i-2 has been read out
-            o = aiter.fused_moe(d_in[b][0], x["w1q"], x["w2q"], d_in[b][1], d_in[b][2],
-                                quant_type=aiter.QuantType.per_1x128, activation=aiter.ActivationType.Silu,
-                                w1_scale=x["w1s"], w2_scale=x["w2s"])
+            o = call(*d_in[b])
             done_cmp[b].record(cmp)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(done_cmp[b])
@@ -709,10 +712,22 @@ def run_tp_moe(args, rank, world, local):
         o = tensor_model_parallel_fused_moe(d_hidden, l1, l2, d_tw, d_tid, **kw)
         h_out.copy_(o, non_blocking=True)
 
-    e2e_ms = _time_loop(e2e_step, K, args.warmup, world) * K
-    same = bool(torch.equal(h_out.to(dev), ref))
+    e2e_serial_ms = _time_loop(e2e_step, K, args.warmup, world) * K
+    # stage 2 scatter-adds in bf16 atomics (no fixed order): equal within bf16 rounding
+    ref_f = ref.float()
+    close = bool(torch.allclose(h_out.to(dev).float(), ref_f, atol=2e-2, rtol=2e-2))
+    max_diff = float((h_out.to(dev).float() - ref_f).abs().max())
     h2d = h_hidden.numel() * 2 + h_tw.numel() * 4 + h_tid.numel() * 4
     d2h = h_out.numel() * 2
+    e2e_mode = "pipelined: H2D of step i+1 and D2H of step i-1 on their own streams overlap step i, every rank"
+    pip_ms, pip_err = _e2e_pipelined(lambda h, tw, tid: tensor_model_parallel_fused_moe(h, l1, l2, tw, tid, **kw),
+                                     x, h_hidden, h_tw, h_tid, ref_f, K, args.warmup, world)
+    if max_over_ranks(0.0 if pip_err is None else 1.0, world) > 0:
+        e2e_ms = e2e_serial_ms
+        why = f"{type(pip_err).__name__}: {pip_err}" if pip_err is not None else "on another rank"
+        e2e_mode = f"serial (pipelined loop failed: {why})"[:300]
+    else:
+        e2e_ms = max_over_ranks(pip_ms, world)
 
     def nccl():
         o = aiter.fused_moe(x["hidden"], l1, l2, x["tw"], x["tid"], **kw)
@@ -746,7 +761,8 @@ def run_tp_moe(args, rank, world, local):
            "gpu_launches": launches_per_step * K,
            "e2e": {"value": round(M * K / (e2e_ms * 1e-3), 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                    "d2h_bytes_per_step": d2h, "api": "aiter_b200.dist.tensor_model_parallel_fused_moe",
-                   "copies": "serial: H2D, call, D2H on one stream, every rank", "matches_device_run": same},
+                   "copies": e2e_mode, "serial_value": round(M * K / (e2e_serial_ms * 1e-3), 1),
+                   "matches_device_run": close, "max_abs_diff_vs_device_run": max_diff},
            "nccl_allreduce_arm": {"ms_per_step": round(ms_nccl, 4), "value": round(M / (ms_nccl * 1e-3), 1)},
            "device_error": bool(err),
            "clocks": clk.summary()}
@@ -1009,9 +1025,11 @@ def run_gemm_ar(args, rank, world, local):
         us = 1e3 * _time_loop(ours, args.steps, args.warmup, world)
         us_b = 1e3 * _time_loop(base, args.steps, args.warmup, world)
         fused = {}
-        if args.fused_gemm_ar:
+        if args.fused_gemm_ar:  # both forms explicitly (ours_us is the default choice between them)
             us_f = 1e3 * _time_loop(lambda: tp.gemm_all_reduce(A, W, fused=True), args.steps, args.warmup, world)
-            fused = {"ours_fused_us": round(us_f, 2), "fused_speedup_vs_cublas_nccl": round(us_b / us_f, 3)}
+            us_2 = 1e3 * _time_loop(lambda: tp.gemm_all_reduce(A, W, fused=False), args.steps, args.warmup, world)
+            fused = {"ours_fused_us": round(us_f, 2), "ours_two_kernel_us": round(us_2, 2),
+                     "fused_speedup_vs_cublas_nccl": round(us_b / us_f, 3)}
         # the two halves alone, to show which one sets each total
         from aiter_b200.gemm import gemm_a16w16
         y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
@@ -1157,15 +1175,29 @@ def run_ep(args, rank, world, local):
             "clocks": clk.summary()}
 
 
+def _claim_stdout():
+    """Sends everything the process and its libraries write to stdout (NCCL's version
+    banner among it) to stderr, and returns a writer for the one JSON line on the
+    original stdout."""
+    sys.stdout.flush()
+    fd = os.dup(1)
+    os.dup2(2, 1)
+
+    def emit(res):
+        os.write(fd, (json.dumps(res) + "\n").encode())
+    return emit
+
+
 def main():
     args = parse()
+    emit = _claim_stdout()
     if args.impl == "reference":
         # the CPU arm touches no GPU and loads none of this repository's kernels
         rank = int(os.environ.get("RANK", "0"))
         world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
         res = run_reference(args, rank, world)
         if res is not None:
-            print(json.dumps(res), flush=True)
+            emit(res)
         return
     rank, world, local = dist_setup(args.gpus)
     try:
@@ -1177,7 +1209,7 @@ def main():
                    }[args.mode](
                 args, rank, world, local)
             if rank == 0:
-                print(json.dumps(res), flush=True)
+                emit(res)
             return
         res, x = run_b200(args, rank, world, local)
         del x
@@ -1185,7 +1217,7 @@ def main():
         if rank == 0 and not args.no_cpu_baseline:
             res["cpu_baseline"] = cpu_baseline(args.M)
         if rank == 0:
-            print(json.dumps(res), flush=True)
+            emit(res)
     finally:
         if world > 1 and torch.distributed.is_initialized():
             torch.distributed.destroy_process_group()

@@ -1,7 +1,6 @@
 """Multi-GPU EP dispatch / combine (EpDispatchCombineOp), one process per GPU, the
 flow of the reference's test (op_tests/multigpu_tests/test_dispatch_combine.py:
-76-171, 202-260).  Skipped with fewer than 2 GPUs, and until the kernels have been
-run on a multi-GPU box, unless AITER_B200_TEST_UNRUN=1.
+76-171, 202-260).  Skipped with fewer than 2 GPUs.
 
 * fp8 tokens with 1x128 scales: every rank's received arrays bit-exact against
   oracle/ep.py; combine of a deterministic expert stand-in bit-exact;
@@ -25,8 +24,6 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 pytestmark = [
     pytest.mark.gpu,
     pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs"),
-    pytest.mark.skipif(os.environ.get("AITER_B200_TEST_UNRUN") != "1",
-                       reason="EP dispatch / combine not yet run on a multi-GPU box"),
 ]
 
 T, D, I, E, K = 96, 1024, 512, 32, 4

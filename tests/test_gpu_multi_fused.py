@@ -1,6 +1,5 @@
 """Multi-GPU parity of the one-kernel GEMM + allreduce (custom_ar_gemm_all_reduce_fused),
-one process per GPU.  Skipped with fewer than 2 GPUs, and until the fused kernels
-have been run on a multi-GPU box, unless AITER_B200_TEST_UNRUN=1.
+one process per GPU.  Skipped with fewer than 2 GPUs.
 
 The fused kernel pushes the same bf16 partial products the two-kernel path stages
 and sums them in the same rank order, so it must return the two-kernel path's bits:
@@ -24,8 +23,6 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 pytestmark = [
     pytest.mark.gpu,
     pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs"),
-    pytest.mark.skipif(os.environ.get("AITER_B200_TEST_UNRUN") != "1",
-                       reason="fused GEMM + allreduce kernels not yet run on a multi-GPU box"),
 ]
 
 

@@ -1,6 +1,5 @@
 """Multi-GPU parity of the quick allreduce (qr_all_reduce), one process per GPU.
-Skipped with fewer than 2 GPUs, and until the kernel has been run on a multi-GPU box,
-unless AITER_B200_TEST_UNRUN=1.
+Skipped with fewer than 2 GPUs.
 
 * every level (FP, FP8, INT6, INT4) for fp16, bf16 and bf16 with cast_bf2half: each
   rank's output bit-exact against the restatement of the reference's QuickReduce
@@ -11,7 +10,8 @@ unless AITER_B200_TEST_UNRUN=1.
 * graph capture: a captured call replayed with fresh inputs, interleaved with eager
   calls of another size;
 * the communicator front-end: GroupCoordinator.all_reduce takes the quick allreduce
-  when AITER_QUICK_REDUCE_QUANTIZATION names a regime.
+  when AITER_QUICK_REDUCE_QUANTIZATION names a regime and the B200 crossover table
+  holds an entry for the world size at or below the message, else the custom one.
 """
 import os
 import sys
@@ -27,8 +27,6 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 pytestmark = [
     pytest.mark.gpu,
     pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs"),
-    pytest.mark.skipif(os.environ.get("AITER_B200_TEST_UNRUN") != "1",
-                       reason="quick allreduce not yet run on a multi-GPU box"),
 ]
 
 MODES = [(torch.float16, False), (torch.bfloat16, False), (torch.bfloat16, True)]
@@ -122,12 +120,28 @@ def _worker(rank, world, port):
         assert np.array_equal(static_out.float().cpu().numpy(), _want(xs, 2, torch.bfloat16, False)), rep
         assert np.array_equal(e_out.float().cpu().numpy(), _want(ys, 1, torch.float16, False)), rep
     del g
-    # front-end: fp16 message above the INT4 minimum for this world size takes the quick allreduce
+    # front-end: with no crossover entry for this world size the message stays on the
+    # custom allreduce (fp32 rank-order sum rounded once); with one, an fp16 message
+    # above it takes the quick allreduce
+    from aiter_b200.dist import quick_all_reduce as qmod
     n = (8 * 1024 * 1024) // 2
     xs = _inputs(n, world, 77, torch.float16)
-    y = tp.all_reduce(xs[rank].to(dev))
-    torch.cuda.synchronize()
-    assert np.array_equal(y.float().cpu().numpy(), _want(xs, 3, torch.float16, True))
+    saved = dict(qmod.B200_MIN_BYTES)
+    try:
+        qmod.B200_MIN_BYTES.pop((world, "INT4"), None)
+        y = tp.all_reduce(xs[rank].to(dev))
+        torch.cuda.synchronize()
+        exact = torch.zeros(n, dtype=torch.float32)
+        for t in xs:
+            exact += t.float()
+        assert torch.equal(y.cpu(), exact.to(torch.float16))
+        qmod.B200_MIN_BYTES[(world, "INT4")] = 1024 * 1024
+        y = tp.all_reduce(xs[rank].to(dev))
+        torch.cuda.synchronize()
+        assert np.array_equal(y.float().cpu().numpy(), _want(xs, 3, torch.float16, True))
+    finally:
+        qmod.B200_MIN_BYTES.clear()
+        qmod.B200_MIN_BYTES.update(saved)
     ps.destroy_model_parallel()
     dist.destroy_process_group()
 
