@@ -122,6 +122,9 @@ SIGNATURES = {
     "scaled_silu_and_mul": [T, T, T],
     "moe_stage1_fp8_blockscale_bias": [T, T, T, T, T, T, T, T, T, I64, I64, I64, OT, I64, T],
     "moe_stage2_fp8_blockscale_bias": [T, T, T, T, T, T, T, OT, T, I64, T],
+    "moe_stage1_a8w4": [T, T, T, T, T, T, T, T, T, I64, I64, I64, OT, I64, OT],
+    "moe_stage2_a8w4": [T, T, T, T, T, T, T, OT, T, I64, OT],
+    "mxfp4_moe_weight_scale_chunks": [T, T],
 }
 
 _CT = {T: ctypes.POINTER(aiter_tensor_t), OT: ctypes.POINTER(aiter_tensor_t), I64: ctypes.c_int64,

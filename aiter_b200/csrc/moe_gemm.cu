@@ -40,24 +40,42 @@ constexpr int SRING_FLOATS = 132;   // 128 row scales + 2 column-block scales, p
 // is split into 512/BN accumulator slabs: the MMA writes one slab per 128-wide K
 // block while the epilogue promotes the previous ones.  The smem ring takes what
 // the operand tiles leave of 192 KB.
-template <int BN_>
+//
+// W4 (MXFP4 weights, kind::mxf8f6f4.block_scale): the weights' e8m0 scales live in
+// TMEM next to the accumulators, so a tile's 256 columns are two N=128 MMAs, each
+// into its own 128-column slab of a 3-deep ring (columns 0-383); columns 384-387
+// hold the unit A scales and 392.. one 8-column buffer of B scales per smem stage
+// (a buffer is rewritten only after the MMAs of its previous K block completed,
+// which the stage's "empty" barrier already guarantees).  A smem stage carries the
+// A box, the two B boxes (unpacked by the TMA to one byte per e2m1 value) and the
+// two 512-byte scale chunks of the B boxes.
+template <int BN_, bool W4 = false>
 struct Cfg {
-    static constexpr int SLABS = TMEM_COLS / BN_;
+    static_assert(!W4 || BN_ == 256, "W4 tiles are 2 x 128 columns");
+    static constexpr int SLAB_COLS = W4 ? 128 : BN_;
+    static constexpr int SLABS = W4 ? 3 : TMEM_COLS / BN_;
     static constexpr int B_TILE = BN_ * BK;
-    static constexpr int STAGE_BYTES = A_TILE + B_TILE;
-    static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
+    static constexpr int SF_BYTES = W4 ? 2 * 512 : 0;
+    static constexpr int STAGE_BYTES = A_TILE + B_TILE + SF_BYTES;
+    static constexpr int STAGES = (W4 ? 200 * 1024 : 192 * 1024) / STAGE_BYTES;
+    // bytes the TMA and bulk copies deliver per stage (packed e2m1: half a byte per value)
+    static constexpr uint32_t TX_BYTES = W4 ? A_TILE + B_TILE / 2 + SF_BYTES : STAGE_BYTES;
     static constexpr int CPT = BN_ / 2;  // accumulator columns per epilogue thread
-    static constexpr uint32_t IDESC = sm100::idesc_e4m3_f32(BM, BN_);
+    static constexpr uint32_t IDESC = W4 ? sm100::idesc_e4m3_e2m1_ue8m0(BM, 128) : sm100::idesc_e4m3_f32(BM, BN_);
     static constexpr uint32_t IDESC64 = sm100::idesc_e4m3_f32(64, BN_);  // half tiles
+    static constexpr uint32_t SFA_COL = 384, SFB_COL = 392;              // W4 scale columns
     static constexpr int BAR_BYTES = 512;
     static constexpr int RED_BYTES = 2 * 256 * 4;                 // stage-1 row amax exchange
     static constexpr int SRING_BYTES = SRING * SRING_FLOATS * 4;  // block-scale ring
     static constexpr int OUT_BYTES = BM * 128;                    // stage-1 fp8 output tile
-    static constexpr int SMEM_BYTES =
-        1024 /*align slack*/ + STAGES * STAGE_BYTES + OUT_BYTES + BAR_BYTES + RED_BYTES + SRING_BYTES;
+    static constexpr int ONES_BYTES = W4 ? 512 : 0;               // W4: chunk of unit A scales
+    static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + OUT_BYTES + BAR_BYTES +
+                                      RED_BYTES + SRING_BYTES + ONES_BYTES;
     static_assert(CPT % 64 == 0, "epilogue works in 64-column chunks");
     static_assert(2 * (STAGES + SLABS + SRING) * 8 + 2 * 8 + 8 <= BAR_BYTES, "barrier area");
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
+    static_assert(!W4 || (SLABS * SLAB_COLS <= (int)SFA_COL && SFB_COL + 8 * STAGES <= (uint32_t)TMEM_COLS),
+                  "TMEM map");
 };
 
 struct GemmArgs {
@@ -66,6 +84,7 @@ struct GemmArgs {
     const int* num_valid;
     const float* a_scale;   // [num_kb][rows_pad], sorted rows
     const float* b_scale;   // [E, N/128, num_kb]
+    const uint8_t* b_sf;    // W4: e8m0 scale chunks [E, N/128, num_kb, 512]
     const float* sorted_w;  // stage 2
     void* out;              // stage 1: fp8 [rows_pad, I] sorted; stage 2: bf16 [M, D]
     float* out_scale;       // stage 1: [I/128][rows_pad]
@@ -198,12 +217,12 @@ __device__ __forceinline__ void scatter_add8(void* out, int64_t off, const float
 // (cp.async of a_scale[kb][tile rows] and the two w-scales of the tile's column
 // blocks into an SRING-deep smem ring, so the epilogue never waits on a global
 // load), 4..11 epilogue.
-template <int STAGE, int BN_, bool BIAS, int ACT>
+template <int STAGE, int BN_, bool BIAS, int ACT, bool W4>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmO, const GemmArgs args) {
     using namespace sm100;
-    using C = Cfg<BN_>;
+    using C = Cfg<BN_, W4>;
     static_assert(STAGE == 2 || BN_ == 256, "stage 1 pairs 128 gate with 128 up columns");
     constexpr int STAGES = C::STAGES, SLABS = C::SLABS, CPT = C::CPT, STAGE_BYTES = C::STAGE_BYTES;
     extern __shared__ uint8_t smem_raw[];
@@ -220,6 +239,7 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     float* red = reinterpret_cast<float*>(out_tile + C::OUT_BYTES + C::BAR_BYTES);
     float* sring = red + 2 * 256;
+    uint8_t* ones = reinterpret_cast<uint8_t*>(sring + SRING * SRING_FLOATS);  // W4 only
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -229,7 +249,8 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         }
         for (int s = 0; s < SLABS; ++s) {
             mbar_init(&tfull[s], 1);
-            mbar_init(&tempty[s], 8);
+            // W4 stage 2: each 128-column slab is read by one epilogue warpgroup
+            mbar_init(&tempty[s], W4 && STAGE == 2 ? 4 : 8);
         }
         for (int s = 0; s < SRING; ++s) {
             mbar_init(&sfull[s], 32);  // one cp.async arrival per prefetcher lane
@@ -268,7 +289,7 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 ok = __all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1, abort_flag));
                 if (!ok) break;
                 if (lane == 0) {
-                    mbar_expect_tx(&full[s], STAGE_BYTES);
+                    mbar_expect_tx(&full[s], C::TX_BYTES);
                     uint8_t* a = smem + s * STAGE_BYTES;
                     uint8_t* b = a + A_TILE;
                     tma_load_2d(a, &tmA, &full[s], kb * BK, m_blk * BM);
@@ -279,6 +300,14 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
 #pragma unroll
                         for (int j = 0; j < BN_ / 128; ++j)
                             tma_load_2d(b + j * 128 * BK, &tmB, &full[s], kb * BK, e * args.N + n_blk * BN_ + j * 128);
+                    }
+                    if constexpr (W4) {
+                        // the e8m0 scale chunks of the two 128-row B boxes for this K block
+                        const int nb0 = STAGE == 1 ? n_blk : 2 * n_blk;
+                        const int nb1 = STAGE == 1 ? nblk128 / 2 + n_blk : 2 * n_blk + 1;
+                        const uint8_t* sf = args.b_sf + ((int64_t)e * nblk128 * args.num_kb + kb) * 512;
+                        bulk_load(b + C::B_TILE, sf + (int64_t)nb0 * args.num_kb * 512, 512, &full[s]);
+                        bulk_load(b + C::B_TILE + 512, sf + (int64_t)nb1 * args.num_kb * 512, 512, &full[s]);
                     }
                 }
                 __syncwarp();
@@ -293,7 +322,54 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
+        if constexpr (W4) {
+            // unit A scales (e8m0 127 = 2^0) for every row: one 512-byte chunk copied
+            // into TMEM once; the A operand's fp32 1x128 scales are promoted in the
+            // epilogue as in the FP8 kernel
+            reinterpret_cast<uint4*>(ones)[lane] = make_uint4(0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) tmem_cp_32x128b_x4(tmem_base + C::SFA_COL, smem_desc_noswz(ones, 128));
+        }
+        if (lane == 0 && W4) {
+            // two N=128 MMAs per K block (gate / up, or the tile's column halves), each
+            // into the next slab of the ring; the B scales of the K block are copied to
+            // TMEM first (tcgen05.cp -> tcgen05.mma is ordered in issue order) into the
+            // buffer of the smem stage: its last readers, the MMAs of K block it -
+            // STAGES, completed before the producer could refill the stage
+            int it = 0, j = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+                for (int kb = 0; kb < args.num_kb && ok; ++kb, ++it) {
+                    const int s = it % STAGES;
+                    if (!mbar_wait(&full[s], (it / STAGES) & 1, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint8_t* a = smem + s * STAGE_BYTES;
+                    const uint64_t adesc = smem_desc_sw128(a);
+                    const uint32_t sfb = tmem_base + C::SFB_COL + 8 * s;
+                    tmem_cp_32x128b_x4(sfb, smem_desc_noswz(a + A_TILE + C::B_TILE, 128));
+                    tmem_cp_32x128b_x4(sfb + 4, smem_desc_noswz(a + A_TILE + C::B_TILE + 512, 128));
+                    for (int c = 0; c < 2; ++c, ++j) {
+                        const int as = j % SLABS;
+                        if (!mbar_wait(&tempty[as], ((j / SLABS) & 1) ^ 1, abort_flag)) { ok = false; break; }
+                        tc_fence_after();
+                        const uint64_t bdesc = smem_desc_sw128(a + A_TILE + c * 128 * BK);
+                        const uint32_t d = tmem_base + as * C::SLAB_COLS;
+#pragma unroll
+                        for (int kk = 0; kk < BK / 32; ++kk)
+                            mma_mxf8f6f4_bs(d, adesc + 2 * kk, bdesc + 2 * kk, C::IDESC | (kk << 4) | (kk << 29),
+                                            (tmem_base + C::SFA_COL) | ((uint32_t)kk << 30),
+                                            (sfb + 4 * c) | ((uint32_t)kk << 30), kk > 0 ? 1u : 0u);
+                        mma_commit(&tfull[as]);
+                    }
+                    mma_commit(&empty[s]);
+                }
+            }
+            if (j > 0) {
+                const int jl = j - 1;
+                mbar_wait(&tfull[jl % SLABS], (jl / SLABS) & 1, abort_flag, 200000000ull, false);
+            }
+        } else if (lane == 0) {
             int it = 0, acc_it = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
@@ -334,9 +410,10 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
             const int m_blk = tile / args.n_tiles, n_blk = tile % args.n_tiles;
             const int e = min(max(args.sorted_eids[m_blk], 0), args.E - 1);
-            const float* sbA;
-            const float* sbB;
-            if (STAGE == 1) {
+            const float* sbA = nullptr;
+            const float* sbB = nullptr;
+            if (W4) {
+            } else if (STAGE == 1) {
                 sbA = args.b_scale + ((int64_t)e * nblk128 + n_blk) * args.num_kb;
                 sbB = args.b_scale + ((int64_t)e * nblk128 + (nblk128 >> 1) + n_blk) * args.num_kb;
             } else {
@@ -352,7 +429,7 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 const float* src = sa + (int64_t)kb * args.rows_pad;
 #pragma unroll
                 for (int j = 0; j < 4; ++j) cp_async4(dst + lane + 32 * j, src + 32 * j);
-                if (lane == 0) {
+                if (lane == 0 && !W4) {  // W4: the weight scales are applied by the MMA
                     cp_async4(dst + 128, sbA + kb);
                     cp_async4(dst + 129, sbB + kb);
                 }
@@ -373,7 +450,7 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             const int m_blk = tile / args.n_tiles, n_blk = tile % args.n_tiles;
             // half tile: this thread holds row 16q + lane%16 and the column half lane/16
             // of its warp's columns (16x32bx2 loads); full tile: row 32q + lane
-            const bool half = half_block(args, m_blk);
+            const bool half = !W4 && half_block(args, m_blk);
             const int hh = lane >> 4;
             const int erow = half ? q * 16 + (lane & 15) : row;
             const int srow = m_blk * BM + erow;
@@ -392,8 +469,43 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 const float sa = se[erow], sbA = se[128], sbB = se[129];
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&sempty[si]);
-                const float s0 = sa * (STAGE == 2 && h * CPT >= 128 ? sbB : sbA);
-                const float s1 = sa * sbB;
+                const float s0 = W4 ? sa : sa * (STAGE == 2 && h * CPT >= 128 ? sbB : sbA);
+                const float s1 = W4 ? sa : sa * sbB;
+                if constexpr (W4) {
+                    // stage 1: gate columns 64h.. of slab 2i, up columns 64h.. of slab
+                    // 2i+1; stage 2: columns 0..127 of slab 2i+h
+#pragma unroll
+                    for (int ch = 0; ch < 2; ++ch) {
+                        const int jj = 2 * acc_it + (STAGE == 1 ? ch : h);
+                        const int as = jj % SLABS;
+                        if (STAGE == 1 || ch == 0) {
+                            if (!__all_sync(0xffffffffu, mbar_wait(&tfull[as], (jj / SLABS) & 1, abort_flag))) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                        }
+                        const uint32_t t = lane_base + as * C::SLAB_COLS + (STAGE == 1 ? 64 * h : 64 * ch);
+                        tmem_ld32(t, *reinterpret_cast<float(*)[32]>(&v[0]));
+                        tmem_ld32(t + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
+                        tmem_wait_ld();
+                        if (STAGE == 1 || ch == 1) {
+                            tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(&tempty[as]);
+                        }
+                        if (kb == 0) {
+#pragma unroll
+                            for (int q2 = 0; q2 < 64; ++q2) acc[64 * ch + q2] = v[q2] * sa;
+                        } else {
+                            const uint64_t sc2 = splat2(sa);
+#pragma unroll
+                            for (int q2 = 0; q2 < 64; q2 += 2) fma2(&acc[64 * ch + q2], &v[q2], sc2);
+                        }
+                    }
+                    if (!ok) break;
+                    continue;
+                }
                 const int as = acc_it % SLABS;
                 const uint32_t aph = (acc_it / SLABS) & 1;
                 if (!__all_sync(0xffffffffu, mbar_wait(&tfull[as], aph, abort_flag))) { ok = false; break; }
@@ -661,6 +773,21 @@ void make_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t
     next = (next + 1) % kEntries;
     e = Entry{base, rows, cols, box_cols, box_rows, swizzle128, true, *map};
 }
+
+void make_tmap_2d_e2m1(CUtensorMap* map, const void* base, uint64_t rows, uint64_t k, uint32_t box_rows) {
+    // 16U4_ALIGN16B: every 16 packed values (8 bytes) land in 16 bytes of shared
+    // memory, so a 128-value box row fills one 128-byte swizzle row like an fp8 row.
+    AB_CHECK(((uintptr_t)base & 31) == 0, "e2m1 TMA base address must be 32-byte aligned");
+    AB_CHECK(k % 128 == 0, "e2m1 K must be a multiple of 128");
+    cuuint64_t dims[2] = {k, rows};
+    cuuint64_t strides[1] = {k / 2};
+    cuuint32_t box[2] = {128, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = get_encode()(map, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 2, const_cast<void*>(base), dims, strides,
+                              box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) fail("cuTensorMapEncodeTiled (e2m1) failed with code ", (int)r);
+}
 }  // namespace ab
 
 namespace {
@@ -711,42 +838,60 @@ int half_tiles_enabled() {
     return on;
 }
 
-template <int STAGE, int BN_, bool BIAS, int ACT>
+template <int STAGE, int BN_, bool BIAS, int ACT, bool W4>
 void launch_k(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO, const GemmArgs& a, int grid,
               int dev, cudaStream_t st) {
-    constexpr int smem = Cfg<BN_>::SMEM_BYTES;
-    ab::set_max_smem_once((const void*)moe_gemm_fp8_kernel<STAGE, BN_, BIAS, ACT>, smem, dev);
-    moe_gemm_fp8_kernel<STAGE, BN_, BIAS, ACT><<<grid, NUM_THREADS, smem, st>>>(tmA, tmB, tmO, a);
+    constexpr int smem = Cfg<BN_, W4>::SMEM_BYTES;
+    ab::set_max_smem_once((const void*)moe_gemm_fp8_kernel<STAGE, BN_, BIAS, ACT, W4>, smem, dev);
+    moe_gemm_fp8_kernel<STAGE, BN_, BIAS, ACT, W4><<<grid, NUM_THREADS, smem, st>>>(tmA, tmB, tmO, a);
 }
 
 // Stage 1 instantiates one kernel per activation (the stage-2 kernel has none).
-template <int STAGE, int BN_, bool BIAS>
+template <int STAGE, int BN_, bool BIAS, bool W4>
 void launch_act(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO, const GemmArgs& a, int grid,
                 int dev, cudaStream_t st) {
     if constexpr (STAGE == 2) {
-        launch_k<STAGE, BN_, BIAS, AITER_ACT_SILU>(tmA, tmB, tmO, a, grid, dev, st);
+        launch_k<STAGE, BN_, BIAS, AITER_ACT_SILU, W4>(tmA, tmB, tmO, a, grid, dev, st);
     } else if (a.act == AITER_ACT_GELU) {
-        launch_k<STAGE, BN_, BIAS, AITER_ACT_GELU>(tmA, tmB, tmO, a, grid, dev, st);
+        launch_k<STAGE, BN_, BIAS, AITER_ACT_GELU, W4>(tmA, tmB, tmO, a, grid, dev, st);
     } else if (a.act == AITER_ACT_SWIGLU) {
-        launch_k<STAGE, BN_, BIAS, AITER_ACT_SWIGLU>(tmA, tmB, tmO, a, grid, dev, st);
+        launch_k<STAGE, BN_, BIAS, AITER_ACT_SWIGLU, W4>(tmA, tmB, tmO, a, grid, dev, st);
     } else {
-        launch_k<STAGE, BN_, BIAS, AITER_ACT_SILU>(tmA, tmB, tmO, a, grid, dev, st);
+        launch_k<STAGE, BN_, BIAS, AITER_ACT_SILU, W4>(tmA, tmB, tmO, a, grid, dev, st);
     }
 }
 
-template <int STAGE, int BN_>
+template <int STAGE, int BN_, bool W4>
 void launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO, GemmArgs a, int dev,
             cudaStream_t st) {
-    a.half_tiles = half_tiles_enabled();
+    a.half_tiles = W4 ? 0 : half_tiles_enabled();
     a.n_tiles = STAGE == 1 ? a.n_tiles : a.N / BN_;
     const int tiles = a.max_m_blocks * a.n_tiles;
     if (tiles == 0) return;
     const int grid = std::min(tiles, ab::num_sms(dev));
     if (a.bias)
-        launch_act<STAGE, BN_, true>(tmA, tmB, tmO, a, grid, dev, st);
+        launch_act<STAGE, BN_, true, W4>(tmA, tmB, tmO, a, grid, dev, st);
     else
-        launch_act<STAGE, BN_, false>(tmA, tmB, tmO, a, grid, dev, st);
-    ab::check_launch(STAGE == 1 ? "moe_stage1_fp8_blockscale" : "moe_stage2_fp8_blockscale");
+        launch_act<STAGE, BN_, false, W4>(tmA, tmB, tmO, a, grid, dev, st);
+    ab::check_launch(W4 ? (STAGE == 1 ? "moe_stage1_a8w4" : "moe_stage2_a8w4")
+                        : (STAGE == 1 ? "moe_stage1_fp8_blockscale" : "moe_stage2_fp8_blockscale"));
+}
+
+// MXFP4 weights [E, N, K/2] (e2m1 pairs) with their e8m0 scales arranged in chunks
+// [E, N/128, K/128, 512] (mxfp4_moe_weight_scale_chunks).
+void check_w4(aiter_tensor_t* w, aiter_tensor_t* sf, int E, int N, int K, const char* wn, const char* sn) {
+    using namespace ab;
+    AB_CHECK(w->dtype_ == AITER_DTYPE_fp4x2 || w->dtype_ == AITER_DTYPE_u8 || w->dtype_ == AITER_DTYPE_i8, wn,
+             " must be fp4x2 (MXFP4, or its uint8 view)");
+    AB_CHECK(sf->dtype_ == AITER_DTYPE_fp8_e8m0 || sf->dtype_ == AITER_DTYPE_u8, sn,
+             " must be e8m0 scale chunks (or their uint8 view)");
+    need_contig(w, wn);
+    need_contig(sf, sn);
+    AB_CHECK(w->ndim == 3 && w->shape[0] == E && w->shape[1] == N && w->shape[2] * 2 == K, wn, " must be [E, ", N,
+             ", ", K / 2, "] packed e2m1");
+    AB_CHECK((int64_t)sf->numel_ == (int64_t)E * (N / 128) * (K / 128) * 512, sn,
+             " must hold the scale chunks [E, N/128, K/128, 512] (mxfp4_moe_weight_scale_chunks)");
+    AB_CHECK(((uintptr_t)w->ptr & 31) == 0 && ((uintptr_t)sf->ptr & 15) == 0, wn, " / ", sn, " misaligned");
 }
 
 }  // namespace
@@ -759,28 +904,33 @@ void run_stage1(aiter_tensor_t* a1, aiter_tensor_t* a1_scale, aiter_tensor_t* w1
                 aiter_tensor_t* sorted_token_ids, aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids,
                 aiter_tensor_t* out, aiter_tensor_t* out_scale, int64_t num_tokens, int64_t block_m,
                 int64_t activation, aiter_tensor_t* sorted_weights, int64_t inter_dtype, aiter_tensor_t* bias,
-                void* stream) {
+                void* stream, bool w4 = false) {
     using namespace ab;
     Sorted c = check_sorting(sorted_token_ids, sorted_expert_ids, num_valid_ids, block_m);
     check_sorted_operand(a1, a1_scale, c.rows_pad, "a1", "a1_scale");
     need(w1, "w1");
     need(w1_scale, "w1_scale");
-    need_dtype(w1, AITER_DTYPE_fp8, "w1");
-    need_dtype(w1_scale, AITER_DTYPE_fp32, "w1_scale");
-    need_contig(w1, "w1");
-    need_contig(w1_scale, "w1_scale");
     need_ndim(w1, 3, "w1");
     AB_CHECK(activation == AITER_ACT_SILU || activation == AITER_ACT_GELU || activation == AITER_ACT_SWIGLU,
              "activation must be Silu, Gelu or Swiglu");
     AB_CHECK(inter_dtype == AITER_DTYPE_bf16 || inter_dtype == AITER_DTYPE_fp16, "inter_dtype must be bf16 or fp16");
     const int D = (int)a1->shape[1];
     const int E = (int)w1->shape[0], N = (int)w1->shape[1];
-    AB_CHECK(w1->shape[2] == D, "w1 K dim must equal the activation width");
     AB_CHECK(N % 256 == 0, "2 * inter_dim must be a multiple of 256");
+    if (w4) {
+        check_w4(w1, w1_scale, E, N, D, "w1", "w1_scale");
+    } else {
+        need_dtype(w1, AITER_DTYPE_fp8, "w1");
+        need_dtype(w1_scale, AITER_DTYPE_fp32, "w1_scale");
+        need_contig(w1, "w1");
+        need_contig(w1_scale, "w1_scale");
+        AB_CHECK(w1->shape[2] == D, "w1 K dim must equal the activation width");
+        AB_CHECK((int64_t)w1_scale->numel_ == (int64_t)E * (N / 128) * (D / 128),
+                 "w1_scale must be [E, 2I/128, D/128]");
+    }
     const int I = N / 2;
     check_sorted_operand(out, out_scale, c.rows_pad, "out", "out_scale");
     AB_CHECK(out->shape[1] == I, "out must be [rows, inter_dim]");
-    AB_CHECK((int64_t)w1_scale->numel_ == (int64_t)E * (N / 128) * (D / 128), "w1_scale must be [E, 2I/128, D/128]");
     AB_CHECK(num_tokens >= 0 && num_tokens < (1 << 24), "bad num_tokens");
     if (num_tokens == 0) return;
     GemmArgs a{};
@@ -788,7 +938,10 @@ void run_stage1(aiter_tensor_t* a1, aiter_tensor_t* a1_scale, aiter_tensor_t* w1
     a.sorted_eids = (const int*)sorted_expert_ids->ptr;
     a.num_valid = (const int*)num_valid_ids->ptr;
     a.a_scale = (const float*)a1_scale->ptr;
-    a.b_scale = (const float*)w1_scale->ptr;
+    if (w4)
+        a.b_sf = (const uint8_t*)w1_scale->ptr;
+    else
+        a.b_scale = (const float*)w1_scale->ptr;
     a.out = out->ptr;
     a.out_scale = (float*)out_scale->ptr;
     a.M = (int)num_tokens;
@@ -817,10 +970,16 @@ void run_stage1(aiter_tensor_t* a1, aiter_tensor_t* a1_scale, aiter_tensor_t* w1
     DeviceGuard dg(a1->device_id);
     CUtensorMap tmA, tmB, tmO;
     make_tmap_2d_u8(&tmA, a1->ptr, (uint64_t)c.rows_pad, D, 128, 128, true);
-    make_tmap_2d_u8(&tmB, w1->ptr, (uint64_t)E * N, D, 128, 128, true);
+    if (w4)
+        make_tmap_2d_e2m1(&tmB, w1->ptr, (uint64_t)E * N, D, 128);
+    else
+        make_tmap_2d_u8(&tmB, w1->ptr, (uint64_t)E * N, D, 128, 128, true);
     // output tiles: 128 sorted rows x 128 fp8 columns
     make_tmap_2d_u8(&tmO, out->ptr, (uint64_t)c.rows_pad, I, 128, 128, true);
-    launch<1, 256>(tmA, tmB, tmO, a, a1->device_id, as_stream(stream));
+    if (w4)
+        launch<1, 256, true>(tmA, tmB, tmO, a, a1->device_id, as_stream(stream));
+    else
+        launch<1, 256, false>(tmA, tmB, tmO, a, a1->device_id, as_stream(stream));
 }
 }  // namespace
 
@@ -863,28 +1022,34 @@ namespace {
 void run_stage2(aiter_tensor_t* a2, aiter_tensor_t* a2_scale, aiter_tensor_t* w2, aiter_tensor_t* w2_scale,
                 aiter_tensor_t* sorted_token_ids, aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids,
                 aiter_tensor_t* sorted_weights, aiter_tensor_t* out, int64_t block_m, aiter_tensor_t* bias,
-                void* stream) {
+                void* stream, bool w4 = false) {
     using namespace ab;
     Sorted c = check_sorting(sorted_token_ids, sorted_expert_ids, num_valid_ids, block_m);
     check_sorted_operand(a2, a2_scale, c.rows_pad, "a2", "a2_scale");
     need(w2, "w2");
     need(w2_scale, "w2_scale");
     need(out, "out");
-    need_dtype(w2, AITER_DTYPE_fp8, "w2");
-    need_dtype(w2_scale, AITER_DTYPE_fp32, "w2_scale");
     AB_CHECK(out->dtype_ == AITER_DTYPE_bf16 || out->dtype_ == AITER_DTYPE_fp16, "out must be bf16 or fp16");
     if (sorted_weights) need_dtype(sorted_weights, AITER_DTYPE_fp32, "sorted_weights");
-    for (auto* t : {w2, w2_scale, out}) need_contig(t, "operand");
+    need_contig(out, "out");
     need_ndim(w2, 3, "w2");
     need_ndim(out, 2, "out");
     AB_CHECK(!sorted_weights || (int64_t)sorted_weights->numel_ >= c.rows_pad, "sorted_weights too small");
     const int I = (int)a2->shape[1];
     const int E = (int)w2->shape[0], D = (int)w2->shape[1];
     const int M = (int)out->shape[0];
-    AB_CHECK(w2->shape[2] == I, "w2 must be [E, D, I]");
     AB_CHECK(out->shape[1] == D, "out must be [M, D]");
     AB_CHECK(D % 256 == 0, "model_dim must be a multiple of 256");
-    AB_CHECK((int64_t)w2_scale->numel_ == (int64_t)E * (D / 128) * (I / 128), "w2_scale must be [E, D/128, I/128]");
+    if (w4) {
+        check_w4(w2, w2_scale, E, D, I, "w2", "w2_scale");
+    } else {
+        need_dtype(w2, AITER_DTYPE_fp8, "w2");
+        need_dtype(w2_scale, AITER_DTYPE_fp32, "w2_scale");
+        for (auto* t : {w2, w2_scale}) need_contig(t, "operand");
+        AB_CHECK(w2->shape[2] == I, "w2 must be [E, D, I]");
+        AB_CHECK((int64_t)w2_scale->numel_ == (int64_t)E * (D / 128) * (I / 128),
+                 "w2_scale must be [E, D/128, I/128]");
+    }
     AB_CHECK(((uintptr_t)out->ptr & 15) == 0, "out must be 16-byte aligned");
     if (M == 0) return;
     GemmArgs a{};
@@ -892,7 +1057,10 @@ void run_stage2(aiter_tensor_t* a2, aiter_tensor_t* a2_scale, aiter_tensor_t* w2
     a.sorted_eids = (const int*)sorted_expert_ids->ptr;
     a.num_valid = (const int*)num_valid_ids->ptr;
     a.a_scale = (const float*)a2_scale->ptr;
-    a.b_scale = (const float*)w2_scale->ptr;
+    if (w4)
+        a.b_sf = (const uint8_t*)w2_scale->ptr;
+    else
+        a.b_scale = (const float*)w2_scale->ptr;
     a.sorted_w = sorted_weights ? (const float*)sorted_weights->ptr : nullptr;  // none: weight 1
     a.out_f16 = out->dtype_ == AITER_DTYPE_fp16 ? 1 : 0;
     a.out = out->ptr;
@@ -913,8 +1081,13 @@ void run_stage2(aiter_tensor_t* a2, aiter_tensor_t* a2_scale, aiter_tensor_t* w2
     DeviceGuard dg(a2->device_id);
     CUtensorMap tmA, tmB;
     make_tmap_2d_u8(&tmA, a2->ptr, (uint64_t)c.rows_pad, I, 128, 128, true);
-    make_tmap_2d_u8(&tmB, w2->ptr, (uint64_t)E * D, I, 128, 128, true);
-    launch<2, 256>(tmA, tmB, tmA, a, a2->device_id, as_stream(stream));
+    if (w4) {
+        make_tmap_2d_e2m1(&tmB, w2->ptr, (uint64_t)E * D, I, 128);
+        launch<2, 256, true>(tmA, tmB, tmA, a, a2->device_id, as_stream(stream));
+    } else {
+        make_tmap_2d_u8(&tmB, w2->ptr, (uint64_t)E * D, I, 128, 128, true);
+        launch<2, 256, false>(tmA, tmB, tmA, a, a2->device_id, as_stream(stream));
+    }
 }
 }  // namespace
 
@@ -939,6 +1112,32 @@ AB_ENTRY(moe_stage2_fp8_blockscale_bias,
           block_m, bias, stream)) {
     run_stage2(a2, a2_scale, w2, w2_scale, sorted_token_ids, sorted_expert_ids, num_valid_ids, sorted_weights, out,
                block_m, bias, stream);
+}
+
+// A8W4 grouped GEMMs (the MXFP4 path of moe_cktile2stages_gemm1 / gemm2,
+// aiter/ops/moe_op.py:343-465): fp8 1x128 sorted activations x MXFP4 weights kept at
+// 4 bits in HBM, their e8m0 scales (arranged by mxfp4_moe_weight_scale_chunks)
+// applied by tcgen05.mma.kind::mxf8f6f4.block_scale, the activation scales promoted
+// per 128-wide K block as in the FP8 kernels.  Same options as the _bias entries.
+AB_ENTRY(moe_stage1_a8w4,
+         (aiter_tensor_t * a1, aiter_tensor_t* a1_scale, aiter_tensor_t* w1, aiter_tensor_t* w1_scale_chunks,
+          aiter_tensor_t* sorted_token_ids, aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids,
+          aiter_tensor_t* out, aiter_tensor_t* out_scale, int64_t num_tokens, int64_t block_m, int64_t activation,
+          aiter_tensor_t* sorted_weights, int64_t inter_dtype, aiter_tensor_t* bias, void* stream),
+         (a1, a1_scale, w1, w1_scale_chunks, sorted_token_ids, sorted_expert_ids, num_valid_ids, out, out_scale,
+          num_tokens, block_m, activation, sorted_weights, inter_dtype, bias, stream)) {
+    run_stage1(a1, a1_scale, w1, w1_scale_chunks, sorted_token_ids, sorted_expert_ids, num_valid_ids, out, out_scale,
+               num_tokens, block_m, activation, sorted_weights, inter_dtype, bias, stream, true);
+}
+
+AB_ENTRY(moe_stage2_a8w4,
+         (aiter_tensor_t * a2, aiter_tensor_t* a2_scale, aiter_tensor_t* w2, aiter_tensor_t* w2_scale_chunks,
+          aiter_tensor_t* sorted_token_ids, aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids,
+          aiter_tensor_t* sorted_weights, aiter_tensor_t* out, int64_t block_m, aiter_tensor_t* bias, void* stream),
+         (a2, a2_scale, w2, w2_scale_chunks, sorted_token_ids, sorted_expert_ids, num_valid_ids, sorted_weights, out,
+          block_m, bias, stream)) {
+    run_stage2(a2, a2_scale, w2, w2_scale_chunks, sorted_token_ids, sorted_expert_ids, num_valid_ids, sorted_weights,
+               out, block_m, bias, stream, true);
 }
 
 // Error word of every mbarrier wait outside the allreduce context: this unit's

@@ -82,7 +82,43 @@ mxfp4_to_fp8_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ s
     }
 }
 
+// Scale chunks of the native A8W4 GEMMs: for every 128 weight rows x 128 K values,
+// the 128 x 4 e8m0 scales as the 512 bytes tcgen05.cp moves into TMEM (32 lines of 16
+// bytes; line r, word w, byte b = scale of row 32w + r, K group b), laid out
+// [E, N/128, K/128, 512].  grid: (K/128, N/128, E), 128 threads; thread t = row t.
+__global__ void __launch_bounds__(128)
+mxfp4_scale_chunks_kernel(const uint8_t* __restrict__ sc, uint8_t* __restrict__ out, int N, int K) {
+    const int kb = blockIdx.x, nb = blockIdx.y, e = blockIdx.z, t = threadIdx.x;
+    const int gpr = K / 32;
+    const int64_t row = (int64_t)e * N + nb * 128 + t;
+    const uint32_t word = *reinterpret_cast<const uint32_t*>(sc + row * gpr + kb * 4);  // K groups 4kb..4kb+3
+    uint8_t* chunk = out + (((int64_t)e * (N / 128) + nb) * (K / 128) + kb) * 512;
+    *reinterpret_cast<uint32_t*>(chunk + (t & 31) * 16 + (t >> 5) * 4) = word;
+}
+
 }  // namespace
+
+AB_ENTRY(mxfp4_moe_weight_scale_chunks, (aiter_tensor_t * w_scale, aiter_tensor_t* out, void* stream),
+         (w_scale, out, stream)) {
+    using namespace ab;
+    need(w_scale, "w_scale");
+    need(out, "out");
+    AB_CHECK(w_scale->dtype_ == AITER_DTYPE_fp8_e8m0 || w_scale->dtype_ == AITER_DTYPE_u8,
+             "w_scale must be e8m0 (or its uint8 view)");
+    AB_CHECK(out->dtype_ == AITER_DTYPE_fp8_e8m0 || out->dtype_ == AITER_DTYPE_u8, "out must be e8m0 or uint8");
+    need_contig(w_scale, "w_scale");
+    need_contig(out, "out");
+    need_ndim(w_scale, 3, "w_scale");
+    const int E = (int)w_scale->shape[0], N = (int)w_scale->shape[1], K = (int)w_scale->shape[2] * 32;
+    AB_CHECK(N % 128 == 0 && K % 128 == 0, "N and K must be multiples of 128");
+    AB_CHECK((int64_t)out->numel_ == (int64_t)E * (N / 128) * (K / 128) * 512, "out must be [E, N/128, K/128, 512]");
+    AB_CHECK(((uintptr_t)w_scale->ptr & 3) == 0 && ((uintptr_t)out->ptr & 15) == 0, "misaligned buffers");
+    if (E == 0) return;
+    DeviceGuard dg(w_scale->device_id);
+    mxfp4_scale_chunks_kernel<<<dim3(K / 128, N / 128, E), 128, 0, as_stream(stream)>>>(
+        (const uint8_t*)w_scale->ptr, (uint8_t*)out->ptr, N, K);
+    check_launch("mxfp4_moe_weight_scale_chunks");
+}
 
 AB_ENTRY(mxfp4_to_fp8_blockscale,
          (aiter_tensor_t * w_fp4, aiter_tensor_t* w_scale, aiter_tensor_t* out, aiter_tensor_t* out_scale,

@@ -150,6 +150,48 @@ __host__ __device__ constexpr uint32_t idesc_e4m3_f32(int M, int N) {
     return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// Instruction descriptor: kind::mxf8f6f4.block_scale, A = E4M3, B = E2M1 (both K-major),
+// D = F32, UE8M0 scale factors.  Bits 4-5 / 29-30 select the scale byte of B / A (the
+// 32-wide K group inside a scale column); the caller ORs them in per MMA.
+__host__ __device__ constexpr uint32_t idesc_e4m3_e2m1_ue8m0(int M, int N) {
+    return (0u << 7) | (5u << 10) | ((uint32_t)(N >> 3) << 17) | (1u << 23) | ((uint32_t)(M >> 4) << 24);
+}
+
+// D (+)= (A * 2^(sfa - 127)) (B * 2^(sfb - 127)) over K = 32; the scale factors are
+// read from TMEM at `sfa` / `sfb` (one byte per row per 32-wide K group).
+__device__ __forceinline__ void mma_mxf8f6f4_bs(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                                uint32_t sfa, uint32_t sfb, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb));
+}
+
+// Shared-memory matrix descriptor without swizzle: K-major core matrices of 8 rows x
+// 16 bytes, consecutive 8-row groups `sbo` bytes apart.
+__device__ __forceinline__ uint64_t smem_desc_noswz(const void* p, uint32_t sbo) {
+    const uint64_t addr = smem_u32(p);
+    return ((addr & 0x3FFFFull) >> 4) | (1ull << 16) | ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46);
+}
+
+// 32 rows x 128 bits of shared memory -> TMEM lanes 0-31 of every subpartition (the
+// same data four times), 4 columns from `taddr`; ordered with the MMAs this thread
+// issues after it.
+__device__ __forceinline__ void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
+    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// Contiguous global -> shared bulk copy completing on an mbarrier (16-byte aligned,
+// size a multiple of 16).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
 __device__ __forceinline__ void mma_f8f6f4(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                            uint32_t accumulate) {
     asm volatile(
@@ -232,4 +274,8 @@ namespace ab {
 // Host: encode a 2-D tensor map over a row-major [rows, cols] byte matrix.
 void make_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_cols,
                      uint32_t box_rows, bool swizzle128);
+// Host: 2-D tensor map over [rows, k] packed e2m1 values (two per byte), unpacked by
+// the TMA into one byte per value in shared memory (the operand layout of
+// kind::mxf8f6f4 for 4-bit types); boxes of 128 values x box_rows, 128-byte swizzle.
+void make_tmap_2d_e2m1(CUtensorMap* map, const void* base, uint64_t rows, uint64_t k, uint32_t box_rows);
 }  // namespace ab

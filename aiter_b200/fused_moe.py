@@ -206,18 +206,23 @@ def _fused_moe_impl(hidden_states, w1, w2, topk_weight, topk_ids, expert_mask=No
             if b2.shape[1] != model_dim:
                 raise ValueError(f"bias2 must be [E, model_dim], got {tuple(bias2.shape)}")
     global_E = expert_mask.numel() if expert_mask is not None else E
-    if quant_type == QuantType.per_1x32:
-        # A8W4 as BASELINE defines it: fp8 1x128 activations, MXFP4 weights.  The
-        # MXFP4 weights are expanded exactly into the FP8 block-scale format (do this
-        # once with weights.prepare_a8w4 and call with per_1x128 to skip it per call).
+    w4 = quant_type == QuantType.per_1x32
+    if w4:
+        # A8W4: fp8 1x128 activations x MXFP4 weights, which stay at 4 bits; their e8m0
+        # scales are applied by the block-scaled MMA and are taken either as the
+        # reference passes them, [E, N, K/32] (rearranged here by one small kernel),
+        # or already as chunks (weights.prepare_a8w4_native, once).
         from . import weights as _w
         if w1.dtype not in (dtypes.fp4x2, torch.uint8) or w2.dtype not in (dtypes.fp4x2, torch.uint8):
             raise TypeError("per_1x32 needs MXFP4 (fp4x2) weights")
-        w1, w1_scale = _w.mxfp4_to_fp8_blockscale(w1, w1_scale)
-        w2, w2_scale = _w.mxfp4_to_fp8_blockscale(w2, w2_scale)
-        quant_type = QuantType.per_1x128
-    if quant_type == QuantType.per_1x128:
-        if w1.dtype != dtypes.fp8 or w2.dtype != dtypes.fp8:
+        if w1_scale is None or w2_scale is None:
+            raise ValueError("per_1x32 needs the e8m0 scales w1_scale and w2_scale")
+        if not _w.is_scale_chunks(w1_scale):
+            w1_scale = _w.mxfp4_moe_weight_scale_chunks(w1_scale.view(E, w1.shape[1], -1))
+        if not _w.is_scale_chunks(w2_scale):
+            w2_scale = _w.mxfp4_moe_weight_scale_chunks(w2_scale.view(E, w2.shape[1], -1))
+    if quant_type in (QuantType.per_1x128, QuantType.per_1x32):
+        if not w4 and (w1.dtype != dtypes.fp8 or w2.dtype != dtypes.fp8):
             raise TypeError("per_1x128 needs fp8 weights")
         meta = get_2stage_cfgs(get_padded_M(M), model_dim, inter_dim, E, topk, dtype, dtypes.fp8,
                                w1.dtype, quant_type, True, activation, doweight_stage1)
@@ -244,11 +249,11 @@ def _fused_moe_impl(hidden_states, w1, w2, topk_weight, topk_ids, expert_mask=No
         a2s = torch.empty((inter_dim // 128, rows), dtype=dtypes.fp32, device=dev)
         # doweight_stage1: the top-k weight scales the stage-1 GEMM output (before the
         # activation) and stage 2 adds unweighted rows (torch_moe_stage1/2 `doweight`)
-        moe_op.moe_stage1_fp8_blockscale(a1, a1s, w1, w1_scale, sorted_ids, sorted_expert_ids, num_valid_ids,
-                                         a2, a2s, M, block_m, activation,
-                                         sorted_weights=sorted_weights if doweight_stage1 else None,
-                                         inter_dtype=dtype, bias=b1)
-        moe_op.moe_stage2_fp8_blockscale(a2, a2s, w2, w2_scale, sorted_ids, sorted_expert_ids, num_valid_ids,
-                                         None if doweight_stage1 else sorted_weights, moe_buf, block_m, bias=b2)
+        stage1 = moe_op.moe_stage1_a8w4 if w4 else moe_op.moe_stage1_fp8_blockscale
+        stage2 = moe_op.moe_stage2_a8w4 if w4 else moe_op.moe_stage2_fp8_blockscale
+        stage1(a1, a1s, w1, w1_scale, sorted_ids, sorted_expert_ids, num_valid_ids, a2, a2s, M, block_m, activation,
+               sorted_weights=sorted_weights if doweight_stage1 else None, inter_dtype=dtype, bias=b1)
+        stage2(a2, a2s, w2, w2_scale, sorted_ids, sorted_expert_ids, num_valid_ids,
+               None if doweight_stage1 else sorted_weights, moe_buf, block_m, bias=b2)
         return moe_buf
     raise NotImplementedError(f"quant_type {quant_type} is not supported by the B200 path")

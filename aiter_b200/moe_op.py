@@ -246,3 +246,28 @@ def moe_stage2_fp8_blockscale(a2: Tensor, a2_scale: Tensor, w2: Tensor, w2_scale
         _lib.call("moe_stage2_fp8_blockscale", a2, a2_scale, w2, w2_scale, sorted_token_ids, sorted_expert_ids,
                   num_valid_ids, sorted_weights, out, block_m)
     return out
+
+
+def moe_stage1_a8w4(a1: Tensor, a1_scale: Tensor, w1: Tensor, w1_scale_chunks: Tensor,
+                    sorted_token_ids: Tensor, sorted_expert_ids: Tensor, num_valid_ids: Tensor,
+                    out: Tensor, out_scale: Tensor, num_tokens: int, block_m: int = 128,
+                    activation=ActivationType.Silu, sorted_weights: Optional[Tensor] = None,
+                    inter_dtype=dtypes.bf16, bias: Optional[Tensor] = None) -> Tuple[Tensor, Tensor]:
+    """moe_stage1_fp8_blockscale with MXFP4 weights (the A8W4 path of
+    moe_cktile2stages_gemm1, aiter/ops/moe_op.py:343-403): w1 [E, 2I, D/2] fp4x2 kept at
+    4 bits, its e8m0 scales as chunks (weights.mxfp4_moe_weight_scale_chunks)."""
+    _lib.call("moe_stage1_a8w4", a1, a1_scale, w1, w1_scale_chunks, sorted_token_ids, sorted_expert_ids,
+              num_valid_ids, out, out_scale, num_tokens, block_m, int(activation), sorted_weights,
+              _lib.dtype_code(inter_dtype), bias)
+    return out, out_scale
+
+
+def moe_stage2_a8w4(a2: Tensor, a2_scale: Tensor, w2: Tensor, w2_scale_chunks: Tensor,
+                    sorted_token_ids: Tensor, sorted_expert_ids: Tensor, num_valid_ids: Tensor,
+                    sorted_weights: Optional[Tensor], out: Tensor, block_m: int = 128,
+                    bias: Optional[Tensor] = None) -> Tensor:
+    """moe_stage2_fp8_blockscale with MXFP4 weights (the A8W4 path of
+    moe_cktile2stages_gemm2, aiter/ops/moe_op.py:406-465): w2 [E, D, I/2] fp4x2."""
+    _lib.call("moe_stage2_a8w4", a2, a2_scale, w2, w2_scale_chunks, sorted_token_ids, sorted_expert_ids,
+              num_valid_ids, sorted_weights, out, block_m, bias)
+    return out

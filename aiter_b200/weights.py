@@ -117,6 +117,32 @@ def mxfp4_to_fp8_blockscale(w_fp4: torch.Tensor, w_scale: torch.Tensor, check: b
     return out, out_s
 
 
+def mxfp4_moe_weight_scale_chunks(w_scale: torch.Tensor) -> torch.Tensor:
+    """e8m0 scales [E, N, K/32] of MXFP4 weights -> the chunks the native A8W4 GEMMs
+    copy into tensor memory: [E, N/128, K/128, 512] uint8, per 128 weight rows x 128 K
+    values the 128 x 4 scales, line r / word w / byte b = row 32w + r, K group b
+    (CUDA kernel `mxfp4_moe_weight_scale_chunks`).  The role of the reference's
+    e8m0_shuffle of the scales (aiter/utility/fp4_utils.py) for this GEMM."""
+    from . import _lib
+    ws = w_scale.view(torch.uint8) if w_scale.dtype != torch.uint8 else w_scale
+    if ws.dim() != 3:
+        raise ValueError("w_scale must be [E, N, K/32]")
+    E, N, G = ws.shape
+    out = torch.empty((E, N // 128, G * 32 // 128, 512), dtype=torch.uint8, device=ws.device)
+    _lib.call("mxfp4_moe_weight_scale_chunks", ws.contiguous(), out)
+    return out
+
+
+def is_scale_chunks(s: torch.Tensor) -> bool:
+    return s.dim() == 4 and s.shape[-1] == 512
+
+
+def prepare_a8w4_native(w1_fp4, w1_scale, w2_fp4, w2_scale):
+    """One-time preparation for fused_moe(..., quant_type=QuantType.per_1x32): the MXFP4
+    weights unchanged, their scales as chunks (so no call rearranges them)."""
+    return w1_fp4, mxfp4_moe_weight_scale_chunks(w1_scale), w2_fp4, mxfp4_moe_weight_scale_chunks(w2_scale)
+
+
 def prepare_a8w4(w1_fp4, w1_scale, w2_fp4, w2_scale):
     """One-time A8W4 weight preparation (the role of the reference's shuffle_weight):
     returns (w1_fp8, w1_scale_f32, w2_fp8, w2_scale_f32) for

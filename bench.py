@@ -857,10 +857,12 @@ def run_a8w4(args, rank, world, local):
     """Config 2 (A8W4) on one GPU: hidden 4096, inter 2048, E = 256, top-8, MXFP4
     weights (e2m1 + ue8m0 per 32 along K, quantised from N(0,1)/sqrt(K)), fp8 1x128
     activations, skewed routing: N(0,1) logits plus log p_e with p Zipf(s=1.1) over a
-    random expert order.  The MXFP4 weights are expanded once into the fp8
-    block-scale format (`prepare_a8w4`, timed separately); each step is then the
-    device-resident fused MoE.  The HBM fraction uses the algorithmic bytes of the
-    MXFP4 weights (0.5 B + 1/32 B per element) of the experts the batch routes to."""
+    random expert order.  Each step is the device-resident fused MoE on the native
+    A8W4 grouped GEMMs (weights read at 4 bits, e8m0 scales applied by the
+    block-scaled MMA; the scale chunks prepared once).  The HBM fraction uses the
+    algorithmic bytes of the MXFP4 weights (0.5 B + 1/32 B per element) of the experts
+    the batch routes to.  `expanded_fp8_ms`: the same step on the FP8 kernels with the
+    weights expanded once to e4m3 + 128x128 block scales (twice the weight bytes)."""
     import aiter_b200 as aiter
     from aiter_b200 import moe_op, dtypes
     from aiter_b200 import weights as Wt
@@ -883,10 +885,11 @@ def run_a8w4(args, rank, world, local):
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record()
-    w1q, w1s, w2q, w2s = Wt.prepare_a8w4(w1p, w1e, w2p, w2e)
+    _, k1, _, k2 = Wt.prepare_a8w4_native(w1p, w1e, w2p, w2e)
     t1.record()
     torch.cuda.synchronize()
     prep_ms = t0.elapsed_time(t1)
+    w1q, w1s, w2q, w2s = Wt.prepare_a8w4(w1p, w1e, w2p, w2e)
     torch.cuda.empty_cache()
     pk, src = peaks()
     peak_fp8, _ = fp8_peak()
@@ -911,15 +914,34 @@ def run_a8w4(args, rank, world, local):
         a1s = torch.empty(De // 128, max_pad, dtype=torch.float32, device=dev)
         a2 = torch.empty(max_pad, Ie, dtype=dtypes.fp8, device=dev)
         a2s = torch.empty(Ie // 128, max_pad, dtype=torch.float32, device=dev)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
 
-        def step():
+        def front():
             moe_op.moe_sorting_fwd(tid, tw, sid, sw, seid, nv, out, Ee, B, None, None, 0, ws if ws_n else None, pos)
             moe_op.moe_gather_quant_1x128(hid, pos, TOPK, max_pad, out=a1, out_scale=a1s)
+
+        def step():
+            front()
+            moe_op.moe_stage1_a8w4(a1, a1s, w1p, k1, sid, seid, nv, a2, a2s, M, B)
+            moe_op.moe_stage2_a8w4(a2, a2s, w2p, k2, sid, seid, nv, sw, out, B)
+
+        def step_fp8():
+            front()
             moe_op.moe_stage1_fp8_blockscale(a1, a1s, w1q, w1s, sid, seid, nv, a2, a2s, M, B)
             moe_op.moe_stage2_fp8_blockscale(a2, a2s, w2q, w2s, sid, seid, nv, sw, out, B)
 
+        ms_fp8 = _time_loop(step_fp8, args.steps, args.warmup, world)
         ms = _time_loop(step, args.steps, args.warmup, world)
-        # the same step through the public A8W4 call (per-call MXFP4 expansion included)
+        # per-stage split of one native step
+        front()
+        ev[0].record()
+        moe_op.moe_stage1_a8w4(a1, a1s, w1p, k1, sid, seid, nv, a2, a2s, M, B)
+        ev[1].record()
+        moe_op.moe_stage2_a8w4(a2, a2s, w2p, k2, sid, seid, nv, sw, out, B)
+        ev[2].record()
+        torch.cuda.synchronize()
+        s1_ms, s2_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+        # the same step through the public A8W4 call (scales rearranged per call)
         ref = aiter.fused_moe(hid, w1p.view(dtypes.fp4x2), w2p.view(dtypes.fp4x2), tw, tid,
                               quant_type=aiter.QuantType.per_1x32, w1_scale=w1e.view(dtypes.fp8_e8m0),
                               w2_scale=w2e.view(dtypes.fp8_e8m0))
@@ -932,15 +954,17 @@ def run_a8w4(args, rank, world, local):
         tfl = fl / (ms * 1e-3) / 1e12
         gbs = bytes_ / (ms * 1e-3) / 1e9
         rows.append({"M": M, "ms_per_step": round(ms, 4), "tokens_per_s": round(M / (ms * 1e-3), 1),
+                     "stage1_ms": round(s1_ms, 4), "stage2_ms": round(s2_ms, 4),
                      "tflops": round(tfl, 2), "active_experts": active, "tensor_frac": round(tfl / peak_fp8, 4),
-                     "hbm_GBs_algorithmic": round(gbs, 1), "hbm_frac": round(gbs / pk["hbm_gbs"], 4)})
+                     "hbm_GBs_algorithmic": round(gbs, 1), "hbm_frac": round(gbs / pk["hbm_gbs"], 4),
+                     "expanded_fp8_ms": round(ms_fp8, 4)})
     return {"metric": METRIC.replace("E=128", "E=256").replace("inter 1536", "inter 2048").replace(
                 "FP8 blockscale", "A8W4: fp8 activations, MXFP4 weights"),
             "mode": "a8w4", "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-            "higher_is_better": True, "dtype": "fp8-e4m3 x (MXFP4 expanded to fp8 block-scale)",
+            "higher_is_better": True, "dtype": "fp8-e4m3 x e2m1 (kind::mxf8f6f4 block-scaled MMA, fp32 accumulate)",
             "data": "synthetic", "config": {"workload": "BASELINE config 2: A8W4 fused MoE", "hidden": De,
                                             "inter": Ie, "experts": Ee, "topk": TOPK, "routing": "zipf s=1.1 bias"},
-            "weight_prep_ms": round(prep_ms, 2),
+            "scale_prep_ms": round(prep_ms, 3),
             "peaks": {"fp8_tflops": peak_fp8, "hbm_gbs": pk["hbm_gbs"], "source": src}, "sweep": rows}
 
 

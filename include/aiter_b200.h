@@ -214,6 +214,13 @@ int fused_dynamic_mxfp4_quant_moe_sort_hip(aiter_tensor_t* out, aiter_tensor_t* 
 int mxfp4_to_fp8_blockscale(aiter_tensor_t* w_fp4, aiter_tensor_t* w_scale, aiter_tensor_t* out,
                             aiter_tensor_t* out_scale, aiter_tensor_t* status, void* stream);
 
+/* A8W4 scale preparation for the native MXFP4 grouped GEMMs: e8m0 scales [E, N, K/32]
+ * -> chunks [E, N/128, K/128, 512] u8, per 128 weight rows x 128 K values the 128 x 4
+ * scales as the 32 lines of 16 bytes that tcgen05.cp copies into tensor memory (line
+ * r, word w, byte b = scale of row 32w + r, K group b).  The role of the reference's
+ * e8m0_shuffle of the weight scales (aiter/utility/fp4_utils.py) for these kernels. */
+int mxfp4_moe_weight_scale_chunks(aiter_tensor_t* w_scale, aiter_tensor_t* out, void* stream);
+
 /* ---- grouped GEMMs (FP8 block-scale, tcgen05) ----------------------------- */
 
 /* Stage 1: replaces ck_moe_stage1_fwd + the intermediate requant
@@ -276,6 +283,25 @@ int moe_stage2_fp8_blockscale_bias(aiter_tensor_t* a2, aiter_tensor_t* a2_scale,
                                    aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids,
                                    aiter_tensor_t* sorted_weights, aiter_tensor_t* out, int64_t block_m,
                                    aiter_tensor_t* bias, void* stream);
+
+/* A8W4 stages: replace moe_cktile2stages_gemm1 / gemm2 for MXFP4 weights
+ * (aiter/ops/moe_op.py:343-465, called by fused_moe for per_1x32,
+ * aiter/fused_moe.py:985-1008).  Same operands and options as the _bias entries
+ * except the weights: w1 [E, 2 * inter_dim, D/2] / w2 [E, D, inter_dim/2] fp4x2 (e2m1
+ * pairs, low nibble first), read at 4 bits by the TMA, with their scales as chunks
+ * from mxfp4_moe_weight_scale_chunks; the scales are applied by
+ * tcgen05.mma.kind::mxf8f6f4.block_scale, the activations' 1x128 f32 scales promoted
+ * per 128-wide K block.  bias may be NULL. */
+int moe_stage1_a8w4(aiter_tensor_t* a1, aiter_tensor_t* a1_scale, aiter_tensor_t* w1,
+                    aiter_tensor_t* w1_scale_chunks, aiter_tensor_t* sorted_token_ids,
+                    aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids, aiter_tensor_t* out,
+                    aiter_tensor_t* out_scale, int64_t num_tokens, int64_t block_m, int64_t activation,
+                    aiter_tensor_t* sorted_weights, int64_t inter_dtype, aiter_tensor_t* bias, void* stream);
+int moe_stage2_a8w4(aiter_tensor_t* a2, aiter_tensor_t* a2_scale, aiter_tensor_t* w2,
+                    aiter_tensor_t* w2_scale_chunks, aiter_tensor_t* sorted_token_ids,
+                    aiter_tensor_t* sorted_expert_ids, aiter_tensor_t* num_valid_ids,
+                    aiter_tensor_t* sorted_weights, aiter_tensor_t* out, int64_t block_m, aiter_tensor_t* bias,
+                    void* stream);
 
 /* ---- gated activations (the split-K tail of the reference's fused_moe) ----- */
 /* Replace aiter.silu_and_mul / gelu_and_mul / gelu_tanh_and_mul / scaled_silu_and_mul

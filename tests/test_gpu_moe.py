@@ -4,8 +4,9 @@
   outputs (tests/golden, torch_moe_stage1 -> requant -> torch_moe_stage2);
 * shape sweeps against the numpy oracle;
 * the full single-GPU config (D=4096, I=1536, E=128, k=8, M=4096) against a
-  plain fp32 torch reference on a sample of tokens (the MoE is independent per
-  token, so a sample checks the full-size launch).
+  plain fp32 torch reference (its own 1x128 quantiser, dequantised weights,
+  per-expert GEMMs) on a sample of tokens (the MoE is independent per token, so a
+  sample checks the full-size launch).
 Tolerance: rtol = atol = 2e-2 on bf16 outputs, plus at most
 1 % of elements off by more than 1e-2 (op_tests/test_moe_2stage.py:253-269 uses
 1e-2 with a mismatch ratio)."""
@@ -155,10 +156,24 @@ def test_fused_moe_preq_input_and_repeat_calls():
 # --------------------------------------------------------------------- full size
 
 
+def torch_quant_1x128(x):
+    """pertoken_quant over 1x128 groups in plain torch: (dequantised values, e4m3
+    values).  scale = amax / 448 (1 for an all-zero group) and the codes of x / scale,
+    both as IEEE divisions of two tensors, as the reference computes them on the CPU
+    (on CUDA, torch turns a division by a Python scalar into a multiplication by its
+    reciprocal, which can move the scale by one ulp and an exact tie to the other
+    code)."""
+    g = x.float().view(x.shape[0], -1, 128)
+    amax = g.abs().amax(dim=-1, keepdim=True)
+    sc = torch.div(amax, torch.full_like(amax, 448.0))
+    sc = torch.where(sc == 0, torch.ones_like(sc), sc)
+    q = torch.div(g, sc).to(torch.float8_e4m3fn)
+    return (q.float() * sc).view(x.shape[0], -1), q.view(x.shape[0], -1)
+
+
 def torch_reference_tokens(hidden, w1q, w1s, w2q, w2s, tw, tid, tokens):
     """fp32 torch reference of the 2-stage blockscale path for a subset of tokens."""
-    a1q, a1s = aiter.per_group_quant_hip(hidden[tokens], quant_dtype=torch.float8_e4m3fn)
-    a1 = (a1q.float().view(len(tokens), -1, 128) * a1s[..., None]).view(len(tokens), -1)
+    a1, _ = torch_quant_1x128(hidden[tokens])
     outs = []
     I = w2q.shape[2]
     for i, t in enumerate(tokens.tolist()):
@@ -167,12 +182,10 @@ def torch_reference_tokens(hidden, w1q, w1s, w2q, w2s, tw, tid, tokens):
             e = int(tid[t, j])
             w1 = W.dequant_128x128(w1q[e:e + 1], w1s[e:e + 1])[0]
             h = w1 @ a1[i]
-            y = (torch.nn.functional.silu(h[:I]) * h[I:]).to(torch.bfloat16).float()
-            amax = y.view(-1, 128).abs().amax(dim=1, keepdim=True)
-            sc = torch.where(amax == 0, torch.ones_like(amax), amax / 448.0)
-            a2 = ((y.view(-1, 128) / sc).to(torch.float8_e4m3fn).float() * sc).view(-1)
+            y = (torch.nn.functional.silu(h[:I]) * h[I:]).to(torch.bfloat16)
+            a2, _ = torch_quant_1x128(y[None])
             w2 = W.dequant_128x128(w2q[e:e + 1], w2s[e:e + 1])[0]
-            acc += tw[t, j] * (w2 @ a2)
+            acc += tw[t, j] * (w2 @ a2[0])
         outs.append(acc.to(torch.bfloat16).float())
     return torch.stack(outs)
 
