@@ -11,17 +11,17 @@ INT4; unset or NONE leaves the communicator disabled), AITER_QUICK_REDUCE_CAST_B
 sets the registered size (default: the library's qr_max_size()).
 
 Which messages take the quick allreduce rather than the custom IPC allreduce is a
-property of the interconnect: `B200_MIN_BYTES` holds, per world size and level, the
-smallest message at which the quick allreduce was faster than the custom allreduce
-on B200 GPUs (NVLink 5 through NVSwitch), from `bench.py --mode allreduce`; a level
-that never won at a world size is absent, and such messages stay on the custom
-allreduce.
+property of the interconnect: `B200_WINDOWS` holds, per world size and level, the
+range of message sizes in which the quick allreduce was faster than the custom
+allreduce on B200 GPUs (NVLink 5 through NVSwitch), from `bench.py --mode
+allreduce`; a level that never won at a world size is absent, and such messages
+stay on the custom allreduce.
 """
 import dataclasses
 import logging
 import os
 from enum import Enum
-from typing import Optional, Union
+from typing import Optional, Tuple, Union
 
 import torch
 import torch.distributed as dist
@@ -42,13 +42,22 @@ class QuickReduceRegime(Enum):
     NONE = 4
 
 
-# (world size, level) -> smallest message in bytes at which the quick allreduce beat the
-# custom IPC allreduce on B200; measured with bench.py --mode allreduce (fp16 kernels).
-# World size 2: no level won at any size from 64 KB to 256 MB (the custom allreduce ran
-# at 0.46-0.53 of the 770 GB/s peer bandwidth; quantising and decoding cost more than the
-# NVLink bytes they save), so no world-2 entry.  World sizes 4 and 8: not measured yet,
-# no entry.
-B200_MIN_BYTES = {}
+# (world size, level) -> (smallest, largest) message in bytes for which the quick
+# allreduce beat the custom IPC allreduce on B200, measured with bench.py --mode
+# allreduce (fp16 kernels, sizes 64 KB .. 256 MB in powers of two):
+# * world size 2: no level won at any size (the one-shot custom allreduce ran at
+#   0.46-0.53 of the 770 GB/s peer bandwidth; quantising and decoding cost more than the
+#   NVLink bytes they save), so no entry;
+# * world size 8: every level won from 2 MB (where the two-shot's second barrier and
+#   peer reads dominate) up to 4 MB (FP) or 8 MB (FP8, INT6, INT4); from 16 MB on the
+#   custom allreduce was faster again;
+# * world size 4: not measured, no entry.
+B200_WINDOWS = {
+    (8, "FP"): (2 * MB, 4 * MB),
+    (8, "FP8"): (2 * MB, 8 * MB),
+    (8, "INT6"): (2 * MB, 8 * MB),
+    (8, "INT4"): (2 * MB, 8 * MB),
+}
 
 
 @dataclasses.dataclass(frozen=True)
@@ -139,17 +148,17 @@ class QuickAllReduce:
     def use_fp16_kernels(self) -> bool:
         return self.settings.fp16_kernels
 
-    def min_bytes(self) -> Optional[int]:
-        """Smallest message that goes to the quick allreduce at this world size and
-        level, None when the level never beat the custom allreduce on B200."""
-        return B200_MIN_BYTES.get((self.world_size, self.settings.level.name))
+    def window(self) -> Optional[Tuple[int, int]]:
+        """(smallest, largest) message that goes to the quick allreduce at this world
+        size and level, None when the level never beat the custom allreduce on B200."""
+        return B200_WINDOWS.get((self.world_size, self.settings.level.name))
 
     def should_quick_allreduce(self, inp: torch.Tensor) -> bool:
         if self.disabled or inp.dtype not in self.DTYPES or not _dense(inp):
             return False
         nbytes = inp.numel() * inp.element_size()
-        lo = self.min_bytes()
-        return nbytes % 16 == 0 and lo is not None and lo <= nbytes <= self.max_bytes
+        w = self.window()
+        return nbytes % 16 == 0 and w is not None and w[0] <= nbytes <= min(w[1], self.max_bytes)
 
     def quick_all_reduce(self, inp: torch.Tensor, *, out: torch.Tensor = None) -> torch.Tensor:
         """Out-of-place quick allreduce.  Graph capture needs no registration: the

@@ -757,7 +757,7 @@ def run_tp_moe(args, rank, world, local):
                                       "peak": 770.0, "unit": "GB/s", "frac": round(bus / 770.0, 4),
                                       "peak_source": "measured peer copy per direction on this pool "
                                                      "(900 GB/s nominal)",
-                                      "algorithm": "two-shot" if n_bytes > (1 << 20) or world == 2 else "one-shot"}},
+                                      "algorithm": ar_algorithm(n_bytes, world)}},
            "gpu_launches": launches_per_step * K,
            "e2e": {"value": round(M * K / (e2e_ms * 1e-3), 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                    "d2h_bytes_per_step": d2h, "api": "aiter_b200.dist.tensor_model_parallel_fused_moe",
@@ -767,6 +767,14 @@ def run_tp_moe(args, rank, world, local):
            "device_error": bool(err),
            "clocks": clk.summary()}
     return res
+
+
+def ar_algorithm(n_bytes, world):
+    """The form custom_ar_all_reduce picks by size: one-shot always at two ranks, else
+    two-shot above 2 MB (up to four ranks) or 1 MB."""
+    if world == 2:
+        return "one-shot"
+    return "two-shot" if n_bytes > ((2 << 20) if world <= 4 else (1 << 20)) else "one-shot"
 
 
 def ca_error(aiter):

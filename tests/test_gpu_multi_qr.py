@@ -10,8 +10,8 @@ Skipped with fewer than 2 GPUs.
 * graph capture: a captured call replayed with fresh inputs, interleaved with eager
   calls of another size;
 * the communicator front-end: GroupCoordinator.all_reduce takes the quick allreduce
-  when AITER_QUICK_REDUCE_QUANTIZATION names a regime and the B200 crossover table
-  holds an entry for the world size at or below the message, else the custom one.
+  when AITER_QUICK_REDUCE_QUANTIZATION names a regime and the message lies in the B200
+  crossover window of the world size, else the custom one.
 """
 import os
 import sys
@@ -120,28 +120,28 @@ def _worker(rank, world, port):
         assert np.array_equal(static_out.float().cpu().numpy(), _want(xs, 2, torch.bfloat16, False)), rep
         assert np.array_equal(e_out.float().cpu().numpy(), _want(ys, 1, torch.float16, False)), rep
     del g
-    # front-end: with no crossover entry for this world size the message stays on the
-    # custom allreduce (fp32 rank-order sum rounded once); with one, an fp16 message
-    # above it takes the quick allreduce
+    # front-end: with no crossover window for this world size the message stays on the
+    # custom allreduce (fp32 rank-order sum rounded once); inside a window, an fp16
+    # message takes the quick allreduce
     from aiter_b200.dist import quick_all_reduce as qmod
     n = (8 * 1024 * 1024) // 2
     xs = _inputs(n, world, 77, torch.float16)
-    saved = dict(qmod.B200_MIN_BYTES)
+    saved = dict(qmod.B200_WINDOWS)
     try:
-        qmod.B200_MIN_BYTES.pop((world, "INT4"), None)
+        qmod.B200_WINDOWS.pop((world, "INT4"), None)
         y = tp.all_reduce(xs[rank].to(dev))
         torch.cuda.synchronize()
         exact = torch.zeros(n, dtype=torch.float32)
         for t in xs:
             exact += t.float()
         assert torch.equal(y.cpu(), exact.to(torch.float16))
-        qmod.B200_MIN_BYTES[(world, "INT4")] = 1024 * 1024
+        qmod.B200_WINDOWS[(world, "INT4")] = (1024 * 1024, 64 * 1024 * 1024)
         y = tp.all_reduce(xs[rank].to(dev))
         torch.cuda.synchronize()
         assert np.array_equal(y.float().cpu().numpy(), _want(xs, 3, torch.float16, True))
     finally:
-        qmod.B200_MIN_BYTES.clear()
-        qmod.B200_MIN_BYTES.update(saved)
+        qmod.B200_WINDOWS.clear()
+        qmod.B200_WINDOWS.update(saved)
     ps.destroy_model_parallel()
     dist.destroy_process_group()
 

@@ -1,8 +1,8 @@
 """Host logic of QuickAllReduce (aiter_b200/dist/quick_all_reduce.py) on CPU: the
 settings read from the reference's environment variables
 (aiter/dist/device_communicators/quick_all_reduce.py:29-37, 210-233) and the
-eligibility rule (dtype, 16-byte multiple, dense storage, the B200 crossover table,
-the registered size)."""
+eligibility rule (dtype, 16-byte multiple, dense storage, the window of the B200
+crossover table, the registered size)."""
 import pytest
 import torch
 
@@ -44,11 +44,13 @@ def test_settings_from_environment(monkeypatch):
 
 
 def test_crossover_table_decides(monkeypatch):
-    monkeypatch.setattr(qmod, "B200_MIN_BYTES", {(2, "INT4"): 1 * MB, (8, "FP8"): 16 * MB})
+    monkeypatch.setattr(qmod, "B200_WINDOWS", {(2, "INT4"): (1 * MB, 4 * MB), (8, "FP8"): (16 * MB, 64 * MB)})
     q = _enabled(2, "INT4")
     for dtype in (torch.float16, torch.bfloat16):
         assert q.should_quick_allreduce(torch.empty(MB // 2, dtype=dtype))
+        assert q.should_quick_allreduce(torch.empty(4 * MB // 2, dtype=dtype))
         assert not q.should_quick_allreduce(torch.empty(MB // 4, dtype=dtype))
+        assert not q.should_quick_allreduce(torch.empty(8 * MB // 2, dtype=dtype))  # above the window
     q = _enabled(8, "FP8")
     assert q.should_quick_allreduce(torch.empty(16 * MB // 2, dtype=torch.float16))
     assert not q.should_quick_allreduce(torch.empty(8 * MB // 2, dtype=torch.float16))
@@ -56,8 +58,14 @@ def test_crossover_table_decides(monkeypatch):
     assert not _enabled(4, "INT6").should_quick_allreduce(torch.empty(256 * MB // 2, dtype=torch.float16))
 
 
+def test_measured_windows_are_well_formed():
+    for (world, level), (lo, hi) in qmod.B200_WINDOWS.items():
+        assert world in QuickAllReduce.WORLD_SIZES and level in QuickReduceRegime.__members__
+        assert 0 < lo <= hi and lo % 16 == 0
+
+
 def test_eligibility_rules(monkeypatch):
-    monkeypatch.setattr(qmod, "B200_MIN_BYTES", {(2, "INT4"): 1 * MB})
+    monkeypatch.setattr(qmod, "B200_WINDOWS", {(2, "INT4"): (1 * MB, 64 * MB)})
     q = _enabled(2, "INT4", max_bytes=4 * MB)
     assert not q.should_quick_allreduce(torch.empty(2 * MB // 4, dtype=torch.float32))  # dtype
     assert not q.should_quick_allreduce(torch.empty(2 * MB // 2 + 3, dtype=torch.float16))  # 16-byte multiple
