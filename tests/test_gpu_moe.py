@@ -7,7 +7,7 @@
   plain fp32 torch reference (its own 1x128 quantiser, dequantised weights,
   per-expert GEMMs) on a sample of tokens (the MoE is independent per token, so a
   sample checks the full-size launch).
-Tolerance: rtol = atol = 2e-2 on bf16 outputs, plus at most
+Tolerance: rtol = atol = 2e-2 on bf16 outputs (the path's stated tolerance), plus at most
 1 % of elements off by more than 1e-2 (op_tests/test_moe_2stage.py:253-269 uses
 1e-2 with a mismatch ratio)."""
 import numpy as np
