@@ -188,52 +188,55 @@ template <typename T, bool PREQ>
 __global__ void __launch_bounds__(256)
 scatter_quant_kernel(const T* __restrict__ x, const float* __restrict__ xs, const int* __restrict__ pos,
                      uint8_t* __restrict__ q, float* __restrict__ st, int M, int K, int topk, int rows_pad) {
+    // 8 lanes per 128-wide group, 16 values (one 16-byte fp8 store per sorted row) each
     const int gpr = K / 128;
-    const int64_t total_lanes = (int64_t)M * gpr * 16;
+    const int64_t total_lanes = (int64_t)M * gpr * 8;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < ((total_lanes + 31) / 32) * 32;
          t += stride) {
-        const int64_t g = t >> 4;
-        const int sub = (int)(t & 15);
+        const int64_t g = t >> 3;
+        const int sub = (int)(t & 7);
         const bool on = t < total_lanes;
         const int tok = on ? (int)(g / gpr) : 0;
         const int c = on ? (int)(g % gpr) : 0;
-        uint2 packed = make_uint2(0, 0);
+        uint4 packed = make_uint4(0, 0, 0, 0);
         float scale = 0.f;
         if constexpr (PREQ) {
             if (on) {
-                packed = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint8_t*>(x) + (int64_t)tok * K + c * 128 + sub * 8);
+                packed = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(x) + (int64_t)tok * K + c * 128 + sub * 16);
                 scale = xs[(int64_t)tok * gpr + c];
             }
         } else {
-            float v[8];
+            float v[16];
             if (on) {
-                Vec8<T>::load(x + (int64_t)tok * K + c * 128 + sub * 8, v);
+                const T* src = x + (int64_t)tok * K + c * 128 + sub * 16;
+                Vec8<T>::load(src, *reinterpret_cast<float(*)[8]>(&v[0]));
+                Vec8<T>::load(src + 8, *reinterpret_cast<float(*)[8]>(&v[8]));
             } else {
 #pragma unroll
-                for (int i = 0; i < 8; ++i) v[i] = 0.f;
+                for (int i = 0; i < 16; ++i) v[i] = 0.f;
             }
             float amax = 0.f;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+            for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
 #pragma unroll
-            for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            for (int o = 4; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
             scale = amax / 448.0f;
             if (scale == 0.f) scale = 1.0f;
-            uint32_t w[2];
+            uint32_t w[4];
 #pragma unroll
-            for (int i = 0; i < 2; ++i) {
+            for (int i = 0; i < 4; ++i) {
                 __nv_fp8x4_e4m3 p4(make_float4(v[4 * i] / scale, v[4 * i + 1] / scale, v[4 * i + 2] / scale,
                                                v[4 * i + 3] / scale));
                 w[i] = *reinterpret_cast<uint32_t*>(&p4);
             }
-            packed = make_uint2(w[0], w[1]);
+            packed = make_uint4(w[0], w[1], w[2], w[3]);
         }
         if (!on) continue;
         for (int s = 0; s < topk; ++s) {
             const int r = pos[(int64_t)tok * topk + s];
             if (r < 0 || r >= rows_pad) continue;
-            *reinterpret_cast<uint2*>(q + (int64_t)r * K + c * 128 + sub * 8) = packed;
+            *reinterpret_cast<uint4*>(q + (int64_t)r * K + c * 128 + sub * 16) = packed;
             if (sub == 0) st[(int64_t)c * rows_pad + r] = scale;
         }
     }
@@ -274,7 +277,7 @@ AB_ENTRY(moe_gather_quant_1x128,
     if (M == 0 || rows_pad == 0) return;
     DeviceGuard dg(hidden->device_id);
     const int dev = hidden->device_id;
-    const int64_t lanes = (int64_t)M * (K / 128) * 16;
+    const int64_t lanes = (int64_t)M * (K / 128) * 8;
     const int blocks = (int)std::min<int64_t>((lanes + 255) / 256, (int64_t)num_sms(dev) * 8);
     cudaStream_t st = as_stream(stream);
     const int* pos = (const int*)token_sorted_pos->ptr;
