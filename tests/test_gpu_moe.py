@@ -262,3 +262,59 @@ def test_fused_moe_expert_parallel_partials_sum_to_full():
     check_no_device_error()
     # the partials are bf16-rounded before the sum
     assert_moe_close(total.cpu().numpy(), full.float().cpu().numpy())
+
+
+def test_fused_moe_graph_replay_matches_eager():
+    """The four kernels of a step (sorting, gather-quant, stage 1, stage 2) captured in a
+    CUDA graph and replayed with new routing and activations copied into the static
+    inputs give the eager results (the graph replay the token sweep of bench.py times)."""
+    from aiter_b200 import moe_op
+    M, D, I, E, k = 96, 1024, 512, 16, 4
+    cases = [inputs.make_moe_case(40 + i, M, D, I, E, k) for i in range(3)]
+    c0 = cases[0]
+    w1, w2 = fp8_from_codes(c0["w1_q"]), fp8_from_codes(c0["w2_q"])
+    w1s, w2s = to_dev(c0["w1_s"]), to_dev(c0["w2_s"])
+    hid = to_dev(c0["hidden"], torch.bfloat16).clone()
+    tw, tid = to_dev(c0["topk_weights"]).clone(), to_dev(c0["topk_ids"]).clone()
+    B = 128
+    max_pad = M * k + E * B - k
+    sid = torch.empty(max_pad, dtype=torch.int32, device=dev())
+    sw = torch.empty(max_pad, dtype=torch.float32, device=dev())
+    seid = torch.empty((max_pad + B - 1) // B, dtype=torch.int32, device=dev())
+    nv = torch.empty(2, dtype=torch.int32, device=dev())
+    pos = torch.empty(M * k, dtype=torch.int32, device=dev())
+    out = torch.empty(M, D, dtype=torch.bfloat16, device=dev())
+    ws_n = moe_op.moe_sorting_get_workspace_size(M, E, k, 0)
+    ws = torch.empty(max(ws_n, 1), dtype=torch.uint8, device=dev())
+    a1 = torch.empty(max_pad, D, dtype=torch.float8_e4m3fn, device=dev())
+    a1s = torch.empty(D // 128, max_pad, dtype=torch.float32, device=dev())
+    a2 = torch.empty(max_pad, I, dtype=torch.float8_e4m3fn, device=dev())
+    a2s = torch.empty(I // 128, max_pad, dtype=torch.float32, device=dev())
+
+    def step():
+        moe_op.moe_sorting_fwd(tid, tw, sid, sw, seid, nv, out, E, B, None, None, 0, ws if ws_n else None, pos)
+        moe_op.moe_gather_quant_1x128(hid, pos, k, max_pad, out=a1, out_scale=a1s)
+        moe_op.moe_stage1_fp8_blockscale(a1, a1s, w1, w1s, sid, seid, nv, a2, a2s, M, B)
+        moe_op.moe_stage2_fp8_blockscale(a2, a2s, w2, w2s, sid, seid, nv, sw, out, B)
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()  # kernels loaded and attributes set before capture
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            step()
+    torch.cuda.current_stream().wait_stream(s)
+    for c in cases:
+        hid.copy_(to_dev(c["hidden"], torch.bfloat16))
+        tw.copy_(to_dev(c["topk_weights"]))
+        tid.copy_(to_dev(c["topk_ids"]))
+        g.replay()
+        torch.cuda.synchronize()
+        check_no_device_error()
+        eager = aiter.fused_moe(to_dev(c["hidden"], torch.bfloat16), w1, w2, to_dev(c["topk_weights"]),
+                                to_dev(c["topk_ids"]), quant_type=aiter.QuantType.per_1x128, w1_scale=w1s,
+                                w2_scale=w2s)
+        torch.cuda.synchronize()
+        assert_moe_close(out.float().cpu().numpy(), eager.float().cpu().numpy())
+    del g
