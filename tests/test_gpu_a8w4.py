@@ -226,3 +226,28 @@ def test_fused_moe_a8w4_full_size_config2(M, config2_weights):
     assert diff <= 5e-4 * total, f"{diff} of {total} intermediate codes differ"
     assert_moe_close(out[tokens].float().cpu().numpy(), ref.cpu().numpy())
     assert torch.isfinite(out.float()).all()
+
+
+@pytest.mark.parametrize("opt", ["gelu", "swiglu", "doweight", "fp16"])
+def test_native_a8w4_options_match_expanded_fp8(opt):
+    """Every fused_moe option on the native A8W4 kernels against the FP8 kernels run on
+    the exactly expanded weights (whose options are checked against the reference's
+    pipeline and the oracle in test_gpu_moe_options.py), rtol = atol = 2e-2."""
+    c = inputs.make_moe_case(60, 160, 2048, 768, 16, 4, wfmt="mxfp4", zipf_s=1.1)
+    w1p, w1s, w2p, w2s = _prep(c)
+    w1, s1, w2, s2 = W.prepare_a8w4(w1p, w1s, w2p, w2s)
+    tdt = torch.float16 if opt == "fp16" else torch.bfloat16
+    act = {"gelu": aiter.ActivationType.Gelu, "swiglu": aiter.ActivationType.Swiglu}.get(opt,
+                                                                                        aiter.ActivationType.Silu)
+    kw = dict(activation=act, doweight_stage1=opt == "doweight")
+    hidden = to_dev(c["hidden"], tdt)
+    tw, tid = to_dev(c["topk_weights"]), to_dev(c["topk_ids"])
+    native = aiter.fused_moe(hidden, w1p.view(torch.float4_e2m1fn_x2), w2p.view(torch.float4_e2m1fn_x2), tw, tid,
+                             quant_type=aiter.QuantType.per_1x32, w1_scale=w1s.view(torch.float8_e8m0fnu),
+                             w2_scale=w2s.view(torch.float8_e8m0fnu), **kw)
+    expanded = aiter.fused_moe(hidden, w1, w2, tw, tid, quant_type=aiter.QuantType.per_1x128, w1_scale=s1,
+                               w2_scale=s2, **kw)
+    torch.cuda.synchronize()
+    check_no_device_error()
+    assert native.dtype == tdt and expanded.dtype == tdt
+    assert_moe_close(native.float().cpu().numpy(), expanded.float().cpu().numpy())
