@@ -410,17 +410,21 @@ def run_b200(args, rank, world, local):
     return res, x
 
 
-def _e2e_pipelined(call, x, h_hidden, h_tw, h_tid, ref_out, K, W, world):
+def _e2e_pipelined(call, x, h_hidden, h_tw, h_tid, ref_out, K, W, world, out_rows=None):
     """ms of K calls `call(hidden, topk_weights, topk_ids) -> output` from pinned host
     buffers with double-buffered device inputs: step i's H2D (copy stream) overlaps
     step i-1's compute and step i-2's D2H (second copy stream).  Events order each
     buffer's reuse; the last step's output is checked against the device-resident
-    result."""
+    result.  `out_rows` = (lo, hi): copy out only those rows of the output (and check
+    them)."""
     dev = x["hidden"].device
+    lo, hi = out_rows if out_rows is not None else (0, ref_out.shape[0])
+    ref_out = ref_out[lo:hi]
     cmp = torch.cuda.current_stream()
     s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
-    d_in = [(torch.empty_like(x["hidden"]), torch.empty_like(x["tw"]), torch.empty_like(x["tid"])) for _ in range(2)]
-    h_out = [torch.empty(ref_out.shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    d_in = [(torch.empty(h_hidden.shape, dtype=h_hidden.dtype, device=dev), torch.empty_like(x["tw"]),
+             torch.empty_like(x["tid"])) for _ in range(2)]
+    h_out = [torch.empty(ref_out.shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)]  # rows lo..hi
     done_cmp = [torch.cuda.Event() for _ in range(2)]
     done_in = [torch.cuda.Event() for _ in range(2)]
     done_out = [torch.cuda.Event() for _ in range(2)]
@@ -444,7 +448,7 @@ def _e2e_pipelined(call, x, h_hidden, h_tw, h_tid, ref_out, K, W, world):
             done_cmp[b].record(cmp)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(done_cmp[b])
-                h_out[b].copy_(o, non_blocking=True)
+                h_out[b].copy_(o[lo:hi], non_blocking=True)
                 o.record_stream(s_out)
                 done_out[b].record(s_out)
             used[b] = True
@@ -726,15 +730,32 @@ def run_tp_moe(args, rank, world, local):
     ref_f = ref.float()
     close = bool(torch.allclose(h_out.to(dev).float(), ref_f, atol=2e-2, rtol=2e-2))
     max_diff = float((h_out.to(dev).float() - ref_f).abs().max())
-    h2d = h_hidden.numel() * 2 + h_tw.numel() * 4 + h_tid.numel() * 4
-    d2h = h_out.numel() * 2
-    e2e_mode = "pipelined: H2D of step i+1 and D2H of step i-1 on their own streams overlap step i, every rank"
-    pip_ms, pip_err = _e2e_pipelined(lambda h, tw, tid: tensor_model_parallel_fused_moe(h, l1, l2, tw, tid, **kw),
-                                     x, h_hidden, h_tw, h_tid, ref_f, K, args.warmup, world)
+    # The input a step needs is the same on every rank and its result is identical on
+    # every rank after the allreduce, so the end-to-end loop moves each byte across
+    # PCIe once: rank r copies rows [r M/N, (r+1) M/N) of the hidden states in (plus
+    # the routing), the IPC all-gather assembles the full batch on every rank, and
+    # rank r copies the same rows of the result out, so the host receives all M rows.
+    # (The loop above, which copies the whole input into and the whole output out of
+    # every rank, is `replicated_value`.)
+    rows = M // world
+    h_slice = h_hidden[rank * rows:(rank + 1) * rows].clone().pin_memory()
+    h2d = h_slice.numel() * 2 + h_tw.numel() * 4 + h_tid.numel() * 4
+    d2h = rows * D * 2
+    e2e_mode = ("sharded: rank r copies rows [r M/N, (r+1) M/N) of the input in and of the output out, the "
+                "IPC all-gather assembles the input on every rank; pipelined over two copy streams")
+
+    def tp_call(h_part, tw, tid):
+        full = tp.all_gather(h_part, use_custom=True, dim=0)
+        return tensor_model_parallel_fused_moe(full, l1, l2, tw, tid, **kw)
+
+    pip_ms, pip_err = _e2e_pipelined(tp_call, x, h_slice, h_tw, h_tid, ref_f, K, args.warmup, world,
+                                     out_rows=(rank * rows, (rank + 1) * rows))
     if max_over_ranks(0.0 if pip_err is None else 1.0, world) > 0:
         e2e_ms = e2e_serial_ms
+        h2d = h_hidden.numel() * 2 + h_tw.numel() * 4 + h_tid.numel() * 4
+        d2h = h_out.numel() * 2
         why = f"{type(pip_err).__name__}: {pip_err}" if pip_err is not None else "on another rank"
-        e2e_mode = f"serial (pipelined loop failed: {why})"[:300]
+        e2e_mode = f"serial, replicated inputs (sharded pipelined loop failed: {why})"[:300]
     else:
         e2e_ms = max_over_ranks(pip_ms, world)
 
@@ -769,8 +790,9 @@ def run_tp_moe(args, rank, world, local):
                                       "algorithm": ar_algorithm(n_bytes, world)}},
            "gpu_launches": launches_per_step * K,
            "e2e": {"value": round(M * K / (e2e_ms * 1e-3), 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                   "d2h_bytes_per_step": d2h, "api": "aiter_b200.dist.tensor_model_parallel_fused_moe",
-                   "copies": e2e_mode, "serial_value": round(M * K / (e2e_serial_ms * 1e-3), 1),
+                   "d2h_bytes_per_step": d2h, "bytes_are": "per rank (each of the N ranks moves the same amount)",
+                   "api": "aiter_b200.dist.tensor_model_parallel_fused_moe (after tensor_model_parallel_all_gather)",
+                   "copies": e2e_mode, "replicated_value": round(M * K / (e2e_serial_ms * 1e-3), 1),
                    "matches_device_run": close, "max_abs_diff_vs_device_run": max_diff},
            "nccl_allreduce_arm": {"ms_per_step": round(ms_nccl, 4), "value": round(M / (ms_nccl * 1e-3), 1)},
            "device_error": bool(err),
